@@ -1,0 +1,203 @@
+// The C ABI (include/hat_b200.h): exception-to-error-code translation around the
+// engine and the kernel launchers.
+#include <cstdarg>
+#include <cstring>
+#include <memory>
+#include <string>
+
+#include "../../include/hat_b200.h"
+#include "engine.h"
+
+using namespace hat;
+
+struct hat_b200 {
+    std::unique_ptr<Engine> eng;
+};
+
+static void set_err(char* err, size_t errlen, const std::string& msg) {
+    if (!err || errlen == 0) return;
+    size_t n = msg.size() < errlen - 1 ? msg.size() : errlen - 1;
+    memcpy(err, msg.data(), n);
+    err[n] = 0;
+}
+
+template <class F>
+static int guarded(char* err, size_t errlen, F&& f) {
+    try {
+        f();
+        set_err(err, errlen, "");
+        return HAT_B200_OK;
+    } catch (const Error& e) {
+        set_err(err, errlen, e.what());
+        return e.code ? e.code : HAT_B200_EINVAL;
+    } catch (const std::exception& e) {
+        set_err(err, errlen, e.what());
+        return HAT_B200_EINVAL;
+    }
+}
+
+static void fill_info(const Weights& wt, hat_b200_info* o) {
+    memset(o, 0, sizeof *o);
+    o->scale = wt.scale;
+    o->window = wt.window;
+    o->owin = wt.owin;
+    o->embed = wt.embed;
+    o->heads = wt.heads;
+    o->head_dim = wt.head_dim;
+    o->mlp_ratio = wt.mlp_ratio;
+    o->compressed = wt.compressed;
+    o->squeezed = wt.squeezed;
+    o->head_feat = wt.head_feat;
+    o->n_stages = (int)wt.depths.size();
+    for (int d : wt.depths) o->n_blocks += d;
+    o->conv_scale = wt.conv_scale;
+    o->img_range = wt.img_range;
+    for (int i = 0; i < 3; ++i) o->mean[i] = wt.mean[i];
+    snprintf(o->variant, sizeof o->variant, "%s", wt.variant.c_str());
+}
+
+extern "C" {
+
+int hat_b200_create(const char* path, const hat_b200_opts* opts, hat_b200** out, char* err, size_t errlen) {
+    if (!path || !out) {
+        set_err(err, errlen, "hat_b200_create: null path or out");
+        return HAT_B200_EINVAL;
+    }
+    *out = nullptr;
+    hat_b200_opts o{0, HAT_B200_MODE_PARITY, 1, 0};
+    if (opts) o = *opts;
+    return guarded(err, errlen, [&] {
+        auto* h = new hat_b200;
+        try {
+            h->eng.reset(new Engine(path, o.device, o.mode, o.use_graph != 0, o.simt_only != 0));
+        } catch (...) {
+            delete h;
+            throw;
+        }
+        *out = h;
+    });
+}
+
+void hat_b200_destroy(hat_b200* h) { delete h; }
+
+int hat_b200_get_info(const hat_b200* h, hat_b200_info* out) {
+    if (!h || !out) return HAT_B200_EINVAL;
+    fill_info(h->eng->weights(), out);
+    return HAT_B200_OK;
+}
+
+// Checkpoint inspection without a device: what --list-weights and the loader tests use.
+int hat_b200_inspect(const char* path, hat_b200_info* out, char* err, size_t errlen) {
+    return guarded(err, errlen, [&] {
+        Weights wt;
+        wt.load(path ? path : "");
+        if (out) fill_info(wt, out);
+    });
+}
+
+int hat_b200_forward(hat_b200* h, int n, int height, int width, const float* in, float* out, char* err,
+                     size_t errlen) {
+    if (!h || !in || !out) {
+        set_err(err, errlen, "hat_b200_forward: null handle or buffer");
+        return HAT_B200_EINVAL;
+    }
+    return guarded(err, errlen, [&] { h->eng->forward_host(n, height, width, in, out); });
+}
+
+int hat_b200_forward_device(hat_b200* h, int n, int height, int width, const float* d_in, float* d_out,
+                            void* stream, char* err, size_t errlen) {
+    if (!h || !d_in || !d_out) {
+        set_err(err, errlen, "hat_b200_forward_device: null handle or buffer");
+        return HAT_B200_EINVAL;
+    }
+    return guarded(err, errlen, [&] {
+        h->eng->forward_device(n, height, width, d_in, d_out, (cudaStream_t)stream);
+    });
+}
+
+size_t hat_b200_footprint_bytes(const hat_b200* h, int height, int width) {
+    if (!h || height <= 0 || width <= 0) return 0;
+    return h->eng->footprint_bytes(height, width);
+}
+
+int hat_b200_check_memory(const hat_b200* h, int height, int width, char* err, size_t errlen) {
+    if (!h) return HAT_B200_EINVAL;
+    return guarded(err, errlen, [&] { h->eng->check_memory(height, width); });
+}
+
+int hat_b200_free_vram(int device, size_t* free_bytes, size_t* total_bytes) {
+    int prev = 0;
+    if (cudaGetDevice(&prev) != cudaSuccess) return HAT_B200_ECUDA;
+    if (cudaSetDevice(device) != cudaSuccess) return HAT_B200_ECUDA;
+    size_t f = 0, t = 0;
+    cudaError_t e = cudaMemGetInfo(&f, &t);
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) return HAT_B200_ECUDA;
+    if (free_bytes) *free_bytes = f;
+    if (total_bytes) *total_bytes = t;
+    return HAT_B200_OK;
+}
+
+int hat_b200_probe(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return 0;
+    }
+    cudaDeviceProp p;
+    if (cudaGetDeviceProperties(&p, 0) != cudaSuccess) return 0;
+    return p.major == 10 ? 1 : 0;
+}
+
+uint64_t hat_b200_launch_count(const hat_b200* h) { return h ? h->eng->launches() : 0; }
+
+int hat_b200_profile(hat_b200* h, int height, int width, char* json, size_t jsonlen, char* err, size_t errlen) {
+    if (!h) return HAT_B200_EINVAL;
+    return guarded(err, errlen, [&] {
+        std::string j = h->eng->profile(height, width);
+        set_err(json, jsonlen, j);
+    });
+}
+
+int hat_b200_linear(int mode, const float* x, const float* w, const float* b, float* y, int m, int n, int k,
+                    void* stream) {
+    return guarded(nullptr, 0, [&] {
+        Epi e;
+        e.bias = b;
+        launch_linear(mode, x, w, y, m, n, k, e, (cudaStream_t)stream);
+    });
+}
+
+int hat_b200_conv3x3(int mode, const float* x, const float* w, const float* b, float* y, int hgt, int wid,
+                     int cin, int cout, void* stream) {
+    return guarded(nullptr, 0, [&] {
+        cudaStream_t st = (cudaStream_t)stream;
+        float* wr = nullptr;
+        HAT_CUDA(cudaMallocAsync(&wr, (size_t)cout * cin * 9 * sizeof(float), st));
+        launch_reorder_conv(w, wr, cout, cin, st);
+        Epi e;
+        e.bias = b;
+        launch_conv3x3(mode, x, wr, y, hgt, wid, cin, cout, e, st);
+        HAT_CUDA(cudaFreeAsync(wr, st));
+    });
+}
+
+int hat_b200_window_attention(int mode, const float* qkv, const float* table, float* out, int hp, int wp, int c,
+                              int heads, int shift, void* stream) {
+    return guarded(nullptr, 0, [&] {
+        Plan p = Plan::make(hp, wp, 16);
+        if (p.hp != hp || p.wp != wp) throw Error(1, "window attention: plane is not a window multiple");
+        launch_window_attention(mode, qkv, table, out, p, c, heads, shift, (cudaStream_t)stream);
+    });
+}
+
+int hat_b200_overlap_attention(int mode, const float* qkv, const float* table, float* out, int hp, int wp,
+                               int c, int heads, void* stream) {
+    return guarded(nullptr, 0, [&] {
+        Plan p = Plan::make(hp, wp, 16);
+        if (p.hp != hp || p.wp != wp) throw Error(1, "overlap attention: plane is not a window multiple");
+        launch_overlap_attention(mode, qkv, table, out, p, c, heads, (cudaStream_t)stream);
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,115 @@
+// Shared definitions of the B200 HAT backend: error plumbing, the plane geometry and
+// the kernel entry points every layer of the scheduler calls.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <cstdio>
+#include <stdexcept>
+#include <string>
+
+namespace hat {
+
+struct Error : std::runtime_error {
+    int code;
+    Error(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+#define HAT_CUDA(call)                                                                   \
+    do {                                                                                 \
+        cudaError_t e_ = (call);                                                         \
+        if (e_ != cudaSuccess)                                                           \
+            throw ::hat::Error(3, std::string(#call) + ": " + cudaGetErrorString(e_));   \
+    } while (0)
+
+// The padded geometry of one pass (src/plan.rs:32-113): the plane is padded to a
+// window multiple, `shift = win/2`, the OCAB window is `win + win/2` with `opad` on
+// each side.
+struct Plan {
+    int h = 0, w = 0;    // the caller's image
+    int hp = 0, wp = 0;  // padded to window multiples
+    int win = 16, shift = 8, owin = 24, opad = 4;
+    int nx() const { return wp / win; }
+    int ny() const { return hp / win; }
+    int nw() const { return nx() * ny(); }
+    long tokens() const { return (long)hp * wp; }
+    static Plan make(int h, int w, int win) {
+        Plan p;
+        p.h = h;
+        p.w = w;
+        p.win = win;
+        p.hp = (h + win - 1) / win * win;
+        p.wp = (w + win - 1) / win * win;
+        p.shift = win / 2;
+        p.owin = win + win / 2;
+        p.opad = (p.owin - win) / 2;
+        return p;
+    }
+    bool operator==(const Plan& o) const { return h == o.h && w == o.w && hp == o.hp && wp == o.wp && win == o.win; }
+};
+
+// ---------------------------------------------------------------- epilogues
+// What a GEMM-shaped kernel does with its fp32 accumulator before the store.
+enum Act : int { ACT_NONE = 0, ACT_GELU = 1, ACT_LEAKY = 2 };
+
+struct Epi {
+    const float* bias = nullptr;   // [n]
+    int act = ACT_NONE;            // applied to acc + bias
+    // residual: out = res + v, or the HAB sum out = (res + v) + (cx * gate) * cscale
+    const float* res = nullptr;    // [m][ldo] (may alias out)
+    const float* cx = nullptr;     // [m][ldo] the CAB output (HAB sum only)
+    const float* gate = nullptr;   // [n] channel-attention gate (HAB sum only)
+    float cscale = 0.f;
+    // channel sums of the stored value (the channel attention's average pool)
+    float* colsum = nullptr;       // [n], accumulated with atomics
+    // PixelShuffle(r) on store: channel n = c*r*r + i*r + j of pixel (y, x) goes to
+    // channel c of pixel (r*y + i, r*x + j) of a [hgt*r][wid*r][n/(r*r)] plane.
+    int shuffle = 0;
+    // Final store: crop to (oh, ow), `v / img_range + mean[n]`, planar [n][oh][ow].
+    int planar_out = 0;
+    int oh = 0, ow = 0;
+    float img_range = 1.f, mean[3] = {0, 0, 0};
+};
+
+// ---------------------------------------------------------------- kernels (launchers)
+// All launchers enqueue on `st` and throw hat::Error on a launch failure. `launches`
+// counts kernels issued (the reference's `launched()`, src/cuda.rs:542-555).
+extern thread_local uint64_t* g_launch_counter;
+inline void count_launch(int n = 1) {
+    if (g_launch_counter) *g_launch_counter += n;
+}
+
+// planar [3][h][w] in [0,1] → token-major [hp][wp][3], edge-replicated and
+// mean-adjusted (src/backend.rs:71-89).
+void launch_pre(const float* in, float* out, const Plan& p, const float mean[3], float img_range,
+                cudaStream_t st);
+
+// LayerNorm over the channel axis of a [m][c] token plane (src/cpu.rs:563-581).
+void launch_layernorm(const float* x, const float* g, const float* b, float* y, long m, int c,
+                      cudaStream_t st);
+
+// y[m][n] = epi(x[m][:k] . w[n][:k]) with w [n][k] row-major.
+void launch_linear(int mode, const float* x, const float* w, float* y, long m, int n, int k,
+                   const Epi& e, cudaStream_t st);
+
+// 3x3 conv (zero pad 1) of a token plane [hgt][wid][cin]; `wr` is the weight
+// reordered to [cout][9][cin] (tap-major K).
+void launch_conv3x3(int mode, const float* x, const float* wr, float* y, int hgt, int wid,
+                    int cin, int cout, const Epi& e, cudaStream_t st);
+
+// Reorder a PyTorch [cout][cin][3][3] conv weight into [cout][9][cin].
+void launch_reorder_conv(const float* w, float* wr, int cout, int cin, cudaStream_t st);
+
+// Window attention of one HAB over the [hp][wp][3c] qkv plane (hat_arch.py:165-196).
+void launch_window_attention(int mode, const float* qkv, const float* table, float* out,
+                             const Plan& p, int c, int heads, int shift, cudaStream_t st);
+
+// OCAB attention over the [hp][wp][3c] qkv plane (hat_arch.py:392-438).
+void launch_overlap_attention(int mode, const float* qkv, const float* table, float* out,
+                              const Plan& p, int c, int heads, cudaStream_t st);
+
+// gate[c] = sigmoid(W2 relu(W1 (sum / count) + b1) + b2) (hat_arch.py:40-57).
+void launch_ca_gate(const float* sums, float inv_count, const float* w1, const float* b1,
+                    const float* w2, const float* b2, float* gate, int c, int sq, cudaStream_t st);
+
+}  // namespace hat

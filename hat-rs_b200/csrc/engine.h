@@ -1,0 +1,83 @@
+// The layer scheduler: the HAT graph as a sequence of fused kernel launches on one
+// stream of one device (the role of src/gpu.rs in the reference).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "weights.h"
+
+namespace hat {
+
+// Every device buffer one pass needs, as one list used both to allocate and to
+// predict (the reference's `Sizes`, src/gpu.rs:166-290): a pass allocates exactly
+// `total()` floats, and the memory guard refuses on the same number.
+struct Sizes {
+    long x0 = 0, body = 0, xa = 0, xb = 0, n1 = 0, cmid = 0, convx = 0, qkv = 0, attn = 0, hid = 0;
+    long chsum = 0, gate = 0, headA = 0, headB = 0, din = 0, dout = 0;
+    static Sizes of(const Weights& wt, const Plan& p);
+    long total() const {
+        return x0 + body + xa + xb + n1 + cmid + convx + qkv + attn + hid + chsum + gate + headA + headB + din + dout;
+    }
+};
+
+class Engine {
+public:
+    Engine(const std::string& path, int device, int mode, bool use_graph, bool simt_only);
+    ~Engine();
+    const Weights& weights() const { return wt_; }
+    int device() const { return device_; }
+    // Host in / host out (Backend::forward).
+    void forward_host(int n, int h, int w, const float* in, float* out);
+    // Device in / device out, enqueued on `st` (nullptr: the engine's stream).
+    void forward_device(int n, int h, int w, const float* din, float* dout, cudaStream_t st);
+    size_t footprint_bytes(int h, int w) const;
+    void check_memory(int h, int w) const;  // throws Error(4, refusal) when it does not fit
+    uint64_t launches() const { return launches_; }
+    // Per-kind device time of one eager pass, as JSON (see Engine::profile).
+    std::string profile(int h, int w);
+    cudaStream_t stream() const { return stream_; }
+
+private:
+    struct Acts;
+    void ensure_plan(int h, int w);
+    void run_graph(cudaStream_t run);  // the whole pass over the internal din/dout buffers
+    void enqueue_pass();     // the launch sequence itself
+    void hab(int stage, int blk, const float* in, float* out);
+    void ocab(int stage, const float* in, float* out);
+    void mlp(const std::string& p, float* x);
+    void mark(const char* kind, double flops, double bytes);
+    const float* W(const std::string& name) const;
+    const float* Wconv(const std::string& name) const;  // reordered [cout][9][cin]
+
+    Weights wt_;
+    int device_ = 0, mode_ = 0;
+    bool use_graph_ = true, simt_only_ = false;
+    cudaStream_t stream_ = nullptr;
+    cudaEvent_t join_ = nullptr;
+    float* dweights_ = nullptr;
+    std::map<std::string, const float*> w_;
+    std::map<std::string, const float*> wconv_;
+    Plan plan_;
+    bool have_plan_ = false;
+    float* arena_ = nullptr;
+    std::unique_ptr<Acts> a_;
+    cudaGraphExec_t graph_ = nullptr;
+    int eager_runs_ = 0;
+    uint64_t launches_ = 0;
+    uint64_t per_pass_ = 0;
+    struct Mark {
+        std::string kind;
+        double flops, bytes;
+        cudaEvent_t ev;
+    };
+    bool profiling_ = false;
+    std::vector<Mark> marks_;  // kernel launches in one pass (counted on the eager run)
+};
+
+}  // namespace hat

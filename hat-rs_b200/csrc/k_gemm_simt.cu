@@ -1,0 +1,214 @@
+// CUDA-core fp32 GEMM for the token linears and the 3x3 convolutions (as implicit
+// GEMM over K = 9 * cin), with the fused epilogues the HAT graph needs. This is the
+// exact-fp32 path: it serves shapes the tensor-core kernel does not take and is the
+// on-device cross-check for it.
+#include "common.cuh"
+
+namespace hat {
+
+// A operand of a token linear: row-major [m][k].
+struct ALinear {
+    const float* x;
+    int k;
+    __device__ __forceinline__ float ld(long m, int kk) const { return x[m * k + kk]; }
+    __device__ __forceinline__ float4 ld4(long m, int kk) const {
+        return *reinterpret_cast<const float4*>(x + m * k + kk);
+    }
+};
+
+// A operand of a 3x3 conv over a token plane [hgt][wid][cin]: row m is pixel m, column
+// kk = tap * cin + ci reads channel ci of the neighbour (dy, dx) = (tap/3 - 1, tap%3 - 1),
+// zero outside the plane (Conv2d padding 1).
+struct AConv {
+    const float* x;
+    int hgt, wid, cin;
+    __device__ __forceinline__ const float* at(long m, int kk, bool& ok) const {
+        int tap = kk / cin, ci = kk - tap * cin;
+        int y = (int)(m / wid) + tap / 3 - 1, xx = (int)(m % wid) + tap % 3 - 1;
+        ok = y >= 0 && y < hgt && xx >= 0 && xx < wid;
+        return x + ((long)y * wid + xx) * cin + ci;
+    }
+    __device__ __forceinline__ float ld(long m, int kk) const {
+        bool ok;
+        const float* p = at(m, kk, ok);
+        return ok ? *p : 0.f;
+    }
+    __device__ __forceinline__ float4 ld4(long m, int kk) const {
+        bool ok;
+        const float* p = at(m, kk, ok);
+        return ok ? *reinterpret_cast<const float4*>(p) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+};
+
+__device__ __forceinline__ float apply_act(float v, int act) {
+    if (act == ACT_GELU) return 0.5f * v * (1.f + erff(v * 0.70710678118654752f));
+    if (act == ACT_LEAKY) return v > 0.f ? v : 0.01f * v;
+    return v;
+}
+
+// Store one finished value; `wid` is the plane width for the spatial epilogues.
+__device__ __forceinline__ void epi_store(const Epi& e, float* y, long gm, int gn, int n, float v,
+                                          int wid) {
+    if (e.planar_out) {
+        int py = (int)(gm / wid), px = (int)(gm % wid);
+        if (py < e.oh && px < e.ow)
+            y[((long)gn * e.oh + py) * e.ow + px] = v / e.img_range + e.mean[gn];
+        return;
+    }
+    if (e.shuffle) {
+        int r = e.shuffle, cout = n / (r * r);
+        int c = gn / (r * r), rem = gn - c * r * r, i = rem / r, j = rem - i * r;
+        int py = (int)(gm / wid), px = (int)(gm % wid);
+        long oy = (long)py * r + i, ox = (long)px * r + j;
+        y[(oy * ((long)wid * r) + ox) * cout + c] = v;
+        return;
+    }
+    long idx = gm * n + gn;
+    if (e.cx)
+        v = (e.res[idx] + v) + (e.cx[idx] * e.gate[gn]) * e.cscale;
+    else if (e.res)
+        v = e.res[idx] + v;
+    y[idx] = v;
+}
+
+template <int BN, bool VEC, class AL>
+__global__ void __launch_bounds__(256) k_gemm_simt(AL al, const float* __restrict__ w,
+                                                   float* __restrict__ y, long M, int N, int K,
+                                                   Epi e, int wid) {
+    constexpr int BM = 128, BK = 16, TN = BN / 16;
+    __shared__ __align__(16) float As[BK][BM + 4];
+    __shared__ __align__(16) float Bs[BK][BN + 4];
+    __shared__ float red[16][BN];
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const long m0 = (long)blockIdx.x * BM;
+    const int n0 = blockIdx.y * BN;
+    float acc[8][TN];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
+
+    for (int k0 = 0; k0 < K; k0 += BK) {
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            int idx = tid + r * 256, kq = idx & 3, mm = idx >> 2;
+            long gm = m0 + mm;
+            int gk = k0 + kq * 4;
+            float v[4];
+            if (VEC) {
+                float4 t = (gm < M && gk < K) ? al.ld4(gm, gk) : make_float4(0.f, 0.f, 0.f, 0.f);
+                v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+            } else {
+#pragma unroll
+                for (int u = 0; u < 4; ++u) v[u] = (gm < M && gk + u < K) ? al.ld(gm, gk + u) : 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) As[kq * 4 + u][mm] = v[u];
+        }
+        for (int idx = tid; idx < BN * 4; idx += 256) {
+            int kq = idx & 3, nn = idx >> 2, gn = n0 + nn, gk = k0 + kq * 4;
+            float v[4];
+            if (VEC) {
+                float4 t = (gn < N && gk < K) ? *reinterpret_cast<const float4*>(w + (long)gn * K + gk)
+                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+                v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+            } else {
+#pragma unroll
+                for (int u = 0; u < 4; ++u) v[u] = (gn < N && gk + u < K) ? w[(long)gn * K + gk + u] : 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) Bs[kq * 4 + u][nn] = v[u];
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < BK; ++kk) {
+            float a[8], b[TN];
+            float4 a0 = *reinterpret_cast<const float4*>(&As[kk][ty * 8]);
+            float4 a1 = *reinterpret_cast<const float4*>(&As[kk][ty * 8 + 4]);
+            a[0] = a0.x; a[1] = a0.y; a[2] = a0.z; a[3] = a0.w;
+            a[4] = a1.x; a[5] = a1.y; a[6] = a1.z; a[7] = a1.w;
+#pragma unroll
+            for (int j = 0; j < TN; ++j) b[j] = Bs[kk][tx + 16 * j];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+
+    float cs[TN];
+#pragma unroll
+    for (int j = 0; j < TN; ++j) cs[j] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        long gm = m0 + ty * 8 + i;
+        if (gm >= M) continue;
+#pragma unroll
+        for (int j = 0; j < TN; ++j) {
+            int gn = n0 + tx + 16 * j;
+            if (gn >= N) continue;
+            float v = acc[i][j] + (e.bias ? e.bias[gn] : 0.f);
+            v = apply_act(v, e.act);
+            epi_store(e, y, gm, gn, N, v, wid);
+            cs[j] += v;
+        }
+    }
+    if (e.colsum) {
+#pragma unroll
+        for (int j = 0; j < TN; ++j) red[ty][tx + 16 * j] = cs[j];
+        __syncthreads();
+        if (tid < BN && n0 + tid < N) {
+            float s = 0.f;
+#pragma unroll
+            for (int r = 0; r < 16; ++r) s += red[r][tid];
+            atomicAdd(e.colsum + n0 + tid, s);
+        }
+    }
+}
+
+static int pick_bn(int n) {
+    int best = 64, waste = 1 << 30;
+    for (int bn : {64, 48, 32, 16}) {
+        int wst = (n + bn - 1) / bn * bn - n;
+        if (wst < waste) {
+            waste = wst;
+            best = bn;
+        }
+    }
+    return best;
+}
+
+template <class AL>
+static void run_simt(const AL& al, bool vec, const float* w, float* y, long m, int n, int k,
+                     const Epi& e, int wid, cudaStream_t st) {
+    int bn = pick_bn(n);
+    dim3 grid((unsigned)((m + 127) / 128), (unsigned)((n + bn - 1) / bn));
+#define HAT_GEMM_CASE(BN)                                                                      \
+    if (bn == BN) {                                                                            \
+        if (vec)                                                                               \
+            k_gemm_simt<BN, true, AL><<<grid, 256, 0, st>>>(al, w, y, m, n, k, e, wid);        \
+        else                                                                                   \
+            k_gemm_simt<BN, false, AL><<<grid, 256, 0, st>>>(al, w, y, m, n, k, e, wid);       \
+    }
+    HAT_GEMM_CASE(16)
+    HAT_GEMM_CASE(32)
+    HAT_GEMM_CASE(48)
+    HAT_GEMM_CASE(64)
+#undef HAT_GEMM_CASE
+    HAT_CUDA(cudaGetLastError());
+    count_launch();
+}
+
+void launch_linear_simt(const float* x, const float* w, float* y, long m, int n, int k,
+                        const Epi& e, cudaStream_t st) {
+    run_simt(ALinear{x, k}, k % 4 == 0, w, y, m, n, k, e, 1, st);
+}
+
+void launch_conv3x3_simt(const float* x, const float* wr, float* y, int hgt, int wid, int cin,
+                         int cout, const Epi& e, cudaStream_t st) {
+    run_simt(AConv{x, hgt, wid, cin}, cin % 4 == 0, wr, y, (long)hgt * wid, cout, 9 * cin, e,
+             wid, st);
+}
+
+}  // namespace hat

@@ -1,0 +1,141 @@
+// Bandwidth-bound kernels of the HAT forward: the input adjustment, LayerNorm over
+// the channel axis, the conv weight reorder, and the channel-attention head.
+#include "common.cuh"
+
+namespace hat {
+
+thread_local uint64_t* g_launch_counter = nullptr;
+
+// ---------------------------------------------------------------- pre
+// Pre::adjust (src/backend.rs:71-89): edge replication to the padded plane, then
+// `(x - mean) * img_range`, written token-major [hp][wp][3].
+__global__ void k_pre(const float* __restrict__ in, float* __restrict__ out, int h, int w, int hp,
+                      int wp, float m0, float m1, float m2, float range) {
+    long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    long n = (long)hp * wp;
+    if (i >= n) return;
+    int y = (int)(i / wp), x = (int)(i % wp);
+    int sy = min(y, h - 1), sx = min(x, w - 1);
+    long src = (long)sy * w + sx, plane = (long)h * w;
+    out[i * 3 + 0] = (in[src] - m0) * range;
+    out[i * 3 + 1] = (in[plane + src] - m1) * range;
+    out[i * 3 + 2] = (in[2 * plane + src] - m2) * range;
+}
+
+void launch_pre(const float* in, float* out, const Plan& p, const float mean[3], float img_range,
+                cudaStream_t st) {
+    long n = p.tokens();
+    k_pre<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(in, out, p.h, p.w, p.hp, p.wp, mean[0], mean[1],
+                                                       mean[2], img_range);
+    HAT_CUDA(cudaGetLastError());
+    count_launch();
+}
+
+// ---------------------------------------------------------------- layernorm
+// One warp per token; the row stays in registers: the mean first, then the biased
+// variance of the centred values (src/cpu.rs:563-581), eps 1e-5.
+template <int MAXV>
+__global__ void k_layernorm(const float* __restrict__ x, const float* __restrict__ g,
+                            const float* __restrict__ b, float* __restrict__ y, long m, int c) {
+    long row = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    int lane = threadIdx.x & 31;
+    if (row >= m) return;
+    const float* xr = x + row * c;
+    float v[MAXV];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        int ch = i * 32 + lane;
+        v[i] = ch < c ? xr[ch] : 0.f;
+        s += v[i];
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    float mean = s / (float)c;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        int ch = i * 32 + lane;
+        float d = ch < c ? v[i] - mean : 0.f;
+        q += d * d;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    float rstd = 1.f / sqrtf(q / (float)c + 1e-5f);
+    float* yr = y + row * c;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        int ch = i * 32 + lane;
+        if (ch < c) yr[ch] = (v[i] - mean) * rstd * g[ch] + b[ch];
+    }
+}
+
+void launch_layernorm(const float* x, const float* g, const float* b, float* y, long m, int c,
+                      cudaStream_t st) {
+    if (c > 256) throw Error(1, "layernorm: c > 256 is not supported");
+    unsigned grid = (unsigned)((m + 7) / 8);
+    if (c <= 160)
+        k_layernorm<5><<<grid, 256, 0, st>>>(x, g, b, y, m, c);
+    else
+        k_layernorm<8><<<grid, 256, 0, st>>>(x, g, b, y, m, c);
+    HAT_CUDA(cudaGetLastError());
+    count_launch();
+}
+
+// ---------------------------------------------------------------- conv weight reorder
+// [cout][cin][3][3] → [cout][9][cin]: the GEMM's K index becomes tap * cin + ci, so a
+// K run of one tap is a contiguous channel run of one neighbour pixel.
+__global__ void k_reorder_conv(const float* __restrict__ w, float* __restrict__ wr, int cout, int cin) {
+    long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    long n = (long)cout * cin * 9;
+    if (i >= n) return;
+    int tap = (int)(i % 9);
+    long r = i / 9;
+    int ci = (int)(r % cin);
+    int co = (int)(r / cin);
+    wr[((long)co * 9 + tap) * cin + ci] = w[i];
+}
+
+void launch_reorder_conv(const float* w, float* wr, int cout, int cin, cudaStream_t st) {
+    long n = (long)cout * cin * 9;
+    k_reorder_conv<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(w, wr, cout, cin);
+    HAT_CUDA(cudaGetLastError());
+    count_launch();
+}
+
+// ---------------------------------------------------------------- channel attention
+// ChannelAttention after the pool (hat_arch.py:40-57): `sums` holds the per-channel
+// sums of the CAB's second conv over the plane; one CTA computes the gate.
+__global__ void k_ca_gate(const float* __restrict__ sums, float inv_count, const float* __restrict__ w1,
+                          const float* __restrict__ b1, const float* __restrict__ w2,
+                          const float* __restrict__ b2, float* __restrict__ gate, int c, int sq) {
+    extern __shared__ float sm[];
+    float* mean = sm;        // [c]
+    float* hid = sm + c;     // [sq]
+    for (int i = threadIdx.x; i < c; i += blockDim.x) mean[i] = sums[i] * inv_count;
+    __syncthreads();
+    // one warp per squeezed channel
+    int warp = threadIdx.x / 32, lane = threadIdx.x & 31, nwarp = blockDim.x / 32;
+    for (int j = warp; j < sq; j += nwarp) {
+        float a = 0.f;
+        for (int i = lane; i < c; i += 32) a += w1[(long)j * c + i] * mean[i];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+        if (lane == 0) hid[j] = fmaxf(a + b1[j], 0.f);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < c; i += blockDim.x) {
+        float a = b2[i];
+        for (int j = 0; j < sq; ++j) a += w2[(long)i * sq + j] * hid[j];
+        gate[i] = 1.f / (1.f + expf(-a));
+    }
+}
+
+void launch_ca_gate(const float* sums, float inv_count, const float* w1, const float* b1,
+                    const float* w2, const float* b2, float* gate, int c, int sq, cudaStream_t st) {
+    k_ca_gate<<<1, 256, (c + sq) * sizeof(float), st>>>(sums, inv_count, w1, b1, w2, b2, gate, c, sq);
+    HAT_CUDA(cudaGetLastError());
+    count_launch();
+}
+
+}  // namespace hat

@@ -1,0 +1,227 @@
+"""Python host side of the B200 HAT backend: a ctypes binding of `libhat_b200.so`.
+
+The class `B200` mirrors the reference's `Backend` trait (src/backend.rs:29-36):
+`name()` and `forward(h, w, input)` taking a planar `[3][h][w]` float32 image in
+[0, 1] and returning `[3][h*scale][w*scale]`. Errors come back as `HatError`
+carrying the library's code and message, the way the reference returns
+`Result<_, String>`.
+
+There is no fallback: if the CUDA library cannot be loaded, or the device cannot be
+brought up, construction raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import numpy as np
+
+_LIB_PATH = Path(__file__).resolve().parent / "libhat_b200.so"
+
+MODE_PARITY = 0
+MODE_FAST = 1
+
+E_INVAL, E_IO, E_CUDA, E_NOMEM, E_SELFTEST = 1, 2, 3, 4, 5
+
+
+class HatError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(msg)
+        self.code = code
+
+
+class Opts(ctypes.Structure):
+    _fields_ = [("device", ctypes.c_int), ("mode", ctypes.c_int), ("use_graph", ctypes.c_int),
+                ("simt_only", ctypes.c_int)]
+
+
+class Info(ctypes.Structure):
+    _fields_ = [("scale", ctypes.c_int), ("window", ctypes.c_int), ("owin", ctypes.c_int),
+                ("embed", ctypes.c_int), ("heads", ctypes.c_int), ("head_dim", ctypes.c_int),
+                ("mlp_ratio", ctypes.c_int), ("compressed", ctypes.c_int),
+                ("squeezed", ctypes.c_int), ("head_feat", ctypes.c_int),
+                ("n_stages", ctypes.c_int), ("n_blocks", ctypes.c_int),
+                ("conv_scale", ctypes.c_float), ("img_range", ctypes.c_float),
+                ("mean", ctypes.c_float * 3), ("variant", ctypes.c_char * 32)]
+
+    def as_dict(self) -> dict:
+        d = {k: getattr(self, k) for k, _ in self._fields_}
+        d["mean"] = list(self.mean)
+        d["variant"] = self.variant.decode()
+        return d
+
+
+# Every symbol the C header declares, with its ctypes signature.
+_P, _I, _F, _S, _C = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_size_t, ctypes.c_char_p
+SIGNATURES = {
+    "hat_b200_create": (_I, [_C, ctypes.POINTER(Opts), ctypes.POINTER(_P), _C, _S]),
+    "hat_b200_destroy": (None, [_P]),
+    "hat_b200_get_info": (_I, [_P, ctypes.POINTER(Info)]),
+    "hat_b200_forward": (_I, [_P, _I, _I, _I, _P, _P, _C, _S]),
+    "hat_b200_forward_device": (_I, [_P, _I, _I, _I, _P, _P, _P, _C, _S]),
+    "hat_b200_footprint_bytes": (_S, [_P, _I, _I]),
+    "hat_b200_check_memory": (_I, [_P, _I, _I, _C, _S]),
+    "hat_b200_free_vram": (_I, [_I, ctypes.POINTER(_S), ctypes.POINTER(_S)]),
+    "hat_b200_probe": (_I, []),
+    "hat_b200_selftest": (_I, [_I, _C, _S]),
+    "hat_b200_inspect": (_I, [_C, ctypes.POINTER(Info), _C, _S]),
+    "hat_b200_linear": (_I, [_I, _P, _P, _P, _P, _I, _I, _I, _P]),
+    "hat_b200_conv3x3": (_I, [_I, _P, _P, _P, _P, _I, _I, _I, _I, _P]),
+    "hat_b200_window_attention": (_I, [_I, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
+    "hat_b200_overlap_attention": (_I, [_I, _P, _P, _P, _I, _I, _I, _I, _P]),
+    "hat_b200_launch_count": (ctypes.c_uint64, [_P]),
+    "hat_b200_profile": (_I, [_P, _I, _I, _C, _S, _C, _S]),
+}
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library (built on demand when the .so is missing)."""
+    global _lib
+    if _lib is None:
+        if not _LIB_PATH.exists():
+            from . import build as _b
+            _b.build()
+        _lib = ctypes.CDLL(str(_LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(_lib, name)
+            fn.restype = res
+            fn.argtypes = args
+    return _lib
+
+
+def _err():
+    return ctypes.create_string_buffer(4096)
+
+
+def _check(rc: int, buf) -> None:
+    if rc != 0:
+        raise HatError(rc, buf.value.decode(errors="replace"))
+
+
+def inspect(path: str) -> dict:
+    """Read and validate a checkpoint without a device (src/weights.rs:60-265)."""
+    info, e = Info(), _err()
+    _check(lib().hat_b200_inspect(str(path).encode(), ctypes.byref(info), e, len(e)), e)
+    return info.as_dict()
+
+
+def probe() -> bool:
+    return bool(lib().hat_b200_probe())
+
+
+def free_vram(device: int = 0):
+    f, t = ctypes.c_size_t(), ctypes.c_size_t()
+    rc = lib().hat_b200_free_vram(device, ctypes.byref(f), ctypes.byref(t))
+    if rc:
+        raise HatError(rc, f"free_vram: device {device} unavailable")
+    return f.value, t.value
+
+
+def selftest(device: int = 0):
+    """`--cuda-selftest`: (passed, report)."""
+    buf = ctypes.create_string_buffer(1 << 16)
+    rc = lib().hat_b200_selftest(device, buf, len(buf))
+    return rc == 0, buf.value.decode(errors="replace")
+
+
+def _ptr(a: np.ndarray):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+class B200:
+    """The B200 backend behind the reference's `Backend` contract."""
+
+    def __init__(self, path: str, device: int = 0, mode: int = MODE_PARITY, use_graph: bool = True,
+                 simt_only: bool = False):
+        self._h = ctypes.c_void_p()
+        opts = Opts(device, mode, int(use_graph), int(simt_only))
+        e = _err()
+        _check(lib().hat_b200_create(str(path).encode(), ctypes.byref(opts), ctypes.byref(self._h), e,
+                                     len(e)), e)
+        info = Info()
+        lib().hat_b200_get_info(self._h, ctypes.byref(info))
+        self.info = info.as_dict()
+        self.scale = self.info["scale"]
+        self.device = device
+
+    def close(self):
+        if self._h:
+            lib().hat_b200_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @staticmethod
+    def name() -> str:
+        return "b200"
+
+    def forward(self, h: int, w: int, image: np.ndarray) -> np.ndarray:
+        """Backend::forward: planar `[3][h][w]` → `[3][h*s][w*s]` (host arrays)."""
+        return self.forward_batch(np.asarray(image, np.float32).reshape(1, 3, h, w))[0]
+
+    def forward_batch(self, images: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(images, dtype=np.float32)
+        n, ch, h, w = x.shape
+        if ch != 3:
+            raise HatError(E_INVAL, f"expected 3 channels, got {ch}")
+        s = self.scale
+        out = np.empty((n, 3, h * s, w * s), np.float32)
+        e = _err()
+        _check(lib().hat_b200_forward(self._h, n, h, w, _ptr(x), _ptr(out), e, len(e)), e)
+        return out
+
+    def forward_device(self, d_in: int, d_out: int, n: int, h: int, w: int, stream: int = 0) -> None:
+        """Enqueue a pass on device pointers (`int` addresses) on `stream`."""
+        e = _err()
+        _check(lib().hat_b200_forward_device(self._h, n, h, w, ctypes.c_void_p(d_in),
+                                             ctypes.c_void_p(d_out), ctypes.c_void_p(stream), e,
+                                             len(e)), e)
+
+    def footprint_bytes(self, h: int, w: int) -> int:
+        return int(lib().hat_b200_footprint_bytes(self._h, h, w))
+
+    def check_memory(self, h: int, w: int) -> None:
+        e = _err()
+        _check(lib().hat_b200_check_memory(self._h, h, w, e, len(e)), e)
+
+    def launch_count(self) -> int:
+        return int(lib().hat_b200_launch_count(self._h))
+
+    def profile(self, h: int, w: int) -> dict:
+        """Per-kind device time of one eager pass: {kind: {launches, ms, flops, bytes}}."""
+        import json
+        buf, e = ctypes.create_string_buffer(1 << 16), _err()
+        _check(lib().hat_b200_profile(self._h, h, w, buf, len(buf), e, len(e)), e)
+        return json.loads(buf.value.decode())
+
+
+# Kernel-level calls on device pointers (ints), the units --cuda-selftest checks.
+def linear(mode, x, w, b, y, m, n, k, stream=0):
+    rc = lib().hat_b200_linear(mode, x, w, b, y, m, n, k, stream)
+    if rc:
+        raise HatError(rc, "linear launch failed")
+
+
+def conv3x3(mode, x, w, b, y, hgt, wid, cin, cout, stream=0):
+    rc = lib().hat_b200_conv3x3(mode, x, w, b, y, hgt, wid, cin, cout, stream)
+    if rc:
+        raise HatError(rc, "conv3x3 launch failed")
+
+
+def window_attention(mode, qkv, table, out, hp, wp, c, heads, shift, stream=0):
+    rc = lib().hat_b200_window_attention(mode, qkv, table, out, hp, wp, c, heads, shift, stream)
+    if rc:
+        raise HatError(rc, "window attention launch failed")
+
+
+def overlap_attention(mode, qkv, table, out, hp, wp, c, heads, stream=0):
+    rc = lib().hat_b200_overlap_attention(mode, qkv, table, out, hp, wp, c, heads, stream)
+    if rc:
+        raise HatError(rc, "overlap attention launch failed")

@@ -1,0 +1,148 @@
+/*
+ * hat_b200.h — C ABI of the B200-native HAT super-resolution backend.
+ *
+ * This is the drop-in boundary for the GPU forward pass of hat-rs. Each entry point
+ * replaces one piece of the reference's Rust interface; the comment on each names the
+ * reference item (path within the hat-rs project, line numbers). Plain pointers and
+ * sizes only; no ownership crosses the boundary except the opaque handle.
+ *
+ * Errors: every int-returning call returns 0 on success and a nonzero HAT_B200_E*
+ * code on failure, writing a NUL-terminated message into `err` (when err != NULL and
+ * errlen > 0). This replaces the reference's `Result<_, String>` (src/backend.rs:29-36).
+ *
+ * Threading: a handle is not thread-safe (the reference's `&mut self`,
+ * src/gpu.rs:751-803). Use one handle per GPU; handles on different devices may be
+ * driven from different host threads.
+ */
+#ifndef HAT_B200_H
+#define HAT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define HAT_B200_API __attribute__((visibility("default")))
+#else
+#define HAT_B200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HAT_B200_OK 0
+#define HAT_B200_EINVAL 1   /* bad argument or shape */
+#define HAT_B200_EIO 2      /* checkpoint unreadable / malformed */
+#define HAT_B200_ECUDA 3    /* a CUDA runtime error */
+#define HAT_B200_ENOMEM 4   /* the memory guard refused the pass (src/memguard.rs:183-201) */
+#define HAT_B200_ESELFTEST 5
+
+/* Arithmetic mode. PARITY: fp32-accurate (3xTF32 split on the tensor cores, fp32
+ * everywhere else); matches the reference's fp32 output to <= 1e-4. FAST: single
+ * TF32 products on the tensor cores. */
+#define HAT_B200_MODE_PARITY 0
+#define HAT_B200_MODE_FAST 1
+
+typedef struct hat_b200 hat_b200;
+
+typedef struct hat_b200_opts {
+    int device;      /* CUDA device ordinal this handle runs on */
+    int mode;        /* HAT_B200_MODE_* */
+    int use_graph;   /* 1: capture each plan's launch sequence in a CUDA graph */
+    int simt_only;   /* 1: CUDA-core fp32 kernels only (debug / cross-check path) */
+} hat_b200_opts;
+
+/* What the checkpoint describes (src/weights.rs:28-57). */
+typedef struct hat_b200_info {
+    int scale, window, owin, embed, heads, head_dim, mlp_ratio, compressed, squeezed,
+        head_feat, n_stages, n_blocks;
+    float conv_scale, img_range, mean[3];
+    char variant[32];
+} hat_b200_info;
+
+/* Gpu::new(&Weights) (src/gpu.rs:372-386) + Weights::load (src/weights.rs:60-129):
+ * read and validate a checkpoint in the tools/convert.py safetensors layout, bring up
+ * the device, check the weights fit (src/memguard.rs:211-225) and upload them. */
+HAT_B200_API int hat_b200_create(const char* safetensors_path, const hat_b200_opts* opts,
+                    hat_b200** out, char* err, size_t errlen);
+
+/* Drop the handle and every device buffer it owns. */
+HAT_B200_API void hat_b200_destroy(hat_b200* h);
+
+HAT_B200_API int hat_b200_get_info(const hat_b200* h, hat_b200_info* out);
+
+/* Backend::forward (src/backend.rs:29-36, src/gpu.rs:759-803): `in` is
+ * [n][3][height][width] float32 in [0,1] on the HOST (not mean-adjusted); `out` is
+ * [n][3][height*scale][width*scale] on the host after denormalisation. Pads to a
+ * window multiple by edge replication (src/backend.rs:71-89) and crops after
+ * (src/backend.rs:94-109). n = 1 is the reference's contract; n > 1 runs the images
+ * back to back on this device. Blocks until `out` is written. */
+HAT_B200_API int hat_b200_forward(hat_b200* h, int n, int height, int width, const float* in, float* out,
+                     char* err, size_t errlen);
+
+/* The same pass with `in`/`out` already in this device's memory, enqueued on `stream`
+ * (a cudaStream_t, or NULL for the handle's own stream). Returns once enqueued. */
+HAT_B200_API int hat_b200_forward_device(hat_b200* h, int n, int height, int width, const float* d_in,
+                            float* d_out, void* stream, char* err, size_t errlen);
+
+/* gpu::footprint_floats (src/gpu.rs:288-290) as bytes: the device bytes a pass at
+ * this size allocates, computed without touching the device. */
+HAT_B200_API size_t hat_b200_footprint_bytes(const hat_b200* h, int height, int width);
+
+/* memguard::check_gpu (src/memguard.rs:183-201): 0 when a pass at this size fits the
+ * free memory of the handle's device, HAT_B200_ENOMEM with the refusal text if not. */
+HAT_B200_API int hat_b200_check_memory(const hat_b200* h, int height, int width, char* err, size_t errlen);
+
+/* lightgpu::vm::free_vram (src/memguard.rs:174). */
+HAT_B200_API int hat_b200_free_vram(int device, size_t* free_bytes, size_t* total_bytes);
+
+/* vm::device() probe (src/main.rs:165-174): 1 if a CUDA device of compute
+ * capability 10.x can be brought up, else 0. */
+HAT_B200_API int hat_b200_probe(void);
+
+/* --cuda-selftest (src/selftest.rs:437-523): every kernel against a host twin on
+ * seeded inputs; the report goes to `log`. */
+HAT_B200_API int hat_b200_selftest(int device, char* log, size_t loglen);
+
+/* Weights::load + validate without a device (the --list-weights path, src/main.rs):
+ * reads the checkpoint header and checks every tensor shape; fills `out`. */
+HAT_B200_API int hat_b200_inspect(const char* safetensors_path, hat_b200_info* out, char* err, size_t errlen);
+
+/* Kernel-level entry points (device pointers, enqueued on `stream`, NULL = default
+ * stream), the units --cuda-selftest checks (src/cuda.rs:88-522 wrappers). */
+
+/* y[m][n] = sum_k x[m][k] * w[n][k] + b[n]  (lg_linear / lg_conv1x1_rb, src/cuda.rs:162-169,440-453) */
+HAT_B200_API int hat_b200_linear(int mode, const float* x, const float* w, const float* b, float* y,
+                    int m, int n, int k, void* stream);
+
+/* 3x3 conv, zero padding 1, on token-major [hgt][wid][cin] planes; w in PyTorch
+ * [cout][cin][3][3] layout (lg_conv3x3_winograd, src/cuda.rs:88-106). */
+HAT_B200_API int hat_b200_conv3x3(int mode, const float* x, const float* w, const float* b, float* y,
+                     int hgt, int wid, int cin, int cout, void* stream);
+
+/* Windowed multi-head attention of one HAB (hat_attention_d24/_d30, cuda/hat.cu:246-316
+ * + hat_bias_gather + hat_mask_build): qkv is the token-major [hp][wp][3c] projection,
+ * table the block's [(2win-1)^2][heads] bias table; shift 0 or win/2. */
+HAT_B200_API int hat_b200_window_attention(int mode, const float* qkv, const float* table, float* out,
+                              int hp, int wp, int c, int heads, int shift, void* stream);
+
+/* The OCAB's overlapping attention (hat_unfold_kv, cuda/hat.cu:170-198, + attention):
+ * 16x16 queries against the zero-padded 24x24 unfold of k and v. */
+HAT_B200_API int hat_b200_overlap_attention(int mode, const float* qkv, const float* table, float* out,
+                               int hp, int wp, int c, int heads, void* stream);
+
+/* One eager pass at this size with a CUDA event between every launch, on the handle's
+ * stream: per kind of kernel, its launch count, summed device time (ms) and the
+ * algorithmic FLOPs and bytes of those launches, as a JSON object in `json`. (No
+ * counterpart in the reference, which prints only the pass's wall time,
+ * src/main.rs:285-288.) */
+HAT_B200_API int hat_b200_profile(hat_b200* h, int height, int width, char* json, size_t jsonlen,
+                                  char* err, size_t errlen);
+
+/* Kernel launches issued by this handle since creation (src/cuda.rs:542-555). */
+HAT_B200_API uint64_t hat_b200_launch_count(const hat_b200* h);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,126 @@
+"""Parity of the CUDA path with the reference, on a B200, through the C ABI.
+
+* whole-network: every golden fixture (the reference network's own output) at the
+  reference's verify tolerance, 1e-4 max abs on [0, 1] pixels (src/main.rs:310);
+* a larger non-square image against the CPU oracle;
+* the device-pointer entry point, batches, graph replay, the memory guard;
+* kernel level: --cuda-selftest's host twins, and linear / conv against torch fp32.
+"""
+import numpy as np
+import pytest
+
+import hat_b200
+from golden_io import GOLDEN, cases, checkpoint_for, read_hatf
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-4  # src/main.rs:310 VERIFY_TOL
+
+
+@pytest.fixture(scope="module")
+def ckdir(tmp_path_factory):
+    return tmp_path_factory.mktemp("ck")
+
+
+@pytest.fixture(scope="module")
+def torch_cuda():
+    import torch
+    assert torch.cuda.is_available(), "the gpu tests need a CUDA device"
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    return torch
+
+
+def test_cuda_selftest():
+    ok, report = hat_b200.selftest(0)
+    print(report)
+    assert ok, report
+
+
+@pytest.mark.parametrize("case", cases(), ids=lambda c: c["name"])
+def test_golden_parity(case, ckdir):
+    fx = read_hatf(GOLDEN / f"{case['name']}.bin")
+    be = hat_b200.B200(checkpoint_for(case, ckdir))
+    got = be.forward(fx["h"], fx["w"], fx["input"])
+    assert be.launch_count() > 0, "no kernel of the library ran"
+    err = np.abs(got - fx["expected"])
+    print(f"{case['name']}: max {err.max():.3e} mean {err.mean():.3e}")
+    assert got.shape == fx["expected"].shape
+    assert float(err.max()) <= TOL
+    be.close()
+
+
+def test_larger_image_against_oracle(ckdir):
+    from oracle import hat_oracle as O
+    from hat_b200 import checkpoint, synth
+    p = str(ckdir / "s4_big.safetensors")
+    checkpoint.make_checkpoint(p, "hat-s", 4, 21, perturb=True)
+    img = synth.image(70, 45, 7)
+    want = O.forward(O.Model.load(p), img)
+    be = hat_b200.B200(p)
+    got = be.forward(70, 45, img)
+    assert float(np.abs(got - want).max()) <= TOL
+
+
+def test_device_entry_batch_and_graph_replay(ckdir, torch_cuda):
+    torch = torch_cuda
+    from hat_b200 import checkpoint, synth
+    p = str(ckdir / "s2.safetensors")
+    checkpoint.make_checkpoint(p, "hat-s", 2, 22, perturb=True)
+    imgs = synth.batch(3, 32, 48, 9)
+    host_be = hat_b200.B200(p, use_graph=False)
+    ref = host_be.forward_batch(imgs)
+    for i in range(3):
+        assert np.array_equal(ref[i], host_be.forward(32, 48, imgs[i]))
+    be = hat_b200.B200(p, use_graph=True)
+    x = torch.from_numpy(imgs).cuda()
+    y = torch.empty((3, 3, 64, 96), device="cuda")
+    for _ in range(3):  # eager run, capture, replay
+        y.zero_()
+        be.forward_device(x.data_ptr(), y.data_ptr(), 3, 32, 48, torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        assert np.array_equal(y.cpu().numpy(), ref)
+
+
+def test_memory_guard_refuses_before_allocating(ckdir):
+    from hat_b200 import checkpoint
+    p = str(ckdir / "s4.safetensors")
+    checkpoint.make_checkpoint(p, "hat-s", 4, 23)
+    be = hat_b200.B200(p)
+    assert be.footprint_bytes(512, 512) > be.footprint_bytes(256, 256) > 0
+    with pytest.raises(hat_b200.HatError, match="not enough video memory") as e:
+        be.check_memory(30000, 30000)
+    assert e.value.code == hat_b200.E_NOMEM
+    with pytest.raises(hat_b200.HatError) as e:
+        be.forward(30000, 30000, np.zeros((3, 30000, 30000), np.float32))
+    assert e.value.code == hat_b200.E_NOMEM
+    be.check_memory(64, 64)
+
+
+@pytest.mark.parametrize("m,n,k", [(4096, 432, 144), (1000, 144, 288), (777, 540, 180), (262, 360, 180)])
+def test_linear_kernel_vs_torch(torch_cuda, m, n, k):
+    torch = torch_cuda
+    g = torch.Generator(device="cuda").manual_seed(m)
+    x = torch.randn(m, k, device="cuda", generator=g)
+    w = torch.randn(n, k, device="cuda", generator=g) * 0.05
+    b = torch.randn(n, device="cuda", generator=g)
+    y = torch.empty(m, n, device="cuda")
+    hat_b200.linear(hat_b200.MODE_PARITY, x.data_ptr(), w.data_ptr(), b.data_ptr(), y.data_ptr(), m, n, k)
+    torch.cuda.synchronize()
+    want = (x.double() @ w.double().T + b.double()).float()
+    assert float((y - want).abs().max()) < 2e-5
+
+
+@pytest.mark.parametrize("hg,wd,ci,co", [(64, 48, 144, 144), (32, 32, 144, 6), (32, 32, 6, 144),
+                                         (48, 16, 64, 256), (16, 48, 3, 180), (16, 16, 64, 3)])
+def test_conv_kernel_vs_torch(torch_cuda, hg, wd, ci, co):
+    torch = torch_cuda
+    g = torch.Generator(device="cuda").manual_seed(hg * 1000 + co)
+    x = torch.randn(hg, wd, ci, device="cuda", generator=g)
+    w = torch.randn(co, ci, 3, 3, device="cuda", generator=g) * 0.05
+    b = torch.randn(co, device="cuda", generator=g)
+    y = torch.empty(hg, wd, co, device="cuda")
+    hat_b200.conv3x3(hat_b200.MODE_PARITY, x.data_ptr(), w.data_ptr(), b.data_ptr(), y.data_ptr(), hg, wd, ci, co)
+    torch.cuda.synchronize()
+    want = torch.nn.functional.conv2d(x.double().permute(2, 0, 1)[None], w.double(), b.double(), padding=1)
+    want = want[0].permute(1, 2, 0).float()
+    assert float((y - want).abs().max()) < 5e-5
