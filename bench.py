@@ -174,7 +174,10 @@ def run_ours(args):
     mode = hat_b200.MODE_FAST if args.mode == "fast" else hat_b200.MODE_PARITY
     be = hat_b200.B200(ck, device=local, mode=mode, use_graph=True)
     img = synth.image(H, W, CFG_ID * 1000 + rank)
-    st = torch.cuda.current_stream()
+    # A dedicated stream: the library's kernels run on it and the timing events are
+    # recorded on it (torch's default stream is the legacy NULL stream).
+    st = torch.cuda.Stream()
+    torch.cuda.set_stream(st)
     d_in = torch.from_numpy(img).cuda()
     d_out = torch.empty((3, H * SCALE, W * SCALE), device="cuda")
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")  # > 126 MB L2

@@ -159,12 +159,51 @@ int hat_b200_profile(hat_b200* h, int height, int width, char* json, size_t json
     });
 }
 
+// The GEMM operand of one kernel-level call, prepared on the caller's stream.
+struct TempW {
+    float* buf = nullptr;
+    int* err = nullptr;
+    GemmW g;
+    cudaStream_t st = nullptr;
+    ~TempW() {
+        if (buf) cudaFreeAsync(buf, st);
+        if (err) cudaFreeAsync(err, st);
+    }
+};
+
+static void temp_gemm_w(TempW& t, const float* w, int n, int k_or_cin, bool conv, int cin_plane, cudaStream_t st) {
+    t.st = st;
+    plan_gemm_w(t.g, n, k_or_cin, conv, cin_plane);
+    HAT_CUDA(cudaMallocAsync(&t.buf, (gemm_w_floats(t.g) + 64) * sizeof(float), st));
+    HAT_CUDA(cudaMallocAsync(&t.err, sizeof(int), st));
+    HAT_CUDA(cudaMemsetAsync(t.err, 0, sizeof(int), st));
+    float* simt = t.buf;
+    float* hi = simt + (size_t)t.g.n * t.g.k;
+    float* lo = hi + (size_t)t.g.n_pad * t.g.k_pad;
+    launch_prep_gemm_w(w, simt, t.g.umma ? hi : nullptr, t.g.umma ? lo : nullptr, t.g, st);
+    t.g.simt = simt;
+    t.g.hi = hi;
+    t.g.lo = lo;
+}
+
+static void finish_kernel_call(TempW& t) {
+    int v = 0;
+    HAT_CUDA(cudaMemcpyAsync(&v, t.err, sizeof(int), cudaMemcpyDeviceToHost, t.st));
+    HAT_CUDA(cudaStreamSynchronize(t.st));
+    if (v) throw Error(3, "tensor-core kernel gave up waiting on its pipeline (code " + std::to_string(v) + ")");
+}
+
 int hat_b200_linear(int mode, const float* x, const float* w, const float* b, float* y, int m, int n, int k,
                     void* stream) {
     return guarded(nullptr, 0, [&] {
+        cudaStream_t st = (cudaStream_t)stream;
+        TempW t;
+        temp_gemm_w(t, w, n, k, false, 0, st);
         Epi e;
         e.bias = b;
-        launch_linear(mode, x, w, y, m, n, k, e, (cudaStream_t)stream);
+        GemmCtx c{mode == HAT_B200_MODE_SIMT ? 0 : mode, mode == HAT_B200_MODE_SIMT, t.err};
+        gemm_linear(c, x, t.g, y, m, e, st);
+        finish_kernel_call(t);
     });
 }
 
@@ -172,13 +211,13 @@ int hat_b200_conv3x3(int mode, const float* x, const float* w, const float* b, f
                      int cin, int cout, void* stream) {
     return guarded(nullptr, 0, [&] {
         cudaStream_t st = (cudaStream_t)stream;
-        float* wr = nullptr;
-        HAT_CUDA(cudaMallocAsync(&wr, (size_t)cout * cin * 9 * sizeof(float), st));
-        launch_reorder_conv(w, wr, cout, cin, st);
+        TempW t;
+        temp_gemm_w(t, w, cout, cin, true, cin, st);
         Epi e;
         e.bias = b;
-        launch_conv3x3(mode, x, wr, y, hgt, wid, cin, cout, e, st);
-        HAT_CUDA(cudaFreeAsync(wr, st));
+        GemmCtx c{mode == HAT_B200_MODE_SIMT ? 0 : mode, mode == HAT_B200_MODE_SIMT, t.err};
+        gemm_conv3x3(c, x, t.g, y, hgt, wid, e, st);
+        finish_kernel_call(t);
     });
 }
 

@@ -60,8 +60,13 @@ struct Epi {
     const float* cx = nullptr;     // [m][ldo] the CAB output (HAB sum only)
     const float* gate = nullptr;   // [n] channel-attention gate (HAB sum only)
     float cscale = 0.f;
-    // channel sums of the stored value (the channel attention's average pool)
-    float* colsum = nullptr;       // [n], accumulated with atomics
+    // Channel sums of the stored value (the channel attention's average pool): one
+    // partial row [n] per M tile of the launch, written without atomics so the sum
+    // (taken by the gate in tile order) is the same on every run.
+    float* colsum = nullptr;       // [partial rows][n]; the conv launcher returns the row count
+    // Channel stride of the output plane for plain stores (0: the GEMM's n). Columns in
+    // [n, ldo) are left as they are (the tensor-core path writes zeros there).
+    int ldo = 0;
     // PixelShuffle(r) on store: channel n = c*r*r + i*r + j of pixel (y, x) goes to
     // channel c of pixel (r*y + i, r*x + j) of a [hgt*r][wid*r][n/(r*r)] plane.
     int shuffle = 0;
@@ -88,18 +93,6 @@ void launch_pre(const float* in, float* out, const Plan& p, const float mean[3],
 void launch_layernorm(const float* x, const float* g, const float* b, float* y, long m, int c,
                       cudaStream_t st);
 
-// y[m][n] = epi(x[m][:k] . w[n][:k]) with w [n][k] row-major.
-void launch_linear(int mode, const float* x, const float* w, float* y, long m, int n, int k,
-                   const Epi& e, cudaStream_t st);
-
-// 3x3 conv (zero pad 1) of a token plane [hgt][wid][cin]; `wr` is the weight
-// reordered to [cout][9][cin] (tap-major K).
-void launch_conv3x3(int mode, const float* x, const float* wr, float* y, int hgt, int wid,
-                    int cin, int cout, const Epi& e, cudaStream_t st);
-
-// Reorder a PyTorch [cout][cin][3][3] conv weight into [cout][9][cin].
-void launch_reorder_conv(const float* w, float* wr, int cout, int cin, cudaStream_t st);
-
 // Window attention of one HAB over the [hp][wp][3c] qkv plane (hat_arch.py:165-196).
 void launch_window_attention(int mode, const float* qkv, const float* table, float* out,
                              const Plan& p, int c, int heads, int shift, cudaStream_t st);
@@ -108,8 +101,9 @@ void launch_window_attention(int mode, const float* qkv, const float* table, flo
 void launch_overlap_attention(int mode, const float* qkv, const float* table, float* out,
                               const Plan& p, int c, int heads, cudaStream_t st);
 
-// gate[c] = sigmoid(W2 relu(W1 (sum / count) + b1) + b2) (hat_arch.py:40-57).
-void launch_ca_gate(const float* sums, float inv_count, const float* w1, const float* b1,
+// gate[c] = sigmoid(W2 relu(W1 mean + b1) + b2) (hat_arch.py:40-57), where the mean
+// over the plane is the sum of `rows` partial rows [rows][c] times `inv_count`.
+void launch_ca_gate(const float* partial, long rows, float inv_count, const float* w1, const float* b1,
                     const float* w2, const float* b2, float* gate, int c, int sq, cudaStream_t st);
 
 }  // namespace hat

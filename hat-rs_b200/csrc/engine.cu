@@ -1,9 +1,11 @@
 // The layer scheduler. Activations are token-major planes [hp][wp][c] (channels
 // innermost), so a token linear is a plain row-major GEMM over the whole plane, a 3x3
 // conv is an implicit GEMM over K = 9*cin, and the windowed attentions read their
-// windows out of the qkv plane by address arithmetic. Every layer is one launch.
+// windows out of the qkv plane by address arithmetic. Every layer is one launch; the
+// whole pass is captured once per plan in a CUDA graph and replayed.
 #include "engine.h"
 
+#include <algorithm>
 #include <cstring>
 #include <sstream>
 
@@ -13,17 +15,19 @@ namespace hat {
 Sizes Sizes::of(const Weights& wt, const Plan& p) {
     Sizes s;
     const long P = p.tokens(), c = wt.embed;
+    s.cmid_stride = wt.compressed <= 8 ? 8 : (wt.compressed + 3) / 4 * 4;
     s.x0 = P * 3;
     s.body = P * c;
     s.xa = P * c;
     s.xb = P * c;
     s.n1 = P * c;
-    s.cmid = P * wt.compressed;
+    s.cmid = P * s.cmid_stride;
     s.convx = P * c;
     s.qkv = P * 3 * c;
     s.attn = P * c;
     s.hid = P * wt.mlp_ratio * c;
-    s.chsum = c;
+    // The channel-attention pool's partial sums: at most four rows of c per 128-pixel tile.
+    s.chsum = (P + 127) / 128 * 4 * c;
     s.gate = c;
     // The head's planes ping-pong between two buffers: plane 0 (conv_before_upsample's
     // output, at P) and every other shuffled plane go to A, the rest to B.
@@ -32,7 +36,10 @@ Sizes Sizes::of(const Weights& wt, const Plan& p) {
     for (auto& blk : wt.up_blocks()) {
         res *= (long)blk.first * blk.first;
         long need = res * wt.head_feat;
-        if (i % 2) b = std::max(b, need); else a = std::max(a, need);
+        if (i % 2)
+            b = std::max(b, need);
+        else
+            a = std::max(a, need);
         ++i;
     }
     s.headA = a;
@@ -43,31 +50,14 @@ Sizes Sizes::of(const Weights& wt, const Plan& p) {
 }
 
 struct Engine::Acts {
-    float *x0, *body, *xa, *xb, *n1, *cmid, *convx, *qkv, *attn, *hid, *chsum, *gate, *headA, *headB,
-        *din, *dout;
+    float *x0, *body, *xa, *xb, *n1, *cmid, *convx, *qkv, *attn, *hid, *chsum, *gate, *headA, *headB, *din, *dout;
 };
 
-// ------------------------------------------------------------------ dispatch
-void launch_linear_simt(const float* x, const float* w, float* y, long m, int n, int k, const Epi& e,
-                        cudaStream_t st);
-void launch_conv3x3_simt(const float* x, const float* wr, float* y, int hgt, int wid, int cin, int cout,
-                         const Epi& e, cudaStream_t st);
-void launch_window_attention_simt(const float* qkv, const float* table, float* out, const Plan& p, int c,
-                                  int heads, int shift, cudaStream_t st);
-void launch_overlap_attention_simt(const float* qkv, const float* table, float* out, const Plan& p, int c,
-                                   int heads, cudaStream_t st);
-
-void launch_linear(int mode, const float* x, const float* w, float* y, long m, int n, int k, const Epi& e,
-                   cudaStream_t st) {
-    (void)mode;
-    launch_linear_simt(x, w, y, m, n, k, e, st);
-}
-
-void launch_conv3x3(int mode, const float* x, const float* wr, float* y, int hgt, int wid, int cin, int cout,
-                    const Epi& e, cudaStream_t st) {
-    (void)mode;
-    launch_conv3x3_simt(x, wr, y, hgt, wid, cin, cout, e, st);
-}
+// ------------------------------------------------------------------ attention dispatch
+void launch_window_attention_simt(const float* qkv, const float* table, float* out, const Plan& p, int c, int heads,
+                                  int shift, cudaStream_t st);
+void launch_overlap_attention_simt(const float* qkv, const float* table, float* out, const Plan& p, int c, int heads,
+                                   cudaStream_t st);
 
 void launch_window_attention(int mode, const float* qkv, const float* table, float* out, const Plan& p, int c,
                              int heads, int shift, cudaStream_t st) {
@@ -75,8 +65,8 @@ void launch_window_attention(int mode, const float* qkv, const float* table, flo
     launch_window_attention_simt(qkv, table, out, p, c, heads, shift, st);
 }
 
-void launch_overlap_attention(int mode, const float* qkv, const float* table, float* out, const Plan& p,
-                              int c, int heads, cudaStream_t st) {
+void launch_overlap_attention(int mode, const float* qkv, const float* table, float* out, const Plan& p, int c,
+                              int heads, cudaStream_t st) {
     (void)mode;
     launch_overlap_attention_simt(qkv, table, out, p, c, heads, st);
 }
@@ -92,8 +82,15 @@ static std::string fmt_bytes(double n) {
     return buf;
 }
 
-static const double SLACK = 1.05;           // src/memguard.rs:42
+static const double SLACK = 1.05;            // src/memguard.rs:42
 static const double BASE = 128.0 * 1048576;  // src/memguard.rs:49
+
+static bool is_gemm_weight(const std::string& name, const TensorInfo& ti) {
+    if (ti.shape.size() == 4 && ti.shape[2] == 3 && ti.shape[3] == 3) return true;  // 3x3 conv
+    if (ti.shape.size() != 2) return false;
+    // Linear weights; the relative-position tables are 2-D too but are not GEMM operands.
+    return name.find("relative_position") == std::string::npos;
+}
 
 Engine::Engine(const std::string& path, int device, int mode, bool use_graph, bool simt_only)
     : device_(device), mode_(mode), use_graph_(use_graph), simt_only_(simt_only) {
@@ -117,44 +114,77 @@ Engine::Engine(const std::string& path, int device, int mode, bool use_graph, bo
                            " is free on the device\nhat: a smaller checkpoint is what fits");
     HAT_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
     HAT_CUDA(cudaEventCreateWithFlags(&join_, cudaEventDisableTiming));
+    HAT_CUDA(cudaMalloc(&derr_, sizeof(int)));
+    HAT_CUDA(cudaMemsetAsync(derr_, 0, sizeof(int), stream_));
 
-    // Upload every f32 tensor once, plus a tap-major copy of every 3x3 conv weight.
+    // One device allocation: every f32 tensor as stored, then every GEMM operand in the
+    // kernels' layouts (CUDA-core layout, tensor-core hi/lo split).
+    const int cmid_stride = Sizes::of(wt_, Plan::make(16, 16, wt_.window)).cmid_stride;
     size_t total = 0;
     std::vector<std::string> names;
     for (auto& kv : wt_.st.tensors) {
         if (kv.second.dtype != "F32") continue;
         names.push_back(kv.first);
-        size_t n = (size_t)kv.second.numel();
-        total += (n + 63) / 64 * 64;
-        if (kv.second.shape.size() == 4 && kv.second.shape[2] == 3) total += (n + 63) / 64 * 64;
+        total += ((size_t)kv.second.numel() + 63) / 64 * 64;
+        if (is_gemm_weight(kv.first, kv.second)) {
+            GemmW g;
+            const auto& s = kv.second.shape;
+            if (s.size() == 4) {
+                const bool cab2 = kv.first.find("conv_block.cab.2.weight") != std::string::npos;
+                plan_gemm_w(g, (int)s[0], (int)s[1], true, cab2 ? cmid_stride : (int)s[1]);
+            } else {
+                plan_gemm_w(g, (int)s[0], (int)s[1], false, 0);
+            }
+            gw_[kv.first] = g;
+            total += (gemm_w_floats(g) + 64) / 64 * 64 + 192;
+        }
     }
     HAT_CUDA(cudaMalloc(&dweights_, total * sizeof(float)));
     size_t off = 0;
     uint64_t* prev = g_launch_counter;
     g_launch_counter = &launches_;
-    for (auto& name : names) {
-        const TensorInfo& ti = wt_.st.tensors[name];
-        size_t n = (size_t)ti.numel();
-        float* d = dweights_ + off;
-        HAT_CUDA(cudaMemcpyAsync(d, wt_.st.f32(name), n * sizeof(float), cudaMemcpyHostToDevice, stream_));
-        w_[name] = d;
-        off += (n + 63) / 64 * 64;
-        if (ti.shape.size() == 4 && ti.shape[2] == 3) {
-            float* r = dweights_ + off;
-            launch_reorder_conv(d, r, (int)ti.shape[0], (int)ti.shape[1], stream_);
-            wconv_[name] = r;
+    try {
+        for (auto& name : names) {
+            const TensorInfo& ti = wt_.st.tensors[name];
+            size_t n = (size_t)ti.numel();
+            float* d = dweights_ + off;
+            HAT_CUDA(cudaMemcpyAsync(d, wt_.st.f32(name), n * sizeof(float), cudaMemcpyHostToDevice, stream_));
+            w_[name] = d;
             off += (n + 63) / 64 * 64;
+            auto it = gw_.find(name);
+            if (it != gw_.end()) {
+                GemmW& g = it->second;
+                float* simt = dweights_ + off;
+                off += ((size_t)g.n * g.k + 63) / 64 * 64;
+                float *hi = nullptr, *lo = nullptr;
+                if (g.umma) {
+                    hi = dweights_ + off;
+                    off += ((size_t)g.n_pad * g.k_pad + 63) / 64 * 64;
+                    lo = dweights_ + off;
+                    off += ((size_t)g.n_pad * g.k_pad + 63) / 64 * 64;
+                }
+                launch_prep_gemm_w(d, simt, hi, lo, g, stream_);
+                g.simt = simt;
+                g.hi = hi;
+                g.lo = lo;
+            }
         }
+    } catch (...) {
+        g_launch_counter = prev;
+        throw;
     }
     g_launch_counter = prev;
+    if (off > total) throw Error(3, "gpu: weight arena overflow");
     HAT_CUDA(cudaStreamSynchronize(stream_));
 }
 
 Engine::~Engine() {
     cudaSetDevice(device_);
     if (graph_) cudaGraphExecDestroy(graph_);
+    for (auto& m : marks_) cudaEventDestroy(m.ev);
     if (arena_) cudaFree(arena_);
     if (dweights_) cudaFree(dweights_);
+    if (derr_) cudaFree(derr_);
     if (join_) cudaEventDestroy(join_);
     if (stream_) cudaStreamDestroy(stream_);
 }
@@ -165,10 +195,20 @@ const float* Engine::W(const std::string& name) const {
     return it->second;
 }
 
-const float* Engine::Wconv(const std::string& name) const {
-    auto it = wconv_.find(name);
-    if (it == wconv_.end()) throw Error(2, "gpu: no conv weight `" + name + "`");
+const GemmW& Engine::G(const std::string& name) const {
+    auto it = gw_.find(name);
+    if (it == gw_.end()) throw Error(2, "gpu: no GEMM weight `" + name + "`");
     return it->second;
+}
+
+long Engine::linear(const std::string& wname, const float* x, float* y, const Epi& e) {
+    GemmCtx c{mode_, simt_only_, derr_};
+    return gemm_linear(c, x, G(wname), y, plan_.tokens(), e, stream_);
+}
+
+long Engine::conv(const std::string& wname, const float* x, float* y, int hgt, int wid, const Epi& e) {
+    GemmCtx c{mode_, simt_only_, derr_};
+    return gemm_conv3x3(c, x, G(wname), y, hgt, wid, e, stream_);
 }
 
 size_t Engine::footprint_bytes(int h, int w) const {
@@ -182,17 +222,28 @@ void Engine::check_memory(int h, int w) const {
     size_t fr = 0, tot = 0;
     HAT_CUDA(cudaSetDevice(device_));
     HAT_CUDA(cudaMemGetInfo(&fr, &tot));
-    // The engine's own current arena is reusable, so it counts as available.
-    double avail = (double)fr + (have_plan_ ? (double)Sizes::of(wt_, plan_).total() * sizeof(float) : 0.0);
+    // The engine's current arena is released before a new plan allocates, so it counts.
+    double avail = (double)fr + (have_plan_ ? (double)sizes_.total() * sizeof(float) : 0.0);
     if (need > avail) {
         std::ostringstream o;
         o << "not enough video memory for a " << w << "x" << h << " pass on the GPU\n"
           << "hat: it needs about " << fmt_bytes(need) << " (" << fmt_bytes(acts) << " of device buffers + "
-          << fmt_bytes((double)wt_.f32_bytes) << " of weights + " << fmt_bytes(BASE) << " of runtime, plus "
-          << 5 << "% of slack); " << fmt_bytes(avail) << " is free on the device\n"
+          << fmt_bytes((double)wt_.f32_bytes) << " of weights + " << fmt_bytes(BASE) << " of runtime, plus " << 5
+          << "% of slack); " << fmt_bytes(avail) << " is free on the device\n"
           << "hat: `--mem` runs it in tiles on the device (each tile allocates its own buffers, so the "
              "tile's size is the number that must fit); a smaller image does too";
         throw Error(4, o.str());
+    }
+}
+
+void Engine::check_device_error() {
+    int v = 0;
+    HAT_CUDA(cudaMemcpyAsync(&v, derr_, sizeof(int), cudaMemcpyDeviceToHost, stream_));
+    HAT_CUDA(cudaStreamSynchronize(stream_));
+    if (v) {
+        HAT_CUDA(cudaMemsetAsync(derr_, 0, sizeof(int), stream_));
+        throw Error(3, "gpu: a tensor-core kernel gave up waiting on its pipeline (code " + std::to_string(v) +
+                           "); the pass's output is invalid");
     }
 }
 
@@ -237,9 +288,9 @@ void Engine::ensure_plan(int h, int w) {
     a_->din = take(s.din);
     a_->dout = take(s.dout);
     // THE PREDICTION IS HELD TO THE ALLOCATION (src/gpu.rs:779-786).
-    if (q - arena_ != s.total())
-        throw Error(3, "gpu: the buffer set does not match the guard's prediction");
+    if (q - arena_ != s.total()) throw Error(3, "gpu: the buffer set does not match the guard's prediction");
     plan_ = p;
+    sizes_ = s;
     have_plan_ = true;
     eager_runs_ = 0;
 }
@@ -254,12 +305,12 @@ void Engine::mlp(const std::string& p, float* x) {
     e1.bias = W(p + ".mlp.fc1.bias");
     e1.act = ACT_GELU;
     mark("linear.fc1", 2.0 * P * hid * c, 4.0 * P * (c + hid));
-    launch_linear(mode_, a_->n1, W(p + ".mlp.fc1.weight"), a_->hid, P, hid, c, e1, stream_);
+    linear(p + ".mlp.fc1.weight", a_->n1, a_->hid, e1);
     Epi e2;
     e2.bias = W(p + ".mlp.fc2.bias");
     e2.res = x;
     mark("linear.fc2", 2.0 * P * hid * c, 4.0 * P * (hid + 2 * c));
-    launch_linear(mode_, a_->hid, W(p + ".mlp.fc2.weight"), x, P, c, hid, e2, stream_);
+    linear(p + ".mlp.fc2.weight", a_->hid, x, e2);
 }
 
 // One HAB (hat_arch.py:266-309; src/gpu.rs:469-520): `in` is the block input, `out`
@@ -271,27 +322,27 @@ void Engine::hab(int stage, int blk, const float* in, float* out) {
     const std::string cb = p + ".conv_block.cab";
     mark("layernorm", 0, 8.0 * P * c);
     launch_layernorm(in, W(p + ".norm1.weight"), W(p + ".norm1.bias"), a_->n1, P, c, stream_);
-    // CAB: conv c→cc + GELU, conv cc→c with the channel sums of its output, the gate.
+    // CAB: conv c→cc + GELU; conv cc→c with per-tile channel sums of its output; the gate.
     Epi ec1;
     ec1.bias = W(cb + ".0.bias");
     ec1.act = ACT_GELU;
+    ec1.ldo = sizes_.cmid_stride;
     mark("conv.cab1", 18.0 * P * c * cc, 4.0 * P * (c + cc));
-    launch_conv3x3(mode_, a_->n1, Wconv(cb + ".0.weight"), a_->cmid, plan_.hp, plan_.wp, c, cc, ec1, stream_);
-    mark("conv.cab2", 18.0 * P * c * cc, 4.0 * P * (c + cc));
-    HAT_CUDA(cudaMemsetAsync(a_->chsum, 0, c * sizeof(float), stream_));
+    conv(cb + ".0.weight", a_->n1, a_->cmid, plan_.hp, plan_.wp, ec1);
     Epi ec2;
     ec2.bias = W(cb + ".2.bias");
     ec2.colsum = a_->chsum;
-    launch_conv3x3(mode_, a_->cmid, Wconv(cb + ".2.weight"), a_->convx, plan_.hp, plan_.wp, cc, c, ec2, stream_);
-    mark("ca_gate", 0, 0);
-    launch_ca_gate(a_->chsum, 1.f / (float)P, W(cb + ".3.attention.1.weight"), W(cb + ".3.attention.1.bias"),
+    mark("conv.cab2", 18.0 * P * c * cc, 4.0 * P * (c + cc));
+    long rows = conv(cb + ".2.weight", a_->cmid, a_->convx, plan_.hp, plan_.wp, ec2);
+    mark("ca_gate", 0, 4.0 * rows * c);
+    launch_ca_gate(a_->chsum, rows, 1.f / (float)P, W(cb + ".3.attention.1.weight"), W(cb + ".3.attention.1.bias"),
                    W(cb + ".3.attention.3.weight"), W(cb + ".3.attention.3.bias"), a_->gate, c, wt_.squeezed,
                    stream_);
     // Attention on the normed plane; odd blocks are shifted by win/2 with the mask.
     Epi eq;
     eq.bias = W(p + ".attn.qkv.bias");
     mark("linear.qkv", 6.0 * P * c * c, 16.0 * P * c);
-    launch_linear(mode_, a_->n1, W(p + ".attn.qkv.weight"), a_->qkv, P, 3 * c, c, eq, stream_);
+    linear(p + ".attn.qkv.weight", a_->n1, a_->qkv, eq);
     const int shift = blk % 2 ? plan_.shift : 0;
     mark("attn.window", 4.0 * P * 256 * c, 16.0 * P * c);
     launch_window_attention(mode_, a_->qkv, W(p + ".attn.relative_position_bias_table"), a_->attn, plan_, c,
@@ -304,7 +355,7 @@ void Engine::hab(int stage, int blk, const float* in, float* out) {
     ep.gate = a_->gate;
     ep.cscale = wt_.conv_scale;
     mark("linear.proj", 2.0 * P * c * c, 16.0 * P * c);
-    launch_linear(mode_, a_->attn, W(p + ".attn.proj.weight"), out, P, c, c, ep, stream_);
+    linear(p + ".attn.proj.weight", a_->attn, out, ep);
     mlp(p, out);
 }
 
@@ -318,7 +369,7 @@ void Engine::ocab(int stage, const float* in, float* out) {
     Epi eq;
     eq.bias = W(p + ".qkv.bias");
     mark("linear.qkv", 6.0 * P * c * c, 16.0 * P * c);
-    launch_linear(mode_, a_->n1, W(p + ".qkv.weight"), a_->qkv, P, 3 * c, c, eq, stream_);
+    linear(p + ".qkv.weight", a_->n1, a_->qkv, eq);
     mark("attn.overlap", 4.0 * P * 576 * c, 16.0 * P * c);
     launch_overlap_attention(mode_, a_->qkv, W(p + ".relative_position_bias_table"), a_->attn, plan_, c, wt_.heads,
                              stream_);
@@ -326,7 +377,7 @@ void Engine::ocab(int stage, const float* in, float* out) {
     ep.bias = W(p + ".proj.bias");
     ep.res = in;
     mark("linear.proj", 2.0 * P * c * c, 12.0 * P * c);
-    launch_linear(mode_, a_->attn, W(p + ".proj.weight"), out, P, c, c, ep, stream_);
+    linear(p + ".proj.weight", a_->attn, out, ep);
     mlp(p, out);
 }
 
@@ -340,7 +391,7 @@ void Engine::enqueue_pass() {
     Epi ef;
     ef.bias = W("conv_first.bias");
     mark("conv.first", 54.0 * P * c, 4.0 * P * (3 + c));
-    launch_conv3x3(mode_, a_->x0, Wconv("conv_first.weight"), a_->body, pl.hp, pl.wp, 3, c, ef, stream_);
+    conv("conv_first.weight", a_->x0, a_->body, pl.hp, pl.wp, ef);
     mark("layernorm", 0, 8.0 * P * c);
     launch_layernorm(a_->body, W("patch_embed.norm.weight"), W("patch_embed.norm.bias"), a_->xa, P, c, stream_);
     // The stage input stays in `xa` (the RHAG residual); the blocks run in `xb`, and the
@@ -356,8 +407,7 @@ void Engine::enqueue_pass() {
         er.bias = W("layers." + std::to_string(s) + ".conv.bias");
         er.res = a_->xa;
         mark("conv.rhag", 18.0 * P * c * c, 12.0 * P * c);
-        launch_conv3x3(mode_, a_->xb, Wconv("layers." + std::to_string(s) + ".conv.weight"), a_->xa, pl.hp, pl.wp,
-                       c, c, er, stream_);
+        conv("layers." + std::to_string(s) + ".conv.weight", a_->xb, a_->xa, pl.hp, pl.wp, er);
     }
     mark("layernorm", 0, 8.0 * P * c);
     launch_layernorm(a_->xa, W("norm.weight"), W("norm.bias"), a_->n1, P, c, stream_);
@@ -365,14 +415,13 @@ void Engine::enqueue_pass() {
     eb.bias = W("conv_after_body.bias");
     eb.res = a_->body;
     mark("conv.body", 18.0 * P * c * c, 12.0 * P * c);
-    launch_conv3x3(mode_, a_->n1, Wconv("conv_after_body.weight"), a_->xb, pl.hp, pl.wp, c, c, eb, stream_);
+    conv("conv_after_body.weight", a_->n1, a_->xb, pl.hp, pl.wp, eb);
     // Head: conv + LeakyReLU, then per block a conv whose store does the PixelShuffle.
     Epi eh;
     eh.bias = W("conv_before_upsample.0.bias");
     eh.act = ACT_LEAKY;
     mark("conv.head", 18.0 * P * c * feat, 4.0 * P * (c + feat));
-    launch_conv3x3(mode_, a_->xb, Wconv("conv_before_upsample.0.weight"), a_->headA, pl.hp, pl.wp, c, feat, eh,
-                   stream_);
+    conv("conv_before_upsample.0.weight", a_->xb, a_->headA, pl.hp, pl.wp, eh);
     float* cur = a_->headA;
     float* nxt = a_->headB;
     int hh = pl.hp, ww = pl.wp;
@@ -382,8 +431,7 @@ void Engine::enqueue_pass() {
         eu.bias = W("upsample." + std::to_string(2 * i) + ".bias");
         eu.shuffle = blocks[i].first;
         mark("conv.up", 18.0 * hh * ww * feat * blocks[i].second, 4.0 * hh * ww * (feat + blocks[i].second));
-        launch_conv3x3(mode_, cur, Wconv("upsample." + std::to_string(2 * i) + ".weight"), nxt, hh, ww, feat,
-                       blocks[i].second, eu, stream_);
+        conv("upsample." + std::to_string(2 * i) + ".weight", cur, nxt, hh, ww, eu);
         hh *= blocks[i].first;
         ww *= blocks[i].first;
         std::swap(cur, nxt);
@@ -397,7 +445,7 @@ void Engine::enqueue_pass() {
     el.img_range = wt_.img_range;
     for (int i = 0; i < 3; ++i) el.mean[i] = wt_.mean[i];
     mark("conv.last", 18.0 * hh * ww * feat * 3, 4.0 * hh * ww * (feat + 3));
-    launch_conv3x3(mode_, cur, Wconv("conv_last.weight"), a_->dout, hh, ww, feat, 3, el, stream_);
+    conv("conv_last.weight", cur, a_->dout, hh, ww, el);
     mark(nullptr, 0, 0);
 }
 
@@ -429,7 +477,10 @@ std::string Engine::profile(int h, int w) {
     profiling_ = false;
     g_launch_counter = prev;
     HAT_CUDA(cudaStreamSynchronize(stream_));
-    struct Agg { int n = 0; double ms = 0, flops = 0, bytes = 0; };
+    struct Agg {
+        int n = 0;
+        double ms = 0, flops = 0, bytes = 0;
+    };
     std::map<std::string, Agg> agg;
     for (size_t i = 0; i + 1 < marks_.size(); ++i) {
         float ms = 0;
@@ -442,6 +493,7 @@ std::string Engine::profile(int h, int w) {
     }
     for (auto& m : marks_) cudaEventDestroy(m.ev);
     marks_.clear();
+    check_device_error();
     std::ostringstream o;
     o << "{";
     bool first = true;
@@ -527,6 +579,7 @@ void Engine::forward_host(int n, int h, int w, const float* in, float* out) {
         HAT_CUDA(cudaMemcpyAsync(out + i * outN, a_->dout, outN * sizeof(float), cudaMemcpyDeviceToHost, stream_));
     }
     HAT_CUDA(cudaStreamSynchronize(stream_));
+    check_device_error();
 }
 
 }  // namespace hat

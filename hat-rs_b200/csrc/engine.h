@@ -10,6 +10,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "umma.cuh"
 #include "weights.h"
 
 namespace hat {
@@ -20,6 +21,7 @@ namespace hat {
 struct Sizes {
     long x0 = 0, body = 0, xa = 0, xb = 0, n1 = 0, cmid = 0, convx = 0, qkv = 0, attn = 0, hid = 0;
     long chsum = 0, gate = 0, headA = 0, headB = 0, din = 0, dout = 0;
+    int cmid_stride = 0;  // channel stride of the CAB's middle plane
     static Sizes of(const Weights& wt, const Plan& p);
     long total() const {
         return x0 + body + xa + xb + n1 + cmid + convx + qkv + attn + hid + chsum + gate + headA + headB + din + dout;
@@ -39,21 +41,25 @@ public:
     size_t footprint_bytes(int h, int w) const;
     void check_memory(int h, int w) const;  // throws Error(4, refusal) when it does not fit
     uint64_t launches() const { return launches_; }
+    cudaStream_t stream() const { return stream_; }
     // Per-kind device time of one eager pass, as JSON (see Engine::profile).
     std::string profile(int h, int w);
-    cudaStream_t stream() const { return stream_; }
+    // Reads (and clears) the tensor-core kernels' error flag; throws if it was set.
+    void check_device_error();
 
 private:
     struct Acts;
     void ensure_plan(int h, int w);
     void run_graph(cudaStream_t run);  // the whole pass over the internal din/dout buffers
-    void enqueue_pass();     // the launch sequence itself
+    void enqueue_pass();               // the launch sequence itself
     void hab(int stage, int blk, const float* in, float* out);
     void ocab(int stage, const float* in, float* out);
     void mlp(const std::string& p, float* x);
     void mark(const char* kind, double flops, double bytes);
     const float* W(const std::string& name) const;
-    const float* Wconv(const std::string& name) const;  // reordered [cout][9][cin]
+    const GemmW& G(const std::string& name) const;
+    long linear(const std::string& wname, const float* x, float* y, const Epi& e);
+    long conv(const std::string& wname, const float* x, float* y, int hgt, int wid, const Epi& e);
 
     Weights wt_;
     int device_ = 0, mode_ = 0;
@@ -61,23 +67,25 @@ private:
     cudaStream_t stream_ = nullptr;
     cudaEvent_t join_ = nullptr;
     float* dweights_ = nullptr;
+    int* derr_ = nullptr;
     std::map<std::string, const float*> w_;
-    std::map<std::string, const float*> wconv_;
+    std::map<std::string, GemmW> gw_;
     Plan plan_;
     bool have_plan_ = false;
+    Sizes sizes_;
     float* arena_ = nullptr;
     std::unique_ptr<Acts> a_;
     cudaGraphExec_t graph_ = nullptr;
     int eager_runs_ = 0;
     uint64_t launches_ = 0;
-    uint64_t per_pass_ = 0;
+    uint64_t per_pass_ = 0;  // kernel launches in one pass (counted on the eager run)
     struct Mark {
         std::string kind;
         double flops, bytes;
         cudaEvent_t ev;
     };
     bool profiling_ = false;
-    std::vector<Mark> marks_;  // kernel launches in one pass (counted on the eager run)
+    std::vector<Mark> marks_;
 };
 
 }  // namespace hat

@@ -2,7 +2,7 @@
 // GEMM over K = 9 * cin), with the fused epilogues the HAT graph needs. This is the
 // exact-fp32 path: it serves shapes the tensor-core kernel does not take and is the
 // on-device cross-check for it.
-#include "common.cuh"
+#include "umma.cuh"
 
 namespace hat {
 
@@ -21,12 +21,12 @@ struct ALinear {
 // zero outside the plane (Conv2d padding 1).
 struct AConv {
     const float* x;
-    int hgt, wid, cin;
+    int hgt, wid, cin, ldc;  // ldc: channel stride of the plane (>= cin)
     __device__ __forceinline__ const float* at(long m, int kk, bool& ok) const {
         int tap = kk / cin, ci = kk - tap * cin;
         int y = (int)(m / wid) + tap / 3 - 1, xx = (int)(m % wid) + tap % 3 - 1;
         ok = y >= 0 && y < hgt && xx >= 0 && xx < wid;
-        return x + ((long)y * wid + xx) * cin + ci;
+        return x + ((long)y * wid + xx) * ldc + ci;
     }
     __device__ __forceinline__ float ld(long m, int kk) const {
         bool ok;
@@ -63,7 +63,7 @@ __device__ __forceinline__ void epi_store(const Epi& e, float* y, long gm, int g
         y[(oy * ((long)wid * r) + ox) * cout + c] = v;
         return;
     }
-    long idx = gm * n + gn;
+    long idx = gm * (e.ldo ? e.ldo : n) + gn;
     if (e.cx)
         v = (e.res[idx] + v) + (e.cx[idx] * e.gate[gn]) * e.cscale;
     else if (e.res)
@@ -155,6 +155,7 @@ __global__ void __launch_bounds__(256) k_gemm_simt(AL al, const float* __restric
         }
     }
     if (e.colsum) {
+        // Deterministic: one partial row per M tile, summed in tile order by the gate.
 #pragma unroll
         for (int j = 0; j < TN; ++j) red[ty][tx + 16 * j] = cs[j];
         __syncthreads();
@@ -162,7 +163,7 @@ __global__ void __launch_bounds__(256) k_gemm_simt(AL al, const float* __restric
             float s = 0.f;
 #pragma unroll
             for (int r = 0; r < 16; ++r) s += red[r][tid];
-            atomicAdd(e.colsum + n0 + tid, s);
+            e.colsum[(long)blockIdx.x * N + n0 + tid] = s;
         }
     }
 }
@@ -200,15 +201,17 @@ static void run_simt(const AL& al, bool vec, const float* w, float* y, long m, i
     count_launch();
 }
 
-void launch_linear_simt(const float* x, const float* w, float* y, long m, int n, int k,
-                        const Epi& e, cudaStream_t st) {
-    run_simt(ALinear{x, k}, k % 4 == 0, w, y, m, n, k, e, 1, st);
+long simt_linear(const float* x, const GemmW& w, float* y, long m, const Epi& e, cudaStream_t st) {
+    run_simt(ALinear{x, w.k}, w.k % 4 == 0, w.simt, y, m, w.n, w.k, e, 1, st);
+    return (m + 127) / 128;
 }
 
-void launch_conv3x3_simt(const float* x, const float* wr, float* y, int hgt, int wid, int cin,
-                         int cout, const Epi& e, cudaStream_t st) {
-    run_simt(AConv{x, hgt, wid, cin}, cin % 4 == 0, wr, y, (long)hgt * wid, cout, 9 * cin, e,
-             wid, st);
+long simt_conv3x3(const float* x, const GemmW& w, float* y, int hgt, int wid, const Epi& e, cudaStream_t st) {
+    const int ldc = w.cin_plane ? w.cin_plane : w.cin;
+    const long m = (long)hgt * wid;
+    run_simt(AConv{x, hgt, wid, w.cin, ldc}, w.cin % 4 == 0 && ldc % 4 == 0, w.simt, y, m, w.n, 9 * w.cin, e, wid,
+             st);
+    return (m + 127) / 128;
 }
 
 }  // namespace hat

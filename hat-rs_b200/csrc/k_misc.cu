@@ -82,40 +82,26 @@ void launch_layernorm(const float* x, const float* g, const float* b, float* y, 
     count_launch();
 }
 
-// ---------------------------------------------------------------- conv weight reorder
-// [cout][cin][3][3] → [cout][9][cin]: the GEMM's K index becomes tap * cin + ci, so a
-// K run of one tap is a contiguous channel run of one neighbour pixel.
-__global__ void k_reorder_conv(const float* __restrict__ w, float* __restrict__ wr, int cout, int cin) {
-    long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
-    long n = (long)cout * cin * 9;
-    if (i >= n) return;
-    int tap = (int)(i % 9);
-    long r = i / 9;
-    int ci = (int)(r % cin);
-    int co = (int)(r / cin);
-    wr[((long)co * 9 + tap) * cin + ci] = w[i];
-}
-
-void launch_reorder_conv(const float* w, float* wr, int cout, int cin, cudaStream_t st) {
-    long n = (long)cout * cin * 9;
-    k_reorder_conv<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(w, wr, cout, cin);
-    HAT_CUDA(cudaGetLastError());
-    count_launch();
-}
-
 // ---------------------------------------------------------------- channel attention
 // ChannelAttention after the pool (hat_arch.py:40-57): `sums` holds the per-channel
 // sums of the CAB's second conv over the plane; one CTA computes the gate.
-__global__ void k_ca_gate(const float* __restrict__ sums, float inv_count, const float* __restrict__ w1,
-                          const float* __restrict__ b1, const float* __restrict__ w2,
+__global__ void k_ca_gate(const float* __restrict__ partial, long rows, float inv_count,
+                          const float* __restrict__ w1, const float* __restrict__ b1, const float* __restrict__ w2,
                           const float* __restrict__ b2, float* __restrict__ gate, int c, int sq) {
     extern __shared__ float sm[];
     float* mean = sm;        // [c]
     float* hid = sm + c;     // [sq]
-    for (int i = threadIdx.x; i < c; i += blockDim.x) mean[i] = sums[i] * inv_count;
+    const int warp = threadIdx.x / 32, lane = threadIdx.x & 31, nwarp = blockDim.x / 32;
+    // The plane sum: one warp per channel, lanes stride the partial rows, and a fixed
+    // shuffle tree combines them, so the result is identical on every run.
+    for (int i = warp; i < c; i += nwarp) {
+        float a = 0.f;
+        for (long r = lane; r < rows; r += 32) a += partial[r * c + i];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+        if (lane == 0) mean[i] = a * inv_count;
+    }
     __syncthreads();
-    // one warp per squeezed channel
-    int warp = threadIdx.x / 32, lane = threadIdx.x & 31, nwarp = blockDim.x / 32;
     for (int j = warp; j < sq; j += nwarp) {
         float a = 0.f;
         for (int i = lane; i < c; i += 32) a += w1[(long)j * c + i] * mean[i];
@@ -131,9 +117,9 @@ __global__ void k_ca_gate(const float* __restrict__ sums, float inv_count, const
     }
 }
 
-void launch_ca_gate(const float* sums, float inv_count, const float* w1, const float* b1,
+void launch_ca_gate(const float* partial, long rows, float inv_count, const float* w1, const float* b1,
                     const float* w2, const float* b2, float* gate, int c, int sq, cudaStream_t st) {
-    k_ca_gate<<<1, 256, (c + sq) * sizeof(float), st>>>(sums, inv_count, w1, b1, w2, b2, gate, c, sq);
+    k_ca_gate<<<1, 1024, (c + sq) * sizeof(float), st>>>(partial, rows, inv_count, w1, b1, w2, b2, gate, c, sq);
     HAT_CUDA(cudaGetLastError());
     count_launch();
 }

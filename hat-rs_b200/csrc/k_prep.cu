@@ -1,0 +1,96 @@
+// Weight preparation for the GEMM kernels (once, at upload) and the dispatch between
+// the tensor-core and CUDA-core GEMMs.
+#include "umma.cuh"
+
+namespace hat {
+
+void plan_gemm_w(GemmW& g, int n, int k_or_cin, bool conv, int cin_plane) {
+    g.n = n;
+    g.conv = conv;
+    if (conv) {
+        g.cin = k_or_cin;
+        g.k = 9 * k_or_cin;
+        g.cin_plane = cin_plane;
+        g.cinp = k_or_cin <= 8 ? 8 : (k_or_cin + 31) / 32 * 32;
+        // Tensor cores need a 16-byte channel stride for TMA, and the channel chunk of a
+        // tap must fit the plane's padded stride.
+        g.umma = cin_plane % 4 == 0 && cin_plane >= (k_or_cin <= 8 ? 8 : 4) && k_or_cin >= 4;
+        g.k_pad = 9 * g.cinp;
+    } else {
+        g.k = k_or_cin;
+        g.cin_plane = 0;
+        g.umma = k_or_cin % 4 == 0;
+        g.k_pad = (k_or_cin + 31) / 32 * 32;
+    }
+    g.bn = umma_bn(n);
+    g.n_pad = (n + g.bn - 1) / g.bn * g.bn;
+}
+
+size_t gemm_w_floats(const GemmW& g) {
+    size_t s = (size_t)g.n * g.k;
+    if (g.umma) s += 2 * (size_t)g.n_pad * g.k_pad;
+    return s;
+}
+
+// simt: linear copy or conv reorder [n][cin][3][3] → [n][9][cin].
+__global__ void k_prep_simt(const float* __restrict__ w, float* __restrict__ out, int n, int cin, bool conv) {
+    long total = conv ? (long)n * cin * 9 : (long)n * cin;
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        if (!conv) {
+            out[i] = w[i];
+        } else {
+            int tap = (int)(i % 9);
+            long r = i / 9;
+            int ci = (int)(r % cin);
+            int co = (int)(r / cin);
+            out[((long)co * 9 + tap) * cin + ci] = w[i];
+        }
+    }
+}
+
+// hi/lo: the tensor-core layout [n_pad][k_pad] (conv: k = tap * cinp + ci), zero padded.
+__global__ void k_prep_umma(const float* __restrict__ w, float* __restrict__ hi, float* __restrict__ lo, int n,
+                            int k, int n_pad, int k_pad, bool conv, int cin, int cinp) {
+    long total = (long)n_pad * k_pad;
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        int row = (int)(i / k_pad), kk = (int)(i % k_pad);
+        float v = 0.f;
+        if (row < n) {
+            if (!conv) {
+                if (kk < k) v = w[(long)row * k + kk];
+            } else {
+                int tap = kk / cinp, ci = kk - tap * cinp;
+                if (tap < 9 && ci < cin) v = w[((long)row * cin + ci) * 9 + tap];
+            }
+        }
+        float h = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+        hi[i] = h;
+        lo[i] = v - h;
+    }
+}
+
+void launch_prep_gemm_w(const float* w, float* simt, float* hi, float* lo, const GemmW& g, cudaStream_t st) {
+    k_prep_simt<<<256, 256, 0, st>>>(w, simt, g.n, g.conv ? g.cin : g.k, g.conv);
+    HAT_CUDA(cudaGetLastError());
+    count_launch();
+    if (g.umma) {
+        k_prep_umma<<<512, 256, 0, st>>>(w, hi, lo, g.n, g.k, g.n_pad, g.k_pad, g.conv, g.cin, g.cinp);
+        HAT_CUDA(cudaGetLastError());
+        count_launch();
+    }
+}
+
+long gemm_linear(const GemmCtx& c, const float* x, const GemmW& w, float* y, long m, const Epi& e, cudaStream_t st) {
+    if (!c.simt_only && w.umma && !e.planar_out && !e.shuffle)
+        return umma_linear(c.mode, x, w, y, m, e, c.err, st);
+    return simt_linear(x, w, y, m, e, st);
+}
+
+long gemm_conv3x3(const GemmCtx& c, const float* x, const GemmW& w, float* y, int hgt, int wid, const Epi& e,
+                  cudaStream_t st) {
+    if (!c.simt_only && w.umma && hgt % 8 == 0 && wid % 16 == 0)
+        return umma_conv3x3(c.mode, x, w, y, hgt, wid, e, c.err, st);
+    return simt_conv3x3(x, w, y, hgt, wid, e, st);
+}
+
+}  // namespace hat

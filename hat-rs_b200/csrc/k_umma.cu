@@ -1,0 +1,597 @@
+// Tensor-core GEMM for sm_100a: tcgen05.mma (kind::tf32) with the accumulator in
+// tensor memory, operands staged in shared memory by TMA, one persistent CTA per SM.
+//
+//   D[m][n] = sum_k A[m][k] * B[n][k]       A: activations, B: weights (both K-major)
+//
+// A is either a token plane [M][K] (the HAT linears) or, for a 3x3 convolution as an
+// implicit GEMM, an 8x16 pixel patch of an [H][W][C] plane shifted by each tap: the
+// K loop runs over (tap, 32-channel chunk) and TMA's zero fill outside the plane is
+// the conv's zero padding.
+//
+// fp32 parity ("3xTF32"): every operand x is split into x_hi = x with the low 13
+// mantissa bits cleared (exactly representable in tf32) and x_lo = x - x_hi, and
+//   A.B ~= A_hi.B_hi + A_hi.B_lo + A_lo.B_hi,
+// which drops only A_lo.B_lo (relative 2^-22). The weights are split once at upload;
+// the activation tile is split in shared memory by four converter warps between its
+// TMA landing and the MMA. FAST mode issues the single A.B product on the raw tiles.
+//
+// Warp roles (320 threads): 0 TMA producer, 1 MMA issuer + TMEM owner, 2-5 converters,
+// 6-9 epilogue (TMEM -> registers -> fused epilogue -> global). Two TMEM accumulators
+// (2 x 256 columns) let the epilogue of one tile overlap the MMAs of the next.
+//
+// Every mbarrier wait is bounded (1 s of wall time); on expiry the kernel records an
+// error code in `err`, every role leaves its loop, in-flight TMA copies and MMAs are
+// waited for (again bounded) and TMEM is released before the CTA exits.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "umma.cuh"
+
+namespace hat {
+
+namespace {
+
+constexpr int NTHREADS = 320;
+constexpr unsigned long long WAIT_NS = 1000000000ull;  // 1 s per wait
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ unsigned long long now_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* b, int count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait: false (with the abort flag raised and the error recorded) on expiry
+// or when another role has already aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort, int* err, int code) {
+    if (mbar_try(b, parity)) return true;
+    unsigned long long t0 = now_ns();
+    while (true) {
+        if (mbar_try(b, parity)) return true;
+        if (*abort) return false;
+        if (now_ns() - t0 > WAIT_NS) {
+            *abort = 1;
+            atomicCAS(err, 0, code);
+            return false;
+        }
+    }
+}
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(smem_u32(dst)), "l"((uint64_t)map), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tma_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+        ::"r"(smem_u32(dst)), "l"((uint64_t)map), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, rows of `rowbytes` (128: SWIZZLE_128B,
+// 32: SWIZZLE_32B), 8-row core groups `8*rowbytes` apart.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, int rowbytes) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr & 0x3FFFF) >> 4);
+    d |= (uint64_t)1 << 16;                              // leading byte offset (unused here)
+    d |= (uint64_t)((8 * rowbytes) >> 4) << 32;          // stride byte offset
+    d |= (uint64_t)1 << 46;                              // descriptor version (sm_100)
+    d |= (uint64_t)(rowbytes == 128 ? 2 : 6) << 61;      // swizzle mode
+    return d;
+}
+// Instruction descriptor of kind::tf32: f32 accumulate, tf32 A and B, both K-major.
+__host__ __device__ constexpr uint32_t idesc_tf32(int m, int n) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+__device__ __forceinline__ void mma_tf32(uint32_t dtmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n"
+        ::"r"(dtmem), "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ float epi_act(float v, int act) {
+    if (act == ACT_GELU) return 0.5f * v * (1.f + erff(v * 0.70710678118654752f));
+    if (act == ACT_LEAKY) return v > 0.f ? v : 0.01f * v;
+    return v;
+}
+
+}  // namespace
+
+// One launch's geometry.
+struct UmmaArgs {
+    long M;          // rows (tokens / pixels)
+    int N, BN, ntn;  // output columns, columns per tile, tiles along N
+    int KB;          // k-blocks per tile
+    int ckb;         // bytes of K per k-block row: 128 (32 fp32) or 32 (8 fp32)
+    int stages;
+    // conv geometry (MODE 1): plane H x W, channel chunks per tap, patch tiles along x
+    int H, W, cchunks, tx;
+    long mtiles, ntiles;
+    float* y;
+    int ldo;         // row stride of the output plane (channels), for plain stores
+    int nstore;      // columns stored (<= ldo)
+    int* err;
+};
+
+template <int MODE, int TERMS>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    k_umma(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmBh,
+           const __grid_constant__ CUtensorMap tmBl, const UmmaArgs g, const Epi e) {
+    extern __shared__ __align__(1024) uint8_t smraw[];
+    __shared__ uint64_t full[4], ready[4], empty[4], acc_full[2], acc_empty[2], drain;
+    __shared__ uint32_t tmem_slot;
+    __shared__ volatile int abort_flag;
+
+    uint8_t* sm = (uint8_t*)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
+    const int S = g.stages;
+    const uint32_t a_bytes = 128 * g.ckb, b_bytes = g.BN * g.ckb;
+    // per stage: A (raw, then hi in place) | A lo | B hi | B lo
+    const uint32_t st_bytes = 2 * a_bytes + 2 * b_bytes;
+    auto sA = [&](int s) { return sm + s * st_bytes; };
+    auto sAl = [&](int s) { return sm + s * st_bytes + a_bytes; };
+    auto sBh = [&](int s) { return sm + s * st_bytes + 2 * a_bytes; };
+    auto sBl = [&](int s) { return sm + s * st_bytes + 2 * a_bytes + b_bytes; };
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&ready[s], 128);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&acc_full[a], 1);
+            mbar_init(&acc_empty[a], 128);
+        }
+        mbar_init(&drain, 1);
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(&tmem_slot)));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    const long ntiles = g.ntiles;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            uint32_t it = 0;
+            const uint32_t tx = TERMS == 3 ? a_bytes + 2 * b_bytes : a_bytes + b_bytes;
+            for (long t = blockIdx.x; t < ntiles && !abort_flag; t += gridDim.x) {
+                const long mt = t / g.ntn;
+                const int nt = (int)(t % g.ntn);
+                for (int kb = 0; kb < g.KB; ++kb, ++it) {
+                    const int s = it % S;
+                    if (!mbar_wait(&empty[s], ((it / S) & 1) ^ 1, &abort_flag, g.err, 1)) break;
+                    mbar_expect_tx(&full[s], tx);
+                    const int kel = kb * (g.ckb / 4);  // K offset in elements
+                    if (MODE == 0) {
+                        tma_2d(sA(s), &tmA, kel, (int)(mt * 128), &full[s]);
+                    } else {
+                        const int tap = kb / g.cchunks, cc = kb - tap * g.cchunks;
+                        const int py = (int)(mt / g.tx), px = (int)(mt % g.tx);
+                        tma_3d(sA(s), &tmA, cc * (g.ckb / 4), px * 16 + tap % 3 - 1, py * 8 + tap / 3 - 1, &full[s]);
+                    }
+                    tma_2d(sBh(s), &tmBh, kel, nt * g.BN, &full[s]);
+                    if (TERMS == 3) tma_2d(sBl(s), &tmBl, kel, nt * g.BN, &full[s]);
+                }
+            }
+            if (abort_flag) {
+                // Let the copies already issued land before the CTA can exit.
+                for (uint32_t j = (it > (uint32_t)S ? it - S : 0); j < it; ++j) {
+                    unsigned long long t0 = now_ns();
+                    while (!mbar_try(&full[j % S], (j / S) & 1) && now_ns() - t0 < WAIT_NS) {
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            uint32_t it = 0, tl = 0;
+            const uint32_t idesc = idesc_tf32(128, g.BN);
+            const int ksteps = g.ckb / 32;  // MMA k = 8 tf32 = 32 bytes
+            for (long t = blockIdx.x; t < ntiles && !abort_flag; t += gridDim.x, ++tl) {
+                const int a = tl & 1;
+                if (!mbar_wait(&acc_empty[a], ((tl >> 1) & 1) ^ 1, &abort_flag, g.err, 2)) break;
+                tc_fence_after();
+                const uint32_t d = tmem + a * 256;
+                bool ok = true;
+                for (int kb = 0; kb < g.KB; ++kb, ++it) {
+                    const int s = it % S;
+                    uint64_t* rb = TERMS == 3 ? &ready[s] : &full[s];
+                    if (!mbar_wait(rb, (it / S) & 1, &abort_flag, g.err, 3)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t ah = smem_u32(sA(s)), al = smem_u32(sAl(s));
+                    const uint32_t bh = smem_u32(sBh(s)), bl = smem_u32(sBl(s));
+#pragma unroll 1
+                    for (int k = 0; k < ksteps; ++k) {
+                        const uint32_t off = k * 32;
+                        const uint32_t acc0 = (kb | k) ? 1u : 0u;
+                        if (TERMS == 3) {
+                            mma_tf32(d, smem_desc(al + off, g.ckb), smem_desc(bh + off, g.ckb), idesc, acc0);
+                            mma_tf32(d, smem_desc(ah + off, g.ckb), smem_desc(bl + off, g.ckb), idesc, 1u);
+                            mma_tf32(d, smem_desc(ah + off, g.ckb), smem_desc(bh + off, g.ckb), idesc, 1u);
+                        } else {
+                            mma_tf32(d, smem_desc(ah + off, g.ckb), smem_desc(bh + off, g.ckb), idesc, acc0);
+                        }
+                    }
+                    mma_commit(&empty[s]);
+                }
+                if (!ok) break;
+                mma_commit(&acc_full[a]);
+            }
+            // Every MMA issued so far completes before TMEM can be released.
+            mma_commit(&drain);
+            unsigned long long t0 = now_ns();
+            while (!mbar_try(&drain, 0) && now_ns() - t0 < WAIT_NS) {
+            }
+        }
+    } else if (warp < 6) {
+        // ------------------------------------------------------------ converters
+        if (TERMS == 3) {
+            const int ct = threadIdx.x - 64;  // 0..127
+            uint32_t it = 0;
+            const int nvec = a_bytes / 16;    // float4s per A tile
+            for (long t = blockIdx.x; t < ntiles; t += gridDim.x) {
+                if (__any_sync(0xffffffffu, abort_flag != 0)) break;
+                bool ok = true;
+                for (int kb = 0; kb < g.KB; ++kb, ++it) {
+                    const int s = it % S;
+                    // warp-uniform outcome: every lane waits, and the warp leaves together
+                    const bool got = mbar_wait(&full[s], (it / S) & 1, &abort_flag, g.err, 4);
+                    if (!__all_sync(0xffffffffu, got)) {
+                        ok = false;
+                        break;
+                    }
+                    float4* hi = reinterpret_cast<float4*>(sA(s));
+                    float4* lo = reinterpret_cast<float4*>(sAl(s));
+                    for (int i = ct; i < nvec; i += 128) {
+                        float4 v = hi[i], h, l;
+                        h.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+                        h.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+                        h.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+                        h.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+                        l.x = v.x - h.x;
+                        l.y = v.y - h.y;
+                        l.z = v.z - h.z;
+                        l.w = v.w - h.w;
+                        hi[i] = h;
+                        lo[i] = l;
+                    }
+                    // Each thread makes its generic-proxy stores visible to the tensor
+                    // core's async proxy, then arrives (128 arrivals complete the phase).
+                    fence_proxy_async();
+                    mbar_arrive(&ready[s]);
+                }
+                if (!ok) break;
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int q = warp & 3;          // TMEM lane quarter this warp may read
+        const int row = q * 32 + lane;   // tile row of this thread
+        const int ew = warp - 6;         // 0..3 within the epilogue group
+        uint32_t tl = 0;
+        for (long t = blockIdx.x; t < ntiles; t += gridDim.x, ++tl) {
+            if (__any_sync(0xffffffffu, abort_flag != 0)) break;
+            const int a = tl & 1;
+            const bool got = mbar_wait(&acc_full[a], (tl >> 1) & 1, &abort_flag, g.err, 5);
+            if (!__all_sync(0xffffffffu, got)) break;
+            tc_fence_after();
+            const long mt = t / g.ntn;
+            const int nt = (int)(t % g.ntn);
+            long m;
+            bool valid;
+            int py = 0, px = 0;
+            if (MODE == 0) {
+                m = mt * 128 + row;
+                valid = m < g.M;
+            } else {
+                py = (int)(mt / g.tx) * 8 + row / 16;
+                px = (int)(mt % g.tx) * 16 + row % 16;
+                m = (long)py * g.W + px;
+                valid = py < g.H;
+            }
+            const int n0 = nt * g.BN;
+            const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + a * 256;
+            if (e.shuffle == 2 && g.BN % 32 == 0 && g.N % g.BN == 0) {
+                // PixelShuffle(2) store: channel n = 4c + 2i + j goes to channel c of output
+                // pixel (2y + i, 2x + j). 32 columns give 8 consecutive output channels for
+                // each of the 4 sub-pixels: two float4 stores per sub-pixel.
+                const int cout = g.N / 4;
+                for (int c0 = 0; c0 < g.BN; c0 += 32) {
+                    float v[32];
+                    tmem_ld16(taddr + c0, v);
+                    tmem_ld16(taddr + c0 + 16, v + 16);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = epi_act(v[j] + (e.bias ? e.bias[n0 + c0 + j] : 0.f), e.act);
+                    if (valid) {
+                        const int cb = (n0 + c0) / 4;
+#pragma unroll
+                        for (int sub = 0; sub < 4; ++sub) {
+                            const long oy = 2L * py + (sub >> 1), ox = 2L * px + (sub & 1);
+                            float* dst = g.y + (oy * (2L * g.W) + ox) * cout + cb;
+                            *reinterpret_cast<float4*>(dst) = make_float4(v[sub], v[4 + sub], v[8 + sub], v[12 + sub]);
+                            *reinterpret_cast<float4*>(dst + 4) =
+                                make_float4(v[16 + sub], v[20 + sub], v[24 + sub], v[28 + sub]);
+                        }
+                    }
+                }
+                tc_fence_before();
+                mbar_arrive(&acc_empty[a]);
+                continue;
+            }
+            for (int c0 = 0; c0 < g.BN; c0 += 16) {
+                float v[16];
+                tmem_ld16(taddr + c0, v);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int n = n0 + c0 + j;
+                    v[j] = n < g.N ? epi_act(v[j] + (e.bias ? e.bias[n] : 0.f), e.act) : 0.f;
+                }
+                if (valid) {
+                    if (e.planar_out) {
+                        const int wid = MODE == 0 ? 1 : g.W;
+                        const int yy = (int)(m / wid), xx = (int)(m % wid);
+                        if (yy < e.oh && xx < e.ow)
+                            for (int j = 0; j < 16; ++j) {
+                                const int n = n0 + c0 + j;
+                                if (n < g.N) g.y[((long)n * e.oh + yy) * e.ow + xx] = v[j] / e.img_range + e.mean[n];
+                            }
+                    } else if (e.shuffle) {
+                        const int r = e.shuffle, cout = g.N / (r * r);
+                        for (int j = 0; j < 16; ++j) {
+                            const int n = n0 + c0 + j;
+                            if (n >= g.N) break;
+                            const int c = n / (r * r), rem = n - c * r * r, i = rem / r, jj = rem - i * r;
+                            const long oy = (long)py * r + i, ox = (long)px * r + jj;
+                            g.y[(oy * ((long)g.W * r) + ox) * cout + c] = v[j];
+                        }
+                    } else {
+                        float* dst = g.y + m * g.ldo + n0 + c0;
+                        const long base = m * g.ldo + n0 + c0;
+                        if (n0 + c0 + 16 <= g.nstore && (g.ldo % 4) == 0) {
+#pragma unroll
+                            for (int j4 = 0; j4 < 4; ++j4) {
+                                float4 o = make_float4(v[4 * j4], v[4 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3]);
+                                if (e.cx) {
+                                    const float4 r = *reinterpret_cast<const float4*>(e.res + base + 4 * j4);
+                                    const float4 cx = *reinterpret_cast<const float4*>(e.cx + base + 4 * j4);
+                                    const int n = n0 + c0 + 4 * j4;
+                                    o.x = (r.x + o.x) + (cx.x * e.gate[n]) * e.cscale;
+                                    o.y = (r.y + o.y) + (cx.y * e.gate[n + 1]) * e.cscale;
+                                    o.z = (r.z + o.z) + (cx.z * e.gate[n + 2]) * e.cscale;
+                                    o.w = (r.w + o.w) + (cx.w * e.gate[n + 3]) * e.cscale;
+                                } else if (e.res) {
+                                    const float4 r = *reinterpret_cast<const float4*>(e.res + base + 4 * j4);
+                                    o.x = r.x + o.x;
+                                    o.y = r.y + o.y;
+                                    o.z = r.z + o.z;
+                                    o.w = r.w + o.w;
+                                }
+                                *reinterpret_cast<float4*>(dst + 4 * j4) = o;
+                            }
+                        } else {
+                            for (int j = 0; j < 16; ++j) {
+                                const int n = n0 + c0 + j;
+                                if (n >= g.nstore) break;
+                                float o = v[j];
+                                if (e.cx)
+                                    o = (e.res[base + j] + o) + (e.cx[base + j] * e.gate[n]) * e.cscale;
+                                else if (e.res)
+                                    o = e.res[base + j] + o;
+                                dst[j] = o;
+                            }
+                        }
+                    }
+                }
+                if (e.colsum) {
+                    // Column sums of this warp's 32 rows, reduced in a fixed order: one
+                    // partial row per (tile, epilogue warp), no atomics, no cross-warp sync.
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        float s = valid ? v[j] : 0.f;
+#pragma unroll
+                        for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+                        const int n = n0 + c0 + j;
+                        if (lane == 0 && n < g.N) e.colsum[(mt * 4 + ew) * g.N + n] = s;
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&acc_empty[a]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+    }
+}
+
+// ------------------------------------------------------------------ host side
+
+// cuTensorMapEncodeTiled, fetched from the driver through the runtime so the library
+// does not link libcuda itself.
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        cudaDriverEntryPointQueryResult q;
+        void* p = nullptr;
+        HAT_CUDA(cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q));
+        if (q != cudaDriverEntryPointSuccess || !p) throw Error(3, "cuTensorMapEncodeTiled is unavailable");
+        fn = (EncodeTiledFn)p;
+    }
+    return fn;
+}
+
+static CUtensorMap make_map(const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
+                            const uint32_t* box, int rowbytes) {
+    CUtensorMap m;
+    uint32_t es[5] = {1, 1, 1, 1, 1};
+    CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank, const_cast<void*>(base), dims,
+                             strides_bytes, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             rowbytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_32B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw Error(3, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+    return m;
+}
+
+static int num_sms() {
+    static int n[64] = {0};
+    int dev = 0;
+    HAT_CUDA(cudaGetDevice(&dev));
+    if (!n[dev & 63]) HAT_CUDA(cudaDeviceGetAttribute(&n[dev & 63], cudaDevAttrMultiProcessorCount, dev));
+    return n[dev & 63];
+}
+
+template <int MODE, int TERMS>
+static void launch_k(const CUtensorMap& a, const CUtensorMap& bh, const CUtensorMap& bl, const UmmaArgs& g,
+                     const Epi& e, cudaStream_t st) {
+    const size_t smem = (size_t)g.stages * (2 * 128 * g.ckb + 2 * g.BN * g.ckb) + 1024;
+    static unsigned configured = 0;
+    int dev = 0;
+    HAT_CUDA(cudaGetDevice(&dev));
+    if (!(configured & (1u << dev))) {
+        HAT_CUDA(cudaFuncSetAttribute(k_umma<MODE, TERMS>, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448 - 8192));
+        configured |= 1u << dev;
+    }
+    const long grid = std::min<long>(g.ntiles, num_sms());
+    k_umma<MODE, TERMS><<<(unsigned)grid, NTHREADS, smem, st>>>(a, bh, bl, g, e);
+    HAT_CUDA(cudaGetLastError());
+    count_launch();
+}
+
+static int pick_stages(int BN, int ckb) {
+    const long per = 2L * 128 * ckb + 2L * BN * ckb;
+    const long budget = 232448 - 8192 - 1024 - 4096;
+    return (int)std::max(1L, std::min(4L, budget / per));
+}
+
+long umma_linear(int mode, const float* x, const GemmW& w, float* y, long m, const Epi& e, int* err, cudaStream_t st) {
+    const int ckb = 128;
+    uint64_t adims[2] = {(uint64_t)w.k, (uint64_t)m};
+    uint64_t astr[1] = {(uint64_t)w.k * 4};
+    uint32_t abox[2] = {32, 128};
+    CUtensorMap ta = make_map(x, 2, adims, astr, abox, ckb);
+    uint64_t bdims[2] = {(uint64_t)w.k_pad, (uint64_t)w.n_pad};
+    uint64_t bstr[1] = {(uint64_t)w.k_pad * 4};
+    uint32_t bbox[2] = {32, (uint32_t)w.bn};
+    CUtensorMap tbh = make_map(w.hi, 2, bdims, bstr, bbox, ckb);
+    CUtensorMap tbl = make_map(mode == 0 ? w.lo : w.hi, 2, bdims, bstr, bbox, ckb);
+    UmmaArgs g{};
+    g.M = m;
+    g.N = w.n;
+    g.BN = w.bn;
+    g.ntn = w.n_pad / w.bn;
+    g.KB = w.k_pad / 32;
+    g.ckb = ckb;
+    g.stages = pick_stages(w.bn, ckb);
+    g.mtiles = (m + 127) / 128;
+    g.ntiles = g.mtiles * g.ntn;
+    g.y = y;
+    g.ldo = e.ldo ? e.ldo : w.n;
+    g.nstore = e.ldo ? e.ldo : w.n;
+    g.err = err;
+    if (mode == 0)
+        launch_k<0, 3>(ta, tbh, tbl, g, e, st);
+    else
+        launch_k<0, 1>(ta, tbh, tbl, g, e, st);
+    return g.mtiles * 4;  // colsum: one partial row per (tile, epilogue warp)
+}
+
+long umma_conv3x3(int mode, const float* x, const GemmW& w, float* y, int hgt, int wid, const Epi& e, int* err,
+                  cudaStream_t st) {
+    const int ckb = w.cinp == 8 ? 32 : 128;
+    const int cke = ckb / 4;
+    uint64_t adims[3] = {(uint64_t)w.cin_plane, (uint64_t)wid, (uint64_t)hgt};
+    uint64_t astr[2] = {(uint64_t)w.cin_plane * 4, (uint64_t)wid * w.cin_plane * 4};
+    uint32_t abox[3] = {(uint32_t)cke, 16, 8};
+    CUtensorMap ta = make_map(x, 3, adims, astr, abox, ckb);
+    uint64_t bdims[2] = {(uint64_t)w.k_pad, (uint64_t)w.n_pad};
+    uint64_t bstr[1] = {(uint64_t)w.k_pad * 4};
+    uint32_t bbox[2] = {(uint32_t)cke, (uint32_t)w.bn};
+    CUtensorMap tbh = make_map(w.hi, 2, bdims, bstr, bbox, ckb);
+    CUtensorMap tbl = make_map(mode == 0 ? w.lo : w.hi, 2, bdims, bstr, bbox, ckb);
+    UmmaArgs g{};
+    g.M = (long)hgt * wid;
+    g.N = w.n;
+    g.BN = w.bn;
+    g.ntn = w.n_pad / w.bn;
+    g.cchunks = w.cinp / cke;
+    g.KB = 9 * g.cchunks;
+    g.ckb = ckb;
+    g.stages = pick_stages(w.bn, ckb);
+    g.H = hgt;
+    g.W = wid;
+    g.tx = wid / 16;
+    g.mtiles = (long)(hgt / 8) * g.tx;
+    g.ntiles = g.mtiles * g.ntn;
+    g.y = y;
+    g.ldo = e.ldo ? e.ldo : w.n;
+    g.nstore = e.ldo ? e.ldo : w.n;
+    g.err = err;
+    if (mode == 0)
+        launch_k<1, 3>(ta, tbh, tbl, g, e, st);
+    else
+        launch_k<1, 1>(ta, tbh, tbl, g, e, st);
+    return g.mtiles * 4;  // colsum: one partial row per (tile, epilogue warp)
+}
+
+}  // namespace hat

@@ -11,11 +11,6 @@
 #include "../../include/hat_b200.h"
 #include "common.cuh"
 
-namespace hat {
-void launch_linear_simt(const float*, const float*, float*, long, int, int, const Epi&, cudaStream_t);
-void launch_conv3x3_simt(const float*, const float*, float*, int, int, int, int, const Epi&, cudaStream_t);
-}
-
 using namespace hat;
 
 namespace {
@@ -143,11 +138,12 @@ void run_all(Log& log) {
                 ref[(size_t)i * n + j] = a;
             }
         Dev dx(x), dw(w), db(b), dy((size_t)m * n);
-        for (int mode : {HAT_B200_MODE_PARITY}) {
-            hat_b200_linear(mode, dx.p, dw.p, db.p, dy.p, m, n, k, nullptr);
+        for (int mode : {HAT_B200_MODE_SIMT, HAT_B200_MODE_PARITY}) {
+            int rc = hat_b200_linear(mode, dx.p, dw.p, db.p, dy.p, m, n, k, nullptr);
             HAT_CUDA(cudaDeviceSynchronize());
-            log.check("linear " + std::to_string(m) + "x" + std::to_string(n) + "x" + std::to_string(k),
-                      maxdiff(dy.get((size_t)m * n), ref), 2e-5);
+            log.check(std::string(mode == HAT_B200_MODE_SIMT ? "simt " : "tcgen05 3xtf32 ") + "linear " +
+                          std::to_string(m) + "x" + std::to_string(n) + "x" + std::to_string(k),
+                      rc ? 1e9 : maxdiff(dy.get((size_t)m * n), ref), 2e-5);
         }
     }
     // 3x3 convs: the CAB pair, the body conv, the head's thin ends, non-square planes.
@@ -170,11 +166,14 @@ void run_all(Log& log) {
                     ref[((size_t)y * wd + xx) * co + o] = a;
                 }
         Dev dx(x), dw(w), db(b), dy((size_t)hg * wd * co);
-        hat_b200_conv3x3(HAT_B200_MODE_PARITY, dx.p, dw.p, db.p, dy.p, hg, wd, ci, co, nullptr);
-        HAT_CUDA(cudaDeviceSynchronize());
-        log.check("conv3x3 " + std::to_string(hg) + "x" + std::to_string(wd) + " " + std::to_string(ci) + "->" +
-                      std::to_string(co),
-                  maxdiff(dy.get((size_t)hg * wd * co), ref), 5e-5);
+        for (int mode : {HAT_B200_MODE_SIMT, HAT_B200_MODE_PARITY}) {
+            int rc = hat_b200_conv3x3(mode, dx.p, dw.p, db.p, dy.p, hg, wd, ci, co, nullptr);
+            HAT_CUDA(cudaDeviceSynchronize());
+            log.check(std::string(mode == HAT_B200_MODE_SIMT ? "simt " : "tcgen05 3xtf32 ") + "conv3x3 " +
+                          std::to_string(hg) + "x" + std::to_string(wd) + " " + std::to_string(ci) + "->" +
+                          std::to_string(co),
+                      rc ? 1e9 : maxdiff(dy.get((size_t)hg * wd * co), ref), 5e-5);
+        }
     }
     // Attentions: both head dims, shifted and not, square and not.
     for (auto sh : std::vector<std::array<int, 4>>{{32, 48, 144, 8}, {48, 32, 144, 0}, {16, 16, 180, 8}, {32, 32, 180, 0}}) {

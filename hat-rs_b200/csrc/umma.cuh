@@ -1,0 +1,61 @@
+// Weights prepared for the GEMM kernels, and the GEMM launchers (tensor-core and
+// CUDA-core).
+#pragma once
+
+#include "common.cuh"
+
+namespace hat {
+
+// A Linear or 3x3 Conv2d weight in the layouts the kernels read.
+//  * `simt`: linear [n][k]; conv [n][9][cin] (tap-major K).
+//  * `hi`/`lo`: the tensor-core B operand [n_pad][k_pad], K-major, zero padded, split
+//    so that hi is exactly representable in tf32 and hi + lo is the fp32 weight. For a
+//    conv, K = 9 taps x `cinp` channels (cinp = 8, or a multiple of 32).
+struct GemmW {
+    const float* simt = nullptr;
+    const float* hi = nullptr;
+    const float* lo = nullptr;
+    int n = 0, k = 0;       // k = 9 * cin for a conv
+    bool conv = false;
+    int cin = 0;            // conv input channels
+    int cin_plane = 0;      // channel stride of the conv's input plane (>= cin)
+    int cinp = 0;           // conv channels per tap in the tensor-core K layout
+    int bn = 0, n_pad = 0, k_pad = 0;
+    bool umma = false;      // tensor-core layout present
+};
+
+// Columns per tensor-core tile for an output width n: at most 192 (so three pipeline
+// stages fit in shared memory for c = 144), a multiple of 16, tiles of equal width.
+inline int umma_bn(int n) {
+    int tiles = (n + 191) / 192;
+    int per = (n + tiles - 1) / tiles;
+    return (per + 15) / 16 * 16;
+}
+
+// Device-side weight preparation (k_prep.cu). `w` is the PyTorch layout on the device;
+// the outputs are allocated by the caller with the sizes `plan_gemm_w` sets.
+void plan_gemm_w(GemmW& g, int n, int k_or_cin, bool conv, int cin_plane);
+size_t gemm_w_floats(const GemmW& g);  // simt + hi + lo floats
+void launch_prep_gemm_w(const float* w, float* simt, float* hi, float* lo, const GemmW& g, cudaStream_t st);
+
+// Tensor-core launchers; return the number of M tiles (colsum partial rows).
+long umma_linear(int mode, const float* x, const GemmW& w, float* y, long m, const Epi& e, int* err, cudaStream_t st);
+long umma_conv3x3(int mode, const float* x, const GemmW& w, float* y, int hgt, int wid, const Epi& e, int* err,
+                  cudaStream_t st);
+
+// CUDA-core launchers; return the number of M tiles (colsum partial rows).
+long simt_linear(const float* x, const GemmW& w, float* y, long m, const Epi& e, cudaStream_t st);
+long simt_conv3x3(const float* x, const GemmW& w, float* y, int hgt, int wid, const Epi& e, cudaStream_t st);
+
+// What the engine calls: the tensor-core kernel when the shape allows it and
+// `simt_only` is false, else the CUDA-core kernel.
+struct GemmCtx {
+    int mode = 0;
+    bool simt_only = false;
+    int* err = nullptr;   // device error flag of the tensor-core kernels' bounded waits
+};
+long gemm_linear(const GemmCtx& c, const float* x, const GemmW& w, float* y, long m, const Epi& e, cudaStream_t st);
+long gemm_conv3x3(const GemmCtx& c, const float* x, const GemmW& w, float* y, int hgt, int wid, const Epi& e,
+                  cudaStream_t st);
+
+}  // namespace hat

@@ -21,6 +21,7 @@ _LIB_PATH = Path(__file__).resolve().parent / "libhat_b200.so"
 
 MODE_PARITY = 0
 MODE_FAST = 1
+MODE_SIMT = 2  # kernel-level calls only: the CUDA-core fp32 kernels
 
 E_INVAL, E_IO, E_CUDA, E_NOMEM, E_SELFTEST = 1, 2, 3, 4, 5
 

@@ -42,6 +42,8 @@ extern "C" {
  * TF32 products on the tensor cores. */
 #define HAT_B200_MODE_PARITY 0
 #define HAT_B200_MODE_FAST 1
+/* Kernel-level calls only: the CUDA-core fp32 kernels (the on-device cross-check). */
+#define HAT_B200_MODE_SIMT 2
 
 typedef struct hat_b200 hat_b200;
 

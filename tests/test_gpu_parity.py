@@ -49,6 +49,29 @@ def test_golden_parity(case, ckdir):
     be.close()
 
 
+@pytest.mark.parametrize("case", [c for c in cases() if c["name"] in ("hats_x4_48x48_p", "hat_x4_32x48")],
+                         ids=lambda c: c["name"])
+def test_golden_fast_mode_psnr(case, ckdir):
+    """The TF32 fast mode: >= 50 dB PSNR against the reference's fp32 output."""
+    fx = read_hatf(GOLDEN / f"{case['name']}.bin")
+    be = hat_b200.B200(checkpoint_for(case, ckdir), mode=hat_b200.MODE_FAST)
+    got = be.forward(fx["h"], fx["w"], fx["input"])
+    mse = float(((got.astype(np.float64) - fx["expected"]) ** 2).mean())
+    psnr = 10 * np.log10(1.0 / max(mse, 1e-30))
+    print(f"{case['name']} fast: PSNR {psnr:.1f} dB, max {np.abs(got - fx['expected']).max():.3e}")
+    assert psnr >= 50.0
+
+
+def test_simt_and_tensor_core_paths_agree(ckdir):
+    from hat_b200 import checkpoint, synth
+    p = str(ckdir / "s4_cross.safetensors")
+    checkpoint.make_checkpoint(p, "hat-s", 4, 31, perturb=True)
+    img = synth.image(48, 64, 5)
+    a = hat_b200.B200(p, simt_only=True).forward(48, 64, img)
+    b = hat_b200.B200(p).forward(48, 64, img)
+    assert float(np.abs(a - b).max()) <= 2e-5
+
+
 def test_larger_image_against_oracle(ckdir):
     from oracle import hat_oracle as O
     from hat_b200 import checkpoint, synth
@@ -72,13 +95,15 @@ def test_device_entry_batch_and_graph_replay(ckdir, torch_cuda):
     for i in range(3):
         assert np.array_equal(ref[i], host_be.forward(32, 48, imgs[i]))
     be = hat_b200.B200(p, use_graph=True)
-    x = torch.from_numpy(imgs).cuda()
-    y = torch.empty((3, 3, 64, 96), device="cuda")
-    for _ in range(3):  # eager run, capture, replay
-        y.zero_()
-        be.forward_device(x.data_ptr(), y.data_ptr(), 3, 32, 48, torch.cuda.current_stream().cuda_stream)
-        torch.cuda.synchronize()
-        assert np.array_equal(y.cpu().numpy(), ref)
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side):
+        x = torch.from_numpy(imgs).cuda()
+        y = torch.empty((3, 3, 64, 96), device="cuda")
+        for _ in range(3):  # eager run, capture, replay: all on the caller's stream
+            y.zero_()
+            be.forward_device(x.data_ptr(), y.data_ptr(), 3, 32, 48, side.cuda_stream)
+            side.synchronize()
+            assert np.array_equal(y.cpu().numpy(), ref)
 
 
 def test_memory_guard_refuses_before_allocating(ckdir):
@@ -96,31 +121,40 @@ def test_memory_guard_refuses_before_allocating(ckdir):
     be.check_memory(64, 64)
 
 
-@pytest.mark.parametrize("m,n,k", [(4096, 432, 144), (1000, 144, 288), (777, 540, 180), (262, 360, 180)])
-def test_linear_kernel_vs_torch(torch_cuda, m, n, k):
+KERNEL_TOL = {hat_b200.MODE_SIMT: 2e-5, hat_b200.MODE_PARITY: 2e-5, hat_b200.MODE_FAST: 5e-3}
+MODES = [hat_b200.MODE_SIMT, hat_b200.MODE_PARITY, hat_b200.MODE_FAST]
+
+
+@pytest.mark.parametrize("mode", MODES, ids=["simt", "tcgen05_3xtf32", "tcgen05_tf32"])
+@pytest.mark.parametrize("m,n,k", [(4096, 432, 144), (1000, 144, 288), (777, 540, 180), (262, 360, 180),
+                                   (70000, 288, 144)])
+def test_linear_kernel_vs_torch(torch_cuda, m, n, k, mode):
     torch = torch_cuda
     g = torch.Generator(device="cuda").manual_seed(m)
     x = torch.randn(m, k, device="cuda", generator=g)
     w = torch.randn(n, k, device="cuda", generator=g) * 0.05
     b = torch.randn(n, device="cuda", generator=g)
     y = torch.empty(m, n, device="cuda")
-    hat_b200.linear(hat_b200.MODE_PARITY, x.data_ptr(), w.data_ptr(), b.data_ptr(), y.data_ptr(), m, n, k)
+    hat_b200.linear(mode, x.data_ptr(), w.data_ptr(), b.data_ptr(), y.data_ptr(), m, n, k)
     torch.cuda.synchronize()
     want = (x.double() @ w.double().T + b.double()).float()
-    assert float((y - want).abs().max()) < 2e-5
+    assert float((y - want).abs().max()) < KERNEL_TOL[mode]
 
 
+@pytest.mark.parametrize("mode", MODES, ids=["simt", "tcgen05_3xtf32", "tcgen05_tf32"])
 @pytest.mark.parametrize("hg,wd,ci,co", [(64, 48, 144, 144), (32, 32, 144, 6), (32, 32, 6, 144),
-                                         (48, 16, 64, 256), (16, 48, 3, 180), (16, 16, 64, 3)])
-def test_conv_kernel_vs_torch(torch_cuda, hg, wd, ci, co):
+                                         (48, 16, 64, 256), (16, 48, 3, 180), (16, 16, 64, 3),
+                                         (32, 64, 180, 60), (32, 32, 60, 180), (256, 128, 144, 144)])
+def test_conv_kernel_vs_torch(torch_cuda, hg, wd, ci, co, mode):
     torch = torch_cuda
     g = torch.Generator(device="cuda").manual_seed(hg * 1000 + co)
     x = torch.randn(hg, wd, ci, device="cuda", generator=g)
     w = torch.randn(co, ci, 3, 3, device="cuda", generator=g) * 0.05
     b = torch.randn(co, device="cuda", generator=g)
     y = torch.empty(hg, wd, co, device="cuda")
-    hat_b200.conv3x3(hat_b200.MODE_PARITY, x.data_ptr(), w.data_ptr(), b.data_ptr(), y.data_ptr(), hg, wd, ci, co)
+    hat_b200.conv3x3(mode, x.data_ptr(), w.data_ptr(), b.data_ptr(), y.data_ptr(), hg, wd, ci, co)
     torch.cuda.synchronize()
     want = torch.nn.functional.conv2d(x.double().permute(2, 0, 1)[None], w.double(), b.double(), padding=1)
     want = want[0].permute(1, 2, 0).float()
-    assert float((y - want).abs().max()) < 5e-5
+    tol = KERNEL_TOL[mode] * (2.5 if mode != hat_b200.MODE_FAST else 4)
+    assert float((y - want).abs().max()) < tol
