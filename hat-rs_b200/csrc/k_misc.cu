@@ -88,21 +88,31 @@ void launch_layernorm(const float* x, const float* g, const float* b, float* y, 
 __global__ void k_ca_gate(const float* __restrict__ partial, long rows, float inv_count,
                           const float* __restrict__ w1, const float* __restrict__ b1, const float* __restrict__ w2,
                           const float* __restrict__ b2, float* __restrict__ gate, int c, int sq) {
-    extern __shared__ float sm[];
-    float* mean = sm;        // [c]
-    float* hid = sm + c;     // [sq]
-    const int warp = threadIdx.x / 32, lane = threadIdx.x & 31, nwarp = blockDim.x / 32;
-    // The plane sum: one warp per channel, lanes stride the partial rows, and a fixed
-    // shuffle tree combines them, so the result is identical on every run.
-    for (int i = warp; i < c; i += nwarp) {
-        float a = 0.f;
-        for (long r = lane; r < rows; r += 32) a += partial[r * c + i];
+    // c <= 256: lanes cover channels (coalesced rows), warps stride the partial rows, and
+    // the per-warp sums are combined in warp order, so the result is identical every run.
+    __shared__ float red[32][257];
+    __shared__ float mean[256], hid[64];
+    const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+    float acc[8];
 #pragma unroll
-        for (int o = 16; o; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-        if (lane == 0) mean[i] = a * inv_count;
+    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+    for (long r = warp; r < rows; r += 32) {
+        const float* row = partial + r * c;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (lane + 32 * j < c) acc[j] += row[lane + 32 * j];
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+        if (lane + 32 * j < c) red[warp][lane + 32 * j] = acc[j];
+    __syncthreads();
+    for (int i = threadIdx.x; i < c; i += blockDim.x) {
+        float a = 0.f;
+        for (int w = 0; w < 32; ++w) a += red[w][i];
+        mean[i] = a * inv_count;
     }
     __syncthreads();
-    for (int j = warp; j < sq; j += nwarp) {
+    for (int j = warp; j < sq; j += 32) {
         float a = 0.f;
         for (int i = lane; i < c; i += 32) a += w1[(long)j * c + i] * mean[i];
 #pragma unroll
@@ -119,7 +129,8 @@ __global__ void k_ca_gate(const float* __restrict__ partial, long rows, float in
 
 void launch_ca_gate(const float* partial, long rows, float inv_count, const float* w1, const float* b1,
                     const float* w2, const float* b2, float* gate, int c, int sq, cudaStream_t st) {
-    k_ca_gate<<<1, 1024, (c + sq) * sizeof(float), st>>>(partial, rows, inv_count, w1, b1, w2, b2, gate, c, sq);
+    if (c > 256 || sq > 64) throw Error(1, "channel attention: c > 256 or squeeze > 64 is not supported");
+    k_ca_gate<<<1, 1024, 0, st>>>(partial, rows, inv_count, w1, b1, w2, b2, gate, c, sq);
     HAT_CUDA(cudaGetLastError());
     count_launch();
 }

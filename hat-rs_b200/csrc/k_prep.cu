@@ -63,9 +63,10 @@ __global__ void k_prep_umma(const float* __restrict__ w, float* __restrict__ hi,
                 if (tap < 9 && ci < cin) v = w[((long)row * cin + ci) * 9 + tap];
             }
         }
-        float h = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+        float h, l;
+        split_tf32(v, h, l);
         hi[i] = h;
-        lo[i] = v - h;
+        lo[i] = l;
     }
 }
 

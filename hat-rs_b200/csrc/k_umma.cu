@@ -8,10 +8,10 @@
 // K loop runs over (tap, 32-channel chunk) and TMA's zero fill outside the plane is
 // the conv's zero padding.
 //
-// fp32 parity ("3xTF32"): every operand x is split into x_hi = x with the low 13
-// mantissa bits cleared (exactly representable in tf32) and x_lo = x - x_hi, and
+// fp32 parity ("3xTF32"): every operand x is split into x_hi = x rounded to the nearest
+// tf32 value and x_lo = (x - x_hi) rounded to tf32, and
 //   A.B ~= A_hi.B_hi + A_hi.B_lo + A_lo.B_hi,
-// which drops only A_lo.B_lo (relative 2^-22). The weights are split once at upload;
+// which drops only A_lo.B_lo (relative 2^-22); the rounding keeps the error unbiased. The weights are split once at upload;
 // the activation tile is split in shared memory by four converter warps between its
 // TMA landing and the MMA. FAST mode issues the single A.B product on the raw tiles.
 //
@@ -161,6 +161,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     __shared__ uint64_t full[4], ready[4], empty[4], acc_full[2], acc_empty[2], drain;
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int abort_flag;
+    // The channel-attention pool: per epilogue warp, column sums accumulated over every
+    // tile this CTA owns (in its fixed tile order), written once at the end.
+    __shared__ float colacc[4][256];
 
     uint8_t* sm = (uint8_t*)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
     const int S = g.stages;
@@ -173,6 +176,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     auto sBl = [&](int s) { return sm + s * st_bytes + 2 * a_bytes + b_bytes; };
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = threadIdx.x; i < 4 * 256; i += NTHREADS) (&colacc[0][0])[i] = 0.f;
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
@@ -296,14 +300,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     float4* lo = reinterpret_cast<float4*>(sAl(s));
                     for (int i = ct; i < nvec; i += 128) {
                         float4 v = hi[i], h, l;
-                        h.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
-                        h.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
-                        h.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
-                        h.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
-                        l.x = v.x - h.x;
-                        l.y = v.y - h.y;
-                        l.z = v.z - h.z;
-                        l.w = v.w - h.w;
+                        split_tf32(v.x, h.x, l.x);
+                        split_tf32(v.y, h.y, l.y);
+                        split_tf32(v.z, h.z, l.z);
+                        split_tf32(v.w, h.w, l.w);
                         hi[i] = h;
                         lo[i] = l;
                     }
@@ -435,20 +435,24 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     }
                 }
                 if (e.colsum) {
-                    // Column sums of this warp's 32 rows, reduced in a fixed order: one
-                    // partial row per (tile, epilogue warp), no atomics, no cross-warp sync.
+                    // Column sums of this warp's 32 rows, reduced in a fixed order and
+                    // accumulated per warp across this CTA's tiles.
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         float s = valid ? v[j] : 0.f;
 #pragma unroll
                         for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
                         const int n = n0 + c0 + j;
-                        if (lane == 0 && n < g.N) e.colsum[(mt * 4 + ew) * g.N + n] = s;
+                        if (lane == 0 && n < g.N) colacc[ew][n] += s;
                     }
                 }
             }
             tc_fence_before();
             mbar_arrive(&acc_empty[a]);
+        }
+        if (e.colsum) {
+            __syncwarp();
+            for (int n = lane; n < g.N; n += 32) e.colsum[((long)blockIdx.x * 4 + ew) * g.N + n] = colacc[ew][n];
         }
     }
 
@@ -513,10 +517,13 @@ static void launch_k(const CUtensorMap& a, const CUtensorMap& bh, const CUtensor
         configured |= 1u << dev;
     }
     const long grid = std::min<long>(g.ntiles, num_sms());
+    if (e.colsum && g.N > 256) throw Error(1, "umma: channel sums are limited to 256 columns");
     k_umma<MODE, TERMS><<<(unsigned)grid, NTHREADS, smem, st>>>(a, bh, bl, g, e);
     HAT_CUDA(cudaGetLastError());
     count_launch();
 }
+
+static long colsum_rows(const UmmaArgs& g) { return std::min<long>(g.ntiles, num_sms()) * 4; }
 
 static int pick_stages(int BN, int ckb) {
     const long per = 2L * 128 * ckb + 2L * BN * ckb;
@@ -553,7 +560,7 @@ long umma_linear(int mode, const float* x, const GemmW& w, float* y, long m, con
         launch_k<0, 3>(ta, tbh, tbl, g, e, st);
     else
         launch_k<0, 1>(ta, tbh, tbl, g, e, st);
-    return g.mtiles * 4;  // colsum: one partial row per (tile, epilogue warp)
+    return colsum_rows(g);  // colsum: one partial row per (CTA, epilogue warp)
 }
 
 long umma_conv3x3(int mode, const float* x, const GemmW& w, float* y, int hgt, int wid, const Epi& e, int* err,
@@ -591,7 +598,7 @@ long umma_conv3x3(int mode, const float* x, const GemmW& w, float* y, int hgt, i
         launch_k<1, 3>(ta, tbh, tbl, g, e, st);
     else
         launch_k<1, 1>(ta, tbh, tbl, g, e, st);
-    return g.mtiles * 4;  // colsum: one partial row per (tile, epilogue warp)
+    return colsum_rows(g);  // colsum: one partial row per (CTA, epilogue warp)
 }
 
 }  // namespace hat

@@ -24,6 +24,21 @@ struct GemmW {
     bool umma = false;      // tensor-core layout present
 };
 
+#ifdef __CUDACC__
+// x = hi + lo with hi = x rounded to the nearest tf32 value and lo = (x - hi) rounded
+// to tf32 as well: both halves are exact tf32 operands, the split is unbiased, and
+// hi + lo is within 2^-22 |x| of x. The tensor core then sees exactly these values.
+__device__ __forceinline__ float tf32_rna(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
+    hi = tf32_rna(x);
+    lo = tf32_rna(x - hi);
+}
+#endif
+
 // Columns per tensor-core tile for an output width n: at most 192 (so three pipeline
 // stages fit in shared memory for c = 144), a multiple of 16, tiles of equal width.
 inline int umma_bn(int n) {
