@@ -19,7 +19,7 @@
 // 6-9 epilogue (TMEM -> registers -> fused epilogue -> global). Two TMEM accumulators
 // (2 x 256 columns) let the epilogue of one tile overlap the MMAs of the next.
 //
-// Every mbarrier wait is bounded (1 s of wall time); on expiry the kernel records an
+// Every mbarrier wait is bounded (about 2 s of SM clock cycles); on expiry the kernel records an
 // error code in `err`, every role leaves its loop, in-flight TMA copies and MMAs are
 // waited for (again bounded) and TMEM is released before the CTA exits.
 #include <cuda.h>
@@ -32,15 +32,9 @@ namespace hat {
 namespace {
 
 constexpr int NTHREADS = 320;
-constexpr unsigned long long WAIT_NS = 1000000000ull;  // 1 s per wait
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return (uint32_t)__cvta_generic_to_shared(p);
-}
-__device__ __forceinline__ unsigned long long now_ns() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
 }
 __device__ __forceinline__ void mbar_init(uint64_t* b, int count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
@@ -62,19 +56,29 @@ __device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
     return ok != 0;
 }
 // Bounded wait: false (with the abort flag raised and the error recorded) on expiry
-// or when another role has already aborted.
+// or when another role has already aborted. The bound is counted in SM clock cycles
+// (clock64 is a cheap register read; the global timer is not, and reading it on every
+// poll delayed every hand-off of the pipeline); WAIT_CYCLES is about 2 s at 1.9 GHz.
+constexpr long long WAIT_CYCLES = 4000000000ll;
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort, int* err, int code) {
     if (mbar_try(b, parity)) return true;
-    unsigned long long t0 = now_ns();
+    const long long t0 = clock64();
     while (true) {
         if (mbar_try(b, parity)) return true;
         if (*abort) return false;
-        if (now_ns() - t0 > WAIT_NS) {
+        if (clock64() - t0 > WAIT_CYCLES) {
             *abort = 1;
             atomicCAS(err, 0, code);
             return false;
         }
     }
+}
+// Bounded wait used on the way out (no abort flag): true when the phase completed.
+__device__ __forceinline__ bool mbar_wait_quiet(uint64_t* b, uint32_t parity) {
+    const long long t0 = clock64();
+    while (!mbar_try(b, parity))
+        if (clock64() - t0 > WAIT_CYCLES) return false;
+    return true;
 }
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -228,9 +232,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (abort_flag) {
                 // Let the copies already issued land before the CTA can exit.
                 for (uint32_t j = (it > (uint32_t)S ? it - S : 0); j < it; ++j) {
-                    unsigned long long t0 = now_ns();
-                    while (!mbar_try(&full[j % S], (j / S) & 1) && now_ns() - t0 < WAIT_NS) {
-                    }
+                    mbar_wait_quiet(&full[j % S], (j / S) & 1);
                 }
             }
         }
@@ -275,9 +277,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             // Every MMA issued so far completes before TMEM can be released.
             mma_commit(&drain);
-            unsigned long long t0 = now_ns();
-            while (!mbar_try(&drain, 0) && now_ns() - t0 < WAIT_NS) {
-            }
+            mbar_wait_quiet(&drain, 0);
         }
     } else if (warp < 6) {
         // ------------------------------------------------------------ converters

@@ -28,10 +28,12 @@ struct GemmW {
 // x = hi + lo with hi = x rounded to the nearest tf32 value and lo = (x - hi) rounded
 // to tf32 as well: both halves are exact tf32 operands, the split is unbiased, and
 // hi + lo is within 2^-22 |x| of x. The tensor core then sees exactly these values.
+// tf32 keeps 10 of fp32's 23 mantissa bits: adding half a unit of the 13th bit to the
+// sign-magnitude pattern and clearing the low 13 bits rounds the magnitude to nearest
+// (ties away from zero), carrying into the exponent when the mantissa overflows. Two
+// integer operations, so the split stays off the conversion pipe.
 __device__ __forceinline__ float tf32_rna(float x) {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return __uint_as_float(r);
+    return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
 }
 __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
     hi = tf32_rna(x);
