@@ -52,7 +52,8 @@ __device__ __forceinline__ void epi_store(const Epi& e, float* y, long gm, int g
     if (e.planar_out) {
         int py = (int)(gm / wid), px = (int)(gm % wid);
         if (py < e.oh && px < e.ow)
-            y[((long)gn * e.oh + py) * e.ow + px] = v / e.img_range + e.mean[gn];
+            y[((long)gn * e.oh + py) * e.ow + px] =
+                v / e.img_range + (gn == 0 ? e.mean[0] : gn == 1 ? e.mean[1] : e.mean[2]);
         return;
     }
     if (e.shuffle) {

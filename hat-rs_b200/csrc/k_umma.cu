@@ -15,8 +15,8 @@
 // the activation tile is split in shared memory by four converter warps between its
 // TMA landing and the MMA. FAST mode issues the single A.B product on the raw tiles.
 //
-// Warp roles (320 threads): 0 TMA producer, 1 MMA issuer + TMEM owner, 2-5 converters,
-// 6-9 epilogue (TMEM -> registers -> fused epilogue -> global). Two TMEM accumulators
+// Warp roles (256 threads): 0 TMA producer, 1 MMA issuer + TMEM owner, 2-3 converters,
+// 4-7 epilogue (TMEM -> registers -> fused epilogue -> global). Two TMEM accumulators
 // (2 x 256 columns) let the epilogue of one tile overlap the MMAs of the next.
 //
 // Every mbarrier wait is bounded (about 2 s of SM clock cycles); on expiry the kernel records an
@@ -31,7 +31,7 @@ namespace hat {
 
 namespace {
 
-constexpr int NTHREADS = 320;
+constexpr int NTHREADS = 256;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return (uint32_t)__cvta_generic_to_shared(p);
@@ -184,7 +184,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&ready[s], 128);
+            mbar_init(&ready[s], 64);
             mbar_init(&empty[s], 1);
         }
         for (int a = 0; a < 2; ++a) {
@@ -279,10 +279,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             mma_commit(&drain);
             mbar_wait_quiet(&drain, 0);
         }
-    } else if (warp < 6) {
+    } else if (warp < 4) {
         // ------------------------------------------------------------ converters
         if (TERMS == 3) {
-            const int ct = threadIdx.x - 64;  // 0..127
+            const int ct = threadIdx.x - 64;  // 0..63
             uint32_t it = 0;
             const int nvec = a_bytes / 16;    // float4s per A tile
             for (long t = blockIdx.x; t < ntiles; t += gridDim.x) {
@@ -298,7 +298,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     }
                     float4* hi = reinterpret_cast<float4*>(sA(s));
                     float4* lo = reinterpret_cast<float4*>(sAl(s));
-                    for (int i = ct; i < nvec; i += 128) {
+                    for (int i = ct; i < nvec; i += 64) {
                         float4 v = hi[i], h, l;
                         split_tf32(v.x, h.x, l.x);
                         split_tf32(v.y, h.y, l.y);
@@ -308,7 +308,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         lo[i] = l;
                     }
                     // Each thread makes its generic-proxy stores visible to the tensor
-                    // core's async proxy, then arrives (128 arrivals complete the phase).
+                    // core's async proxy, then arrives (64 arrivals complete the phase).
                     fence_proxy_async();
                     mbar_arrive(&ready[s]);
                 }
@@ -319,7 +319,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // ------------------------------------------------------------ epilogue
         const int q = warp & 3;          // TMEM lane quarter this warp may read
         const int row = q * 32 + lane;   // tile row of this thread
-        const int ew = warp - 6;         // 0..3 within the epilogue group
+        const int ew = warp - 4;         // 0..3 within the epilogue group
         uint32_t tl = 0;
         for (long t = blockIdx.x; t < ntiles; t += gridDim.x, ++tl) {
             if (__any_sync(0xffffffffu, abort_flag != 0)) break;
@@ -378,23 +378,32 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     const int n = n0 + c0 + j;
                     v[j] = n < g.N ? epi_act(v[j] + (e.bias ? e.bias[n] : 0.f), e.act) : 0.f;
                 }
+                // Every loop over v[] is fully unrolled with guards rather than breaks,
+                // so v stays in registers (a dynamically indexed v would live in local
+                // memory, which misses in the small L1 this kernel leaves beside its
+                // shared memory).
                 if (valid) {
                     if (e.planar_out) {
                         const int wid = MODE == 0 ? 1 : g.W;
                         const int yy = (int)(m / wid), xx = (int)(m % wid);
-                        if (yy < e.oh && xx < e.ow)
-                            for (int j = 0; j < 16; ++j) {
-                                const int n = n0 + c0 + j;
-                                if (n < g.N) g.y[((long)n * e.oh + yy) * e.ow + xx] = v[j] / e.img_range + e.mean[n];
-                            }
-                    } else if (e.shuffle) {
-                        const int r = e.shuffle, cout = g.N / (r * r);
+                        const bool inside = yy < e.oh && xx < e.ow;
+#pragma unroll
                         for (int j = 0; j < 16; ++j) {
                             const int n = n0 + c0 + j;
-                            if (n >= g.N) break;
-                            const int c = n / (r * r), rem = n - c * r * r, i = rem / r, jj = rem - i * r;
-                            const long oy = (long)py * r + i, ox = (long)px * r + jj;
-                            g.y[(oy * ((long)g.W * r) + ox) * cout + c] = v[j];
+                            if (inside && n < g.N)
+                                g.y[((long)n * e.oh + yy) * e.ow + xx] =
+                                    v[j] / e.img_range + (n == 0 ? e.mean[0] : n == 1 ? e.mean[1] : e.mean[2]);
+                        }
+                    } else if (e.shuffle) {
+                        const int r = e.shuffle, cout = g.N / (r * r);
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const int n = n0 + c0 + j;
+                            if (n < g.N) {
+                                const int c = n / (r * r), rem = n - c * r * r, i = rem / r, jj = rem - i * r;
+                                const long oy = (long)py * r + i, ox = (long)px * r + jj;
+                                g.y[(oy * ((long)g.W * r) + ox) * cout + c] = v[j];
+                            }
                         }
                     } else {
                         float* dst = g.y + m * g.ldo + n0 + c0;
@@ -421,15 +430,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                                 *reinterpret_cast<float4*>(dst + 4 * j4) = o;
                             }
                         } else {
+#pragma unroll
                             for (int j = 0; j < 16; ++j) {
                                 const int n = n0 + c0 + j;
-                                if (n >= g.nstore) break;
-                                float o = v[j];
-                                if (e.cx)
-                                    o = (e.res[base + j] + o) + (e.cx[base + j] * e.gate[n]) * e.cscale;
-                                else if (e.res)
-                                    o = e.res[base + j] + o;
-                                dst[j] = o;
+                                if (n < g.nstore) {
+                                    float o = v[j];
+                                    if (e.cx)
+                                        o = (e.res[base + j] + o) + (e.cx[base + j] * e.gate[n]) * e.cscale;
+                                    else if (e.res)
+                                        o = e.res[base + j] + o;
+                                    dst[j] = o;
+                                }
                             }
                         }
                     }
