@@ -162,14 +162,24 @@ int hat_b200_profile(hat_b200* h, int height, int width, char* json, size_t json
 // The GEMM operand of one kernel-level call, prepared on the caller's stream.
 struct TempW {
     float* buf = nullptr;
+    float* xs = nullptr;  // the activation split into tf32 hi/lo halves (parity mode)
     int* err = nullptr;
     GemmW g;
     cudaStream_t st = nullptr;
     ~TempW() {
         if (buf) cudaFreeAsync(buf, st);
+        if (xs) cudaFreeAsync(xs, st);
         if (err) cudaFreeAsync(err, st);
     }
 };
+
+// The activation as the GEMMs read it: split for the parity-mode tensor-core path.
+static Opnd temp_operand(TempW& t, int mode, const float* x, long n) {
+    if (mode != HAT_B200_MODE_PARITY) return Opnd{x, nullptr};
+    HAT_CUDA(cudaMallocAsync(&t.xs, 2 * n * sizeof(float) + 64, t.st));
+    launch_split(x, t.xs, t.xs + n, n, t.st);
+    return Opnd{t.xs, t.xs + n};
+}
 
 static void temp_gemm_w(TempW& t, const float* w, int n, int k_or_cin, bool conv, int cin_plane, cudaStream_t st) {
     t.st = st;
@@ -199,10 +209,11 @@ int hat_b200_linear(int mode, const float* x, const float* w, const float* b, fl
         cudaStream_t st = (cudaStream_t)stream;
         TempW t;
         temp_gemm_w(t, w, n, k, false, 0, st);
+        Opnd xo = temp_operand(t, mode, x, (long)m * k);
         Epi e;
         e.bias = b;
         GemmCtx c{mode == HAT_B200_MODE_SIMT ? 0 : mode, mode == HAT_B200_MODE_SIMT, t.err};
-        gemm_linear(c, x, t.g, y, m, e, st);
+        gemm_linear(c, xo, t.g, Dst{y, nullptr}, m, e, st);
         finish_kernel_call(t);
     });
 }
@@ -213,10 +224,11 @@ int hat_b200_conv3x3(int mode, const float* x, const float* w, const float* b, f
         cudaStream_t st = (cudaStream_t)stream;
         TempW t;
         temp_gemm_w(t, w, cout, cin, true, cin, st);
+        Opnd xo = temp_operand(t, mode, x, (long)hgt * wid * cin);
         Epi e;
         e.bias = b;
         GemmCtx c{mode == HAT_B200_MODE_SIMT ? 0 : mode, mode == HAT_B200_MODE_SIMT, t.err};
-        gemm_conv3x3(c, x, t.g, y, hgt, wid, e, st);
+        gemm_conv3x3(c, xo, t.g, Dst{y, nullptr}, hgt, wid, e, st);
         finish_kernel_call(t);
     });
 }
@@ -226,7 +238,7 @@ int hat_b200_window_attention(int mode, const float* qkv, const float* table, fl
     return guarded(nullptr, 0, [&] {
         Plan p = Plan::make(hp, wp, 16);
         if (p.hp != hp || p.wp != wp) throw Error(1, "window attention: plane is not a window multiple");
-        launch_window_attention(mode, qkv, table, out, p, c, heads, shift, (cudaStream_t)stream);
+        launch_window_attention(mode, qkv, table, Dst{out, nullptr}, p, c, heads, shift, (cudaStream_t)stream);
     });
 }
 
@@ -235,7 +247,7 @@ int hat_b200_overlap_attention(int mode, const float* qkv, const float* table, f
     return guarded(nullptr, 0, [&] {
         Plan p = Plan::make(hp, wp, 16);
         if (p.hp != hp || p.wp != wp) throw Error(1, "overlap attention: plane is not a window multiple");
-        launch_overlap_attention(mode, qkv, table, out, p, c, heads, (cudaStream_t)stream);
+        launch_overlap_attention(mode, qkv, table, Dst{out, nullptr}, p, c, heads, (cudaStream_t)stream);
     });
 }
 

@@ -48,6 +48,63 @@ struct Plan {
     bool operator==(const Plan& o) const { return h == o.h && w == o.w && hp == o.hp && wp == o.wp && win == o.win; }
 };
 
+// ---------------------------------------------------------------- operands
+// A GEMM operand plane. In fp32-parity mode every plane a tensor-core GEMM reads is
+// stored pre-split by the kernel that produces it: `hi` holds the value rounded to
+// tf32 and `lo` the rounded remainder (see split_tf32), so hi + lo carries the fp32
+// value to 2^-22 and the GEMM needs no conversion pass. `lo == nullptr` marks a plain
+// fp32 plane (fast mode, the CUDA-core path, and planes read only by CUDA-core code).
+struct Opnd {
+    const float* hi = nullptr;
+    const float* lo = nullptr;
+};
+struct Dst {
+    float* hi = nullptr;
+    float* lo = nullptr;
+};
+
+#ifdef __CUDACC__
+// x = hi + lo with hi = x rounded to the nearest tf32 value and lo = (x - hi) rounded
+// to tf32 as well: both halves are exact tf32 operands, the split is unbiased, and
+// hi + lo is within 2^-22 |x| of x. tf32 keeps 10 of fp32's 23 mantissa bits: adding
+// half a unit of the 13th bit to the sign-magnitude pattern and clearing the low 13
+// bits rounds the magnitude to nearest (ties away from zero), carrying into the
+// exponent when the mantissa overflows.
+__device__ __forceinline__ float tf32_rna(float x) {
+    return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
+}
+__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
+    hi = tf32_rna(x);
+    lo = tf32_rna(x - hi);
+}
+// Store v at index i of a destination plane, split when it has a lo half.
+__device__ __forceinline__ void put(const Dst& d, long i, float v) {
+    if (d.lo) {
+        float h, l;
+        split_tf32(v, h, l);
+        d.hi[i] = h;
+        d.lo[i] = l;
+    } else {
+        d.hi[i] = v;
+    }
+}
+__device__ __forceinline__ void put4(const Dst& d, long i, float4 v) {
+    if (d.lo) {
+        float4 h, l;
+        split_tf32(v.x, h.x, l.x);
+        split_tf32(v.y, h.y, l.y);
+        split_tf32(v.z, h.z, l.z);
+        split_tf32(v.w, h.w, l.w);
+        *reinterpret_cast<float4*>(d.hi + i) = h;
+        *reinterpret_cast<float4*>(d.lo + i) = l;
+    } else {
+        *reinterpret_cast<float4*>(d.hi + i) = v;
+    }
+}
+// The fp32 value of element i of an operand plane.
+__device__ __forceinline__ float get(const Opnd& o, long i) { return o.lo ? o.hi[i] + o.lo[i] : o.hi[i]; }
+#endif
+
 // ---------------------------------------------------------------- epilogues
 // What a GEMM-shaped kernel does with its fp32 accumulator before the store.
 enum Act : int { ACT_NONE = 0, ACT_GELU = 1, ACT_LEAKY = 2 };
@@ -90,15 +147,17 @@ void launch_pre(const float* in, float* out, const Plan& p, const float mean[3],
                 cudaStream_t st);
 
 // LayerNorm over the channel axis of a [m][c] token plane (src/cpu.rs:563-581).
-void launch_layernorm(const float* x, const float* g, const float* b, float* y, long m, int c,
-                      cudaStream_t st);
+void launch_layernorm(const float* x, const float* g, const float* b, Dst y, long m, int c, cudaStream_t st);
+
+// Split a plain fp32 array into tf32 hi/lo halves (for callers that hand in fp32 operands).
+void launch_split(const float* x, float* hi, float* lo, long n, cudaStream_t st);
 
 // Window attention of one HAB over the [hp][wp][3c] qkv plane (hat_arch.py:165-196).
-void launch_window_attention(int mode, const float* qkv, const float* table, float* out,
+void launch_window_attention(int mode, const float* qkv, const float* table, Dst out,
                              const Plan& p, int c, int heads, int shift, cudaStream_t st);
 
 // OCAB attention over the [hp][wp][3c] qkv plane (hat_arch.py:392-438).
-void launch_overlap_attention(int mode, const float* qkv, const float* table, float* out,
+void launch_overlap_attention(int mode, const float* qkv, const float* table, Dst out,
                               const Plan& p, int c, int heads, cudaStream_t st);
 
 // gate[c] = sigmoid(W2 relu(W1 mean + b1) + b2) (hat_arch.py:40-57), where the mean

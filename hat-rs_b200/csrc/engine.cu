@@ -21,11 +21,15 @@ Sizes Sizes::of(const Weights& wt, const Plan& p) {
     s.xa = P * c;
     s.xb = P * c;
     s.n1 = P * c;
+    s.n1lo = P * c;
     s.cmid = P * s.cmid_stride;
+    s.cmidlo = P * s.cmid_stride;
     s.convx = P * c;
     s.qkv = P * 3 * c;
     s.attn = P * c;
+    s.attnlo = P * c;
     s.hid = P * wt.mlp_ratio * c;
+    s.hidlo = P * wt.mlp_ratio * c;
     // The channel-attention pool's partial sums: at most four rows of c per 128-pixel tile.
     s.chsum = (P + 127) / 128 * 4 * c;
     s.gate = c;
@@ -43,29 +47,32 @@ Sizes Sizes::of(const Weights& wt, const Plan& p) {
         ++i;
     }
     s.headA = a;
+    s.headAlo = a;
     s.headB = b;
+    s.headBlo = b;
     s.din = 3L * p.h * p.w;
     s.dout = 3L * p.h * wt.scale * p.w * wt.scale;
     return s;
 }
 
 struct Engine::Acts {
-    float *x0, *body, *xa, *xb, *n1, *cmid, *convx, *qkv, *attn, *hid, *chsum, *gate, *headA, *headB, *din, *dout;
+    float *x0, *body, *xa, *xb, *n1, *n1lo, *cmid, *cmidlo, *convx, *qkv, *attn, *attnlo, *hid, *hidlo, *chsum,
+        *gate, *headA, *headAlo, *headB, *headBlo, *din, *dout;
 };
 
 // ------------------------------------------------------------------ attention dispatch
-void launch_window_attention_simt(const float* qkv, const float* table, float* out, const Plan& p, int c, int heads,
+void launch_window_attention_simt(const float* qkv, const float* table, Dst out, const Plan& p, int c, int heads,
                                   int shift, cudaStream_t st);
-void launch_overlap_attention_simt(const float* qkv, const float* table, float* out, const Plan& p, int c, int heads,
+void launch_overlap_attention_simt(const float* qkv, const float* table, Dst out, const Plan& p, int c, int heads,
                                    cudaStream_t st);
 
-void launch_window_attention(int mode, const float* qkv, const float* table, float* out, const Plan& p, int c,
+void launch_window_attention(int mode, const float* qkv, const float* table, Dst out, const Plan& p, int c,
                              int heads, int shift, cudaStream_t st) {
     (void)mode;
     launch_window_attention_simt(qkv, table, out, p, c, heads, shift, st);
 }
 
-void launch_overlap_attention(int mode, const float* qkv, const float* table, float* out, const Plan& p, int c,
+void launch_overlap_attention(int mode, const float* qkv, const float* table, Dst out, const Plan& p, int c,
                               int heads, cudaStream_t st) {
     (void)mode;
     launch_overlap_attention_simt(qkv, table, out, p, c, heads, st);
@@ -201,12 +208,12 @@ const GemmW& Engine::G(const std::string& name) const {
     return it->second;
 }
 
-long Engine::linear(const std::string& wname, const float* x, float* y, const Epi& e) {
+long Engine::linear(const std::string& wname, Opnd x, Dst y, const Epi& e) {
     GemmCtx c{mode_, simt_only_, derr_};
     return gemm_linear(c, x, G(wname), y, plan_.tokens(), e, stream_);
 }
 
-long Engine::conv(const std::string& wname, const float* x, float* y, int hgt, int wid, const Epi& e) {
+long Engine::conv(const std::string& wname, Opnd x, Dst y, int hgt, int wid, const Epi& e) {
     GemmCtx c{mode_, simt_only_, derr_};
     return gemm_conv3x3(c, x, G(wname), y, hgt, wid, e, stream_);
 }
@@ -276,15 +283,21 @@ void Engine::ensure_plan(int h, int w) {
     a_->xa = take(s.xa);
     a_->xb = take(s.xb);
     a_->n1 = take(s.n1);
+    a_->n1lo = take(s.n1lo);
     a_->cmid = take(s.cmid);
+    a_->cmidlo = take(s.cmidlo);
     a_->convx = take(s.convx);
     a_->qkv = take(s.qkv);
     a_->attn = take(s.attn);
+    a_->attnlo = take(s.attnlo);
     a_->hid = take(s.hid);
+    a_->hidlo = take(s.hidlo);
     a_->chsum = take(s.chsum);
     a_->gate = take(s.gate);
     a_->headA = take(s.headA);
+    a_->headAlo = take(s.headAlo);
     a_->headB = take(s.headB);
+    a_->headBlo = take(s.headBlo);
     a_->din = take(s.din);
     a_->dout = take(s.dout);
     // THE PREDICTION IS HELD TO THE ALLOCATION (src/gpu.rs:779-786).
@@ -295,22 +308,23 @@ void Engine::ensure_plan(int h, int w) {
     eager_runs_ = 0;
 }
 
-// `x + fc2(gelu(fc1(norm2(x))))`, in place on x (src/gpu.rs:449-466).
-void Engine::mlp(const std::string& p, float* x) {
+// `out = x + fc2(gelu(fc1(norm2(x))))` (src/gpu.rs:449-466). `out` may be `x` itself,
+// or the split n1 planes when the result feeds only the stage's conv.
+void Engine::mlp(const std::string& p, float* x, Dst out) {
     const long P = plan_.tokens();
     const int c = wt_.embed, hid = wt_.mlp_ratio * c;
     mark("layernorm", 0, 8.0 * P * c);
-    launch_layernorm(x, W(p + ".norm2.weight"), W(p + ".norm2.bias"), a_->n1, P, c, stream_);
+    launch_layernorm(x, W(p + ".norm2.weight"), W(p + ".norm2.bias"), D(a_->n1, a_->n1lo), P, c, stream_);
     Epi e1;
     e1.bias = W(p + ".mlp.fc1.bias");
     e1.act = ACT_GELU;
     mark("linear.fc1", 2.0 * P * hid * c, 4.0 * P * (c + hid));
-    linear(p + ".mlp.fc1.weight", a_->n1, a_->hid, e1);
+    linear(p + ".mlp.fc1.weight", O(a_->n1, a_->n1lo), D(a_->hid, a_->hidlo), e1);
     Epi e2;
     e2.bias = W(p + ".mlp.fc2.bias");
     e2.res = x;
     mark("linear.fc2", 2.0 * P * hid * c, 4.0 * P * (hid + 2 * c));
-    linear(p + ".mlp.fc2.weight", a_->hid, x, e2);
+    linear(p + ".mlp.fc2.weight", O(a_->hid, a_->hidlo), out, e2);
 }
 
 // One HAB (hat_arch.py:266-309; src/gpu.rs:469-520): `in` is the block input, `out`
@@ -321,19 +335,19 @@ void Engine::hab(int stage, int blk, const float* in, float* out) {
     const std::string p = "layers." + std::to_string(stage) + ".residual_group.blocks." + std::to_string(blk);
     const std::string cb = p + ".conv_block.cab";
     mark("layernorm", 0, 8.0 * P * c);
-    launch_layernorm(in, W(p + ".norm1.weight"), W(p + ".norm1.bias"), a_->n1, P, c, stream_);
+    launch_layernorm(in, W(p + ".norm1.weight"), W(p + ".norm1.bias"), D(a_->n1, a_->n1lo), P, c, stream_);
     // CAB: conv c→cc + GELU; conv cc→c with per-tile channel sums of its output; the gate.
     Epi ec1;
     ec1.bias = W(cb + ".0.bias");
     ec1.act = ACT_GELU;
     ec1.ldo = sizes_.cmid_stride;
     mark("conv.cab1", 18.0 * P * c * cc, 4.0 * P * (c + cc));
-    conv(cb + ".0.weight", a_->n1, a_->cmid, plan_.hp, plan_.wp, ec1);
+    conv(cb + ".0.weight", O(a_->n1, a_->n1lo), D(a_->cmid, a_->cmidlo), plan_.hp, plan_.wp, ec1);
     Epi ec2;
     ec2.bias = W(cb + ".2.bias");
     ec2.colsum = a_->chsum;
     mark("conv.cab2", 18.0 * P * c * cc, 4.0 * P * (c + cc));
-    long rows = conv(cb + ".2.weight", a_->cmid, a_->convx, plan_.hp, plan_.wp, ec2);
+    long rows = conv(cb + ".2.weight", O(a_->cmid, a_->cmidlo), Dst{a_->convx, nullptr}, plan_.hp, plan_.wp, ec2);
     mark("ca_gate", 0, 4.0 * rows * c);
     launch_ca_gate(a_->chsum, rows, 1.f / (float)P, W(cb + ".3.attention.1.weight"), W(cb + ".3.attention.1.bias"),
                    W(cb + ".3.attention.3.weight"), W(cb + ".3.attention.3.bias"), a_->gate, c, wt_.squeezed,
@@ -342,11 +356,11 @@ void Engine::hab(int stage, int blk, const float* in, float* out) {
     Epi eq;
     eq.bias = W(p + ".attn.qkv.bias");
     mark("linear.qkv", 6.0 * P * c * c, 16.0 * P * c);
-    linear(p + ".attn.qkv.weight", a_->n1, a_->qkv, eq);
+    linear(p + ".attn.qkv.weight", O(a_->n1, a_->n1lo), Dst{a_->qkv, nullptr}, eq);
     const int shift = blk % 2 ? plan_.shift : 0;
     mark("attn.window", 4.0 * P * 256 * c, 16.0 * P * c);
-    launch_window_attention(mode_, a_->qkv, W(p + ".attn.relative_position_bias_table"), a_->attn, plan_, c,
-                            wt_.heads, shift, stream_);
+    launch_window_attention(mode_, a_->qkv, W(p + ".attn.relative_position_bias_table"), D(a_->attn, a_->attnlo),
+                            plan_, c, wt_.heads, shift, stream_);
     // proj, then `(shortcut + attn) + conv_x * conv_scale` in the epilogue.
     Epi ep;
     ep.bias = W(p + ".attn.proj.bias");
@@ -355,30 +369,31 @@ void Engine::hab(int stage, int blk, const float* in, float* out) {
     ep.gate = a_->gate;
     ep.cscale = wt_.conv_scale;
     mark("linear.proj", 2.0 * P * c * c, 16.0 * P * c);
-    linear(p + ".attn.proj.weight", a_->attn, out, ep);
-    mlp(p, out);
+    linear(p + ".attn.proj.weight", O(a_->attn, a_->attnlo), Dst{out, nullptr}, ep);
+    mlp(p, out, Dst{out, nullptr});
 }
 
-// The OCAB (hat_arch.py:392-438; src/gpu.rs:533-588).
+// The OCAB (hat_arch.py:392-438; src/gpu.rs:533-588). Its result feeds only the
+// stage's 3x3 conv, so the last MLP writes it (split) into the n1 planes.
 void Engine::ocab(int stage, const float* in, float* out) {
     const long P = plan_.tokens();
     const int c = wt_.embed;
     const std::string p = "layers." + std::to_string(stage) + ".residual_group.overlap_attn";
     mark("layernorm", 0, 8.0 * P * c);
-    launch_layernorm(in, W(p + ".norm1.weight"), W(p + ".norm1.bias"), a_->n1, P, c, stream_);
+    launch_layernorm(in, W(p + ".norm1.weight"), W(p + ".norm1.bias"), D(a_->n1, a_->n1lo), P, c, stream_);
     Epi eq;
     eq.bias = W(p + ".qkv.bias");
     mark("linear.qkv", 6.0 * P * c * c, 16.0 * P * c);
-    linear(p + ".qkv.weight", a_->n1, a_->qkv, eq);
+    linear(p + ".qkv.weight", O(a_->n1, a_->n1lo), Dst{a_->qkv, nullptr}, eq);
     mark("attn.overlap", 4.0 * P * 576 * c, 16.0 * P * c);
-    launch_overlap_attention(mode_, a_->qkv, W(p + ".relative_position_bias_table"), a_->attn, plan_, c, wt_.heads,
-                             stream_);
+    launch_overlap_attention(mode_, a_->qkv, W(p + ".relative_position_bias_table"), D(a_->attn, a_->attnlo),
+                             plan_, c, wt_.heads, stream_);
     Epi ep;
     ep.bias = W(p + ".proj.bias");
     ep.res = in;
     mark("linear.proj", 2.0 * P * c * c, 12.0 * P * c);
-    linear(p + ".proj.weight", a_->attn, out, ep);
-    mlp(p, out);
+    linear(p + ".proj.weight", O(a_->attn, a_->attnlo), Dst{out, nullptr}, ep);
+    mlp(p, out, D(a_->n1, a_->n1lo));
 }
 
 // The whole forward over din → dout (hat_arch.py:971-984; src/gpu.rs:714-748).
@@ -391,11 +406,12 @@ void Engine::enqueue_pass() {
     Epi ef;
     ef.bias = W("conv_first.bias");
     mark("conv.first", 54.0 * P * c, 4.0 * P * (3 + c));
-    conv("conv_first.weight", a_->x0, a_->body, pl.hp, pl.wp, ef);
+    conv("conv_first.weight", Opnd{a_->x0, nullptr}, Dst{a_->body, nullptr}, pl.hp, pl.wp, ef);
     mark("layernorm", 0, 8.0 * P * c);
-    launch_layernorm(a_->body, W("patch_embed.norm.weight"), W("patch_embed.norm.bias"), a_->xa, P, c, stream_);
-    // The stage input stays in `xa` (the RHAG residual); the blocks run in `xb`, and the
-    // stage conv adds the two back into `xa`.
+    launch_layernorm(a_->body, W("patch_embed.norm.weight"), W("patch_embed.norm.bias"), Dst{a_->xa, nullptr}, P,
+                     c, stream_);
+    // The stage input stays in `xa` (the RHAG residual); the blocks run in `xb`, the OCAB
+    // leaves the stage's result split in n1, and the stage conv adds xa back into xa.
     for (size_t s = 0; s < wt_.depths.size(); ++s) {
         const float* in = a_->xa;
         for (int b = 0; b < wt_.depths[s]; ++b) {
@@ -407,23 +423,24 @@ void Engine::enqueue_pass() {
         er.bias = W("layers." + std::to_string(s) + ".conv.bias");
         er.res = a_->xa;
         mark("conv.rhag", 18.0 * P * c * c, 12.0 * P * c);
-        conv("layers." + std::to_string(s) + ".conv.weight", a_->xb, a_->xa, pl.hp, pl.wp, er);
+        conv("layers." + std::to_string(s) + ".conv.weight", O(a_->n1, a_->n1lo), Dst{a_->xa, nullptr}, pl.hp, pl.wp,
+             er);
     }
     mark("layernorm", 0, 8.0 * P * c);
-    launch_layernorm(a_->xa, W("norm.weight"), W("norm.bias"), a_->n1, P, c, stream_);
+    launch_layernorm(a_->xa, W("norm.weight"), W("norm.bias"), D(a_->n1, a_->n1lo), P, c, stream_);
     Epi eb;
     eb.bias = W("conv_after_body.bias");
     eb.res = a_->body;
     mark("conv.body", 18.0 * P * c * c, 12.0 * P * c);
-    conv("conv_after_body.weight", a_->n1, a_->xb, pl.hp, pl.wp, eb);
+    conv("conv_after_body.weight", O(a_->n1, a_->n1lo), D(a_->attn, a_->attnlo), pl.hp, pl.wp, eb);
     // Head: conv + LeakyReLU, then per block a conv whose store does the PixelShuffle.
     Epi eh;
     eh.bias = W("conv_before_upsample.0.bias");
     eh.act = ACT_LEAKY;
     mark("conv.head", 18.0 * P * c * feat, 4.0 * P * (c + feat));
-    conv("conv_before_upsample.0.weight", a_->xb, a_->headA, pl.hp, pl.wp, eh);
-    float* cur = a_->headA;
-    float* nxt = a_->headB;
+    conv("conv_before_upsample.0.weight", O(a_->attn, a_->attnlo), D(a_->headA, a_->headAlo), pl.hp, pl.wp, eh);
+    float *cur = a_->headA, *curlo = a_->headAlo;
+    float *nxt = a_->headB, *nxtlo = a_->headBlo;
     int hh = pl.hp, ww = pl.wp;
     auto blocks = wt_.up_blocks();
     for (size_t i = 0; i < blocks.size(); ++i) {
@@ -431,10 +448,11 @@ void Engine::enqueue_pass() {
         eu.bias = W("upsample." + std::to_string(2 * i) + ".bias");
         eu.shuffle = blocks[i].first;
         mark("conv.up", 18.0 * hh * ww * feat * blocks[i].second, 4.0 * hh * ww * (feat + blocks[i].second));
-        conv("upsample." + std::to_string(2 * i) + ".weight", cur, nxt, hh, ww, eu);
+        conv("upsample." + std::to_string(2 * i) + ".weight", O(cur, curlo), D(nxt, nxtlo), hh, ww, eu);
         hh *= blocks[i].first;
         ww *= blocks[i].first;
         std::swap(cur, nxt);
+        std::swap(curlo, nxtlo);
     }
     // conv_last with the crop and `x / img_range + mean` in its store (src/backend.rs:94-109).
     Epi el;
@@ -445,7 +463,7 @@ void Engine::enqueue_pass() {
     el.img_range = wt_.img_range;
     for (int i = 0; i < 3; ++i) el.mean[i] = wt_.mean[i];
     mark("conv.last", 18.0 * hh * ww * feat * 3, 4.0 * hh * ww * (feat + 3));
-    conv("conv_last.weight", cur, a_->dout, hh, ww, el);
+    conv("conv_last.weight", O(cur, curlo), Dst{a_->dout, nullptr}, hh, ww, el);
     mark(nullptr, 0, 0);
 }
 

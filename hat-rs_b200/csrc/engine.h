@@ -19,12 +19,14 @@ namespace hat {
 // predict (the reference's `Sizes`, src/gpu.rs:166-290): a pass allocates exactly
 // `total()` floats, and the memory guard refuses on the same number.
 struct Sizes {
-    long x0 = 0, body = 0, xa = 0, xb = 0, n1 = 0, cmid = 0, convx = 0, qkv = 0, attn = 0, hid = 0;
-    long chsum = 0, gate = 0, headA = 0, headB = 0, din = 0, dout = 0;
+    long x0 = 0, body = 0, xa = 0, xb = 0, n1 = 0, n1lo = 0, cmid = 0, cmidlo = 0, convx = 0, qkv = 0, attn = 0,
+         attnlo = 0, hid = 0, hidlo = 0;
+    long chsum = 0, gate = 0, headA = 0, headAlo = 0, headB = 0, headBlo = 0, din = 0, dout = 0;
     int cmid_stride = 0;  // channel stride of the CAB's middle plane
     static Sizes of(const Weights& wt, const Plan& p);
     long total() const {
-        return x0 + body + xa + xb + n1 + cmid + convx + qkv + attn + hid + chsum + gate + headA + headB + din + dout;
+        return x0 + body + xa + xb + n1 + n1lo + cmid + cmidlo + convx + qkv + attn + attnlo + hid + hidlo + chsum +
+               gate + headA + headAlo + headB + headBlo + din + dout;
     }
 };
 
@@ -54,12 +56,17 @@ private:
     void enqueue_pass();               // the launch sequence itself
     void hab(int stage, int blk, const float* in, float* out);
     void ocab(int stage, const float* in, float* out);
-    void mlp(const std::string& p, float* x);
+    void mlp(const std::string& p, float* x, Dst out);
     void mark(const char* kind, double flops, double bytes);
     const float* W(const std::string& name) const;
     const GemmW& G(const std::string& name) const;
-    long linear(const std::string& wname, const float* x, float* y, const Epi& e);
-    long conv(const std::string& wname, const float* x, float* y, int hgt, int wid, const Epi& e);
+    long linear(const std::string& wname, Opnd x, Dst y, const Epi& e);
+    long conv(const std::string& wname, Opnd x, Dst y, int hgt, int wid, const Epi& e);
+    // Operand planes: split into tf32 hi/lo halves when the tensor cores run in
+    // fp32-parity mode, plain fp32 otherwise.
+    bool split() const { return mode_ == 0 && !simt_only_; }
+    Dst D(float* hi, float* lo) const { return Dst{hi, split() ? lo : nullptr}; }
+    Opnd O(const float* hi, const float* lo) const { return Opnd{hi, split() ? lo : nullptr}; }
 
     Weights wt_;
     int device_ = 0, mode_ = 0;

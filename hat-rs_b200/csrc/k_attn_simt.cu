@@ -19,7 +19,7 @@ __device__ __forceinline__ int band(int v, int n, int win, int shift) {
 template <int D, bool OCA>
 __global__ void __launch_bounds__(256) k_attn_simt(const float* __restrict__ qkv,
                                                    const float* __restrict__ table,
-                                                   float* __restrict__ out, int hp, int wp, int c,
+                                                   Dst out, int hp, int wp, int c,
                                                    int heads, int shift, float scale) {
     constexpr int WIN = 16, OWIN = 24, OPAD = 4;
     constexpr int DP = (D + 3) / 4 * 4;
@@ -117,13 +117,13 @@ __global__ void __launch_bounds__(256) k_attn_simt(const float* __restrict__ qkv
         m = mn;
     }
     float inv = 1.f / l;
-    float* dst = out + qpos * c + (long)h * D;
+    const long o = qpos * c + (long)h * D;
 #pragma unroll
-    for (int dd = 0; dd < D; ++dd) dst[dd] = acc[dd] * inv;
+    for (int dd = 0; dd < D; ++dd) put(out, o + dd, acc[dd] * inv);
 }
 
 template <int D, bool OCA>
-static void run_attn(const float* qkv, const float* table, float* out, const Plan& p, int c,
+static void run_attn(const float* qkv, const float* table, Dst out, const Plan& p, int c,
                      int heads, int shift, cudaStream_t st) {
     constexpr int DP = (D + 3) / 4 * 4;
     constexpr int NK = OCA ? 576 : 256;
@@ -150,7 +150,7 @@ static void check_geometry(const Plan& p, int c, int heads) {
     if (heads <= 0 || c % heads) throw Error(1, "attention: c is not divisible by heads");
 }
 
-void launch_window_attention_simt(const float* qkv, const float* table, float* out, const Plan& p,
+void launch_window_attention_simt(const float* qkv, const float* table, Dst out, const Plan& p,
                                   int c, int heads, int shift, cudaStream_t st) {
     check_geometry(p, c, heads);
     int d = c / heads;
@@ -162,7 +162,7 @@ void launch_window_attention_simt(const float* qkv, const float* table, float* o
         throw Error(1, "window attention: head dim " + std::to_string(d) + " is not 24 or 30");
 }
 
-void launch_overlap_attention_simt(const float* qkv, const float* table, float* out, const Plan& p,
+void launch_overlap_attention_simt(const float* qkv, const float* table, Dst out, const Plan& p,
                                    int c, int heads, cudaStream_t st) {
     check_geometry(p, c, heads);
     int d = c / heads;

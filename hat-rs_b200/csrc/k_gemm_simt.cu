@@ -6,37 +6,47 @@
 
 namespace hat {
 
-// A operand of a token linear: row-major [m][k].
-struct ALinear {
-    const float* x;
-    int k;
-    __device__ __forceinline__ float ld(long m, int kk) const { return x[m * k + kk]; }
-    __device__ __forceinline__ float4 ld4(long m, int kk) const {
-        return *reinterpret_cast<const float4*>(x + m * k + kk);
+__device__ __forceinline__ float4 ld4o(const Opnd& o, long i) {
+    float4 v = *reinterpret_cast<const float4*>(o.hi + i);
+    if (o.lo) {
+        const float4 l = *reinterpret_cast<const float4*>(o.lo + i);
+        v.x += l.x;
+        v.y += l.y;
+        v.z += l.z;
+        v.w += l.w;
     }
+    return v;
+}
+
+// A operand of a token linear: row-major [m][k] (hi + lo when split).
+struct ALinear {
+    Opnd x;
+    int k;
+    __device__ __forceinline__ float ld(long m, int kk) const { return get(x, m * k + kk); }
+    __device__ __forceinline__ float4 ld4(long m, int kk) const { return ld4o(x, m * k + kk); }
 };
 
 // A operand of a 3x3 conv over a token plane [hgt][wid][cin]: row m is pixel m, column
 // kk = tap * cin + ci reads channel ci of the neighbour (dy, dx) = (tap/3 - 1, tap%3 - 1),
 // zero outside the plane (Conv2d padding 1).
 struct AConv {
-    const float* x;
+    Opnd x;
     int hgt, wid, cin, ldc;  // ldc: channel stride of the plane (>= cin)
-    __device__ __forceinline__ const float* at(long m, int kk, bool& ok) const {
+    __device__ __forceinline__ long at(long m, int kk, bool& ok) const {
         int tap = kk / cin, ci = kk - tap * cin;
         int y = (int)(m / wid) + tap / 3 - 1, xx = (int)(m % wid) + tap % 3 - 1;
         ok = y >= 0 && y < hgt && xx >= 0 && xx < wid;
-        return x + ((long)y * wid + xx) * ldc + ci;
+        return ((long)y * wid + xx) * ldc + ci;
     }
     __device__ __forceinline__ float ld(long m, int kk) const {
         bool ok;
-        const float* p = at(m, kk, ok);
-        return ok ? *p : 0.f;
+        const long i = at(m, kk, ok);
+        return ok ? get(x, i) : 0.f;
     }
     __device__ __forceinline__ float4 ld4(long m, int kk) const {
         bool ok;
-        const float* p = at(m, kk, ok);
-        return ok ? *reinterpret_cast<const float4*>(p) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const long i = at(m, kk, ok);
+        return ok ? ld4o(x, i) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 };
 
@@ -47,12 +57,12 @@ __device__ __forceinline__ float apply_act(float v, int act) {
 }
 
 // Store one finished value; `wid` is the plane width for the spatial epilogues.
-__device__ __forceinline__ void epi_store(const Epi& e, float* y, long gm, int gn, int n, float v,
+__device__ __forceinline__ void epi_store(const Epi& e, const Dst& y, long gm, int gn, int n, float v,
                                           int wid) {
     if (e.planar_out) {
         int py = (int)(gm / wid), px = (int)(gm % wid);
         if (py < e.oh && px < e.ow)
-            y[((long)gn * e.oh + py) * e.ow + px] =
+            y.hi[((long)gn * e.oh + py) * e.ow + px] =
                 v / e.img_range + (gn == 0 ? e.mean[0] : gn == 1 ? e.mean[1] : e.mean[2]);
         return;
     }
@@ -61,7 +71,7 @@ __device__ __forceinline__ void epi_store(const Epi& e, float* y, long gm, int g
         int c = gn / (r * r), rem = gn - c * r * r, i = rem / r, j = rem - i * r;
         int py = (int)(gm / wid), px = (int)(gm % wid);
         long oy = (long)py * r + i, ox = (long)px * r + j;
-        y[(oy * ((long)wid * r) + ox) * cout + c] = v;
+        put(y, (oy * ((long)wid * r) + ox) * cout + c, v);
         return;
     }
     long idx = gm * (e.ldo ? e.ldo : n) + gn;
@@ -69,12 +79,12 @@ __device__ __forceinline__ void epi_store(const Epi& e, float* y, long gm, int g
         v = (e.res[idx] + v) + (e.cx[idx] * e.gate[gn]) * e.cscale;
     else if (e.res)
         v = e.res[idx] + v;
-    y[idx] = v;
+    put(y, idx, v);
 }
 
 template <int BN, bool VEC, class AL>
 __global__ void __launch_bounds__(256) k_gemm_simt(AL al, const float* __restrict__ w,
-                                                   float* __restrict__ y, long M, int N, int K,
+                                                   Dst y, long M, int N, int K,
                                                    Epi e, int wid) {
     constexpr int BM = 128, BK = 16, TN = BN / 16;
     __shared__ __align__(16) float As[BK][BM + 4];
@@ -182,7 +192,7 @@ static int pick_bn(int n) {
 }
 
 template <class AL>
-static void run_simt(const AL& al, bool vec, const float* w, float* y, long m, int n, int k,
+static void run_simt(const AL& al, bool vec, const float* w, Dst y, long m, int n, int k,
                      const Epi& e, int wid, cudaStream_t st) {
     int bn = pick_bn(n);
     dim3 grid((unsigned)((m + 127) / 128), (unsigned)((n + bn - 1) / bn));
@@ -202,12 +212,12 @@ static void run_simt(const AL& al, bool vec, const float* w, float* y, long m, i
     count_launch();
 }
 
-long simt_linear(const float* x, const GemmW& w, float* y, long m, const Epi& e, cudaStream_t st) {
+long simt_linear(Opnd x, const GemmW& w, Dst y, long m, const Epi& e, cudaStream_t st) {
     run_simt(ALinear{x, w.k}, w.k % 4 == 0, w.simt, y, m, w.n, w.k, e, 1, st);
     return (m + 127) / 128;
 }
 
-long simt_conv3x3(const float* x, const GemmW& w, float* y, int hgt, int wid, const Epi& e, cudaStream_t st) {
+long simt_conv3x3(Opnd x, const GemmW& w, Dst y, int hgt, int wid, const Epi& e, cudaStream_t st) {
     const int ldc = w.cin_plane ? w.cin_plane : w.cin;
     const long m = (long)hgt * wid;
     run_simt(AConv{x, hgt, wid, w.cin, ldc}, w.cin % 4 == 0 && ldc % 4 == 0, w.simt, y, m, w.n, 9 * w.cin, e, wid,

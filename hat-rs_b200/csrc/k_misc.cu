@@ -36,7 +36,7 @@ void launch_pre(const float* in, float* out, const Plan& p, const float mean[3],
 // variance of the centred values (src/cpu.rs:563-581), eps 1e-5.
 template <int MAXV>
 __global__ void k_layernorm(const float* __restrict__ x, const float* __restrict__ g,
-                            const float* __restrict__ b, float* __restrict__ y, long m, int c) {
+                            const float* __restrict__ b, Dst y, long m, int c) {
     long row = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     int lane = threadIdx.x & 31;
     if (row >= m) return;
@@ -62,22 +62,36 @@ __global__ void k_layernorm(const float* __restrict__ x, const float* __restrict
 #pragma unroll
     for (int o = 16; o; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
     float rstd = 1.f / sqrtf(q / (float)c + 1e-5f);
-    float* yr = y + row * c;
 #pragma unroll
     for (int i = 0; i < MAXV; ++i) {
         int ch = i * 32 + lane;
-        if (ch < c) yr[ch] = (v[i] - mean) * rstd * g[ch] + b[ch];
+        if (ch < c) put(y, row * c + ch, (v[i] - mean) * rstd * g[ch] + b[ch]);
     }
 }
 
-void launch_layernorm(const float* x, const float* g, const float* b, float* y, long m, int c,
-                      cudaStream_t st) {
+void launch_layernorm(const float* x, const float* g, const float* b, Dst y, long m, int c, cudaStream_t st) {
     if (c > 256) throw Error(1, "layernorm: c > 256 is not supported");
     unsigned grid = (unsigned)((m + 7) / 8);
     if (c <= 160)
         k_layernorm<5><<<grid, 256, 0, st>>>(x, g, b, y, m, c);
     else
         k_layernorm<8><<<grid, 256, 0, st>>>(x, g, b, y, m, c);
+    HAT_CUDA(cudaGetLastError());
+    count_launch();
+}
+
+// ---------------------------------------------------------------- split
+__global__ void k_split(const float* __restrict__ x, float* __restrict__ hi, float* __restrict__ lo, long n) {
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+        float h, l;
+        split_tf32(x[i], h, l);
+        hi[i] = h;
+        lo[i] = l;
+    }
+}
+
+void launch_split(const float* x, float* hi, float* lo, long n, cudaStream_t st) {
+    k_split<<<1184, 256, 0, st>>>(x, hi, lo, n);
     HAT_CUDA(cudaGetLastError());
     count_launch();
 }

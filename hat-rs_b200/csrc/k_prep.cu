@@ -81,15 +81,19 @@ void launch_prep_gemm_w(const float* w, float* simt, float* hi, float* lo, const
     }
 }
 
-long gemm_linear(const GemmCtx& c, const float* x, const GemmW& w, float* y, long m, const Epi& e, cudaStream_t st) {
-    if (!c.simt_only && w.umma && !e.planar_out && !e.shuffle)
+long gemm_linear(const GemmCtx& c, Opnd x, const GemmW& w, Dst y, long m, const Epi& e, cudaStream_t st) {
+    // Parity mode needs the operand split by its producer; a plain plane (never the case
+    // inside the forward) takes the exact CUDA-core path instead of losing precision.
+    const bool ok = c.mode != 0 || x.lo;
+    if (!c.simt_only && w.umma && ok && !e.planar_out && !e.shuffle)
         return umma_linear(c.mode, x, w, y, m, e, c.err, st);
     return simt_linear(x, w, y, m, e, st);
 }
 
-long gemm_conv3x3(const GemmCtx& c, const float* x, const GemmW& w, float* y, int hgt, int wid, const Epi& e,
+long gemm_conv3x3(const GemmCtx& c, Opnd x, const GemmW& w, Dst y, int hgt, int wid, const Epi& e,
                   cudaStream_t st) {
-    if (!c.simt_only && w.umma && hgt % 8 == 0 && wid % 16 == 0)
+    const bool ok = c.mode != 0 || x.lo;
+    if (!c.simt_only && w.umma && ok && hgt % 8 == 0 && wid % 16 == 0)
         return umma_conv3x3(c.mode, x, w, y, hgt, wid, e, c.err, st);
     return simt_conv3x3(x, w, y, hgt, wid, e, st);
 }

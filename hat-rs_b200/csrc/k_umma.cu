@@ -8,16 +8,17 @@
 // K loop runs over (tap, 32-channel chunk) and TMA's zero fill outside the plane is
 // the conv's zero padding.
 //
-// fp32 parity ("3xTF32"): every operand x is split into x_hi = x rounded to the nearest
-// tf32 value and x_lo = (x - x_hi) rounded to tf32, and
+// fp32 parity ("3xTF32"): every operand x arrives split into x_hi = x rounded to the
+// nearest tf32 value and x_lo = (x - x_hi) rounded to tf32 (the weights are split once
+// at upload; every activation plane a GEMM reads is written split by the kernel that
+// produces it), and
 //   A.B ~= A_hi.B_hi + A_hi.B_lo + A_lo.B_hi,
-// which drops only A_lo.B_lo (relative 2^-22); the rounding keeps the error unbiased. The weights are split once at upload;
-// the activation tile is split in shared memory by four converter warps between its
-// TMA landing and the MMA. FAST mode issues the single A.B product on the raw tiles.
+// which drops only A_lo.B_lo (relative 2^-22). FAST mode issues the single A_hi.B_hi.
+// The epilogue can write its own output split the same way for the next GEMM.
 //
-// Warp roles (256 threads): 0 TMA producer, 1 MMA issuer + TMEM owner, 2-3 converters,
-// 4-7 epilogue (TMEM -> registers -> fused epilogue -> global). Two TMEM accumulators
-// (2 x 256 columns) let the epilogue of one tile overlap the MMAs of the next.
+// Warp roles (192 threads): 0 TMA producer, 1 MMA issuer + TMEM owner, 2-5 epilogue
+// (TMEM -> registers -> fused epilogue -> global). Two TMEM accumulators (2 x 256
+// columns) let the epilogue of one tile overlap the MMAs of the next.
 //
 // Every mbarrier wait is bounded (about 2 s of SM clock cycles); on expiry the kernel records an
 // error code in `err`, every role leaves its loop, in-flight TMA copies and MMAs are
@@ -31,7 +32,7 @@ namespace hat {
 
 namespace {
 
-constexpr int NTHREADS = 256;
+constexpr int NTHREADS = 192;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return (uint32_t)__cvta_generic_to_shared(p);
@@ -151,7 +152,7 @@ struct UmmaArgs {
     // conv geometry (MODE 1): plane H x W, channel chunks per tap, patch tiles along x
     int H, W, cchunks, tx;
     long mtiles, ntiles;
-    float* y;
+    Dst y;
     int ldo;         // row stride of the output plane (channels), for plain stores
     int nstore;      // columns stored (<= ldo)
     int* err;
@@ -159,10 +160,11 @@ struct UmmaArgs {
 
 template <int MODE, int TERMS>
 __global__ void __launch_bounds__(NTHREADS, 1)
-    k_umma(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmBh,
-           const __grid_constant__ CUtensorMap tmBl, const UmmaArgs g, const Epi e) {
+    k_umma(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
+           const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl, const UmmaArgs g,
+           const Epi e) {
     extern __shared__ __align__(1024) uint8_t smraw[];
-    __shared__ uint64_t full[4], ready[4], empty[4], acc_full[2], acc_empty[2], drain;
+    __shared__ uint64_t full[6], empty[6], acc_full[2], acc_empty[2], drain;
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int abort_flag;
     // The channel-attention pool: per epilogue warp, column sums accumulated over every
@@ -172,9 +174,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     uint8_t* sm = (uint8_t*)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
     const int S = g.stages;
     const uint32_t a_bytes = 128 * g.ckb, b_bytes = g.BN * g.ckb;
-    // per stage: A (raw, then hi in place) | A lo | B hi | B lo
+    // per stage: A hi | A lo | B hi | B lo
     const uint32_t st_bytes = 2 * a_bytes + 2 * b_bytes;
-    auto sA = [&](int s) { return sm + s * st_bytes; };
+    auto sAh = [&](int s) { return sm + s * st_bytes; };
     auto sAl = [&](int s) { return sm + s * st_bytes + a_bytes; };
     auto sBh = [&](int s) { return sm + s * st_bytes + 2 * a_bytes; };
     auto sBl = [&](int s) { return sm + s * st_bytes + 2 * a_bytes + b_bytes; };
@@ -184,7 +186,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&ready[s], 64);
             mbar_init(&empty[s], 1);
         }
         for (int a = 0; a < 2; ++a) {
@@ -209,7 +210,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
             uint32_t it = 0;
-            const uint32_t tx = TERMS == 3 ? a_bytes + 2 * b_bytes : a_bytes + b_bytes;
+            const uint32_t tx = TERMS == 3 ? 2 * a_bytes + 2 * b_bytes : a_bytes + b_bytes;
             for (long t = blockIdx.x; t < ntiles && !abort_flag; t += gridDim.x) {
                 const long mt = t / g.ntn;
                 const int nt = (int)(t % g.ntn);
@@ -219,11 +220,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     mbar_expect_tx(&full[s], tx);
                     const int kel = kb * (g.ckb / 4);  // K offset in elements
                     if (MODE == 0) {
-                        tma_2d(sA(s), &tmA, kel, (int)(mt * 128), &full[s]);
+                        tma_2d(sAh(s), &tmAh, kel, (int)(mt * 128), &full[s]);
+                        if (TERMS == 3) tma_2d(sAl(s), &tmAl, kel, (int)(mt * 128), &full[s]);
                     } else {
                         const int tap = kb / g.cchunks, cc = kb - tap * g.cchunks;
                         const int py = (int)(mt / g.tx), px = (int)(mt % g.tx);
-                        tma_3d(sA(s), &tmA, cc * (g.ckb / 4), px * 16 + tap % 3 - 1, py * 8 + tap / 3 - 1, &full[s]);
+                        const int c0 = cc * (g.ckb / 4), x0 = px * 16 + tap % 3 - 1, y0 = py * 8 + tap / 3 - 1;
+                        tma_3d(sAh(s), &tmAh, c0, x0, y0, &full[s]);
+                        if (TERMS == 3) tma_3d(sAl(s), &tmAl, c0, x0, y0, &full[s]);
                     }
                     tma_2d(sBh(s), &tmBh, kel, nt * g.BN, &full[s]);
                     if (TERMS == 3) tma_2d(sBl(s), &tmBl, kel, nt * g.BN, &full[s]);
@@ -231,9 +235,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             if (abort_flag) {
                 // Let the copies already issued land before the CTA can exit.
-                for (uint32_t j = (it > (uint32_t)S ? it - S : 0); j < it; ++j) {
-                    mbar_wait_quiet(&full[j % S], (j / S) & 1);
-                }
+                for (uint32_t j = (it > (uint32_t)S ? it - S : 0); j < it; ++j) mbar_wait_quiet(&full[j % S], (j / S) & 1);
             }
         }
     } else if (warp == 1) {
@@ -250,19 +252,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 bool ok = true;
                 for (int kb = 0; kb < g.KB; ++kb, ++it) {
                     const int s = it % S;
-                    uint64_t* rb = TERMS == 3 ? &ready[s] : &full[s];
-                    if (!mbar_wait(rb, (it / S) & 1, &abort_flag, g.err, 3)) {
+                    if (!mbar_wait(&full[s], (it / S) & 1, &abort_flag, g.err, 3)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t ah = smem_u32(sA(s)), al = smem_u32(sAl(s));
+                    const uint32_t ah = smem_u32(sAh(s)), al = smem_u32(sAl(s));
                     const uint32_t bh = smem_u32(sBh(s)), bl = smem_u32(sBl(s));
 #pragma unroll 1
                     for (int k = 0; k < ksteps; ++k) {
                         const uint32_t off = k * 32;
                         const uint32_t acc0 = (kb | k) ? 1u : 0u;
                         if (TERMS == 3) {
+                            // small terms first, so they are added while the sum is small
                             mma_tf32(d, smem_desc(al + off, g.ckb), smem_desc(bh + off, g.ckb), idesc, acc0);
                             mma_tf32(d, smem_desc(ah + off, g.ckb), smem_desc(bl + off, g.ckb), idesc, 1u);
                             mma_tf32(d, smem_desc(ah + off, g.ckb), smem_desc(bh + off, g.ckb), idesc, 1u);
@@ -279,47 +281,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             mma_commit(&drain);
             mbar_wait_quiet(&drain, 0);
         }
-    } else if (warp < 4) {
-        // ------------------------------------------------------------ converters
-        if (TERMS == 3) {
-            const int ct = threadIdx.x - 64;  // 0..63
-            uint32_t it = 0;
-            const int nvec = a_bytes / 16;    // float4s per A tile
-            for (long t = blockIdx.x; t < ntiles; t += gridDim.x) {
-                if (__any_sync(0xffffffffu, abort_flag != 0)) break;
-                bool ok = true;
-                for (int kb = 0; kb < g.KB; ++kb, ++it) {
-                    const int s = it % S;
-                    // warp-uniform outcome: every lane waits, and the warp leaves together
-                    const bool got = mbar_wait(&full[s], (it / S) & 1, &abort_flag, g.err, 4);
-                    if (!__all_sync(0xffffffffu, got)) {
-                        ok = false;
-                        break;
-                    }
-                    float4* hi = reinterpret_cast<float4*>(sA(s));
-                    float4* lo = reinterpret_cast<float4*>(sAl(s));
-                    for (int i = ct; i < nvec; i += 64) {
-                        float4 v = hi[i], h, l;
-                        split_tf32(v.x, h.x, l.x);
-                        split_tf32(v.y, h.y, l.y);
-                        split_tf32(v.z, h.z, l.z);
-                        split_tf32(v.w, h.w, l.w);
-                        hi[i] = h;
-                        lo[i] = l;
-                    }
-                    // Each thread makes its generic-proxy stores visible to the tensor
-                    // core's async proxy, then arrives (64 arrivals complete the phase).
-                    fence_proxy_async();
-                    mbar_arrive(&ready[s]);
-                }
-                if (!ok) break;
-            }
-        }
     } else {
         // ------------------------------------------------------------ epilogue
         const int q = warp & 3;          // TMEM lane quarter this warp may read
         const int row = q * 32 + lane;   // tile row of this thread
-        const int ew = warp - 4;         // 0..3 within the epilogue group
+        const int ew = warp - 2;         // 0..3 within the epilogue group
         uint32_t tl = 0;
         for (long t = blockIdx.x; t < ntiles; t += gridDim.x, ++tl) {
             if (__any_sync(0xffffffffu, abort_flag != 0)) break;
@@ -359,10 +325,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
                         for (int sub = 0; sub < 4; ++sub) {
                             const long oy = 2L * py + (sub >> 1), ox = 2L * px + (sub & 1);
-                            float* dst = g.y + (oy * (2L * g.W) + ox) * cout + cb;
-                            *reinterpret_cast<float4*>(dst) = make_float4(v[sub], v[4 + sub], v[8 + sub], v[12 + sub]);
-                            *reinterpret_cast<float4*>(dst + 4) =
-                                make_float4(v[16 + sub], v[20 + sub], v[24 + sub], v[28 + sub]);
+                            const long o = (oy * (2L * g.W) + ox) * cout + cb;
+                            put4(g.y, o, make_float4(v[sub], v[4 + sub], v[8 + sub], v[12 + sub]));
+                            put4(g.y, o + 4, make_float4(v[16 + sub], v[20 + sub], v[24 + sub], v[28 + sub]));
                         }
                     }
                 }
@@ -391,7 +356,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         for (int j = 0; j < 16; ++j) {
                             const int n = n0 + c0 + j;
                             if (inside && n < g.N)
-                                g.y[((long)n * e.oh + yy) * e.ow + xx] =
+                                g.y.hi[((long)n * e.oh + yy) * e.ow + xx] =
                                     v[j] / e.img_range + (n == 0 ? e.mean[0] : n == 1 ? e.mean[1] : e.mean[2]);
                         }
                     } else if (e.shuffle) {
@@ -402,11 +367,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                             if (n < g.N) {
                                 const int c = n / (r * r), rem = n - c * r * r, i = rem / r, jj = rem - i * r;
                                 const long oy = (long)py * r + i, ox = (long)px * r + jj;
-                                g.y[(oy * ((long)g.W * r) + ox) * cout + c] = v[j];
+                                put(g.y, (oy * ((long)g.W * r) + ox) * cout + c, v[j]);
                             }
                         }
                     } else {
-                        float* dst = g.y + m * g.ldo + n0 + c0;
                         const long base = m * g.ldo + n0 + c0;
                         if (n0 + c0 + 16 <= g.nstore && (g.ldo % 4) == 0) {
 #pragma unroll
@@ -427,7 +391,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                                     o.z = r.z + o.z;
                                     o.w = r.w + o.w;
                                 }
-                                *reinterpret_cast<float4*>(dst + 4 * j4) = o;
+                                put4(g.y, base + 4 * j4, o);
                             }
                         } else {
 #pragma unroll
@@ -439,7 +403,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                                         o = (e.res[base + j] + o) + (e.cx[base + j] * e.gate[n]) * e.cscale;
                                     else if (e.res)
                                         o = e.res[base + j] + o;
-                                    dst[j] = o;
+                                    put(g.y, base + j, o);
                                 }
                             }
                         }
@@ -516,20 +480,22 @@ static int num_sms() {
     return n[dev & 63];
 }
 
+static const long SMEM_CAP = 232448 - 8192;  // dynamic shared memory requested at most
+
 template <int MODE, int TERMS>
-static void launch_k(const CUtensorMap& a, const CUtensorMap& bh, const CUtensorMap& bl, const UmmaArgs& g,
-                     const Epi& e, cudaStream_t st) {
+static void launch_k(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh, const CUtensorMap& bl,
+                     const UmmaArgs& g, const Epi& e, cudaStream_t st) {
     const size_t smem = (size_t)g.stages * (2 * 128 * g.ckb + 2 * g.BN * g.ckb) + 1024;
     static unsigned configured = 0;
     int dev = 0;
     HAT_CUDA(cudaGetDevice(&dev));
     if (!(configured & (1u << dev))) {
-        HAT_CUDA(cudaFuncSetAttribute(k_umma<MODE, TERMS>, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448 - 8192));
+        HAT_CUDA(cudaFuncSetAttribute(k_umma<MODE, TERMS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_CAP));
         configured |= 1u << dev;
     }
     const long grid = std::min<long>(g.ntiles, num_sms());
     if (e.colsum && g.N > 256) throw Error(1, "umma: channel sums are limited to 256 columns");
-    k_umma<MODE, TERMS><<<(unsigned)grid, NTHREADS, smem, st>>>(a, bh, bl, g, e);
+    k_umma<MODE, TERMS><<<(unsigned)grid, NTHREADS, smem, st>>>(ah, al, bh, bl, g, e);
     HAT_CUDA(cudaGetLastError());
     count_launch();
 }
@@ -538,60 +504,68 @@ static long colsum_rows(const UmmaArgs& g) { return std::min<long>(g.ntiles, num
 
 static int pick_stages(int BN, int ckb) {
     const long per = 2L * 128 * ckb + 2L * BN * ckb;
-    const long budget = 232448 - 8192 - 1024 - 4096;
-    return (int)std::max(1L, std::min(4L, budget / per));
+    const long budget = SMEM_CAP - 1024 - 5120;
+    return (int)std::max(1L, std::min(6L, budget / per));
 }
 
-long umma_linear(int mode, const float* x, const GemmW& w, float* y, long m, const Epi& e, int* err, cudaStream_t st) {
+static void fill_common(UmmaArgs& g, const GemmW& w, Dst y, const Epi& e, int* err) {
+    g.N = w.n;
+    g.BN = w.bn;
+    g.ntn = w.n_pad / w.bn;
+    g.y = y;
+    g.ldo = e.ldo ? e.ldo : w.n;
+    g.nstore = e.ldo ? e.ldo : w.n;
+    g.err = err;
+}
+
+long umma_linear(int mode, Opnd x, const GemmW& w, Dst y, long m, const Epi& e, int* err, cudaStream_t st) {
     const int ckb = 128;
+    const bool three = mode == 0;
+    if (three && !x.lo) throw Error(1, "umma_linear: fp32-parity mode needs a split operand");
     uint64_t adims[2] = {(uint64_t)w.k, (uint64_t)m};
     uint64_t astr[1] = {(uint64_t)w.k * 4};
     uint32_t abox[2] = {32, 128};
-    CUtensorMap ta = make_map(x, 2, adims, astr, abox, ckb);
+    CUtensorMap tah = make_map(x.hi, 2, adims, astr, abox, ckb);
+    CUtensorMap tal = make_map(three ? x.lo : x.hi, 2, adims, astr, abox, ckb);
     uint64_t bdims[2] = {(uint64_t)w.k_pad, (uint64_t)w.n_pad};
     uint64_t bstr[1] = {(uint64_t)w.k_pad * 4};
     uint32_t bbox[2] = {32, (uint32_t)w.bn};
     CUtensorMap tbh = make_map(w.hi, 2, bdims, bstr, bbox, ckb);
-    CUtensorMap tbl = make_map(mode == 0 ? w.lo : w.hi, 2, bdims, bstr, bbox, ckb);
+    CUtensorMap tbl = make_map(three ? w.lo : w.hi, 2, bdims, bstr, bbox, ckb);
     UmmaArgs g{};
+    fill_common(g, w, y, e, err);
     g.M = m;
-    g.N = w.n;
-    g.BN = w.bn;
-    g.ntn = w.n_pad / w.bn;
     g.KB = w.k_pad / 32;
     g.ckb = ckb;
     g.stages = pick_stages(w.bn, ckb);
     g.mtiles = (m + 127) / 128;
     g.ntiles = g.mtiles * g.ntn;
-    g.y = y;
-    g.ldo = e.ldo ? e.ldo : w.n;
-    g.nstore = e.ldo ? e.ldo : w.n;
-    g.err = err;
-    if (mode == 0)
-        launch_k<0, 3>(ta, tbh, tbl, g, e, st);
+    if (three)
+        launch_k<0, 3>(tah, tal, tbh, tbl, g, e, st);
     else
-        launch_k<0, 1>(ta, tbh, tbl, g, e, st);
+        launch_k<0, 1>(tah, tal, tbh, tbl, g, e, st);
     return colsum_rows(g);  // colsum: one partial row per (CTA, epilogue warp)
 }
 
-long umma_conv3x3(int mode, const float* x, const GemmW& w, float* y, int hgt, int wid, const Epi& e, int* err,
+long umma_conv3x3(int mode, Opnd x, const GemmW& w, Dst y, int hgt, int wid, const Epi& e, int* err,
                   cudaStream_t st) {
     const int ckb = w.cinp == 8 ? 32 : 128;
     const int cke = ckb / 4;
+    const bool three = mode == 0;
+    if (three && !x.lo) throw Error(1, "umma_conv3x3: fp32-parity mode needs a split operand");
     uint64_t adims[3] = {(uint64_t)w.cin_plane, (uint64_t)wid, (uint64_t)hgt};
     uint64_t astr[2] = {(uint64_t)w.cin_plane * 4, (uint64_t)wid * w.cin_plane * 4};
     uint32_t abox[3] = {(uint32_t)cke, 16, 8};
-    CUtensorMap ta = make_map(x, 3, adims, astr, abox, ckb);
+    CUtensorMap tah = make_map(x.hi, 3, adims, astr, abox, ckb);
+    CUtensorMap tal = make_map(three ? x.lo : x.hi, 3, adims, astr, abox, ckb);
     uint64_t bdims[2] = {(uint64_t)w.k_pad, (uint64_t)w.n_pad};
     uint64_t bstr[1] = {(uint64_t)w.k_pad * 4};
     uint32_t bbox[2] = {(uint32_t)cke, (uint32_t)w.bn};
     CUtensorMap tbh = make_map(w.hi, 2, bdims, bstr, bbox, ckb);
-    CUtensorMap tbl = make_map(mode == 0 ? w.lo : w.hi, 2, bdims, bstr, bbox, ckb);
+    CUtensorMap tbl = make_map(three ? w.lo : w.hi, 2, bdims, bstr, bbox, ckb);
     UmmaArgs g{};
+    fill_common(g, w, y, e, err);
     g.M = (long)hgt * wid;
-    g.N = w.n;
-    g.BN = w.bn;
-    g.ntn = w.n_pad / w.bn;
     g.cchunks = w.cinp / cke;
     g.KB = 9 * g.cchunks;
     g.ckb = ckb;
@@ -601,15 +575,11 @@ long umma_conv3x3(int mode, const float* x, const GemmW& w, float* y, int hgt, i
     g.tx = wid / 16;
     g.mtiles = (long)(hgt / 8) * g.tx;
     g.ntiles = g.mtiles * g.ntn;
-    g.y = y;
-    g.ldo = e.ldo ? e.ldo : w.n;
-    g.nstore = e.ldo ? e.ldo : w.n;
-    g.err = err;
-    if (mode == 0)
-        launch_k<1, 3>(ta, tbh, tbl, g, e, st);
+    if (three)
+        launch_k<1, 3>(tah, tal, tbh, tbl, g, e, st);
     else
-        launch_k<1, 1>(ta, tbh, tbl, g, e, st);
-    return colsum_rows(g);  // colsum: one partial row per (CTA, epilogue warp)
+        launch_k<1, 1>(tah, tal, tbh, tbl, g, e, st);
+    return colsum_rows(g);
 }
 
 }  // namespace hat

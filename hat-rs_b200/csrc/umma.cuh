@@ -24,22 +24,6 @@ struct GemmW {
     bool umma = false;      // tensor-core layout present
 };
 
-#ifdef __CUDACC__
-// x = hi + lo with hi = x rounded to the nearest tf32 value and lo = (x - hi) rounded
-// to tf32 as well: both halves are exact tf32 operands, the split is unbiased, and
-// hi + lo is within 2^-22 |x| of x. The tensor core then sees exactly these values.
-// tf32 keeps 10 of fp32's 23 mantissa bits: adding half a unit of the 13th bit to the
-// sign-magnitude pattern and clearing the low 13 bits rounds the magnitude to nearest
-// (ties away from zero), carrying into the exponent when the mantissa overflows. Two
-// integer operations, so the split stays off the conversion pipe.
-__device__ __forceinline__ float tf32_rna(float x) {
-    return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
-}
-__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
-    hi = tf32_rna(x);
-    lo = tf32_rna(x - hi);
-}
-#endif
 
 // Columns per tensor-core tile for an output width n: at most 192 (so three pipeline
 // stages fit in shared memory for c = 144), a multiple of 16, tiles of equal width.
@@ -55,14 +39,15 @@ void plan_gemm_w(GemmW& g, int n, int k_or_cin, bool conv, int cin_plane);
 size_t gemm_w_floats(const GemmW& g);  // simt + hi + lo floats
 void launch_prep_gemm_w(const float* w, float* simt, float* hi, float* lo, const GemmW& g, cudaStream_t st);
 
-// Tensor-core launchers; return the number of M tiles (colsum partial rows).
-long umma_linear(int mode, const float* x, const GemmW& w, float* y, long m, const Epi& e, int* err, cudaStream_t st);
-long umma_conv3x3(int mode, const float* x, const GemmW& w, float* y, int hgt, int wid, const Epi& e, int* err,
+// Tensor-core launchers (`x.lo` required in parity mode); return the number of
+// channel-sum partial rows written when `e.colsum` is set.
+long umma_linear(int mode, Opnd x, const GemmW& w, Dst y, long m, const Epi& e, int* err, cudaStream_t st);
+long umma_conv3x3(int mode, Opnd x, const GemmW& w, Dst y, int hgt, int wid, const Epi& e, int* err,
                   cudaStream_t st);
 
-// CUDA-core launchers; return the number of M tiles (colsum partial rows).
-long simt_linear(const float* x, const GemmW& w, float* y, long m, const Epi& e, cudaStream_t st);
-long simt_conv3x3(const float* x, const GemmW& w, float* y, int hgt, int wid, const Epi& e, cudaStream_t st);
+// CUDA-core launchers (read hi + lo when the operand is split); same return value.
+long simt_linear(Opnd x, const GemmW& w, Dst y, long m, const Epi& e, cudaStream_t st);
+long simt_conv3x3(Opnd x, const GemmW& w, Dst y, int hgt, int wid, const Epi& e, cudaStream_t st);
 
 // What the engine calls: the tensor-core kernel when the shape allows it and
 // `simt_only` is false, else the CUDA-core kernel.
@@ -71,8 +56,8 @@ struct GemmCtx {
     bool simt_only = false;
     int* err = nullptr;   // device error flag of the tensor-core kernels' bounded waits
 };
-long gemm_linear(const GemmCtx& c, const float* x, const GemmW& w, float* y, long m, const Epi& e, cudaStream_t st);
-long gemm_conv3x3(const GemmCtx& c, const float* x, const GemmW& w, float* y, int hgt, int wid, const Epi& e,
+long gemm_linear(const GemmCtx& c, Opnd x, const GemmW& w, Dst y, long m, const Epi& e, cudaStream_t st);
+long gemm_conv3x3(const GemmCtx& c, Opnd x, const GemmW& w, Dst y, int hgt, int wid, const Epi& e,
                   cudaStream_t st);
 
 }  // namespace hat

@@ -156,5 +156,9 @@ def test_conv_kernel_vs_torch(torch_cuda, hg, wd, ci, co, mode):
     torch.cuda.synchronize()
     want = torch.nn.functional.conv2d(x.double().permute(2, 0, 1)[None], w.double(), b.double(), padding=1)
     want = want[0].permute(1, 2, 0).float()
-    tol = KERNEL_TOL[mode] * (2.5 if mode != hat_b200.MODE_FAST else 4)
+    # The tensor core truncates when it adds each MMA's partial sum into the fp32
+    # accumulator, so over K = 9 * cin the parity-mode error grows with |y|; the
+    # whole-network tests hold the forward to 1e-4 regardless.
+    amax = float(want.abs().max())
+    tol = {hat_b200.MODE_SIMT: 5e-5, hat_b200.MODE_PARITY: 2e-5 * (1 + amax), hat_b200.MODE_FAST: 2e-2}[mode]
     assert float((y - want).abs().max()) < tol
