@@ -158,6 +158,81 @@ struct UmmaArgs {
     int* err;
 };
 
+// Row `trow` of tile `mt`: its token / pixel index and whether it exists.
+template <int MODE>
+__device__ __forceinline__ void tile_row(const UmmaArgs& g, long mt, int trow, long& m, bool& valid) {
+    if (MODE == 0) {
+        m = mt * 128 + trow;
+        valid = m < g.M;
+    } else {
+        const int py = (int)(mt / g.tx) * 8 + trow / 16, px = (int)(mt % g.tx) * 16 + trow % 16;
+        m = (long)py * g.W + px;
+        valid = py < g.H;
+    }
+}
+
+// One CW-column chunk of an epilogue warp's 32 rows with a plain (possibly residual)
+// store. Phase 1: each thread holds its own row's CW accumulators (TMEM lane = row),
+// adds bias and activation, contributes the channel sums, and parks the values in the
+// warp's staging tile. Phase 2: the warp re-reads the tile so that CW/4 consecutive
+// lanes cover one row's CW columns, and residual loads and the (split) stores become
+// full-line, coalesced accesses instead of one 16-byte piece per row per lane.
+template <int MODE, int CW>
+__device__ __forceinline__ void epi_chunk(const UmmaArgs& g, const Epi& e, uint32_t taddr, int n0, int c0, long mt,
+                                          int q, int lane, bool valid_own, float (*stg)[33], float* cacc) {
+    float v[CW];
+    tmem_ld16(taddr + c0, v);
+    if (CW == 32) tmem_ld16(taddr + c0 + 16, v + 16);
+#pragma unroll
+    for (int j = 0; j < CW; ++j) {
+        const int n = n0 + c0 + j;
+        v[j] = n < g.N ? epi_act(v[j] + (e.bias ? e.bias[n] : 0.f), e.act) : 0.f;
+    }
+    if (e.colsum) {
+#pragma unroll
+        for (int j = 0; j < CW; ++j) {
+            float s = valid_own ? v[j] : 0.f;
+#pragma unroll
+            for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            const int n = n0 + c0 + j;
+            if (lane == 0 && n < g.N) cacc[n] += s;
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < CW; ++j) stg[lane][j] = v[j];
+    __syncwarp();
+    constexpr int LPR = CW / 4, RPI = 32 / LPR;
+    const int lr = lane / LPR, lc = (lane % LPR) * 4;
+    const int n = n0 + c0 + lc;
+#pragma unroll
+    for (int it = 0; it < 32 / RPI; ++it) {
+        const int r = it * RPI + lr;
+        long m;
+        bool valid;
+        tile_row<MODE>(g, mt, q * 32 + r, m, valid);
+        if (valid && n < g.nstore) {
+            float4 o = make_float4(stg[r][lc], stg[r][lc + 1], stg[r][lc + 2], stg[r][lc + 3]);
+            const long base = m * g.ldo + n;
+            if (e.cx) {
+                const float4 rs = *reinterpret_cast<const float4*>(e.res + base);
+                const float4 cx = *reinterpret_cast<const float4*>(e.cx + base);
+                o.x = (rs.x + o.x) + (cx.x * e.gate[n]) * e.cscale;
+                o.y = (rs.y + o.y) + (cx.y * e.gate[n + 1]) * e.cscale;
+                o.z = (rs.z + o.z) + (cx.z * e.gate[n + 2]) * e.cscale;
+                o.w = (rs.w + o.w) + (cx.w * e.gate[n + 3]) * e.cscale;
+            } else if (e.res) {
+                const float4 rs = *reinterpret_cast<const float4*>(e.res + base);
+                o.x = rs.x + o.x;
+                o.y = rs.y + o.y;
+                o.z = rs.z + o.z;
+                o.w = rs.w + o.w;
+            }
+            put4(g.y, base, o);
+        }
+    }
+    __syncwarp();
+}
+
 template <int MODE, int TERMS>
 __global__ void __launch_bounds__(NTHREADS, 1)
     k_umma(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
@@ -170,6 +245,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // The channel-attention pool: per epilogue warp, column sums accumulated over every
     // tile this CTA owns (in its fixed tile order), written once at the end.
     __shared__ float colacc[4][256];
+    // Per epilogue warp: a 32 x 32 staging tile (padded) for the coalesced store.
+    __shared__ float stg[4][32][33];
 
     uint8_t* sm = (uint8_t*)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
     const int S = g.stages;
@@ -335,6 +412,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 mbar_arrive(&acc_empty[a]);
                 continue;
             }
+            if (!e.planar_out && !e.shuffle && g.ldo % 4 == 0 && g.nstore % 4 == 0) {
+                int c0 = 0;
+                for (; c0 + 32 <= g.BN; c0 += 32)
+                    epi_chunk<MODE, 32>(g, e, taddr, n0, c0, mt, q, lane, valid, stg[ew], colacc[ew]);
+                if (c0 < g.BN) epi_chunk<MODE, 16>(g, e, taddr, n0, c0, mt, q, lane, valid, stg[ew], colacc[ew]);
+                tc_fence_before();
+                mbar_arrive(&acc_empty[a]);
+                continue;
+            }
             for (int c0 = 0; c0 < g.BN; c0 += 16) {
                 float v[16];
                 tmem_ld16(taddr + c0, v);
@@ -480,7 +566,9 @@ static int num_sms() {
     return n[dev & 63];
 }
 
-static const long SMEM_CAP = 232448 - 8192;  // dynamic shared memory requested at most
+// Dynamic shared memory at most: the 227 KB per CTA less the static arrays (channel
+// sums 4 KB, staging tiles 16.5 KB, barriers) and some slack.
+static const long SMEM_CAP = 232448 - 22528;
 
 template <int MODE, int TERMS>
 static void launch_k(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh, const CUtensorMap& bl,
@@ -504,7 +592,7 @@ static long colsum_rows(const UmmaArgs& g) { return std::min<long>(g.ntiles, num
 
 static int pick_stages(int BN, int ckb) {
     const long per = 2L * 128 * ckb + 2L * BN * ckb;
-    const long budget = SMEM_CAP - 1024 - 5120;
+    const long budget = SMEM_CAP - 1024;
     return (int)std::max(1L, std::min(6L, budget / per));
 }
 
