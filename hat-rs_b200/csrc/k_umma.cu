@@ -171,42 +171,69 @@ __device__ __forceinline__ void tile_row(const UmmaArgs& g, long mt, int trow, l
     }
 }
 
-// One CW-column chunk of an epilogue warp's 32 rows with a plain (possibly residual)
-// store. Phase 1: each thread holds its own row's CW accumulators (TMEM lane = row),
-// adds bias and activation, contributes the channel sums, and parks the values in the
-// warp's staging tile. Phase 2: the warp re-reads the tile so that CW/4 consecutive
-// lanes cover one row's CW columns, and residual loads and the (split) stores become
-// full-line, coalesced accesses instead of one 16-byte piece per row per lane.
-template <int MODE, int CW>
-__device__ __forceinline__ void epi_chunk(const UmmaArgs& g, const Epi& e, uint32_t taddr, int n0, int c0, long mt,
-                                          int q, int lane, bool valid_own, float (*stg)[33], float* cacc) {
-    float v[CW];
+// Epilogue kinds, one kernel instantiation each so a kernel carries only its own store
+// path (the instruction footprint of all of them together thrashed the instruction
+// cache): EK_STORE plain/residual stores, EK_SHUF2 PixelShuffle(2) stores, EK_GENERIC
+// everything else (planar output, other shuffle factors, odd strides).
+enum { EK_STORE = 0, EK_SHUF2 = 1, EK_GENERIC = 2 };
+
+// One 16-column chunk of an epilogue warp's 32 rows with a plain (possibly residual)
+// store. Phase 1: each thread holds its own row's accumulators (TMEM lane = row), adds
+// bias and activation, contributes the channel sums, and parks the values in the
+// warp's staging tile. Phase 2: the warp re-reads the tile so that four lanes cover one
+// row's 16 columns, and the residual loads and (split) stores are 64-byte row segments.
+template <int MODE>
+__device__ __forceinline__ void epi_chunk16(const UmmaArgs& g, const Epi& e, uint32_t taddr, int n0, int c0,
+                                            long mt, int q, int lane, bool valid_own, float (*stg)[17],
+                                            float* cacc) {
+    float v[16];
     tmem_ld16(taddr + c0, v);
-    if (CW == 32) tmem_ld16(taddr + c0 + 16, v + 16);
+    const int nb = n0 + c0;
+    if (e.bias) {
+        if (nb + 16 <= g.N) {
 #pragma unroll
-    for (int j = 0; j < CW; ++j) {
-        const int n = n0 + c0 + j;
-        v[j] = n < g.N ? epi_act(v[j] + (e.bias ? e.bias[n] : 0.f), e.act) : 0.f;
+            for (int j4 = 0; j4 < 4; ++j4) {
+                const float4 b = __ldg(reinterpret_cast<const float4*>(e.bias + nb) + j4);
+                v[4 * j4] += b.x;
+                v[4 * j4 + 1] += b.y;
+                v[4 * j4 + 2] += b.z;
+                v[4 * j4 + 3] += b.w;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (nb + j < g.N) v[j] += __ldg(e.bias + nb + j);
+        }
+    }
+    if (e.act == ACT_GELU) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = 0.5f * v[j] * (1.f + erff(v[j] * 0.70710678118654752f));
+    } else if (e.act == ACT_LEAKY) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = v[j] > 0.f ? v[j] : 0.01f * v[j];
+    }
+    if (nb + 16 > g.N) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            if (nb + j >= g.N) v[j] = 0.f;
     }
     if (e.colsum) {
 #pragma unroll
-        for (int j = 0; j < CW; ++j) {
+        for (int j = 0; j < 16; ++j) {
             float s = valid_own ? v[j] : 0.f;
 #pragma unroll
             for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-            const int n = n0 + c0 + j;
-            if (lane == 0 && n < g.N) cacc[n] += s;
+            if (lane == 0 && nb + j < g.N) cacc[nb + j] += s;
         }
     }
 #pragma unroll
-    for (int j = 0; j < CW; ++j) stg[lane][j] = v[j];
+    for (int j = 0; j < 16; ++j) stg[lane][j] = v[j];
     __syncwarp();
-    constexpr int LPR = CW / 4, RPI = 32 / LPR;
-    const int lr = lane / LPR, lc = (lane % LPR) * 4;
-    const int n = n0 + c0 + lc;
-#pragma unroll
-    for (int it = 0; it < 32 / RPI; ++it) {
-        const int r = it * RPI + lr;
+    const int lr = lane >> 2, lc = (lane & 3) * 4;
+    const int n = nb + lc;
+#pragma unroll 1
+    for (int it = 0; it < 4; ++it) {
+        const int r = it * 8 + lr;
         long m;
         bool valid;
         tile_row<MODE>(g, mt, q * 32 + r, m, valid);
@@ -216,10 +243,11 @@ __device__ __forceinline__ void epi_chunk(const UmmaArgs& g, const Epi& e, uint3
             if (e.cx) {
                 const float4 rs = *reinterpret_cast<const float4*>(e.res + base);
                 const float4 cx = *reinterpret_cast<const float4*>(e.cx + base);
-                o.x = (rs.x + o.x) + (cx.x * e.gate[n]) * e.cscale;
-                o.y = (rs.y + o.y) + (cx.y * e.gate[n + 1]) * e.cscale;
-                o.z = (rs.z + o.z) + (cx.z * e.gate[n + 2]) * e.cscale;
-                o.w = (rs.w + o.w) + (cx.w * e.gate[n + 3]) * e.cscale;
+                const float4 gt = *reinterpret_cast<const float4*>(e.gate + n);
+                o.x = (rs.x + o.x) + (cx.x * gt.x) * e.cscale;
+                o.y = (rs.y + o.y) + (cx.y * gt.y) * e.cscale;
+                o.z = (rs.z + o.z) + (cx.z * gt.z) * e.cscale;
+                o.w = (rs.w + o.w) + (cx.w * gt.w) * e.cscale;
             } else if (e.res) {
                 const float4 rs = *reinterpret_cast<const float4*>(e.res + base);
                 o.x = rs.x + o.x;
@@ -233,7 +261,7 @@ __device__ __forceinline__ void epi_chunk(const UmmaArgs& g, const Epi& e, uint3
     __syncwarp();
 }
 
-template <int MODE, int TERMS>
+template <int MODE, int TERMS, int EK>
 __global__ void __launch_bounds__(NTHREADS, 1)
     k_umma(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
            const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl, const UmmaArgs g,
@@ -245,8 +273,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // The channel-attention pool: per epilogue warp, column sums accumulated over every
     // tile this CTA owns (in its fixed tile order), written once at the end.
     __shared__ float colacc[4][256];
-    // Per epilogue warp: a 32 x 32 staging tile (padded) for the coalesced store.
-    __shared__ float stg[4][32][33];
+    // Per epilogue warp: a 32 x 16 staging tile (padded) for the coalesced store.
+    __shared__ float stg[4][32][17];
 
     uint8_t* sm = (uint8_t*)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
     const int S = g.stages;
@@ -386,7 +414,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             const int n0 = nt * g.BN;
             const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + a * 256;
-            if (e.shuffle == 2 && g.BN % 32 == 0 && g.N % g.BN == 0) {
+            if (EK == EK_SHUF2) {
                 // PixelShuffle(2) store: channel n = 4c + 2i + j goes to channel c of output
                 // pixel (2y + i, 2x + j). 32 columns give 8 consecutive output channels for
                 // each of the 4 sub-pixels: two float4 stores per sub-pixel.
@@ -412,11 +440,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 mbar_arrive(&acc_empty[a]);
                 continue;
             }
-            if (!e.planar_out && !e.shuffle && g.ldo % 4 == 0 && g.nstore % 4 == 0) {
-                int c0 = 0;
-                for (; c0 + 32 <= g.BN; c0 += 32)
-                    epi_chunk<MODE, 32>(g, e, taddr, n0, c0, mt, q, lane, valid, stg[ew], colacc[ew]);
-                if (c0 < g.BN) epi_chunk<MODE, 16>(g, e, taddr, n0, c0, mt, q, lane, valid, stg[ew], colacc[ew]);
+            if (EK == EK_STORE) {
+#pragma unroll 1
+                for (int c0 = 0; c0 < g.BN; c0 += 16)
+                    epi_chunk16<MODE>(g, e, taddr, n0, c0, mt, q, lane, valid, stg[ew], colacc[ew]);
                 tc_fence_before();
                 mbar_arrive(&acc_empty[a]);
                 continue;
@@ -567,25 +594,45 @@ static int num_sms() {
 }
 
 // Dynamic shared memory at most: the 227 KB per CTA less the static arrays (channel
-// sums 4 KB, staging tiles 16.5 KB, barriers) and some slack.
-static const long SMEM_CAP = 232448 - 22528;
+// sums 4 KB, staging tiles 8.5 KB, barriers) and some slack.
+static const long SMEM_CAP = 232448 - 14336;
 
-template <int MODE, int TERMS>
-static void launch_k(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh, const CUtensorMap& bl,
-                     const UmmaArgs& g, const Epi& e, cudaStream_t st) {
+template <int MODE, int TERMS, int EK>
+static void launch_ek(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh, const CUtensorMap& bl,
+                      const UmmaArgs& g, const Epi& e, cudaStream_t st) {
     const size_t smem = (size_t)g.stages * (2 * 128 * g.ckb + 2 * g.BN * g.ckb) + 1024;
     static unsigned configured = 0;
     int dev = 0;
     HAT_CUDA(cudaGetDevice(&dev));
     if (!(configured & (1u << dev))) {
-        HAT_CUDA(cudaFuncSetAttribute(k_umma<MODE, TERMS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_CAP));
+        HAT_CUDA(cudaFuncSetAttribute(k_umma<MODE, TERMS, EK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)SMEM_CAP));
         configured |= 1u << dev;
     }
     const long grid = std::min<long>(g.ntiles, num_sms());
     if (e.colsum && g.N > 256) throw Error(1, "umma: channel sums are limited to 256 columns");
-    k_umma<MODE, TERMS><<<(unsigned)grid, NTHREADS, smem, st>>>(ah, al, bh, bl, g, e);
+    k_umma<MODE, TERMS, EK><<<(unsigned)grid, NTHREADS, smem, st>>>(ah, al, bh, bl, g, e);
     HAT_CUDA(cudaGetLastError());
     count_launch();
+}
+
+// The epilogue kind for this launch (see EK_*).
+static int pick_ek(const UmmaArgs& g, const Epi& e) {
+    if (e.planar_out) return EK_GENERIC;
+    if (e.shuffle == 2 && g.BN % 32 == 0 && g.N % g.BN == 0) return EK_SHUF2;
+    if (e.shuffle) return EK_GENERIC;
+    if (g.ldo % 4 == 0 && g.nstore % 4 == 0 && (!e.cx || g.N % 4 == 0)) return EK_STORE;
+    return EK_GENERIC;
+}
+
+template <int MODE, int TERMS>
+static void launch_k(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh, const CUtensorMap& bl,
+                     const UmmaArgs& g, const Epi& e, cudaStream_t st) {
+    switch (pick_ek(g, e)) {
+        case EK_STORE: launch_ek<MODE, TERMS, EK_STORE>(ah, al, bh, bl, g, e, st); break;
+        case EK_SHUF2: launch_ek<MODE, TERMS, EK_SHUF2>(ah, al, bh, bl, g, e, st); break;
+        default: launch_ek<MODE, TERMS, EK_GENERIC>(ah, al, bh, bl, g, e, st); break;
+    }
 }
 
 static long colsum_rows(const UmmaArgs& g) { return std::min<long>(g.ntiles, num_sms()) * 4; }
