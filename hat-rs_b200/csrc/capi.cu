@@ -238,7 +238,13 @@ int hat_b200_window_attention(int mode, const float* qkv, const float* table, fl
     return guarded(nullptr, 0, [&] {
         Plan p = Plan::make(hp, wp, 16);
         if (p.hp != hp || p.wp != wp) throw Error(1, "window attention: plane is not a window multiple");
-        launch_window_attention(mode, qkv, table, Dst{out, nullptr}, p, c, heads, shift, (cudaStream_t)stream);
+        TempW t;
+        t.st = (cudaStream_t)stream;
+        HAT_CUDA(cudaMallocAsync(&t.err, sizeof(int), t.st));
+        HAT_CUDA(cudaMemsetAsync(t.err, 0, sizeof(int), t.st));
+        launch_window_attention(mode == HAT_B200_MODE_SIMT ? 0 : mode, mode == HAT_B200_MODE_SIMT, qkv, table,
+                                Dst{out, nullptr}, p, c, heads, shift, t.err, t.st);
+        finish_kernel_call(t);
     });
 }
 
@@ -247,7 +253,13 @@ int hat_b200_overlap_attention(int mode, const float* qkv, const float* table, f
     return guarded(nullptr, 0, [&] {
         Plan p = Plan::make(hp, wp, 16);
         if (p.hp != hp || p.wp != wp) throw Error(1, "overlap attention: plane is not a window multiple");
-        launch_overlap_attention(mode, qkv, table, Dst{out, nullptr}, p, c, heads, (cudaStream_t)stream);
+        TempW t;
+        t.st = (cudaStream_t)stream;
+        HAT_CUDA(cudaMallocAsync(&t.err, sizeof(int), t.st));
+        HAT_CUDA(cudaMemsetAsync(t.err, 0, sizeof(int), t.st));
+        launch_overlap_attention(mode == HAT_B200_MODE_SIMT ? 0 : mode, mode == HAT_B200_MODE_SIMT, qkv, table,
+                                 Dst{out, nullptr}, p, c, heads, t.err, t.st);
+        finish_kernel_call(t);
     });
 }
 

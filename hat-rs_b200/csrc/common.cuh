@@ -152,13 +152,14 @@ void launch_layernorm(const float* x, const float* g, const float* b, Dst y, lon
 // Split a plain fp32 array into tf32 hi/lo halves (for callers that hand in fp32 operands).
 void launch_split(const float* x, float* hi, float* lo, long n, cudaStream_t st);
 
-// Window attention of one HAB over the [hp][wp][3c] qkv plane (hat_arch.py:165-196).
-void launch_window_attention(int mode, const float* qkv, const float* table, Dst out,
-                             const Plan& p, int c, int heads, int shift, cudaStream_t st);
+// Window attention of one HAB over the [hp][wp][3c] qkv plane (hat_arch.py:165-196):
+// the tensor-core kernel (mode: parity / fast), or the CUDA-core one when `simt`.
+void launch_window_attention(int mode, bool simt, const float* qkv, const float* table, Dst out, const Plan& p,
+                             int c, int heads, int shift, int* err, cudaStream_t st);
 
 // OCAB attention over the [hp][wp][3c] qkv plane (hat_arch.py:392-438).
-void launch_overlap_attention(int mode, const float* qkv, const float* table, Dst out,
-                              const Plan& p, int c, int heads, cudaStream_t st);
+void launch_overlap_attention(int mode, bool simt, const float* qkv, const float* table, Dst out, const Plan& p,
+                              int c, int heads, int* err, cudaStream_t st);
 
 // gate[c] = sigmoid(W2 relu(W1 mean + b1) + b2) (hat_arch.py:40-57), where the mean
 // over the plane is the sum of `rows` partial rows [rows][c] times `inv_count`.

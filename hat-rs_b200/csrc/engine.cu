@@ -66,16 +66,24 @@ void launch_window_attention_simt(const float* qkv, const float* table, Dst out,
 void launch_overlap_attention_simt(const float* qkv, const float* table, Dst out, const Plan& p, int c, int heads,
                                    cudaStream_t st);
 
-void launch_window_attention(int mode, const float* qkv, const float* table, Dst out, const Plan& p, int c,
-                             int heads, int shift, cudaStream_t st) {
-    (void)mode;
-    launch_window_attention_simt(qkv, table, out, p, c, heads, shift, st);
+void launch_attention_tc(int mode, bool oca, const float* qkv, const float* table, Dst out, const Plan& p, int c,
+                         int heads, int shift, int* err, cudaStream_t st);
+
+// The tensor-core kernel in parity and fast modes; the CUDA-core one for the debug path.
+void launch_window_attention(int mode, bool simt, const float* qkv, const float* table, Dst out, const Plan& p, int c,
+                             int heads, int shift, int* err, cudaStream_t st) {
+    if (simt)
+        launch_window_attention_simt(qkv, table, out, p, c, heads, shift, st);
+    else
+        launch_attention_tc(mode, false, qkv, table, out, p, c, heads, shift, err, st);
 }
 
-void launch_overlap_attention(int mode, const float* qkv, const float* table, Dst out, const Plan& p, int c,
-                              int heads, cudaStream_t st) {
-    (void)mode;
-    launch_overlap_attention_simt(qkv, table, out, p, c, heads, st);
+void launch_overlap_attention(int mode, bool simt, const float* qkv, const float* table, Dst out, const Plan& p, int c,
+                              int heads, int* err, cudaStream_t st) {
+    if (simt)
+        launch_overlap_attention_simt(qkv, table, out, p, c, heads, st);
+    else
+        launch_attention_tc(mode, true, qkv, table, out, p, c, heads, 0, err, st);
 }
 
 // ------------------------------------------------------------------ engine
@@ -359,8 +367,8 @@ void Engine::hab(int stage, int blk, const float* in, float* out) {
     linear(p + ".attn.qkv.weight", O(a_->n1, a_->n1lo), Dst{a_->qkv, nullptr}, eq);
     const int shift = blk % 2 ? plan_.shift : 0;
     mark("attn.window", 4.0 * P * 256 * c, 16.0 * P * c);
-    launch_window_attention(mode_, a_->qkv, W(p + ".attn.relative_position_bias_table"), D(a_->attn, a_->attnlo),
-                            plan_, c, wt_.heads, shift, stream_);
+    launch_window_attention(mode_, simt_only_, a_->qkv, W(p + ".attn.relative_position_bias_table"),
+                            D(a_->attn, a_->attnlo), plan_, c, wt_.heads, shift, derr_, stream_);
     // proj, then `(shortcut + attn) + conv_x * conv_scale` in the epilogue.
     Epi ep;
     ep.bias = W(p + ".attn.proj.bias");
@@ -386,8 +394,8 @@ void Engine::ocab(int stage, const float* in, float* out) {
     mark("linear.qkv", 6.0 * P * c * c, 16.0 * P * c);
     linear(p + ".qkv.weight", O(a_->n1, a_->n1lo), Dst{a_->qkv, nullptr}, eq);
     mark("attn.overlap", 4.0 * P * 576 * c, 16.0 * P * c);
-    launch_overlap_attention(mode_, a_->qkv, W(p + ".relative_position_bias_table"), D(a_->attn, a_->attnlo),
-                             plan_, c, wt_.heads, stream_);
+    launch_overlap_attention(mode_, simt_only_, a_->qkv, W(p + ".relative_position_bias_table"),
+                             D(a_->attn, a_->attnlo), plan_, c, wt_.heads, derr_, stream_);
     Epi ep;
     ep.bias = W(p + ".proj.bias");
     ep.res = in;

@@ -185,18 +185,22 @@ void run_all(Log& log) {
         auto qkv = rnd((size_t)hp * wp * 3 * c, 7);
         auto tsa = rnd(961 * heads, 8, -0.5f, 0.5f), toca = rnd(1521 * heads, 9, -0.5f, 0.5f);
         Dev dq(qkv), dts(tsa), dto(toca), dout((size_t)hp * wp * c);
-        std::vector<double> ref((size_t)hp * wp * c);
+        std::vector<double> ref((size_t)hp * wp * c), refo((size_t)hp * wp * c);
         attn_twin(qkv, tsa, ref, hp, wp, c, heads, shift, false);
-        hat_b200_window_attention(HAT_B200_MODE_PARITY, dq.p, dts.p, dout.p, hp, wp, c, heads, shift, nullptr);
-        HAT_CUDA(cudaDeviceSynchronize());
-        log.check("window attention " + std::to_string(hp) + "x" + std::to_string(wp) + " c" + std::to_string(c) +
-                      " shift " + std::to_string(shift),
-                  maxdiff(dout.get((size_t)hp * wp * c), ref), 2e-5);
-        attn_twin(qkv, toca, ref, hp, wp, c, heads, 0, true);
-        hat_b200_overlap_attention(HAT_B200_MODE_PARITY, dq.p, dto.p, dout.p, hp, wp, c, heads, nullptr);
-        HAT_CUDA(cudaDeviceSynchronize());
-        log.check("overlap attention " + std::to_string(hp) + "x" + std::to_string(wp) + " c" + std::to_string(c),
-                  maxdiff(dout.get((size_t)hp * wp * c), ref), 2e-5);
+        attn_twin(qkv, toca, refo, hp, wp, c, heads, 0, true);
+        for (int mode : {HAT_B200_MODE_SIMT, HAT_B200_MODE_PARITY}) {
+            const std::string tag = mode == HAT_B200_MODE_SIMT ? "simt " : "tcgen05 3xtf32 ";
+            int rc = hat_b200_window_attention(mode, dq.p, dts.p, dout.p, hp, wp, c, heads, shift, nullptr);
+            HAT_CUDA(cudaDeviceSynchronize());
+            log.check(tag + "window attention " + std::to_string(hp) + "x" + std::to_string(wp) + " c" +
+                          std::to_string(c) + " shift " + std::to_string(shift),
+                      rc ? 1e9 : maxdiff(dout.get((size_t)hp * wp * c), ref), 2e-5);
+            rc = hat_b200_overlap_attention(mode, dq.p, dto.p, dout.p, hp, wp, c, heads, nullptr);
+            HAT_CUDA(cudaDeviceSynchronize());
+            log.check(tag + "overlap attention " + std::to_string(hp) + "x" + std::to_string(wp) + " c" +
+                          std::to_string(c),
+                      rc ? 1e9 : maxdiff(dout.get((size_t)hp * wp * c), refo), 2e-5);
+        }
     }
 }
 

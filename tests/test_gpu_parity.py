@@ -162,3 +162,24 @@ def test_conv_kernel_vs_torch(torch_cuda, hg, wd, ci, co, mode):
     amax = float(want.abs().max())
     tol = {hat_b200.MODE_SIMT: 5e-5, hat_b200.MODE_PARITY: 2e-5 * (1 + amax), hat_b200.MODE_FAST: 2e-2}[mode]
     assert float((y - want).abs().max()) < tol
+
+
+@pytest.mark.parametrize("mode", [hat_b200.MODE_PARITY, hat_b200.MODE_FAST], ids=["tcgen05_3xtf32", "tcgen05_tf32"])
+@pytest.mark.parametrize("hp,wp,c,shift", [(32, 48, 144, 8), (48, 32, 144, 0), (16, 16, 180, 8), (64, 32, 180, 0),
+                                           (96, 64, 144, 8)])
+def test_attention_kernels_vs_cuda_core(torch_cuda, hp, wp, c, shift, mode):
+    """The tensor-core window and overlap attentions against the CUDA-core fp32 kernels
+    (which --cuda-selftest holds to a double-precision host twin)."""
+    torch = torch_cuda
+    g = torch.Generator(device="cuda").manual_seed(hp * 100 + wp + c)
+    qkv = torch.randn(hp, wp, 3 * c, device="cuda", generator=g)
+    tsa = torch.randn(961, 6, device="cuda", generator=g) * 0.5
+    toca = torch.randn(1521, 6, device="cuda", generator=g) * 0.5
+    ref = torch.empty(hp, wp, c, device="cuda")
+    got = torch.empty(hp, wp, c, device="cuda")
+    tol = 2e-5 if mode == hat_b200.MODE_PARITY else 5e-3
+    for table, fn, args in [(tsa, hat_b200.window_attention, (shift,)), (toca, hat_b200.overlap_attention, ())]:
+        fn(hat_b200.MODE_SIMT, qkv.data_ptr(), table.data_ptr(), ref.data_ptr(), hp, wp, c, 6, *args)
+        fn(mode, qkv.data_ptr(), table.data_ptr(), got.data_ptr(), hp, wp, c, 6, *args)
+        torch.cuda.synchronize()
+        assert float((got - ref).abs().max()) < tol, fn.__name__
