@@ -82,7 +82,7 @@ __device__ __forceinline__ uint64_t mdesc(uint32_t saddr, int rowbytes, uint32_t
     d |= (uint64_t)(rowbytes == 128 ? 2 : 6) << 61;
     return d;
 }
-// kind::tf32, f32 accumulate, M = 128; `bmn` selects an MN-major B operand.
+// kind::tf32, f32 accumulate, M = 128, both operands K-major (bmn = 0).
 __host__ __device__ constexpr uint32_t idesc_a(int n, int bmn) {
     return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)bmn << 16) | ((uint32_t)(n >> 3) << 17) |
            ((uint32_t)(128 >> 4) << 24);
@@ -132,7 +132,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     constexpr int TROWS = OCA ? 39 * 39 : 31 * 31;
     constexpr uint32_t Q_BYTES = KS * 4096;         // 128 rows x 32 B per k-step
     constexpr uint32_t K_BYTES = KS * 1024;         // 32 rows x 32 B per k-step
-    constexpr uint32_t V_BYTES = 4096;              // 32 keys x 128 B
+    constexpr uint32_t V_BYTES = 4096;              // V^T: 32 features x 128 B (32 keys)
     constexpr uint32_t KV_BYTES = 2 * K_BYTES + 2 * V_BYTES;
     constexpr uint32_t P_BYTES = 16384;             // 128 rows x 128 B
     constexpr uint32_t OFF_KV = 2 * Q_BYTES;
@@ -179,7 +179,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (warp == 0) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            const uint32_t id_s = idesc_a(32, 0), id_o = idesc_a(32, 1);
+            const uint32_t id_s = idesc_a(32, 0), id_o = idesc_a(32, 0);
             const uint32_t qh = su(sm), ql = su(sm + Q_BYTES);
             long g = 0;  // global key-block counter
             uint32_t ti = 0;
@@ -232,7 +232,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
                     for (int k = 0; k < KBLK / 8; ++k) {
                         const uint64_t aH = mdesc(pb + k * 32, 128, 1024), aL = mdesc(pb + P_BYTES + k * 32, 128, 1024);
-                        const uint64_t bH = mdesc(vb + k * 1024, 128, 1024), bL = mdesc(vb + V_BYTES + k * 1024, 128, 1024);
+                        const uint64_t bH = mdesc(vb + k * 32, 128, 1024), bL = mdesc(vb + V_BYTES + k * 32, 128, 1024);
                         if (TERMS == 3) {
                             mma(d, aL, bH, id_o, k ? 1u : 0u);
                             mma(d, aH, bL, id_o, 1u);
@@ -437,13 +437,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         }
                     }
                 } else {
-                    // V columns [(part-2)*16, +16): MN-major SW128, row = key
+                    // V columns [(part-2)*16, +16), stored transposed: the P.V product's
+                    // B operand is K-major, one 128-byte row of 32 keys per feature.
                     const float* src = qkv + kpos * c3 + 2 * c + (long)head * D;
 #pragma unroll
                     for (int u = 0; u < 16; ++u) {
                         const int cc = (part - 2) * 16 + u;
                         const float v = (inside && cc < D) ? src[cc] : 0.f;
-                        const uint32_t o = 2 * K_BYTES + off_sw128(k, cc);
+                        const uint32_t o = 2 * K_BYTES + off_sw128(cc, k);
                         float h, lo;
                         split_tf32(v, h, lo);
                         *reinterpret_cast<float*>(kvb + o) = TERMS == 3 ? h : tf32_rna(v);
