@@ -31,6 +31,7 @@ namespace {
 constexpr int TC_THREADS = 288;
 constexpr int KBLK = 32;     // keys per block
 constexpr int MT = 128;      // query rows per work item
+constexpr int KVS = 4;       // K/V pipeline stages
 constexpr long long WAIT_CYCLES_A = 4000000000ll;
 
 __device__ __forceinline__ uint32_t su(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -136,13 +137,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     constexpr uint32_t KV_BYTES = 2 * K_BYTES + 2 * V_BYTES;
     constexpr uint32_t P_BYTES = 16384;             // 128 rows x 128 B
     constexpr uint32_t OFF_KV = 2 * Q_BYTES;
-    constexpr uint32_t OFF_P = OFF_KV + 2 * KV_BYTES;
+    constexpr uint32_t OFF_P = OFF_KV + KVS * KV_BYTES;
     constexpr uint32_t OFF_TAB = OFF_P + 2 * 2 * P_BYTES;
 
     extern __shared__ __align__(1024) uint8_t raw[];
     uint8_t* sm = (uint8_t*)(((uintptr_t)raw + 1023) & ~(uintptr_t)1023);
     float* tab = reinterpret_cast<float*>(sm + OFF_TAB);
-    __shared__ uint64_t q_full, q_empty, kv_full[2], kv_empty[2], s_full[2], p_full[2], o_full[2], o_free[2], drain;
+    __shared__ uint64_t q_full, q_empty, kv_full[KVS], kv_empty[KVS], s_full[2], p_full[2], o_full[2], o_free[2], drain;
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int abort_flag;
 
@@ -155,9 +156,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (threadIdx.x == 0) {
         bar_init(&q_full, 128);
         bar_init(&q_empty, 1);
-        for (int s = 0; s < 2; ++s) {
+        for (int s = 0; s < KVS; ++s) {
             bar_init(&kv_full[s], 128);
             bar_init(&kv_empty[s], 1);
+        }
+        for (int s = 0; s < 2; ++s) {
             bar_init(&s_full[s], 1);
             bar_init(&p_full[s], 128);
             bar_init(&o_full[s], 1);
@@ -187,10 +190,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             for (long w = blockIdx.x; w < items && ok; w += gridDim.x, ++ti) {
                 if (!bar_wait(&q_full, ti & 1, &abort_flag, err, 11)) break;
                 auto issue_s = [&](long gb) -> bool {
-                    const int s = (int)(gb & 1);
-                    if (!bar_wait(&kv_full[s], (uint32_t)((gb >> 1) & 1), &abort_flag, err, 12)) return false;
+                    const int s = (int)(gb & 1), kvs = (int)(gb % KVS);
+                    if (!bar_wait(&kv_full[kvs], (uint32_t)((gb / KVS) & 1), &abort_flag, err, 12)) return false;
                     tcf_after();
-                    const uint32_t kb = su(sm + OFF_KV + s * KV_BYTES);
+                    const uint32_t kb = su(sm + OFF_KV + kvs * KV_BYTES);
                     const uint32_t d = tmem + s * 32;
 #pragma unroll
                     for (int k = 0; k < KS; ++k) {
@@ -227,7 +230,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     }
                     tcf_after();
                     const uint32_t pb = su(sm + OFF_P + s * 2 * P_BYTES);
-                    const uint32_t vb = su(sm + OFF_KV + s * KV_BYTES + 2 * K_BYTES);
+                    const int kvs = (int)(gb % KVS);
+                    const uint32_t vb = su(sm + OFF_KV + kvs * KV_BYTES + 2 * K_BYTES);
                     const uint32_t d = tmem + 64 + s * 32;
 #pragma unroll
                     for (int k = 0; k < KBLK / 8; ++k) {
@@ -242,7 +246,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         }
                     }
                     commit(&o_full[s]);
-                    commit(&kv_empty[s]);
+                    commit(&kv_empty[kvs]);
                 }
                 g += NBLK;
             }
@@ -366,18 +370,63 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
     } else {
         // ------------------------------------------------------------ loaders
+        // Thread t = (key k = t/4, part = t%4): parts 0-1 carry K columns [0,16) and
+        // [16,32), parts 2-3 the same columns of V. A block's rows are fetched with vector
+        // loads into registers one block ahead, so the global latency overlaps the wait for
+        // a free stage; the split and the swizzled stores happen when the stage frees up.
+        constexpr int VW = (D % 4 == 0) ? 4 : 2;           // vector width that keeps alignment
+        constexpr int NV = 16 / VW;                        // vectors per 16-column part
         const int t = threadIdx.x - 160;  // 0..127
+        const int k = t >> 2, part = t & 3;
+        const bool is_v = part >= 2;
+        const int col0 = (part & 1) * 16;
         long g = 0;
         uint32_t ti = 0;
+        float buf[16];
+        // Fetch block j of item (wy, wx) into buf (zeros outside the plane and past D).
+        auto fetch = [&](int wy, int wx, int j) {
+            const int kk = j * KBLK + k;
+            bool inside = true;
+            long kpos;
+            if (OCA) {
+                const int ky = kk / 24, kx = kk - ky * 24;
+                const int Y = wy * 16 - 4 + ky, X = wx * 16 - 4 + kx;
+                inside = Y >= 0 && Y < hp && X >= 0 && X < wp;
+                kpos = inside ? (long)Y * wp + X : 0;
+            } else {
+                const int ky = kk >> 4, kx = kk & 15;
+                kpos = (long)((wy * 16 + ky + shift) % hp) * wp + (wx * 16 + kx + shift) % wp;
+            }
+            const float* src = qkv + kpos * c3 + (is_v ? 2 * c : c) + (long)head * D + col0;
+#pragma unroll
+            for (int u = 0; u < NV; ++u) {
+                const int cc = col0 + u * VW;
+                if (inside && cc + VW <= D) {
+                    if (VW == 4) {
+                        const float4 v = *reinterpret_cast<const float4*>(src + u * 4);
+                        buf[u * 4] = v.x;
+                        buf[u * 4 + 1] = v.y;
+                        buf[u * 4 + 2] = v.z;
+                        buf[u * 4 + 3] = v.w;
+                    } else {
+                        const float2 v = *reinterpret_cast<const float2*>(src + u * 2);
+                        buf[u * 2] = v.x;
+                        buf[u * 2 + 1] = v.y;
+                    }
+                } else {
+#pragma unroll
+                    for (int e2 = 0; e2 < VW; ++e2) buf[u * VW + e2] = (inside && cc + e2 < D) ? src[u * VW + e2] : 0.f;
+                }
+            }
+        };
         for (long w = blockIdx.x; w < items; w += gridDim.x, ++ti) {
             if (__any_sync(0xffffffffu, abort_flag != 0)) break;
             const long rest = w / heads;
             const int win = (int)(rest >> 1), mtile = (int)(rest & 1);
             const int wy = win / nx, wx = win - wy * nx;
+            fetch(wy, wx, 0);
             // Q: thread t loads query row t of the item, scaled, split into the SW32 tiles.
             {
-                const bool got = bar_wait(&q_empty, (ti & 1) ^ 1, &abort_flag, err, 17);
-                if (!__all_sync(0xffffffffu, got)) break;
                 const int qi = mtile * MT + t, qy = qi >> 4, qx = qi & 15;
                 long qpos;
                 if (OCA)
@@ -385,9 +434,32 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 else
                     qpos = (long)((wy * 16 + qy + shift) % hp) * wp + (wx * 16 + qx + shift) % wp;
                 const float* src = qkv + qpos * c3 + (long)head * D;
+                float qv[KS * 8];
+#pragma unroll
+                for (int u = 0; u < (KS * 8) / VW; ++u) {
+                    const int cc = u * VW;
+                    if (cc + VW <= D) {
+                        if (VW == 4) {
+                            const float4 v = *reinterpret_cast<const float4*>(src + cc);
+                            qv[cc] = v.x;
+                            qv[cc + 1] = v.y;
+                            qv[cc + 2] = v.z;
+                            qv[cc + 3] = v.w;
+                        } else {
+                            const float2 v = *reinterpret_cast<const float2*>(src + cc);
+                            qv[cc] = v.x;
+                            qv[cc + 1] = v.y;
+                        }
+                    } else {
+#pragma unroll
+                        for (int e2 = 0; e2 < VW; ++e2) qv[cc + e2] = cc + e2 < D ? src[cc + e2] : 0.f;
+                    }
+                }
+                const bool got = bar_wait(&q_empty, (ti & 1) ^ 1, &abort_flag, err, 17);
+                if (!__all_sync(0xffffffffu, got)) break;
 #pragma unroll
                 for (int cc = 0; cc < KS * 8; ++cc) {
-                    const float v = cc < D ? src[cc] * scale : 0.f;
+                    const float v = qv[cc] * scale;
                     const uint32_t o = (cc >> 3) * 4096 + off_sw32(t, cc & 7);
                     float h, lo;
                     split_tf32(v, h, lo);
@@ -397,62 +469,39 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 fence_async();
                 bar_arrive(&q_full);
             }
-            // K and V, one 32-key block per stage: thread t = (key k, part p).
-            const int k = t & 31, part = t >> 5;
             bool ok = true;
             for (int j = 0; j < NBLK; ++j) {
                 const long gb = g + j;
-                const int s = (int)(gb & 1);
-                const bool got = bar_wait(&kv_empty[s], (uint32_t)(((gb >> 1) & 1) ^ 1), &abort_flag, err, 18);
+                const int s = (int)(gb % KVS);
+                const bool got = bar_wait(&kv_empty[s], (uint32_t)(((gb / KVS) & 1) ^ 1), &abort_flag, err, 18);
                 if (!__all_sync(0xffffffffu, got)) {
                     ok = false;
                     break;
                 }
-                const int kk = j * KBLK + k;
-                bool inside = true;
-                long kpos;
-                if (OCA) {
-                    const int ky = kk / 24, kx = kk - ky * 24;
-                    const int Y = wy * 16 - 4 + ky, X = wx * 16 - 4 + kx;
-                    inside = Y >= 0 && Y < hp && X >= 0 && X < wp;
-                    kpos = inside ? (long)Y * wp + X : 0;
-                } else {
-                    const int ky = kk >> 4, kx = kk & 15;
-                    kpos = (long)((wy * 16 + ky + shift) % hp) * wp + (wx * 16 + kx + shift) % wp;
-                }
                 uint8_t* kvb = sm + OFF_KV + s * KV_BYTES;
-                if (part < 2) {
-                    // K columns [part*16, part*16 + 16) of this key, K-major SW32 per k-step
-                    const float* src = qkv + kpos * c3 + c + (long)head * D;
 #pragma unroll
-                    for (int u = 0; u < 16; ++u) {
-                        const int cc = part * 16 + u;
+                for (int u = 0; u < 16; ++u) {
+                    const int cc = col0 + u;
+                    float h, lo;
+                    split_tf32(buf[u], h, lo);
+                    if (!is_v) {
                         if (cc < KS * 8) {
-                            const float v = (inside && cc < D) ? src[cc] : 0.f;
+                            // K: K-major SW32 per k-step, row = key
                             const uint32_t o = (cc >> 3) * 1024 + off_sw32(k, cc & 7);
-                            float h, lo;
-                            split_tf32(v, h, lo);
-                            *reinterpret_cast<float*>(kvb + o) = TERMS == 3 ? h : tf32_rna(v);
+                            *reinterpret_cast<float*>(kvb + o) = h;
                             if (TERMS == 3) *reinterpret_cast<float*>(kvb + K_BYTES + o) = lo;
                         }
-                    }
-                } else {
-                    // V columns [(part-2)*16, +16), stored transposed: the P.V product's
-                    // B operand is K-major, one 128-byte row of 32 keys per feature.
-                    const float* src = qkv + kpos * c3 + 2 * c + (long)head * D;
-#pragma unroll
-                    for (int u = 0; u < 16; ++u) {
-                        const int cc = (part - 2) * 16 + u;
-                        const float v = (inside && cc < D) ? src[cc] : 0.f;
+                    } else {
+                        // V stored transposed: the P.V product's B operand is K-major,
+                        // one 128-byte row of 32 keys per feature.
                         const uint32_t o = 2 * K_BYTES + off_sw128(cc, k);
-                        float h, lo;
-                        split_tf32(v, h, lo);
-                        *reinterpret_cast<float*>(kvb + o) = TERMS == 3 ? h : tf32_rna(v);
+                        *reinterpret_cast<float*>(kvb + o) = h;
                         if (TERMS == 3) *reinterpret_cast<float*>(kvb + V_BYTES + o) = lo;
                     }
                 }
                 fence_async();
                 bar_arrive(&kv_full[s]);
+                if (j + 1 < NBLK) fetch(wy, wx, j + 1);
             }
             if (!ok) break;
             g += NBLK;
@@ -472,7 +521,7 @@ template <int D, bool OCA, int TERMS>
 static void run_tc(const float* qkv, const float* table, Dst out, const Plan& p, int c, int heads, int shift, int* err,
                    cudaStream_t st) {
     constexpr int KS = (D + 7) / 8;
-    constexpr size_t bytes = 2 * KS * 4096 + 2 * (2 * KS * 1024 + 2 * 4096) + 4 * 16384 + (OCA ? 1521 : 961) * 4 + 1024;
+    constexpr size_t bytes = 2 * KS * 4096 + KVS * (2 * KS * 1024 + 2 * 4096) + 4 * 16384 + (OCA ? 1521 : 961) * 4 + 1024;
     static unsigned configured = 0;
     int dev = 0;
     HAT_CUDA(cudaGetDevice(&dev));
