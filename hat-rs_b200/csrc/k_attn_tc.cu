@@ -139,10 +139,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     constexpr uint32_t OFF_KV = 2 * Q_BYTES;
     constexpr uint32_t OFF_P = OFF_KV + KVS * KV_BYTES;
     constexpr uint32_t OFF_TAB = OFF_P + 2 * 2 * P_BYTES;
+    constexpr uint32_t OFF_KOFF = OFF_TAB + ((TROWS * 4 + 15) / 16) * 16;
 
     extern __shared__ __align__(1024) uint8_t raw[];
     uint8_t* sm = (uint8_t*)(((uintptr_t)raw + 1023) & ~(uintptr_t)1023);
     float* tab = reinterpret_cast<float*>(sm + OFF_TAB);
+    int* koff = reinterpret_cast<int*>(sm + OFF_KOFF);  // OCAB: key (ky, kx) -> ky*39 + kx
     __shared__ uint64_t q_full, q_empty, kv_full[KVS], kv_empty[KVS], s_full[2], p_full[2], o_full[2], o_free[2], drain;
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int abort_flag;
@@ -153,6 +155,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const long c3 = 3L * c;
 
     for (int i = threadIdx.x; i < TROWS; i += TC_THREADS) tab[i] = table[(long)i * heads + head];
+    if (OCA)
+        for (int i = threadIdx.x; i < NK; i += TC_THREADS) koff[i] = (i / 24) * 39 + (i % 24);
     if (threadIdx.x == 0) {
         bar_init(&q_full, 128);
         bar_init(&q_empty, 1);
@@ -258,6 +262,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int q4 = warp & 3;
         const int row = q4 * 32 + lane;
         const uint32_t trow = (uint32_t)(q4 * 32) << 16;
+        constexpr float L2E = 1.4426950408889634f;
         long g = 0;
         for (long w = blockIdx.x; w < items; w += gridDim.x) {
             if (__any_sync(0xffffffffu, abort_flag != 0)) break;
@@ -266,7 +271,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const int wy = win / nx, wx = win - wy * nx;
             const int qi = mtile * MT + row, qy = qi >> 4, qx = qi & 15;
             const bool masked = !OCA && shift > 0;
-            const int lq = masked ? band3(wy * 16 + qy, hp, shift) * 3 + band3(wx * 16 + qx, wp, shift) : 0;
+            // Bias row of this query: SA index (qy-ky+15)*31 + (qx-kx+15) = A0 - (ky*31+kx);
+            // OCAB index (ky*39+kx) - B0, wrapped into the table.
+            const int A0 = qy * 31 + qx + 480, B0 = qy * 39 + qx + 280;
+            // Shift mask: key column kx is masked against target label t when
+            // band(wx*16+kx) != t; one 16-bit mask per possible row band.
+            uint32_t cm[3] = {0, 0, 0};
+            int lq = 0;
+            if (masked) {
+                lq = band3(wy * 16 + qy, hp, shift) * 3 + band3(wx * 16 + qx, wp, shift);
+#pragma unroll
+                for (int kx = 0; kx < 16; ++kx) {
+                    const int bx = band3(wx * 16 + kx, wp, shift);
+#pragma unroll
+                    for (int by = 0; by < 3; ++by)
+                        if (by * 3 + bx != lq) cm[by] |= 1u << kx;
+                }
+            }
             float m = -INFINITY, l = 0.f, a_prev = 1.f;
             float o[32];
 #pragma unroll
@@ -298,51 +319,52 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 float sv[32];
                 tld16(tmem + trow + s * 32, sv);
                 tld16(tmem + trow + s * 32 + 16, sv + 16);
+                uint32_t mrow0 = 0, mrow1 = 0;
+                if (masked) {
+                    // the block's two key rows ky = 2j, 2j+1
+                    mrow0 = cm[band3(wy * 16 + 2 * j, hp, shift)];
+                    mrow1 = cm[band3(wy * 16 + 2 * j + 1, hp, shift)];
+                }
+                const float* trow_sa = tab + (A0 - 62 * j);  // SA: minus (k>>4)*31 + (k&15)
                 float bmax = -INFINITY;
 #pragma unroll
                 for (int k = 0; k < 32; ++k) {
-                    const int kk = j * KBLK + k;
-                    int bi;
+                    float v;
                     if (OCA) {
-                        const int ky = kk / 24, kx = kk - ky * 24;
-                        bi = (ky - qy - 7) * 39 + (kx - qx - 7);
-                        if (bi < 0) bi += TROWS;
+                        int bi = koff[j * KBLK + k] - B0;
+                        bi += bi < 0 ? TROWS : 0;
+                        v = sv[k] + tab[bi];
                     } else {
-                        const int ky = kk >> 4, kx = kk & 15;
-                        bi = (qy - ky + 15) * 31 + (qx - kx + 15);
-                    }
-                    float v = sv[k] + tab[bi];
-                    if (masked) {
-                        const int ky = kk >> 4, kx = kk & 15;
-                        const int lk = band3(wy * 16 + ky, hp, shift) * 3 + band3(wx * 16 + kx, wp, shift);
-                        if (lk != lq) v += -100.f;
+                        v = sv[k] + trow_sa[-((k >> 4) * 31 + (k & 15))];
+                        if (masked) {
+                            const uint32_t mr = (k >> 4) ? mrow1 : mrow0;
+                            if ((mr >> (k & 15)) & 1u) v += -100.f;
+                        }
                     }
                     sv[k] = v;
                     bmax = fmaxf(bmax, v);
                 }
                 const float mn = fmaxf(m, bmax);
-                const float a = exp2f((m - mn) * 1.4426950408889634f);
+                const float a = exp2f((m - mn) * L2E);
+                const float nmn = -mn * L2E;
                 float psum = 0.f;
                 uint8_t* pb = sm + OFF_P + s * 2 * P_BYTES;
 #pragma unroll
                 for (int k4 = 0; k4 < 8; ++k4) {
-                    float4 ph, pl;
                     float p[4];
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
-                        p[u] = exp2f((sv[4 * k4 + u] - mn) * 1.4426950408889634f);
+                        p[u] = exp2f(fmaf(sv[4 * k4 + u], L2E, nmn));
                         psum += p[u];
                     }
-                    if (TERMS == 3) {
-                        split_tf32(p[0], ph.x, pl.x);
-                        split_tf32(p[1], ph.y, pl.y);
-                        split_tf32(p[2], ph.z, pl.z);
-                        split_tf32(p[3], ph.w, pl.w);
-                        *reinterpret_cast<float4*>(pb + P_BYTES + off_sw128(row, 4 * k4)) = pl;
-                    } else {
-                        ph = make_float4(tf32_rna(p[0]), tf32_rna(p[1]), tf32_rna(p[2]), tf32_rna(p[3]));
-                    }
-                    *reinterpret_cast<float4*>(pb + off_sw128(row, 4 * k4)) = ph;
+                    float4 ph, pl;
+                    split_tf32(p[0], ph.x, pl.x);
+                    split_tf32(p[1], ph.y, pl.y);
+                    split_tf32(p[2], ph.z, pl.z);
+                    split_tf32(p[3], ph.w, pl.w);
+                    const uint32_t off = off_sw128(row, 4 * k4);
+                    *reinterpret_cast<float4*>(pb + off) = ph;
+                    if (TERMS == 3) *reinterpret_cast<float4*>(pb + P_BYTES + off) = pl;
                 }
                 l = l * a + psum;
                 m = mn;
@@ -370,52 +392,66 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
     } else {
         // ------------------------------------------------------------ loaders
-        // Thread t = (key k = t/4, part = t%4): parts 0-1 carry K columns [0,16) and
-        // [16,32), parts 2-3 the same columns of V. A block's rows are fetched with vector
-        // loads into registers one block ahead, so the global latency overlaps the wait for
-        // a free stage; the split and the swizzled stores happen when the stage frees up.
-        constexpr int VW = (D % 4 == 0) ? 4 : 2;           // vector width that keeps alignment
-        constexpr int NV = 16 / VW;                        // vectors per 16-column part
-        const int t = threadIdx.x - 160;  // 0..127
-        const int k = t >> 2, part = t & 3;
-        const bool is_v = part >= 2;
-        const int col0 = (part & 1) * 16;
+        // Warps 5-6 load K: lane = key, warp = column half [0,16) / [16,32); each 4-column
+        // chunk is one 16-byte store into the K-major SW32 tiles. Warps 7-8 load V: a
+        // thread owns a 4-key x 4-feature block, transposes it in registers and writes
+        // four 16-byte rows of V^T (K-major SW128: one row of 32 keys per feature). Loads
+        // for the next key block are issued before waiting for a free stage.
+        constexpr int VW = (D % 4 == 0) ? 4 : 2;  // vector width that keeps the row alignment
+        const int t = threadIdx.x - 160;           // 0..127
+        const int lw = warp - 5;                   // 0..3
+        const bool is_v = lw >= 2;
+        const int kk0 = is_v ? (((lw - 2) * 32 + lane) & 7) * 4 : lane;  // first key of this thread
+        const int col0 = is_v ? (((lw - 2) * 32 + lane) >> 3) * 4 : lw * 16;
         long g = 0;
         uint32_t ti = 0;
         float buf[16];
-        // Fetch block j of item (wy, wx) into buf (zeros outside the plane and past D).
-        auto fetch = [&](int wy, int wx, int j) {
-            const int kk = j * KBLK + k;
-            bool inside = true;
-            long kpos;
+        auto key_pos = [&](int wy, int wx, int kk, bool& inside) -> long {
+            inside = true;
             if (OCA) {
                 const int ky = kk / 24, kx = kk - ky * 24;
                 const int Y = wy * 16 - 4 + ky, X = wx * 16 - 4 + kx;
                 inside = Y >= 0 && Y < hp && X >= 0 && X < wp;
-                kpos = inside ? (long)Y * wp + X : 0;
-            } else {
-                const int ky = kk >> 4, kx = kk & 15;
-                kpos = (long)((wy * 16 + ky + shift) % hp) * wp + (wx * 16 + kx + shift) % wp;
+                return inside ? (long)Y * wp + X : 0;
             }
-            const float* src = qkv + kpos * c3 + (is_v ? 2 * c : c) + (long)head * D + col0;
+            const int ky = kk >> 4, kx = kk & 15;
+            return (long)((wy * 16 + ky + shift) % hp) * wp + (wx * 16 + kx + shift) % wp;
+        };
+        // n floats of row `src` from column `cc` (zeros past D or outside the plane)
+        auto load_cols = [&](const float* src, int cc, bool inside, float* dst, int n) {
 #pragma unroll
-            for (int u = 0; u < NV; ++u) {
-                const int cc = col0 + u * VW;
-                if (inside && cc + VW <= D) {
+            for (int u = 0; u < 16; u += VW) {
+                if (u >= n) break;
+                const int col = cc + u;
+                if (inside && col + VW <= D) {
                     if (VW == 4) {
-                        const float4 v = *reinterpret_cast<const float4*>(src + u * 4);
-                        buf[u * 4] = v.x;
-                        buf[u * 4 + 1] = v.y;
-                        buf[u * 4 + 2] = v.z;
-                        buf[u * 4 + 3] = v.w;
+                        const float4 v = *reinterpret_cast<const float4*>(src + col);
+                        dst[u] = v.x;
+                        dst[u + 1] = v.y;
+                        dst[u + 2] = v.z;
+                        dst[u + 3] = v.w;
                     } else {
-                        const float2 v = *reinterpret_cast<const float2*>(src + u * 2);
-                        buf[u * 2] = v.x;
-                        buf[u * 2 + 1] = v.y;
+                        const float2 v = *reinterpret_cast<const float2*>(src + col);
+                        dst[u] = v.x;
+                        dst[u + 1] = v.y;
                     }
                 } else {
 #pragma unroll
-                    for (int e2 = 0; e2 < VW; ++e2) buf[u * VW + e2] = (inside && cc + e2 < D) ? src[u * VW + e2] : 0.f;
+                    for (int e2 = 0; e2 < VW; ++e2) dst[u + e2] = (inside && col + e2 < D) ? src[col + e2] : 0.f;
+                }
+            }
+        };
+        auto fetch = [&](int wy, int wx, int j) {
+            if (!is_v) {
+                bool inside;
+                const long kpos = key_pos(wy, wx, j * KBLK + kk0, inside);
+                load_cols(qkv + kpos * c3 + c + (long)head * D, col0, inside, buf, 16);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    bool inside;
+                    const long kpos = key_pos(wy, wx, j * KBLK + kk0 + i, inside);
+                    load_cols(qkv + kpos * c3 + 2 * c + (long)head * D, col0, inside, buf + 4 * i, 4);
                 }
             }
         };
@@ -435,36 +471,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     qpos = (long)((wy * 16 + qy + shift) % hp) * wp + (wx * 16 + qx + shift) % wp;
                 const float* src = qkv + qpos * c3 + (long)head * D;
                 float qv[KS * 8];
-#pragma unroll
-                for (int u = 0; u < (KS * 8) / VW; ++u) {
-                    const int cc = u * VW;
-                    if (cc + VW <= D) {
-                        if (VW == 4) {
-                            const float4 v = *reinterpret_cast<const float4*>(src + cc);
-                            qv[cc] = v.x;
-                            qv[cc + 1] = v.y;
-                            qv[cc + 2] = v.z;
-                            qv[cc + 3] = v.w;
-                        } else {
-                            const float2 v = *reinterpret_cast<const float2*>(src + cc);
-                            qv[cc] = v.x;
-                            qv[cc + 1] = v.y;
-                        }
-                    } else {
-#pragma unroll
-                        for (int e2 = 0; e2 < VW; ++e2) qv[cc + e2] = cc + e2 < D ? src[cc + e2] : 0.f;
-                    }
-                }
+                load_cols(src, 0, true, qv, 16);
+                if (KS * 8 > 16) load_cols(src, 16, true, qv + 16, KS * 8 - 16);
                 const bool got = bar_wait(&q_empty, (ti & 1) ^ 1, &abort_flag, err, 17);
                 if (!__all_sync(0xffffffffu, got)) break;
 #pragma unroll
-                for (int cc = 0; cc < KS * 8; ++cc) {
-                    const float v = qv[cc] * scale;
-                    const uint32_t o = (cc >> 3) * 4096 + off_sw32(t, cc & 7);
-                    float h, lo;
-                    split_tf32(v, h, lo);
-                    *reinterpret_cast<float*>(sm + o) = TERMS == 3 ? h : tf32_rna(v);
-                    if (TERMS == 3) *reinterpret_cast<float*>(sm + Q_BYTES + o) = lo;
+                for (int c4 = 0; c4 < KS * 2; ++c4) {
+                    float4 h, lo;
+                    split_tf32(qv[4 * c4] * scale, h.x, lo.x);
+                    split_tf32(qv[4 * c4 + 1] * scale, h.y, lo.y);
+                    split_tf32(qv[4 * c4 + 2] * scale, h.z, lo.z);
+                    split_tf32(qv[4 * c4 + 3] * scale, h.w, lo.w);
+                    const uint32_t o = (c4 >> 1) * 4096 + t * 32 + ((((c4 & 1) ^ (t >> 2)) & 1) << 4);
+                    *reinterpret_cast<float4*>(sm + o) = h;
+                    if (TERMS == 3) *reinterpret_cast<float4*>(sm + Q_BYTES + o) = lo;
                 }
                 fence_async();
                 bar_arrive(&q_full);
@@ -479,24 +499,33 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     break;
                 }
                 uint8_t* kvb = sm + OFF_KV + s * KV_BYTES;
+                if (!is_v) {
 #pragma unroll
-                for (int u = 0; u < 16; ++u) {
-                    const int cc = col0 + u;
-                    float h, lo;
-                    split_tf32(buf[u], h, lo);
-                    if (!is_v) {
+                    for (int c4 = 0; c4 < 4; ++c4) {
+                        const int cc = col0 + 4 * c4;
                         if (cc < KS * 8) {
-                            // K: K-major SW32 per k-step, row = key
-                            const uint32_t o = (cc >> 3) * 1024 + off_sw32(k, cc & 7);
-                            *reinterpret_cast<float*>(kvb + o) = h;
-                            if (TERMS == 3) *reinterpret_cast<float*>(kvb + K_BYTES + o) = lo;
+                            float4 h, lo;
+                            split_tf32(buf[4 * c4], h.x, lo.x);
+                            split_tf32(buf[4 * c4 + 1], h.y, lo.y);
+                            split_tf32(buf[4 * c4 + 2], h.z, lo.z);
+                            split_tf32(buf[4 * c4 + 3], h.w, lo.w);
+                            const uint32_t o = (cc >> 3) * 1024 + kk0 * 32 + (((((cc >> 2) & 1) ^ (kk0 >> 2)) & 1) << 4);
+                            *reinterpret_cast<float4*>(kvb + o) = h;
+                            if (TERMS == 3) *reinterpret_cast<float4*>(kvb + K_BYTES + o) = lo;
                         }
-                    } else {
-                        // V stored transposed: the P.V product's B operand is K-major,
-                        // one 128-byte row of 32 keys per feature.
-                        const uint32_t o = 2 * K_BYTES + off_sw128(cc, k);
-                        *reinterpret_cast<float*>(kvb + o) = h;
-                        if (TERMS == 3) *reinterpret_cast<float*>(kvb + V_BYTES + o) = lo;
+                    }
+                } else {
+#pragma unroll
+                    for (int f = 0; f < 4; ++f) {
+                        const int n = col0 + f;  // feature = row of V^T
+                        float4 h, lo;
+                        split_tf32(buf[f], h.x, lo.x);
+                        split_tf32(buf[4 + f], h.y, lo.y);
+                        split_tf32(buf[8 + f], h.z, lo.z);
+                        split_tf32(buf[12 + f], h.w, lo.w);
+                        const uint32_t o = 2 * K_BYTES + off_sw128(n, kk0);
+                        *reinterpret_cast<float4*>(kvb + o) = h;
+                        if (TERMS == 3) *reinterpret_cast<float4*>(kvb + V_BYTES + o) = lo;
                     }
                 }
                 fence_async();
@@ -521,7 +550,9 @@ template <int D, bool OCA, int TERMS>
 static void run_tc(const float* qkv, const float* table, Dst out, const Plan& p, int c, int heads, int shift, int* err,
                    cudaStream_t st) {
     constexpr int KS = (D + 7) / 8;
-    constexpr size_t bytes = 2 * KS * 4096 + KVS * (2 * KS * 1024 + 2 * 4096) + 4 * 16384 + (OCA ? 1521 : 961) * 4 + 1024;
+    constexpr int TROWS = OCA ? 1521 : 961;
+    constexpr size_t bytes = 2 * KS * 4096 + KVS * (2 * KS * 1024 + 2 * 4096) + 4 * 16384 + ((TROWS * 4 + 15) / 16) * 16 +
+                             (OCA ? 576 * 4 : 0) + 1024;
     static unsigned configured = 0;
     int dev = 0;
     HAT_CUDA(cudaGetDevice(&dev));
