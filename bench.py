@@ -40,6 +40,10 @@ REF_GPU_MPIXS = 8.6  # seconds, README.md:18 of the reference (HAT-S x4 512x512,
 BASELINE_MPIXS = (H * SCALE) * (W * SCALE) / 1e6 / REF_GPU_MPIXS
 # Algorithmic FLOPs of HAT-S x4 per padded input pixel (QK^T and PV counted once).
 FLOPS_PER_PIX = 26.67e6
+# DRAM bytes (read + write) per launch of a kernel kind at this workload, from one ncu
+# capture (dram__bytes_read.sum + dram__bytes_write.sum); profiles/ holds the capture's
+# summary and command. Kinds without a capture report null.
+NCU_TRAFFIC_BYTES = {"attn.window": 722.2e6}  # profiles/k_attn_tc_window_hats_x4_512.md
 
 
 def peaks():
@@ -243,15 +247,22 @@ def run_ours(args):
     total_ms = sum(v["ms"] for v in prof.values())
     if top["flops"] > 0:
         achieved = top["flops"] / (top["ms"] / 1e3) / 1e12
+        # Parity mode issues every product as 3 TF32 MMAs, and the TF32 pipe runs at half
+        # the bf16 rate: tf32_pipe_frac is the tensor pipe's own utilisation.
+        terms = 3 if mode == hat_b200.MODE_PARITY else 1
         roof = {"kernel": top_kind, "bound": "tensor", "achieved": achieved, "peak": tf,
                 "unit": "TFLOP/s", "frac": achieved / tf, "traffic": None,
                 "peak_source": f"{src} bf16 dense (MEASURED_PEAKS.json)",
+                "tf32_pipe_frac": terms * achieved / (tf / 2),
                 "share_of_pass": top["ms"] / total_ms, "launches": top["launches"]}
     else:
         achieved = top["bytes"] / (top["ms"] / 1e3) / 1e9
         roof = {"kernel": top_kind, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                 "frac": achieved / hbm, "traffic": None, "peak_source": f"{src} HBM copy",
                 "share_of_pass": top["ms"] / total_ms, "launches": top["launches"]}
+    if top_kind in NCU_TRAFFIC_BYTES:
+        roof["traffic"] = NCU_TRAFFIC_BYTES[top_kind]
+        roof["alg_bytes_per_launch"] = top["bytes"] / max(top["launches"], 1)
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
         dt, mpix = cpu_oracle_sample(ck, img, args.ref_crop)
