@@ -71,6 +71,7 @@ SIGNATURES = {
     "hat_b200_conv3x3": (_I, [_I, _P, _P, _P, _P, _I, _I, _I, _I, _P]),
     "hat_b200_window_attention": (_I, [_I, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "hat_b200_overlap_attention": (_I, [_I, _P, _P, _P, _I, _I, _I, _I, _P]),
+    "hat_b200_linear_noalloc": (_I, [_I, _P, _P, _P, _P, _I, _I, _I, _P, _C, _S]),
     "hat_b200_launch_count": (ctypes.c_uint64, [_P]),
     "hat_b200_profile": (_I, [_P, _I, _I, _C, _S, _C, _S]),
 }
@@ -208,6 +209,16 @@ def linear(mode, x, w, b, y, m, n, k, stream=0):
     rc = lib().hat_b200_linear(mode, x, w, b, y, m, n, k, stream)
     if rc:
         raise HatError(rc, "linear launch failed")
+
+
+def linear_noalloc(mode, x, w, b, y, m, n, k, stream=0):
+    """`linear` with all scratch in the library's fixed device array (no allocation);
+    sizes beyond NOALLOC_SCRATCH_BYTES raise HatError(EINVAL)."""
+    e = _err()
+    _check(lib().hat_b200_linear_noalloc(mode, x, w, b, y, m, n, k, stream, e, len(e)), e)
+
+
+NOALLOC_SCRATCH_BYTES = 8 << 20
 
 
 def conv3x3(mode, x, w, b, y, hgt, wid, cin, cout, stream=0):

@@ -133,6 +133,29 @@ HAT_B200_API int hat_b200_window_attention(int mode, const float* qkv, const flo
 HAT_B200_API int hat_b200_overlap_attention(int mode, const float* qkv, const float* table, float* out,
                                int hp, int wp, int c, int heads, void* stream);
 
+/* hat_b200_linear without device allocation. No counterpart in the reference: it is for
+ * callers that may not allocate device memory on this path (device memory already
+ * reserved by another allocator, latency-critical loops, callers that must know the
+ * call's device-memory use in advance).
+ *
+ * All scratch (the prepared weights, the tf32 hi/lo split of x in parity mode, and the
+ * kernels' error word) lives in one statically allocated device array of
+ * HAT_B200_NOALLOC_SCRATCH_BYTES per device; the call makes no cudaMalloc/cudaFree and
+ * calls no allocating library routine. Sizes whose scratch exceeds the limit are refused
+ * with HAT_B200_EINVAL and a message in `err` naming the bytes needed: about
+ * 4*(n*k + 2*n_pad*k_pad + 2*m*k) + 256 bytes in parity mode, where n_pad and k_pad are
+ * n and k rounded up to the tile sizes. The error word is zeroed by each call before its
+ * first launch; everything else is rewritten before it is read.
+ *
+ * The first call on each device looks up the array's address (cudaGetSymbolAddress, with
+ * that device current); make that first call before any stream capture begins on it.
+ * Calls share the array: two calls in flight at once on the same device (from different
+ * host threads) race on it and give wrong results, so serialise them. The call blocks
+ * until its result is in `y`. Arguments otherwise as hat_b200_linear. */
+#define HAT_B200_NOALLOC_SCRATCH_BYTES ((size_t)8 << 20)
+HAT_B200_API int hat_b200_linear_noalloc(int mode, const float* x, const float* w, const float* b, float* y,
+                                         int m, int n, int k, void* stream, char* err, size_t errlen);
+
 /* One eager pass at this size with a CUDA event between every launch, on the handle's
  * stream: per kind of kernel, its launch count, summed device time (ms) and the
  * algorithmic FLOPs and bytes of those launches, as a JSON object in `json`. (No
