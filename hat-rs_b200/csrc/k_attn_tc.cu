@@ -3,25 +3,34 @@
 // 392-438), one fused kernel per launch:
 //
 //   S = (q*scale) K^T + bias (+ shift mask)      tcgen05.mma, S in tensor memory
-//   P = exp(S - running max), row sums            CUDA cores, one thread per query row
-//   O += P V                                      tcgen05.mma, O block in tensor memory
+//   P = exp(S - m), row sums                      CUDA cores, one thread per query row
+//   O += P V                                      tcgen05.mma, P and O in tensor memory
 //
 // Work item = (window, head, half of the window's 256 queries); 128 query rows per
 // item, keys streamed in blocks of 32 (8 blocks for 256 keys, 18 for 576). Every
-// operand is split into tf32 hi/lo halves on the way into shared memory, and both
-// products use the 3-term split (A_lo.B_hi + A_hi.B_lo + A_hi.B_hi) in fp32-parity
-// mode; fast mode issues the single A_hi.B_hi. The softmax is the online form: each
-// block's P uses the running row max, and O (kept in registers, fp32) is rescaled when
-// the max grows, so S never needs more than one block of tensor memory.
+// operand is split into tf32 hi/lo halves, and both products use the 3-term split
+// (A_lo.B_hi + A_hi.B_lo + A_hi.B_hi) in fp32-parity mode; fast mode issues the single
+// A_hi.B_hi.
+//
+// Softmax: P is written back into tensor memory (P_hi over the block's S columns, P_lo
+// beside it) and the PV product reads its A operand from there. O accumulates in tensor
+// memory across the item's key blocks. Each row keeps a reference max m: P = exp(S - m)
+// with the row sum l accumulated against the same m, so O / l is exact whatever m is.
+// m is the first block's max and moves only when a later block's max exceeds it by more
+// than RESCALE_LOG2 (in log2 units, so every P stays below 2^RESCALE_LOG2); then the
+// row's O in tensor memory and l are scaled by exp(m_old - m_new) first. With
+// RESCALE_LOG2 = 8 that is rare, so O is read once per item, not once per key block.
 //
 // The window partition, the cyclic roll, the nn.Unfold of the keys with its zero
 // padding, the relative-position bias gather and the shift mask are address
-// arithmetic: nothing is materialised.
+// arithmetic: nothing is materialised. The bias table is staged in shared memory with
+// rows 48 floats apart, which puts the two half-warps (two query rows of the window)
+// on disjoint banks.
 //
-// Warp roles (288 threads): 0 MMA issuer + TMEM owner, 1-4 softmax (TMEM lane quarters
-// 1,2,3,0), 5-8 loaders (gather, scale, split, swizzled stores). Every mbarrier wait is
-// bounded; on expiry the kernel records an error code, all roles leave, and TMEM is
-// released.
+// Warp roles (288 threads, two CTAs per SM): 0 MMA issuer + TMEM owner, 1-4 softmax
+// (TMEM lane quarters 1,2,3,0), 5-8 loaders (gather, scale, split, swizzled stores).
+// Every mbarrier wait is bounded; on expiry the kernel records an error code, all roles
+// leave, and TMEM is released.
 #include "common.cuh"
 
 namespace hat {
@@ -32,6 +41,9 @@ constexpr int TC_THREADS = 288;
 constexpr int KBLK = 32;     // keys per block
 constexpr int MT = 128;      // query rows per work item
 constexpr int KVS = 4;       // K/V pipeline stages
+constexpr int TSTRIDE = 48;  // shared bias-table row stride (floats)
+constexpr int TMEM_COLS = 256;
+constexpr float RESCALE_LOG2 = 8.f;
 constexpr long long WAIT_CYCLES_A = 4000000000ll;
 
 __device__ __forceinline__ uint32_t su(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -83,36 +95,60 @@ __device__ __forceinline__ uint64_t mdesc(uint32_t saddr, int rowbytes, uint32_t
     d |= (uint64_t)(rowbytes == 128 ? 2 : 6) << 61;
     return d;
 }
-// kind::tf32, f32 accumulate, M = 128, both operands K-major (bmn = 0).
-__host__ __device__ constexpr uint32_t idesc_a(int n, int bmn) {
-    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)bmn << 16) | ((uint32_t)(n >> 3) << 17) |
-           ((uint32_t)(128 >> 4) << 24);
+// kind::tf32, f32 accumulate, M = 128, both operands K-major.
+__host__ __device__ constexpr uint32_t idesc_a(int n) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
-__device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+// D (tmem) (+)= A (smem) . B (smem)
+__device__ __forceinline__ void mma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
     asm volatile(
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n"
         ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+// D (tmem) (+)= A (tmem: lane = row, column = k) . B (smem)
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n}\n"
+        ::"r"(d), "r"(a), "l"(b), "r"(idesc), "r"(acc));
 }
 __device__ __forceinline__ void commit(uint64_t* b) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su(b))
                  : "memory");
 }
-__device__ __forceinline__ void tld16(uint32_t taddr, float* v) {
-    uint32_t r[16];
+// 32 consecutive columns of this warp's 32 TMEM lanes (one row per thread).
+__device__ __forceinline__ void tld32(uint32_t taddr, float* v) {
+    uint32_t r[32];
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+__device__ __forceinline__ void tst32(uint32_t taddr, const float* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+        ::"r"(taddr), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+          "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+          "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+          "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+          "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+          "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+          "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+          "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+          "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+          "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+          "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+}
+__device__ __forceinline__ void tst_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// Byte offset of element (row, c), c < 8, in a K-major SWIZZLE_32B tile of 32-byte rows.
-__device__ __forceinline__ uint32_t off_sw32(int row, int c) {
-    return row * 32 + ((((c >> 2) ^ (row >> 2)) & 1) << 4) + (c & 3) * 4;
-}
 // Byte offset of element (row, c), c < 32, in a SWIZZLE_128B tile of 128-byte rows.
 __device__ __forceinline__ uint32_t off_sw128(int row, int c) {
     return row * 128 + ((((c >> 2) ^ row) & 7) << 4) + (c & 3) * 4;
@@ -124,28 +160,30 @@ __device__ __forceinline__ int band3(int v, int n, int shift) { return v < n - 1
 
 // D: head dim (24 or 30); OCA: overlapping attention; TERMS: 3 (parity) or 1 (fast).
 template <int D, bool OCA, int TERMS>
-__global__ void __launch_bounds__(TC_THREADS, 1)
+__global__ void __launch_bounds__(TC_THREADS, 2)
     k_attn_tc(const float* __restrict__ qkv, const float* __restrict__ table, Dst out, int hp, int wp, int c,
               int heads, int shift, float scale, long items, int* err) {
     constexpr int KS = (D + 7) / 8;                 // k-steps of the QK^T product
     constexpr int NK = OCA ? 576 : 256;             // keys per window
     constexpr int NBLK = NK / KBLK;
-    constexpr int TROWS = OCA ? 39 * 39 : 31 * 31;
+    constexpr int TR = OCA ? 39 : 31;               // bias-table rows (and columns)
+    constexpr int TW = OCA ? 39 : 31;               // the checkpoint table's row length
     constexpr uint32_t Q_BYTES = KS * 4096;         // 128 rows x 32 B per k-step
     constexpr uint32_t K_BYTES = KS * 1024;         // 32 rows x 32 B per k-step
     constexpr uint32_t V_BYTES = 4096;              // V^T: 32 features x 128 B (32 keys)
     constexpr uint32_t KV_BYTES = 2 * K_BYTES + 2 * V_BYTES;
-    constexpr uint32_t P_BYTES = 16384;             // 128 rows x 128 B
     constexpr uint32_t OFF_KV = 2 * Q_BYTES;
-    constexpr uint32_t OFF_P = OFF_KV + KVS * KV_BYTES;
-    constexpr uint32_t OFF_TAB = OFF_P + 2 * 2 * P_BYTES;
-    constexpr uint32_t OFF_KOFF = OFF_TAB + ((TROWS * 4 + 15) / 16) * 16;
+    constexpr uint32_t OFF_TAB = OFF_KV + KVS * KV_BYTES;
+    constexpr uint32_t OFF_KOFF = OFF_TAB + TR * TSTRIDE * 4;
+    // TMEM columns: S / P_hi blocks at 0 and 32, P_lo at 64 and 96, O (per item parity)
+    // at 128 and 160.
+    constexpr uint32_t T_PLO = 64, T_O = 128;
 
     extern __shared__ __align__(1024) uint8_t raw[];
     uint8_t* sm = (uint8_t*)(((uintptr_t)raw + 1023) & ~(uintptr_t)1023);
     float* tab = reinterpret_cast<float*>(sm + OFF_TAB);
-    int* koff = reinterpret_cast<int*>(sm + OFF_KOFF);  // OCAB: key (ky, kx) -> ky*39 + kx
-    __shared__ uint64_t q_full, q_empty, kv_full[KVS], kv_empty[KVS], s_full[2], p_full[2], o_full[2], o_free[2], drain;
+    int* koff = reinterpret_cast<int*>(sm + OFF_KOFF);  // OCAB: key (ky, kx) -> ky*48 + kx
+    __shared__ uint64_t q_full, q_empty, kv_full[KVS], kv_empty[KVS], s_full[2], p_full[2], o_done, o_free[2], drain;
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int abort_flag;
 
@@ -154,9 +192,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int nx = wp / 16;
     const long c3 = 3L * c;
 
-    for (int i = threadIdx.x; i < TROWS; i += TC_THREADS) tab[i] = table[(long)i * heads + head];
+    // Bias table of this head, rows TSTRIDE apart. SA: tab[r][s] = table[r*31 + s], the
+    // bias of (qy - ky + 15, qx - kx + 15). OCAB: tab[r][s] is the bias of key - query
+    // offset (r - 22, s - 22), i.e. table[((r - 22)*39 + (s - 22)) mod 1521].
+    for (int i = threadIdx.x; i < TR * TR; i += TC_THREADS) {
+        const int r = i / TR, s = i - r * TR;
+        int src = OCA ? (r - 22) * TW + (s - 22) : r * TW + s;
+        if (src < 0) src += TR * TW;
+        tab[r * TSTRIDE + s] = table[(long)src * heads + head];
+    }
     if (OCA)
-        for (int i = threadIdx.x; i < NK; i += TC_THREADS) koff[i] = (i / 24) * 39 + (i % 24);
+        for (int i = threadIdx.x; i < NK; i += TC_THREADS) koff[i] = (i / 24) * TSTRIDE + (i % 24);
     if (threadIdx.x == 0) {
         bar_init(&q_full, 128);
         bar_init(&q_empty, 1);
@@ -167,32 +213,36 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         for (int s = 0; s < 2; ++s) {
             bar_init(&s_full[s], 1);
             bar_init(&p_full[s], 128);
-            bar_init(&o_full[s], 1);
             bar_init(&o_free[s], 128);
         }
+        bar_init(&o_done, 1);
         bar_init(&drain, 1);
         abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 128;" ::"r"(su(&tmem_slot)));
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su(&tmem_slot)),
+                     "n"(TMEM_COLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     tcf_before();
     __syncthreads();
     tcf_after();
-    const uint32_t tmem = tmem_slot;  // S buffers at columns 0 and 32, O blocks at 64 and 96
+    const uint32_t tmem = tmem_slot;
 
     if (warp == 0) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            const uint32_t id_s = idesc_a(32, 0), id_o = idesc_a(32, 0);
+            const uint32_t id_s = idesc_a(32), id_o = idesc_a(32);
             const uint32_t qh = su(sm), ql = su(sm + Q_BYTES);
             long g = 0;  // global key-block counter
             uint32_t ti = 0;
             bool ok = true;
             for (long w = blockIdx.x; w < items && ok; w += gridDim.x, ++ti) {
                 if (!bar_wait(&q_full, ti & 1, &abort_flag, err, 11)) break;
+                // The O block of this item's parity must have been read by the softmax.
+                if (!bar_wait(&o_free[ti & 1], ((ti >> 1) & 1) ^ 1, &abort_flag, err, 19)) break;
+                const uint32_t od = tmem + T_O + (ti & 1) * 32;
                 auto issue_s = [&](long gb) -> bool {
                     const int s = (int)(gb & 1), kvs = (int)(gb % KVS);
                     if (!bar_wait(&kv_full[kvs], (uint32_t)((gb / KVS) & 1), &abort_flag, err, 12)) return false;
@@ -204,11 +254,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         const uint64_t aH = mdesc(qh + k * 4096, 32, 256), aL = mdesc(ql + k * 4096, 32, 256);
                         const uint64_t bH = mdesc(kb + k * 1024, 32, 256), bL = mdesc(kb + K_BYTES + k * 1024, 32, 256);
                         if (TERMS == 3) {
-                            mma(d, aL, bH, id_s, k ? 1u : 0u);
-                            mma(d, aH, bL, id_s, 1u);
-                            mma(d, aH, bH, id_s, 1u);
+                            mma_ss(d, aL, bH, id_s, k ? 1u : 0u);
+                            mma_ss(d, aH, bL, id_s, 1u);
+                            mma_ss(d, aH, bH, id_s, 1u);
                         } else {
-                            mma(d, aH, bH, id_s, k ? 1u : 0u);
+                            mma_ss(d, aH, bH, id_s, k ? 1u : 0u);
                         }
                     }
                     commit(&s_full[s]);
@@ -217,6 +267,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 if (!issue_s(g)) break;
                 for (int j = 0; j < NBLK; ++j) {
                     const long gb = g + j;
+                    // S of the next block goes into the other S buffer, whose P the
+                    // previous PV (issued earlier, executed in order) has consumed.
                     if (j + 1 < NBLK) {
                         if (!issue_s(gb + 1)) {
                             ok = false;
@@ -226,30 +278,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         if (j + 1 == NBLK - 1) commit(&q_empty);
                     }
                     const int s = (int)(gb & 1);
-                    const uint32_t ph = (uint32_t)((gb >> 1) & 1);
-                    if (!bar_wait(&p_full[s], ph, &abort_flag, err, 13) ||
-                        !bar_wait(&o_free[s], ph ^ 1, &abort_flag, err, 14)) {
+                    if (!bar_wait(&p_full[s], (uint32_t)((gb >> 1) & 1), &abort_flag, err, 13)) {
                         ok = false;
                         break;
                     }
                     tcf_after();
-                    const uint32_t pb = su(sm + OFF_P + s * 2 * P_BYTES);
                     const int kvs = (int)(gb % KVS);
                     const uint32_t vb = su(sm + OFF_KV + kvs * KV_BYTES + 2 * K_BYTES);
-                    const uint32_t d = tmem + 64 + s * 32;
+                    const uint32_t ph = tmem + s * 32, pl = tmem + T_PLO + s * 32;
 #pragma unroll
                     for (int k = 0; k < KBLK / 8; ++k) {
-                        const uint64_t aH = mdesc(pb + k * 32, 128, 1024), aL = mdesc(pb + P_BYTES + k * 32, 128, 1024);
                         const uint64_t bH = mdesc(vb + k * 32, 128, 1024), bL = mdesc(vb + V_BYTES + k * 32, 128, 1024);
+                        const uint32_t acc = (j | k) ? 1u : 0u;
                         if (TERMS == 3) {
-                            mma(d, aL, bH, id_o, k ? 1u : 0u);
-                            mma(d, aH, bL, id_o, 1u);
-                            mma(d, aH, bH, id_o, 1u);
+                            mma_ts(od, pl + k * 8, bH, id_o, acc);
+                            mma_ts(od, ph + k * 8, bL, id_o, 1u);
+                            mma_ts(od, ph + k * 8, bH, id_o, 1u);
                         } else {
-                            mma(d, aH, bH, id_o, k ? 1u : 0u);
+                            mma_ts(od, ph + k * 8, bH, id_o, acc);
                         }
                     }
-                    commit(&o_full[s]);
+                    commit(&o_done);
                     commit(&kv_empty[kvs]);
                 }
                 g += NBLK;
@@ -263,23 +312,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int row = q4 * 32 + lane;
         const uint32_t trow = (uint32_t)(q4 * 32) << 16;
         constexpr float L2E = 1.4426950408889634f;
+        constexpr int VW = (D % 4 == 0) ? 4 : 2;
         long g = 0;
-        for (long w = blockIdx.x; w < items; w += gridDim.x) {
+        uint32_t ti = 0;
+        for (long w = blockIdx.x; w < items; w += gridDim.x, ++ti) {
             if (__any_sync(0xffffffffu, abort_flag != 0)) break;
             const long rest = w / heads;
             const int win = (int)(rest >> 1), mtile = (int)(rest & 1);
             const int wy = win / nx, wx = win - wy * nx;
             const int qi = mtile * MT + row, qy = qi >> 4, qx = qi & 15;
             const bool masked = !OCA && shift > 0;
-            // Bias row of this query: SA index (qy-ky+15)*31 + (qx-kx+15) = A0 - (ky*31+kx);
-            // OCAB index (ky*39+kx) - B0, wrapped into the table.
-            const int A0 = qy * 31 + qx + 480, B0 = qy * 39 + qx + 280;
+            // Bias of key (ky, kx): SA tab[(qy-ky+15)*48 + (qx-kx+15)] = tab[A0 - (ky*48 + kx)];
+            // OCAB tab[(ky-qy+15)*48 + (kx-qx+15)] = tab[koff[k] - B0].
+            const int A0 = qy * TSTRIDE + qx + 15 * TSTRIDE + 15, B0 = qy * TSTRIDE + qx - 15 * TSTRIDE - 15;
             // Shift mask: key column kx is masked against target label t when
             // band(wx*16+kx) != t; one 16-bit mask per possible row band.
             uint32_t cm[3] = {0, 0, 0};
-            int lq = 0;
             if (masked) {
-                lq = band3(wy * 16 + qy, hp, shift) * 3 + band3(wx * 16 + qx, wp, shift);
+                const int lq = band3(wy * 16 + qy, hp, shift) * 3 + band3(wx * 16 + qx, wp, shift);
 #pragma unroll
                 for (int kx = 0; kx < 16; ++kx) {
                     const int bx = band3(wx * 16 + kx, wp, shift);
@@ -288,25 +338,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         if (by * 3 + bx != lq) cm[by] |= 1u << kx;
                 }
             }
-            float m = -INFINITY, l = 0.f, a_prev = 1.f;
-            float o[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = 0.f;
+            const uint32_t t_o = tmem + trow + T_O + (ti & 1) * 32;
+            float m = 0.f, l = 0.f;
             bool ok = true;
-            auto o_update = [&](long gb, float a) -> bool {
-                const int s = (int)(gb & 1);
-                const bool got = bar_wait(&o_full[s], (uint32_t)((gb >> 1) & 1), &abort_flag, err, 15);
-                if (!__all_sync(0xffffffffu, got)) return false;
-                tcf_after();
-                float ob[32];
-                tld16(tmem + trow + 64 + s * 32, ob);
-                tld16(tmem + trow + 64 + s * 32 + 16, ob + 16);
-#pragma unroll
-                for (int i = 0; i < 32; ++i) o[i] = o[i] * a + ob[i];
-                tcf_before();
-                bar_arrive(&o_free[s]);
-                return true;
-            };
             for (int j = 0; j < NBLK; ++j) {
                 const long gb = g + j;
                 const int s = (int)(gb & 1);
@@ -317,68 +351,86 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 }
                 tcf_after();
                 float sv[32];
-                tld16(tmem + trow + s * 32, sv);
-                tld16(tmem + trow + s * 32 + 16, sv + 16);
+                tld32(tmem + trow + s * 32, sv);
                 uint32_t mrow0 = 0, mrow1 = 0;
                 if (masked) {
                     // the block's two key rows ky = 2j, 2j+1
-                    mrow0 = cm[band3(wy * 16 + 2 * j, hp, shift)];
-                    mrow1 = cm[band3(wy * 16 + 2 * j + 1, hp, shift)];
+                    const int b0 = band3(wy * 16 + 2 * j, hp, shift), b1 = band3(wy * 16 + 2 * j + 1, hp, shift);
+                    mrow0 = b0 == 0 ? cm[0] : (b0 == 1 ? cm[1] : cm[2]);  // selects: no local memory
+                    mrow1 = b1 == 0 ? cm[0] : (b1 == 1 ? cm[1] : cm[2]);
                 }
-                const float* trow_sa = tab + (A0 - 62 * j);  // SA: minus (k>>4)*31 + (k&15)
+                const float* trow_sa = tab + (A0 - 2 * TSTRIDE * j);  // SA: minus (k>>4)*48 + (k&15)
                 float bmax = -INFINITY;
 #pragma unroll
                 for (int k = 0; k < 32; ++k) {
                     float v;
                     if (OCA) {
-                        int bi = koff[j * KBLK + k] - B0;
-                        bi += bi < 0 ? TROWS : 0;
-                        v = sv[k] + tab[bi];
+                        v = sv[k] + tab[koff[j * KBLK + k] - B0];
                     } else {
-                        v = sv[k] + trow_sa[-((k >> 4) * 31 + (k & 15))];
+                        v = sv[k] + trow_sa[-((k >> 4) * TSTRIDE + (k & 15))];
                         if (masked) {
                             const uint32_t mr = (k >> 4) ? mrow1 : mrow0;
                             if ((mr >> (k & 15)) & 1u) v += -100.f;
                         }
                     }
-                    sv[k] = v;
+                    sv[k] = v * L2E;  // log2 units from here on
                     bmax = fmaxf(bmax, v);
                 }
-                const float mn = fmaxf(m, bmax);
-                const float a = exp2f((m - mn) * L2E);
-                const float nmn = -mn * L2E;
-                float psum = 0.f;
-                uint8_t* pb = sm + OFF_P + s * 2 * P_BYTES;
-#pragma unroll
-                for (int k4 = 0; k4 < 8; ++k4) {
-                    float p[4];
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        p[u] = exp2f(fmaf(sv[4 * k4 + u], L2E, nmn));
-                        psum += p[u];
-                    }
-                    float4 ph, pl;
-                    split_tf32(p[0], ph.x, pl.x);
-                    split_tf32(p[1], ph.y, pl.y);
-                    split_tf32(p[2], ph.z, pl.z);
-                    split_tf32(p[3], ph.w, pl.w);
-                    const uint32_t off = off_sw128(row, 4 * k4);
-                    *reinterpret_cast<float4*>(pb + off) = ph;
-                    if (TERMS == 3) *reinterpret_cast<float4*>(pb + P_BYTES + off) = pl;
+                bmax *= L2E;
+                // The row's reference max moves only on a large jump (first block: set).
+                const bool need = j == 0 || bmax > m + RESCALE_LOG2;
+                float a = 1.f;
+                if (need) {
+                    a = j == 0 ? 0.f : exp2f(m - bmax);
+                    m = bmax;
+                    l *= a;
                 }
-                l = l * a + psum;
-                m = mn;
-                fence_async();
+                float psum = 0.f;
+                float pl[32];
+#pragma unroll
+                for (int k = 0; k < 32; ++k) {
+                    const float p = exp2f(sv[k] - m);
+                    psum += p;
+                    if (TERMS == 3) {
+                        split_tf32(p, sv[k], pl[k]);
+                    } else {
+                        sv[k] = tf32_rna(p);
+                    }
+                }
+                tst32(tmem + trow + s * 32, sv);
+                if (TERMS == 3) tst32(tmem + trow + T_PLO + s * 32, pl);
+                l += psum;
+                if (j > 0) {
+                    // PV of the previous block has finished (this also keeps every
+                    // o_done phase consumed in order); a moved max then rescales the
+                    // row's O before this block's PV adds to it.
+                    const bool done = bar_wait(&o_done, (uint32_t)((gb - 1) & 1), &abort_flag, err, 15);
+                    if (!__all_sync(0xffffffffu, done)) {
+                        ok = false;
+                        break;
+                    }
+                    if (__any_sync(0xffffffffu, need)) {
+                        tcf_after();
+                        float ov[32];
+                        tld32(t_o, ov);
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) ov[i] *= a;
+                        tst32(t_o, ov);
+                    }
+                }
+                tst_wait();
                 tcf_before();
                 bar_arrive(&p_full[s]);
-                if (j > 0 && !o_update(gb - 1, a_prev)) {
-                    ok = false;
-                    break;
-                }
-                a_prev = a;
             }
-            if (!ok || !o_update(g + NBLK - 1, a_prev)) break;
+            if (!ok) break;
             // O / l at the query's plane position (the roll of the shifted windows undone).
+            const bool done = bar_wait(&o_done, (uint32_t)((g + NBLK - 1) & 1), &abort_flag, err, 15);
+            if (!__all_sync(0xffffffffu, done)) break;
+            tcf_after();
+            float ov[32];
+            tld32(t_o, ov);
+            tcf_before();
+            bar_arrive(&o_free[ti & 1]);
             const float inv = 1.f / l;
             long qpos;
             if (OCA)
@@ -386,8 +438,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             else
                 qpos = (long)((wy * 16 + qy + shift) % hp) * wp + (wx * 16 + qx + shift) % wp;
             const long ob = qpos * c + (long)head * D;
+            if (VW == 4) {
 #pragma unroll
-            for (int i = 0; i < D; ++i) put(out, ob + i, o[i] * inv);
+                for (int i = 0; i < D; i += 4)
+                    put4(out, ob + i, make_float4(ov[i] * inv, ov[i + 1] * inv, ov[i + 2] * inv, ov[i + 3] * inv));
+            } else {
+#pragma unroll
+                for (int i = 0; i < D; ++i) put(out, ob + i, ov[i] * inv);
+            }
             g += NBLK;
         }
     } else {
@@ -542,7 +600,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (warp == 0) {
         __syncwarp();
         tcf_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 128;" ::"r"(tmem));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(TMEM_COLS));
     }
 }
 
@@ -550,9 +608,9 @@ template <int D, bool OCA, int TERMS>
 static void run_tc(const float* qkv, const float* table, Dst out, const Plan& p, int c, int heads, int shift, int* err,
                    cudaStream_t st) {
     constexpr int KS = (D + 7) / 8;
-    constexpr int TROWS = OCA ? 1521 : 961;
-    constexpr size_t bytes = 2 * KS * 4096 + KVS * (2 * KS * 1024 + 2 * 4096) + 4 * 16384 + ((TROWS * 4 + 15) / 16) * 16 +
-                             (OCA ? 576 * 4 : 0) + 1024;
+    constexpr int TR = OCA ? 39 : 31;
+    constexpr size_t bytes =
+        2 * KS * 4096 + KVS * (2 * KS * 1024 + 2 * 4096) + TR * TSTRIDE * 4 + (OCA ? 576 * 4 : 0) + 1024;
     static unsigned configured = 0;
     int dev = 0;
     HAT_CUDA(cudaGetDevice(&dev));
@@ -563,8 +621,9 @@ static void run_tc(const float* qkv, const float* table, Dst out, const Plan& p,
     const long items = (long)p.nw() * heads * 2;
     int sms = 0;
     HAT_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    // A multiple of the head count, so every CTA keeps one head (and one bias table).
-    long grid = std::min<long>(items, (long)(sms / heads) * heads);
+    // Two CTAs per SM; a multiple of the head count, so every CTA keeps one head (and
+    // one bias table).
+    long grid = std::min<long>(items, (long)(2 * sms / heads) * heads);
     k_attn_tc<D, OCA, TERMS><<<(unsigned)grid, TC_THREADS, bytes, st>>>(qkv, table, out, p.hp, p.wp, c, heads, shift,
                                                                         1.f / sqrtf((float)D), items, err);
     HAT_CUDA(cudaGetLastError());
