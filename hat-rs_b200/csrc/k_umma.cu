@@ -16,8 +16,9 @@
 // which drops only A_lo.B_lo (relative 2^-22). FAST mode issues the single A_hi.B_hi.
 // The epilogue can write its own output split the same way for the next GEMM.
 //
-// Warp roles (192 threads): 0 TMA producer, 1 MMA issuer + TMEM owner, 2-5 epilogue
-// (TMEM -> registers -> fused epilogue -> global). Two TMEM accumulators (2 x 256
+// Warp roles (320 threads): 0 TMA producer, 1 MMA issuer + TMEM owner, 2-9 epilogue
+// (TMEM -> registers -> fused epilogue -> global). Two epilogue warps share each TMEM
+// lane quarter and take alternate 16-column chunks. Two TMEM accumulators (2 x 256
 // columns) let the epilogue of one tile overlap the MMAs of the next.
 //
 // Every mbarrier wait is bounded (about 2 s of SM clock cycles); on expiry the kernel records an
@@ -32,7 +33,8 @@ namespace hat {
 
 namespace {
 
-constexpr int NTHREADS = 192;
+constexpr int NTHREADS = 320;
+constexpr int EPI_WARPS = 8;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return (uint32_t)__cvta_generic_to_shared(p);
@@ -186,9 +188,31 @@ template <int MODE>
 __device__ __forceinline__ void epi_chunk16(const UmmaArgs& g, const Epi& e, uint32_t taddr, int n0, int c0,
                                             long mt, int q, int lane, bool valid_own, float (*stg)[17],
                                             float* cacc) {
+    const int nb = n0 + c0;
+    // Phase-2 geometry and the residual loads first, so their latency overlaps the TMEM
+    // load and the register work of phase 1.
+    const int lr = lane >> 2, lc = (lane & 3) * 4;
+    const int n = nb + lc;
+    long base[4];
+    bool ok[4];
+    float4 rs[4], cx[4];
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+        long m;
+        bool valid;
+        tile_row<MODE>(g, mt, q * 32 + it * 8 + lr, m, valid);
+        ok[it] = valid && n < g.nstore;
+        base[it] = m * g.ldo + n;
+        rs[it] = make_float4(0.f, 0.f, 0.f, 0.f);
+        cx[it] = rs[it];
+        if (ok[it] && e.res) rs[it] = *reinterpret_cast<const float4*>(e.res + base[it]);
+        if (ok[it] && e.cx) cx[it] = *reinterpret_cast<const float4*>(e.cx + base[it]);
+    }
+    float4 gt = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (e.cx && n < g.nstore) gt = *reinterpret_cast<const float4*>(e.gate + n);
+
     float v[16];
     tmem_ld16(taddr + c0, v);
-    const int nb = n0 + c0;
     if (e.bias) {
         if (nb + 16 <= g.N) {
 #pragma unroll
@@ -229,34 +253,23 @@ __device__ __forceinline__ void epi_chunk16(const UmmaArgs& g, const Epi& e, uin
 #pragma unroll
     for (int j = 0; j < 16; ++j) stg[lane][j] = v[j];
     __syncwarp();
-    const int lr = lane >> 2, lc = (lane & 3) * 4;
-    const int n = nb + lc;
-#pragma unroll 1
+#pragma unroll
     for (int it = 0; it < 4; ++it) {
+        if (!ok[it]) continue;
         const int r = it * 8 + lr;
-        long m;
-        bool valid;
-        tile_row<MODE>(g, mt, q * 32 + r, m, valid);
-        if (valid && n < g.nstore) {
-            float4 o = make_float4(stg[r][lc], stg[r][lc + 1], stg[r][lc + 2], stg[r][lc + 3]);
-            const long base = m * g.ldo + n;
-            if (e.cx) {
-                const float4 rs = *reinterpret_cast<const float4*>(e.res + base);
-                const float4 cx = *reinterpret_cast<const float4*>(e.cx + base);
-                const float4 gt = *reinterpret_cast<const float4*>(e.gate + n);
-                o.x = (rs.x + o.x) + (cx.x * gt.x) * e.cscale;
-                o.y = (rs.y + o.y) + (cx.y * gt.y) * e.cscale;
-                o.z = (rs.z + o.z) + (cx.z * gt.z) * e.cscale;
-                o.w = (rs.w + o.w) + (cx.w * gt.w) * e.cscale;
-            } else if (e.res) {
-                const float4 rs = *reinterpret_cast<const float4*>(e.res + base);
-                o.x = rs.x + o.x;
-                o.y = rs.y + o.y;
-                o.z = rs.z + o.z;
-                o.w = rs.w + o.w;
-            }
-            put4(g.y, base, o);
+        float4 o = make_float4(stg[r][lc], stg[r][lc + 1], stg[r][lc + 2], stg[r][lc + 3]);
+        if (e.cx) {
+            o.x = (rs[it].x + o.x) + (cx[it].x * gt.x) * e.cscale;
+            o.y = (rs[it].y + o.y) + (cx[it].y * gt.y) * e.cscale;
+            o.z = (rs[it].z + o.z) + (cx[it].z * gt.z) * e.cscale;
+            o.w = (rs[it].w + o.w) + (cx[it].w * gt.w) * e.cscale;
+        } else if (e.res) {
+            o.x = rs[it].x + o.x;
+            o.y = rs[it].y + o.y;
+            o.z = rs[it].z + o.z;
+            o.w = rs[it].w + o.w;
         }
+        put4(g.y, base[it], o);
     }
     __syncwarp();
 }
@@ -270,11 +283,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     __shared__ uint64_t full[6], empty[6], acc_full[2], acc_empty[2], drain;
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int abort_flag;
-    // The channel-attention pool: per epilogue warp, column sums accumulated over every
-    // tile this CTA owns (in its fixed tile order), written once at the end.
+    // The channel-attention pool: per TMEM lane quarter, column sums accumulated over
+    // every tile this CTA owns (in its fixed tile order), written once at the end. The
+    // quarter's two epilogue warps own disjoint columns.
     __shared__ float colacc[4][256];
     // Per epilogue warp: a 32 x 16 staging tile (padded) for the coalesced store.
-    __shared__ float stg[4][32][17];
+    __shared__ float stg[EPI_WARPS][32][17];
 
     uint8_t* sm = (uint8_t*)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
     const int S = g.stages;
@@ -295,7 +309,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&acc_full[a], 1);
-            mbar_init(&acc_empty[a], 128);
+            mbar_init(&acc_empty[a], 32 * EPI_WARPS);
         }
         mbar_init(&drain, 1);
         abort_flag = 0;
@@ -390,7 +404,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // ------------------------------------------------------------ epilogue
         const int q = warp & 3;          // TMEM lane quarter this warp may read
         const int row = q * 32 + lane;   // tile row of this thread
-        const int ew = warp - 2;         // 0..3 within the epilogue group
+        const int ew = warp - 2;         // 0..7 within the epilogue group
+        const int half = ew >> 2;        // which of the quarter's alternate chunks
         uint32_t tl = 0;
         for (long t = blockIdx.x; t < ntiles; t += gridDim.x, ++tl) {
             if (__any_sync(0xffffffffu, abort_flag != 0)) break;
@@ -419,7 +434,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 // pixel (2y + i, 2x + j). 32 columns give 8 consecutive output channels for
                 // each of the 4 sub-pixels: two float4 stores per sub-pixel.
                 const int cout = g.N / 4;
-                for (int c0 = 0; c0 < g.BN; c0 += 32) {
+                for (int c0 = 32 * half; c0 < g.BN; c0 += 64) {
                     float v[32];
                     tmem_ld16(taddr + c0, v);
                     tmem_ld16(taddr + c0 + 16, v + 16);
@@ -442,13 +457,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             if (EK == EK_STORE) {
 #pragma unroll 1
-                for (int c0 = 0; c0 < g.BN; c0 += 16)
-                    epi_chunk16<MODE>(g, e, taddr, n0, c0, mt, q, lane, valid, stg[ew], colacc[ew]);
+                for (int c0 = 16 * half; c0 < g.BN; c0 += 32)
+                    epi_chunk16<MODE>(g, e, taddr, n0, c0, mt, q, lane, valid, stg[ew], colacc[q]);
                 tc_fence_before();
                 mbar_arrive(&acc_empty[a]);
                 continue;
             }
-            for (int c0 = 0; c0 < g.BN; c0 += 16) {
+            for (int c0 = 16 * half; c0 < g.BN; c0 += 32) {
                 float v[16];
                 tmem_ld16(taddr + c0, v);
 #pragma unroll
@@ -531,7 +546,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
                         for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
                         const int n = n0 + c0 + j;
-                        if (lane == 0 && n < g.N) colacc[ew][n] += s;
+                        if (lane == 0 && n < g.N) colacc[q][n] += s;
                     }
                 }
             }
@@ -540,7 +555,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         if (e.colsum) {
             __syncwarp();
-            for (int n = lane; n < g.N; n += 32) e.colsum[((long)blockIdx.x * 4 + ew) * g.N + n] = colacc[ew][n];
+            // Each warp writes the columns it owns (its chunk parity within a tile).
+            for (int n = lane; n < g.N; n += 32)
+                if ((((n % g.BN) >> 4) & 1) == half) e.colsum[((long)blockIdx.x * 4 + q) * g.N + n] = colacc[q][n];
         }
     }
 
@@ -594,8 +611,9 @@ static int num_sms() {
 }
 
 // Dynamic shared memory at most: the 227 KB per CTA less the static arrays (channel
-// sums 4 KB, staging tiles 8.5 KB, barriers) and some slack.
-static const long SMEM_CAP = 232448 - 14336;
+// sums 4 KB, staging tiles 17 KB, barriers) and some slack. Three stages of a 144-wide
+// tile (3 x 68 KB) still fit.
+static const long SMEM_CAP = 232448 - 22528;
 
 template <int MODE, int TERMS, int EK>
 static void launch_ek(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh, const CUtensorMap& bl,
