@@ -161,6 +161,13 @@ void launch_window_attention(int mode, bool simt, const float* qkv, const float*
 void launch_overlap_attention(int mode, bool simt, const float* qkv, const float* table, Dst out, const Plan& p,
                               int c, int heads, int* err, cudaStream_t st);
 
+// The second half of a 3x3 conv computed as a per-tap linear: `taps` is the [hp][wp][ldt]
+// plane of Y[p][tap*cout + co] = sum_ci w[co][ci][tap] x[p][ci] (tap = ky*3 + kx), and
+// out[p][co] = gelu(bias[co] + sum_tap Y[p + (ky-1, kx-1)][tap*cout + co]) with zero
+// padding; channels cout..ldo-1 of `out` are written as zeros. cout <= 8.
+void launch_tapsum_gelu(const float* taps, int ldt, const float* bias, Dst out, int ldo, int cout, int hp, int wp,
+                        cudaStream_t st);
+
 // gate[c] = sigmoid(W2 relu(W1 mean + b1) + b2) (hat_arch.py:40-57), where the mean
 // over the plane is the sum of `rows` partial rows [rows][c] times `inv_count`.
 void launch_ca_gate(const float* partial, long rows, float inv_count, const float* w1, const float* b1,

@@ -135,6 +135,9 @@ Engine::Engine(const std::string& path, int device, int mode, bool use_graph, bo
     // One device allocation: every f32 tensor as stored, then every GEMM operand in the
     // kernels' layouts (CUDA-core layout, tensor-core hi/lo split).
     const int cmid_stride = Sizes::of(wt_, Plan::make(16, 16, wt_.window)).cmid_stride;
+    tap_cab_ = 9 * wt_.compressed <= 64;
+    tap_ld_ = (9 * wt_.compressed + 3) / 4 * 4;
+    auto is_cab1 = [](const std::string& n) { return n.find("conv_block.cab.0.weight") != std::string::npos; };
     size_t total = 0;
     std::vector<std::string> names;
     for (auto& kv : wt_.st.tensors) {
@@ -152,6 +155,12 @@ Engine::Engine(const std::string& path, int device, int mode, bool use_graph, bo
             }
             gw_[kv.first] = g;
             total += (gemm_w_floats(g) + 64) / 64 * 64 + 192;
+            if (tap_cab_ && is_cab1(kv.first)) {
+                GemmW t;
+                plan_gemm_w(t, 9 * (int)s[0], (int)s[1], false, 0);
+                gw_[kv.first + "#taps"] = t;
+                total += ((size_t)t.n * t.k + 63) / 64 * 64 + (gemm_w_floats(t) + 64) / 64 * 64 + 192;
+            }
         }
     }
     HAT_CUDA(cudaMalloc(&dweights_, total * sizeof(float)));
@@ -182,6 +191,25 @@ Engine::Engine(const std::string& path, int device, int mode, bool use_graph, bo
                 g.simt = simt;
                 g.hi = hi;
                 g.lo = lo;
+                if (tap_cab_ && is_cab1(name)) {
+                    GemmW& t = gw_[name + "#taps"];
+                    float* taps = dweights_ + off;
+                    off += ((size_t)t.n * t.k + 63) / 64 * 64;
+                    launch_prep_taps(d, taps, wt_.compressed, wt_.embed, stream_);
+                    float* tsimt = dweights_ + off;
+                    off += ((size_t)t.n * t.k + 63) / 64 * 64;
+                    float *thi = nullptr, *tlo = nullptr;
+                    if (t.umma) {
+                        thi = dweights_ + off;
+                        off += ((size_t)t.n_pad * t.k_pad + 63) / 64 * 64;
+                        tlo = dweights_ + off;
+                        off += ((size_t)t.n_pad * t.k_pad + 63) / 64 * 64;
+                    }
+                    launch_prep_gemm_w(taps, tsimt, thi, tlo, t, stream_);
+                    t.simt = tsimt;
+                    t.hi = thi;
+                    t.lo = tlo;
+                }
             }
         }
     } catch (...) {
@@ -350,7 +378,16 @@ void Engine::hab(int stage, int blk, const float* in, float* out) {
     ec1.act = ACT_GELU;
     ec1.ldo = sizes_.cmid_stride;
     mark("conv.cab1", 18.0 * P * c * cc, 4.0 * P * (c + cc));
-    conv(cb + ".0.weight", O(a_->n1, a_->n1lo), D(a_->cmid, a_->cmidlo), plan_.hp, plan_.wp, ec1);
+    if (tap_cab_) {
+        // Per-tap partial outputs into the (not yet used) qkv buffer, then the tap sum.
+        Epi et;
+        et.ldo = tap_ld_;
+        linear(cb + ".0.weight#taps", O(a_->n1, a_->n1lo), Dst{a_->qkv, nullptr}, et);
+        launch_tapsum_gelu(a_->qkv, tap_ld_, W(cb + ".0.bias"), D(a_->cmid, a_->cmidlo), sizes_.cmid_stride, cc,
+                           plan_.hp, plan_.wp, stream_);
+    } else {
+        conv(cb + ".0.weight", O(a_->n1, a_->n1lo), D(a_->cmid, a_->cmidlo), plan_.hp, plan_.wp, ec1);
+    }
     Epi ec2;
     ec2.bias = W(cb + ".2.bias");
     ec2.colsum = a_->chsum;

@@ -69,6 +69,11 @@ private:
     Opnd O(const float* hi, const float* lo) const { return Opnd{hi, split() ? lo : nullptr}; }
 
     Weights wt_;
+    // The CAB's first conv as a per-tap linear + tap sum when its output is narrow
+    // (9 * compressed <= 64): the linear reads the normed plane once instead of nine
+    // times. tap_ld_ is the row stride of the per-tap plane (it borrows the qkv buffer).
+    bool tap_cab_ = false;
+    int tap_ld_ = 0;
     int device_ = 0, mode_ = 0;
     bool use_graph_ = true, simt_only_ = false;
     cudaStream_t stream_ = nullptr;

@@ -31,6 +31,45 @@ void launch_pre(const float* in, float* out, const Plan& p, const float mean[3],
     count_launch();
 }
 
+// ---------------------------------------------------------------- tap sum
+// The CAB's first conv (c -> c/compress, 3x3, then GELU; hat_arch.py:50-53) when its
+// output is narrow: a linear to 9*cout per-tap partial outputs reads the input plane
+// once, and this kernel adds each pixel's nine neighbours' taps. One thread per pixel.
+template <int CMAX>
+__global__ void k_tapsum_gelu(const float* __restrict__ taps, int ldt, const float* __restrict__ bias, Dst out,
+                              int ldo, int cout, int hp, int wp) {
+    const long p = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (p >= (long)hp * wp) return;
+    const int y = (int)(p / wp), x = (int)(p - (long)y * wp);
+    float acc[CMAX];
+#pragma unroll
+    for (int co = 0; co < CMAX; ++co) acc[co] = co < cout ? bias[co] : 0.f;
+#pragma unroll
+    for (int tap = 0; tap < 9; ++tap) {
+        const int yy = y + tap / 3 - 1, xx = x + tap % 3 - 1;
+        if (yy < 0 || yy >= hp || xx < 0 || xx >= wp) continue;
+        const float* row = taps + ((long)yy * wp + xx) * ldt + tap * cout;
+#pragma unroll
+        for (int co = 0; co < CMAX; ++co)
+            if (co < cout) acc[co] += row[co];
+    }
+#pragma unroll
+    for (int co = 0; co < CMAX; ++co) {
+        if (co >= ldo) break;
+        const float v = co < cout ? 0.5f * acc[co] * (1.f + erff(acc[co] * 0.70710678118654752f)) : 0.f;
+        put(out, p * ldo + co, v);
+    }
+}
+
+void launch_tapsum_gelu(const float* taps, int ldt, const float* bias, Dst out, int ldo, int cout, int hp, int wp,
+                        cudaStream_t st) {
+    if (cout > 8 || ldo > 8 || ldt < 9 * cout) throw Error(1, "tapsum: at most 8 output channels");
+    const long n = (long)hp * wp;
+    k_tapsum_gelu<8><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(taps, ldt, bias, out, ldo, cout, hp, wp);
+    HAT_CUDA(cudaGetLastError());
+    count_launch();
+}
+
 // ---------------------------------------------------------------- layernorm
 // One warp per token; the row stays in registers: the mean first, then the biased
 // variance of the centred values (src/cpu.rs:563-581), eps 1e-5.

@@ -81,6 +81,22 @@ void launch_prep_gemm_w(const float* w, float* simt, float* hi, float* lo, const
     }
 }
 
+__global__ void k_prep_taps(const float* __restrict__ w, float* __restrict__ out, int cout, int cin) {
+    const long total = 9L * cout * cin;
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        const int ci = (int)(i % cin);
+        const long r = i / cin;  // tap * cout + co
+        const int co = (int)(r % cout), tap = (int)(r / cout);
+        out[i] = w[((long)co * cin + ci) * 9 + tap];
+    }
+}
+
+void launch_prep_taps(const float* w, float* out, int cout, int cin, cudaStream_t st) {
+    k_prep_taps<<<64, 256, 0, st>>>(w, out, cout, cin);
+    HAT_CUDA(cudaGetLastError());
+    count_launch();
+}
+
 long gemm_linear(const GemmCtx& c, Opnd x, const GemmW& w, Dst y, long m, const Epi& e, cudaStream_t st) {
     // Parity mode needs the operand split by its producer; a plain plane (never the case
     // inside the forward) takes the exact CUDA-core path instead of losing precision.

@@ -38,6 +38,8 @@ inline int umma_bn(int n) {
 void plan_gemm_w(GemmW& g, int n, int k_or_cin, bool conv, int cin_plane);
 size_t gemm_w_floats(const GemmW& g);  // simt + hi + lo floats
 void launch_prep_gemm_w(const float* w, float* simt, float* hi, float* lo, const GemmW& g, cudaStream_t st);
+// [cout][cin][3][3] conv weights -> the per-tap linear [9*cout][cin] (row tap*cout + co).
+void launch_prep_taps(const float* w, float* out, int cout, int cin, cudaStream_t st);
 
 // Tensor-core launchers (`x.lo` required in parity mode); return the number of
 // channel-sum partial rows written when `e.colsum` is set.
