@@ -7,6 +7,7 @@
 
 #include "../../include/hat_b200.h"
 #include "engine.h"
+#include "nccl_rt.h"
 
 using namespace hat;
 
@@ -157,6 +158,25 @@ int hat_b200_profile(hat_b200* h, int height, int width, char* json, size_t json
         std::string j = h->eng->profile(height, width);
         set_err(json, jsonlen, j);
     });
+}
+
+int hat_b200_strip_rows(int height, int nranks, int rank, int* r0, int* r1) {
+    if (height <= 0 || nranks <= 0 || rank < 0 || rank >= nranks || !r0 || !r1) return HAT_B200_EINVAL;
+    const Plan p = Plan::make_strip(height, 16, 16, rank, nranks, 0);
+    if (p.hp / 16 < nranks) return HAT_B200_EINVAL;  // every rank needs a window row
+    *r0 = p.r0;
+    *r1 = p.r1;
+    return HAT_B200_OK;
+}
+
+int hat_b200_nccl_unique_id(void* id, size_t idlen, char* err, size_t errlen) {
+    return guarded(err, errlen, [&] { nccl_unique_id(id, idlen); });
+}
+
+int hat_b200_attach_strip(hat_b200* h, int rank, int nranks, const void* id, size_t idlen, char* err,
+                          size_t errlen) {
+    if (!h) return HAT_B200_EINVAL;
+    return guarded(err, errlen, [&] { h->eng->attach_strip(rank, nranks, id, idlen); });
 }
 
 // The GEMM operand of one kernel-level call, prepared on the caller's stream.

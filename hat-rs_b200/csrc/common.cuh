@@ -29,10 +29,18 @@ struct Plan {
     int h = 0, w = 0;    // the caller's image
     int hp = 0, wp = 0;  // padded to window multiples
     int win = 16, shift = 8, owin = 24, opad = 4;
+    // Strip sharding (one image over several GPUs): this plan computes the padded rows
+    // [r0, r1) and holds `halo` rows of each neighbour above and below them, so its
+    // planes have `rows` = r1 - r0 + 2 * halo rows (local row i is padded row
+    // r0 - halo + i). Unsharded: r0 = 0, r1 = rows = hp, halo = 0.
+    int r0 = 0, r1 = 0, halo = 0, rows = 0;
+    bool strip() const { return halo > 0; }
+    int own() const { return r1 - r0; }
+    int gy0() const { return r0 - halo; }  // padded row of local row 0 (may be negative)
     int nx() const { return wp / win; }
     int ny() const { return hp / win; }
     int nw() const { return nx() * ny(); }
-    long tokens() const { return (long)hp * wp; }
+    long tokens() const { return (long)rows * wp; }  // tokens of this plan's planes
     static Plan make(int h, int w, int win) {
         Plan p;
         p.h = h;
@@ -43,9 +51,28 @@ struct Plan {
         p.shift = win / 2;
         p.owin = win + win / 2;
         p.opad = (p.owin - win) / 2;
+        p.r0 = 0;
+        p.r1 = p.rows = p.hp;
         return p;
     }
-    bool operator==(const Plan& o) const { return h == o.h && w == o.w && hp == o.hp && wp == o.wp && win == o.win; }
+    // Rank `rank` of `n`: window-aligned row strips as equal as the window rows allow
+    // (the first ny % n ranks take one window row more), each with `halo` rows of its
+    // neighbours. Every rank needs at least one window row.
+    static Plan make_strip(int h, int w, int win, int rank, int n, int halo) {
+        Plan p = make(h, w, win);
+        const int ny = p.hp / win, base = ny / n, extra = ny % n;
+        const int wy0 = rank * base + (rank < extra ? rank : extra);
+        const int wy1 = wy0 + base + (rank < extra ? 1 : 0);
+        p.r0 = wy0 * win;
+        p.r1 = wy1 * win;
+        p.halo = halo;
+        p.rows = p.r1 - p.r0 + 2 * halo;
+        return p;
+    }
+    bool operator==(const Plan& o) const {
+        return h == o.h && w == o.w && hp == o.hp && wp == o.wp && win == o.win && r0 == o.r0 && r1 == o.r1 &&
+               halo == o.halo;
+    }
 };
 
 // ---------------------------------------------------------------- operands
@@ -127,10 +154,15 @@ struct Epi {
     // PixelShuffle(r) on store: channel n = c*r*r + i*r + j of pixel (y, x) goes to
     // channel c of pixel (r*y + i, r*x + j) of a [hgt*r][wid*r][n/(r*r)] plane.
     int shuffle = 0;
-    // Final store: crop to (oh, ow), `v / img_range + mean[n]`, planar [n][oh][ow].
+    // Final store: crop to (oh, ow), `v / img_range + mean[n]`, planar [n][oh][ow]; plane
+    // row y is output row y + oy0 (a strip's offset in the whole output).
     int planar_out = 0;
-    int oh = 0, ow = 0;
+    int oh = 0, ow = 0, oy0 = 0;
     float img_range = 1.f, mean[3] = {0, 0, 0};
+    // 3x3 conv: compute the output rows [y_lo, y_hi) only (multiples of 8; 0, 0 = every
+    // row); the input plane is still read over its full height, so rows next to the range
+    // are real data, not padding. The CUDA-core conv ignores this and computes every row.
+    int y_lo = 0, y_hi = 0;
 };
 
 // ---------------------------------------------------------------- kernels (launchers)
@@ -166,7 +198,11 @@ void launch_overlap_attention(int mode, bool simt, const float* qkv, const float
 // out[p][co] = gelu(bias[co] + sum_tap Y[p + (ky-1, kx-1)][tap*cout + co]) with zero
 // padding; channels cout..ldo-1 of `out` are written as zeros. cout <= 8.
 void launch_tapsum_gelu(const float* taps, int ldt, const float* bias, Dst out, int ldo, int cout, int hp, int wp,
-                        cudaStream_t st);
+                        int ylo, int yhi, cudaStream_t st);
+// Rows [ylo, yhi) of the plane are data; the taps of rows outside are the conv's zero padding.
+
+// sum[c] = the sum of `rows` partial rows [rows][c], in row order.
+void launch_rowsum(const float* partial, long rows, int c, float* sum, cudaStream_t st);
 
 // gate[c] = sigmoid(W2 relu(W1 mean + b1) + b2) (hat_arch.py:40-57), where the mean
 // over the plane is the sum of `rows` partial rows [rows][c] times `inv_count`.

@@ -6,6 +6,8 @@
 #include "engine.h"
 
 #include <algorithm>
+
+#include "nccl_rt.h"
 #include <cstring>
 #include <sstream>
 
@@ -32,6 +34,7 @@ Sizes Sizes::of(const Weights& wt, const Plan& p) {
     s.hidlo = P * wt.mlp_ratio * c;
     // The channel-attention pool's partial sums: at most four rows of c per 128-pixel tile.
     s.chsum = (P + 127) / 128 * 4 * c;
+    s.casum = c;
     s.gate = c;
     // The head's planes ping-pong between two buffers: plane 0 (conv_before_upsample's
     // output, at P) and every other shuffled plane go to A, the rest to B.
@@ -57,7 +60,7 @@ Sizes Sizes::of(const Weights& wt, const Plan& p) {
 
 struct Engine::Acts {
     float *x0, *body, *xa, *xb, *n1, *n1lo, *cmid, *cmidlo, *convx, *qkv, *attn, *attnlo, *hid, *hidlo, *chsum,
-        *gate, *headA, *headAlo, *headB, *headBlo, *din, *dout;
+        *casum, *gate, *headA, *headAlo, *headB, *headBlo, *din, *dout;
 };
 
 // ------------------------------------------------------------------ attention dispatch
@@ -72,6 +75,7 @@ void launch_attention_tc(int mode, bool oca, const float* qkv, const float* tabl
 // The tensor-core kernel in parity and fast modes; the CUDA-core one for the debug path.
 void launch_window_attention(int mode, bool simt, const float* qkv, const float* table, Dst out, const Plan& p, int c,
                              int heads, int shift, int* err, cudaStream_t st) {
+    if (simt && p.strip()) throw Error(1, "attention: strips need the tensor-core kernel");
     if (simt)
         launch_window_attention_simt(qkv, table, out, p, c, heads, shift, st);
     else
@@ -80,6 +84,7 @@ void launch_window_attention(int mode, bool simt, const float* qkv, const float*
 
 void launch_overlap_attention(int mode, bool simt, const float* qkv, const float* table, Dst out, const Plan& p, int c,
                               int heads, int* err, cudaStream_t st) {
+    if (simt && p.strip()) throw Error(1, "attention: strips need the tensor-core kernel");
     if (simt)
         launch_overlap_attention_simt(qkv, table, out, p, c, heads, st);
     else
@@ -254,8 +259,98 @@ long Engine::conv(const std::string& wname, Opnd x, Dst y, int hgt, int wid, con
     return gemm_conv3x3(c, x, G(wname), y, hgt, wid, e, stream_);
 }
 
+// Halo rows a strip holds on each side: the shifted windows reach 8 rows (win / 2) past a
+// window-aligned strip, the OCAB keys 4, a 3x3 conv 1.
+static const int STRIP_HALO = 8;
+
+Plan Engine::plan_for(int h, int w) const {
+    if (comm_) return Plan::make_strip(h, w, wt_.window, comm_->rank(), comm_->size(), STRIP_HALO);
+    return Plan::make(h, w, wt_.window);
+}
+
 size_t Engine::footprint_bytes(int h, int w) const {
-    return (size_t)Sizes::of(wt_, Plan::make(h, w, wt_.window)).total() * sizeof(float);
+    return (size_t)Sizes::of(wt_, plan_for(h, w)).total() * sizeof(float);
+}
+
+void Engine::attach_strip(int rank, int n, const void* id, size_t idlen) {
+    HAT_CUDA(cudaSetDevice(device_));
+    if (simt_only_) throw Error(1, "strip sharding needs the tensor-core kernels (simt_only is set)");
+    if (wt_.window != 16) throw Error(1, "strip sharding is built for window 16");
+    if (graph_) {
+        cudaGraphExecDestroy(graph_);
+        graph_ = nullptr;
+    }
+    if (arena_) {
+        HAT_CUDA(cudaStreamSynchronize(stream_));
+        cudaFree(arena_);
+        arena_ = nullptr;
+    }
+    have_plan_ = false;
+    comm_.reset(new Comm(rank, n, id, idlen, device_));
+}
+
+void Engine::exchange(float* plane, int ch, int res, int n) {
+    if (!comm_) return;
+    const Plan& p = plan_;
+    if (n > p.halo * res) throw Error(1, "exchange: more rows than the halo holds");
+    const long rowf = (long)p.wp * res * ch;
+    const int top = p.halo * res, bot = (p.halo + p.own()) * res;  // first own row, first bottom-halo row
+    const int N = comm_->size(), r = comm_->rank();
+    const int up = (r - 1 + N) % N, down = (r + 1) % N;
+    // Matched per peer in posting order: a rank's first send (its top rows, to `up`) is
+    // the up rank's first receive (from its `down`), and likewise for the second pair.
+    comm_->group_start();
+    comm_->send(plane + top * rowf, n * rowf, up, stream_);
+    comm_->send(plane + (bot - n) * rowf, n * rowf, down, stream_);
+    comm_->recv(plane + bot * rowf, n * rowf, down, stream_);
+    comm_->recv(plane + (top - n) * rowf, n * rowf, up, stream_);
+    comm_->group_end();
+}
+
+void Engine::exchange(Dst d, int ch, int res, int n) {
+    exchange(d.hi, ch, res, n);
+    if (d.lo) exchange(d.lo, ch, res, n);
+}
+
+long Engine::conv_res(const std::string& wname, Opnd x, int xch, Dst y, int ych, int res, bool all_rows, Epi e) {
+    const Plan& p = plan_;
+    const int wid = p.wp * res, R = p.rows * res;
+    int lo = 0, hi = R;
+    if (p.strip()) {
+        if (p.r0 == 0) lo = p.halo * res;                // above the image: zero padding
+        if (p.r1 == p.hp) hi = (p.halo + p.own()) * res;  // below the image
+    }
+    const long xoff = (long)lo * wid * xch;
+    Opnd xv{x.hi + xoff, x.lo ? x.lo + xoff : nullptr};
+    long yoff = 0;
+    if (e.planar_out)
+        e.oy0 += p.gy0() * res + lo;  // padded output row of view row 0
+    else if (e.shuffle)
+        yoff = (long)lo * e.shuffle * wid * e.shuffle * ych;
+    else
+        yoff = (long)lo * wid * ych;
+    Dst yv{y.hi + yoff, y.lo ? y.lo + yoff : nullptr};
+    if (e.res) e.res += yoff;
+    if (e.cx) e.cx += yoff;
+    if (p.strip() && !all_rows) {
+        e.y_lo = p.halo * res - lo;
+        e.y_hi = (p.halo + p.own()) * res - lo;
+    }
+    return conv(wname, xv, yv, hi - lo, wid, e);
+}
+
+void Engine::copy_out(float* dst, cudaMemcpyKind kind, cudaStream_t st) {
+    const Plan& p = plan_;
+    const long OH = (long)p.h * wt_.scale, OW = (long)p.w * wt_.scale;
+    if (!p.strip()) {
+        HAT_CUDA(cudaMemcpyAsync(dst, a_->dout, 3 * OH * OW * sizeof(float), kind, st));
+        return;
+    }
+    const long a = (long)p.r0 * wt_.scale, b = std::min<long>((long)p.r1 * wt_.scale, OH);
+    for (int ch = 0; ch < 3 && a < b; ++ch) {
+        const long off = (ch * OH + a) * OW;
+        HAT_CUDA(cudaMemcpyAsync(dst + off, a_->dout + off, (b - a) * OW * sizeof(float), kind, st));
+    }
 }
 
 void Engine::check_memory(int h, int w) const {
@@ -291,7 +386,7 @@ void Engine::check_device_error() {
 }
 
 void Engine::ensure_plan(int h, int w) {
-    Plan p = Plan::make(h, w, wt_.window);
+    Plan p = plan_for(h, w);
     if (have_plan_ && p == plan_) return;
     check_memory(h, w);
     if (graph_) {
@@ -329,6 +424,7 @@ void Engine::ensure_plan(int h, int w) {
     a_->hid = take(s.hid);
     a_->hidlo = take(s.hidlo);
     a_->chsum = take(s.chsum);
+    a_->casum = take(s.casum);
     a_->gate = take(s.gate);
     a_->headA = take(s.headA);
     a_->headAlo = take(s.headAlo);
@@ -370,6 +466,8 @@ void Engine::hab(int stage, int blk, const float* in, float* out) {
     const int c = wt_.embed, cc = wt_.compressed;
     const std::string p = "layers." + std::to_string(stage) + ".residual_group.blocks." + std::to_string(blk);
     const std::string cb = p + ".conv_block.cab";
+    // Sharded: the block input's halo rows (the shifted windows reach 8 rows out).
+    exchange(const_cast<float*>(in), c, 1, plan_.halo);
     mark("layernorm", 0, 8.0 * P * c);
     launch_layernorm(in, W(p + ".norm1.weight"), W(p + ".norm1.bias"), D(a_->n1, a_->n1lo), P, c, stream_);
     // CAB: conv c→cc + GELU; conv cc→c with per-tile channel sums of its output; the gate.
@@ -383,18 +481,33 @@ void Engine::hab(int stage, int blk, const float* in, float* out) {
         Epi et;
         et.ldo = tap_ld_;
         linear(cb + ".0.weight#taps", O(a_->n1, a_->n1lo), Dst{a_->qkv, nullptr}, et);
+        // Rows beyond the image (a strip's halo at the top or bottom edge) are padding.
+        const int ylo = plan_.strip() && plan_.r0 == 0 ? plan_.halo : 0;
+        const int yhi = plan_.strip() && plan_.r1 == plan_.hp ? plan_.halo + plan_.own() : plan_.rows;
         launch_tapsum_gelu(a_->qkv, tap_ld_, W(cb + ".0.bias"), D(a_->cmid, a_->cmidlo), sizes_.cmid_stride, cc,
-                           plan_.hp, plan_.wp, stream_);
+                           plan_.rows, plan_.wp, ylo, yhi, stream_);
     } else {
-        conv(cb + ".0.weight", O(a_->n1, a_->n1lo), D(a_->cmid, a_->cmidlo), plan_.hp, plan_.wp, ec1);
+        // Every row: the second conv reads one row past the strip's own rows.
+        conv_res(cb + ".0.weight", O(a_->n1, a_->n1lo), c, D(a_->cmid, a_->cmidlo), sizes_.cmid_stride, 1, true, ec1);
     }
     Epi ec2;
     ec2.bias = W(cb + ".2.bias");
     ec2.colsum = a_->chsum;
     mark("conv.cab2", 18.0 * P * c * cc, 4.0 * P * (c + cc));
-    long rows = conv(cb + ".2.weight", O(a_->cmid, a_->cmidlo), Dst{a_->convx, nullptr}, plan_.hp, plan_.wp, ec2);
+    long rows = conv_res(cb + ".2.weight", O(a_->cmid, a_->cmidlo), sizes_.cmid_stride, Dst{a_->convx, nullptr}, c, 1,
+                         false, ec2);
     mark("ca_gate", 0, 4.0 * rows * c);
-    launch_ca_gate(a_->chsum, rows, 1.f / (float)P, W(cb + ".3.attention.1.weight"), W(cb + ".3.attention.1.bias"),
+    // The pool averages over the whole padded plane (src/gpu.rs:435); sharded, the
+    // strips' channel sums are added across ranks first.
+    const float inv_count = 1.f / (float)((long)plan_.hp * plan_.wp);
+    const float* pooled = a_->chsum;
+    if (comm_) {
+        launch_rowsum(a_->chsum, rows, c, a_->casum, stream_);
+        comm_->allreduce_sum(a_->casum, c, stream_);
+        pooled = a_->casum;
+        rows = 1;
+    }
+    launch_ca_gate(pooled, rows, inv_count, W(cb + ".3.attention.1.weight"), W(cb + ".3.attention.1.bias"),
                    W(cb + ".3.attention.3.weight"), W(cb + ".3.attention.3.bias"), a_->gate, c, wt_.squeezed,
                    stream_);
     // Attention on the normed plane; odd blocks are shifted by win/2 with the mask.
@@ -424,6 +537,7 @@ void Engine::ocab(int stage, const float* in, float* out) {
     const long P = plan_.tokens();
     const int c = wt_.embed;
     const std::string p = "layers." + std::to_string(stage) + ".residual_group.overlap_attn";
+    exchange(const_cast<float*>(in), c, 1, plan_.halo);  // the keys reach 4 rows out
     mark("layernorm", 0, 8.0 * P * c);
     launch_layernorm(in, W(p + ".norm1.weight"), W(p + ".norm1.bias"), D(a_->n1, a_->n1lo), P, c, stream_);
     Epi eq;
@@ -451,7 +565,7 @@ void Engine::enqueue_pass() {
     Epi ef;
     ef.bias = W("conv_first.bias");
     mark("conv.first", 54.0 * P * c, 4.0 * P * (3 + c));
-    conv("conv_first.weight", Opnd{a_->x0, nullptr}, Dst{a_->body, nullptr}, pl.hp, pl.wp, ef);
+    conv_res("conv_first.weight", Opnd{a_->x0, nullptr}, 3, Dst{a_->body, nullptr}, c, 1, false, ef);
     mark("layernorm", 0, 8.0 * P * c);
     launch_layernorm(a_->body, W("patch_embed.norm.weight"), W("patch_embed.norm.bias"), Dst{a_->xa, nullptr}, P,
                      c, stream_);
@@ -467,35 +581,42 @@ void Engine::enqueue_pass() {
         Epi er;
         er.bias = W("layers." + std::to_string(s) + ".conv.bias");
         er.res = a_->xa;
+        exchange(D(a_->n1, a_->n1lo), c, 1, 1);
         mark("conv.rhag", 18.0 * P * c * c, 12.0 * P * c);
-        conv("layers." + std::to_string(s) + ".conv.weight", O(a_->n1, a_->n1lo), Dst{a_->xa, nullptr}, pl.hp, pl.wp,
-             er);
+        conv_res("layers." + std::to_string(s) + ".conv.weight", O(a_->n1, a_->n1lo), c, Dst{a_->xa, nullptr}, c, 1,
+                 false, er);
     }
     mark("layernorm", 0, 8.0 * P * c);
     launch_layernorm(a_->xa, W("norm.weight"), W("norm.bias"), D(a_->n1, a_->n1lo), P, c, stream_);
     Epi eb;
     eb.bias = W("conv_after_body.bias");
     eb.res = a_->body;
+    exchange(D(a_->n1, a_->n1lo), c, 1, 1);
     mark("conv.body", 18.0 * P * c * c, 12.0 * P * c);
-    conv("conv_after_body.weight", O(a_->n1, a_->n1lo), D(a_->attn, a_->attnlo), pl.hp, pl.wp, eb);
+    conv_res("conv_after_body.weight", O(a_->n1, a_->n1lo), c, D(a_->attn, a_->attnlo), c, 1, false, eb);
     // Head: conv + LeakyReLU, then per block a conv whose store does the PixelShuffle.
     Epi eh;
     eh.bias = W("conv_before_upsample.0.bias");
     eh.act = ACT_LEAKY;
+    exchange(D(a_->attn, a_->attnlo), c, 1, 1);
     mark("conv.head", 18.0 * P * c * feat, 4.0 * P * (c + feat));
-    conv("conv_before_upsample.0.weight", O(a_->attn, a_->attnlo), D(a_->headA, a_->headAlo), pl.hp, pl.wp, eh);
+    conv_res("conv_before_upsample.0.weight", O(a_->attn, a_->attnlo), c, D(a_->headA, a_->headAlo), feat, 1, false,
+             eh);
     float *cur = a_->headA, *curlo = a_->headAlo;
     float *nxt = a_->headB, *nxtlo = a_->headBlo;
-    int hh = pl.hp, ww = pl.wp;
+    int hh = pl.rows, ww = pl.wp, res = 1;
     auto blocks = wt_.up_blocks();
     for (size_t i = 0; i < blocks.size(); ++i) {
         Epi eu;
         eu.bias = W("upsample." + std::to_string(2 * i) + ".bias");
         eu.shuffle = blocks[i].first;
+        exchange(D(cur, curlo), feat, res, 1);
         mark("conv.up", 18.0 * hh * ww * feat * blocks[i].second, 4.0 * hh * ww * (feat + blocks[i].second));
-        conv("upsample." + std::to_string(2 * i) + ".weight", O(cur, curlo), D(nxt, nxtlo), hh, ww, eu);
+        conv_res("upsample." + std::to_string(2 * i) + ".weight", O(cur, curlo), feat, D(nxt, nxtlo), feat, res,
+                 false, eu);
         hh *= blocks[i].first;
         ww *= blocks[i].first;
+        res *= blocks[i].first;
         std::swap(cur, nxt);
         std::swap(curlo, nxtlo);
     }
@@ -507,8 +628,9 @@ void Engine::enqueue_pass() {
     el.ow = pl.w * wt_.scale;
     el.img_range = wt_.img_range;
     for (int i = 0; i < 3; ++i) el.mean[i] = wt_.mean[i];
+    exchange(D(cur, curlo), feat, res, 1);
     mark("conv.last", 18.0 * hh * ww * feat * 3, 4.0 * hh * ww * (feat + 3));
-    conv("conv_last.weight", O(cur, curlo), Dst{a_->dout, nullptr}, hh, ww, el);
+    conv_res("conv_last.weight", O(cur, curlo), feat, Dst{a_->dout, nullptr}, 3, res, false, el);
     mark(nullptr, 0, 0);
 }
 
@@ -627,7 +749,7 @@ void Engine::forward_device(int n, int h, int w, const float* din, float* dout, 
     for (int i = 0; i < n; ++i) {
         HAT_CUDA(cudaMemcpyAsync(a_->din, din + i * inN, inN * sizeof(float), cudaMemcpyDeviceToDevice, run));
         run_graph(run);
-        HAT_CUDA(cudaMemcpyAsync(dout + i * outN, a_->dout, outN * sizeof(float), cudaMemcpyDeviceToDevice, run));
+        copy_out(dout + i * outN, cudaMemcpyDeviceToDevice, run);
     }
 }
 
@@ -639,7 +761,7 @@ void Engine::forward_host(int n, int h, int w, const float* in, float* out) {
     for (int i = 0; i < n; ++i) {
         HAT_CUDA(cudaMemcpyAsync(a_->din, in + i * inN, inN * sizeof(float), cudaMemcpyHostToDevice, stream_));
         run_graph(stream_);
-        HAT_CUDA(cudaMemcpyAsync(out + i * outN, a_->dout, outN * sizeof(float), cudaMemcpyDeviceToHost, stream_));
+        copy_out(out + i * outN, cudaMemcpyDeviceToHost, stream_);
     }
     HAT_CUDA(cudaStreamSynchronize(stream_));
     check_device_error();

@@ -15,18 +15,20 @@
 
 namespace hat {
 
+class Comm;
+
 // Every device buffer one pass needs, as one list used both to allocate and to
 // predict (the reference's `Sizes`, src/gpu.rs:166-290): a pass allocates exactly
 // `total()` floats, and the memory guard refuses on the same number.
 struct Sizes {
     long x0 = 0, body = 0, xa = 0, xb = 0, n1 = 0, n1lo = 0, cmid = 0, cmidlo = 0, convx = 0, qkv = 0, attn = 0,
          attnlo = 0, hid = 0, hidlo = 0;
-    long chsum = 0, gate = 0, headA = 0, headAlo = 0, headB = 0, headBlo = 0, din = 0, dout = 0;
+    long chsum = 0, casum = 0, gate = 0, headA = 0, headAlo = 0, headB = 0, headBlo = 0, din = 0, dout = 0;
     int cmid_stride = 0;  // channel stride of the CAB's middle plane
     static Sizes of(const Weights& wt, const Plan& p);
     long total() const {
         return x0 + body + xa + xb + n1 + n1lo + cmid + cmidlo + convx + qkv + attn + attnlo + hid + hidlo + chsum +
-               gate + headA + headAlo + headB + headBlo + din + dout;
+               casum + gate + headA + headAlo + headB + headBlo + din + dout;
     }
 };
 
@@ -48,10 +50,30 @@ public:
     std::string profile(int h, int w);
     // Reads (and clears) the tensor-core kernels' error flag; throws if it was set.
     void check_device_error();
+    // Strip sharding: from now on every pass computes only this rank's window-aligned
+    // row strip of the image (Plan::make_strip), exchanging halo rows with the
+    // neighbouring ranks over NCCL; `id` is the communicator's unique id (the same on
+    // every rank). The output rows of the other ranks are not written.
+    void attach_strip(int rank, int n, const void* id, size_t idlen);
+    bool sharded() const { return comm_ != nullptr; }
 
 private:
     struct Acts;
+    Plan plan_for(int h, int w) const;
     void ensure_plan(int h, int w);
+    // Strip mode: fill `n` halo rows on each side of `plane` (`ch` channels, at `res`
+    // times the base resolution) from the neighbours' own rows; top and bottom ranks
+    // wrap around to each other (what the shifted windows need; elsewhere the rows
+    // beyond the image are never read as data). No-op when not sharded.
+    void exchange(float* plane, int ch, int res, int n);
+    void exchange(Dst d, int ch, int res, int n);
+    // A 3x3 conv over a plane at `res` times the base resolution. Sharded, the input is
+    // read over the local rows that hold image data (the halo rows beyond the image's
+    // top or bottom edge are left out, so the conv's zero padding applies there) and
+    // only this strip's own output rows are computed unless `all_rows`.
+    long conv_res(const std::string& wname, Opnd x, int xch, Dst y, int ych, int res, bool all_rows, Epi e);
+    // Copies this pass's output (all of it, or the strip's own rows) from the arena.
+    void copy_out(float* dst, cudaMemcpyKind kind, cudaStream_t st);
     void run_graph(cudaStream_t run);  // the whole pass over the internal din/dout buffers
     void enqueue_pass();               // the launch sequence itself
     void hab(int stage, int blk, const float* in, float* out);
@@ -75,6 +97,7 @@ private:
     bool tap_cab_ = false;
     int tap_ld_ = 0;
     int device_ = 0, mode_ = 0;
+    std::unique_ptr<Comm> comm_;
     bool use_graph_ = true, simt_only_ = false;
     cudaStream_t stream_ = nullptr;
     cudaEvent_t join_ = nullptr;

@@ -158,11 +158,24 @@ __device__ __forceinline__ int band3(int v, int n, int shift) { return v < n - 1
 
 }  // namespace
 
+// Where a launch's windows lie in its plane (the whole padded plane, or one strip of it
+// with halo rows). Window (wy, wx), wy < nwy, holds plane rows (oy + 16wy + y + sy) mod
+// rows and columns (16wx + x + sx) mod wp for y, x < 16 (SA), or the 16x16 queries at
+// (oy + 16wy + y, 16wx + x) with the 24x24 keys 4 rows / columns further out (OCAB,
+// zero outside padded rows 0..ghp-1, local row i being padded row gy0 + i). The shift
+// mask (mshift > 0) labels a query or key by the rolled-frame position
+// ((yr0 + 16wy + y) mod ghp, 16wx + x) against the bands of the ghp x wp plane. Only
+// queries on plane rows [olo, ohi) are written.
+struct AttnGeom {
+    int rows, wp, nwy, oy, sy, sx, ghp, yr0, gy0, olo, ohi, mshift;
+};
+
 // D: head dim (24 or 30); OCA: overlapping attention; TERMS: 3 (parity) or 1 (fast).
 template <int D, bool OCA, int TERMS>
 __global__ void __launch_bounds__(TC_THREADS, 2)
-    k_attn_tc(const float* __restrict__ qkv, const float* __restrict__ table, Dst out, int hp, int wp, int c,
-              int heads, int shift, float scale, long items, int* err) {
+    k_attn_tc(const float* __restrict__ qkv, const float* __restrict__ table, Dst out, const AttnGeom gm, int c,
+              int heads, float scale, long items, int* err) {
+    const int wp = gm.wp;
     constexpr int KS = (D + 7) / 8;                 // k-steps of the QK^T product
     constexpr int NK = OCA ? 576 : 256;             // keys per window
     constexpr int NBLK = NK / KBLK;
@@ -321,7 +334,9 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
             const int win = (int)(rest >> 1), mtile = (int)(rest & 1);
             const int wy = win / nx, wx = win - wy * nx;
             const int qi = mtile * MT + row, qy = qi >> 4, qx = qi & 15;
-            const bool masked = !OCA && shift > 0;
+            const bool masked = !OCA && gm.mshift > 0;
+            const int shift = gm.mshift, ghp = gm.ghp;
+            const int yrw = gm.yr0 + wy * 16;  // rolled-frame row of the window's first row (mod ghp)
             // Bias of key (ky, kx): SA tab[(qy-ky+15)*48 + (qx-kx+15)] = tab[A0 - (ky*48 + kx)];
             // OCAB tab[(ky-qy+15)*48 + (kx-qx+15)] = tab[koff[k] - B0].
             const int A0 = qy * TSTRIDE + qx + 15 * TSTRIDE + 15, B0 = qy * TSTRIDE + qx - 15 * TSTRIDE - 15;
@@ -329,7 +344,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
             // band(wx*16+kx) != t; one 16-bit mask per possible row band.
             uint32_t cm[3] = {0, 0, 0};
             if (masked) {
-                const int lq = band3(wy * 16 + qy, hp, shift) * 3 + band3(wx * 16 + qx, wp, shift);
+                const int lq = band3((yrw + qy) % ghp, ghp, shift) * 3 + band3(wx * 16 + qx, wp, shift);
 #pragma unroll
                 for (int kx = 0; kx < 16; ++kx) {
                     const int bx = band3(wx * 16 + kx, wp, shift);
@@ -355,7 +370,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
                 uint32_t mrow0 = 0, mrow1 = 0;
                 if (masked) {
                     // the block's two key rows ky = 2j, 2j+1
-                    const int b0 = band3(wy * 16 + 2 * j, hp, shift), b1 = band3(wy * 16 + 2 * j + 1, hp, shift);
+                    const int b0 = band3((yrw + 2 * j) % ghp, ghp, shift), b1 = band3((yrw + 2 * j + 1) % ghp, ghp, shift);
                     mrow0 = b0 == 0 ? cm[0] : (b0 == 1 ? cm[1] : cm[2]);  // selects: no local memory
                     mrow1 = b1 == 0 ? cm[0] : (b1 == 1 ? cm[1] : cm[2]);
                 }
@@ -432,19 +447,18 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
             tcf_before();
             bar_arrive(&o_free[ti & 1]);
             const float inv = 1.f / l;
-            long qpos;
-            if (OCA)
-                qpos = (long)(wy * 16 + qy) * wp + wx * 16 + qx;
-            else
-                qpos = (long)((wy * 16 + qy + shift) % hp) * wp + (wx * 16 + qx + shift) % wp;
+            const int qrow = OCA ? gm.oy + wy * 16 + qy : (gm.oy + wy * 16 + qy + gm.sy) % gm.rows;
+            const long qpos = (long)qrow * wp + (OCA ? wx * 16 + qx : (wx * 16 + qx + gm.sx) % wp);
             const long ob = qpos * c + (long)head * D;
-            if (VW == 4) {
+            if (qrow >= gm.olo && qrow < gm.ohi) {  // rows outside [olo, ohi) are a neighbour's
+                if (VW == 4) {
 #pragma unroll
-                for (int i = 0; i < D; i += 4)
-                    put4(out, ob + i, make_float4(ov[i] * inv, ov[i + 1] * inv, ov[i + 2] * inv, ov[i + 3] * inv));
-            } else {
+                    for (int i = 0; i < D; i += 4)
+                        put4(out, ob + i, make_float4(ov[i] * inv, ov[i + 1] * inv, ov[i + 2] * inv, ov[i + 3] * inv));
+                } else {
 #pragma unroll
-                for (int i = 0; i < D; ++i) put(out, ob + i, ov[i] * inv);
+                    for (int i = 0; i < D; ++i) put(out, ob + i, ov[i] * inv);
+                }
             }
             g += NBLK;
         }
@@ -468,12 +482,12 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
             inside = true;
             if (OCA) {
                 const int ky = kk / 24, kx = kk - ky * 24;
-                const int Y = wy * 16 - 4 + ky, X = wx * 16 - 4 + kx;
-                inside = Y >= 0 && Y < hp && X >= 0 && X < wp;
+                const int Y = gm.oy + wy * 16 - 4 + ky, X = wx * 16 - 4 + kx;
+                inside = Y >= 0 && Y < gm.rows && gm.gy0 + Y >= 0 && gm.gy0 + Y < gm.ghp && X >= 0 && X < wp;
                 return inside ? (long)Y * wp + X : 0;
             }
             const int ky = kk >> 4, kx = kk & 15;
-            return (long)((wy * 16 + ky + shift) % hp) * wp + (wx * 16 + kx + shift) % wp;
+            return (long)((gm.oy + wy * 16 + ky + gm.sy) % gm.rows) * wp + (wx * 16 + kx + gm.sx) % wp;
         };
         // n floats of row `src` from column `cc` (zeros past D or outside the plane)
         auto load_cols = [&](const float* src, int cc, bool inside, float* dst, int n) {
@@ -522,11 +536,9 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
             // Q: thread t loads query row t of the item, scaled, split into the SW32 tiles.
             {
                 const int qi = mtile * MT + t, qy = qi >> 4, qx = qi & 15;
-                long qpos;
-                if (OCA)
-                    qpos = (long)(wy * 16 + qy) * wp + wx * 16 + qx;
-                else
-                    qpos = (long)((wy * 16 + qy + shift) % hp) * wp + (wx * 16 + qx + shift) % wp;
+                const long qpos =
+                    OCA ? (long)(gm.oy + wy * 16 + qy) * wp + wx * 16 + qx
+                        : (long)((gm.oy + wy * 16 + qy + gm.sy) % gm.rows) * wp + (wx * 16 + qx + gm.sx) % wp;
                 const float* src = qkv + qpos * c3 + (long)head * D;
                 float qv[KS * 8];
                 load_cols(src, 0, true, qv, 16);
@@ -618,13 +630,39 @@ static void run_tc(const float* qkv, const float* table, Dst out, const Plan& p,
         HAT_CUDA(cudaFuncSetAttribute(k_attn_tc<D, OCA, TERMS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
         configured |= 1u << dev;
     }
-    const long items = (long)p.nw() * heads * 2;
+    // The windows of this launch (see AttnGeom).
+    AttnGeom gm;
+    gm.rows = p.rows;
+    gm.wp = p.wp;
+    gm.ghp = p.hp;
+    gm.gy0 = p.gy0();
+    gm.olo = p.halo;
+    gm.ohi = p.halo + p.own();
+    gm.yr0 = 0;
+    gm.sy = gm.sx = gm.mshift = 0;
+    if (!p.strip()) {
+        gm.nwy = p.hp / 16;
+        gm.oy = 0;
+        if (!OCA) gm.sy = gm.sx = gm.mshift = shift;
+    } else if (OCA || shift == 0) {
+        gm.nwy = p.own() / 16;  // the strip's own windows
+        gm.oy = p.halo;
+    } else {
+        // Shifted windows overlapping the strip: the rolled frame's window rows start at
+        // padded rows 16k + shift; the first one that reaches row r0 starts at r0 - shift.
+        if (p.halo < shift) throw Error(1, "attention: a strip's halo is narrower than the window shift");
+        gm.nwy = p.own() / 16 + 1;
+        gm.oy = p.halo - shift;
+        gm.sx = gm.mshift = shift;
+        gm.yr0 = ((p.r0 - 2 * shift) % p.hp + p.hp) % p.hp;
+    }
+    const long items = (long)gm.nwy * p.nx() * heads * 2;
     int sms = 0;
     HAT_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     // Two CTAs per SM; a multiple of the head count, so every CTA keeps one head (and
     // one bias table).
     long grid = std::min<long>(items, (long)(2 * sms / heads) * heads);
-    k_attn_tc<D, OCA, TERMS><<<(unsigned)grid, TC_THREADS, bytes, st>>>(qkv, table, out, p.hp, p.wp, c, heads, shift,
+    k_attn_tc<D, OCA, TERMS><<<(unsigned)grid, TC_THREADS, bytes, st>>>(qkv, table, out, gm, c, heads,
                                                                         1.f / sqrtf((float)D), items, err);
     HAT_CUDA(cudaGetLastError());
     count_launch();

@@ -61,8 +61,8 @@ __device__ __forceinline__ void epi_store(const Epi& e, const Dst& y, long gm, i
                                           int wid) {
     if (e.planar_out) {
         int py = (int)(gm / wid), px = (int)(gm % wid);
-        if (py < e.oh && px < e.ow)
-            y.hi[((long)gn * e.oh + py) * e.ow + px] =
+        if (py + e.oy0 >= 0 && py + e.oy0 < e.oh && px < e.ow)
+            y.hi[((long)gn * e.oh + py + e.oy0) * e.ow + px] =
                 v / e.img_range + (gn == 0 ? e.mean[0] : gn == 1 ? e.mean[1] : e.mean[2]);
         return;
     }

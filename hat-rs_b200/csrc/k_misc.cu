@@ -8,14 +8,16 @@ thread_local uint64_t* g_launch_counter = nullptr;
 
 // ---------------------------------------------------------------- pre
 // Pre::adjust (src/backend.rs:71-89): edge replication to the padded plane, then
-// `(x - mean) * img_range`, written token-major [hp][wp][3].
-__global__ void k_pre(const float* __restrict__ in, float* __restrict__ out, int h, int w, int hp,
-                      int wp, float m0, float m1, float m2, float range) {
+// `(x - mean) * img_range`, written token-major [rows][wp][3]; local row i is padded row
+// gy0 + i (rows outside the padded plane, a strip's halo at the image edge, are filled
+// by the same clamping and never read as data).
+__global__ void k_pre(const float* __restrict__ in, float* __restrict__ out, int h, int w, int rows,
+                      int wp, int gy0, float m0, float m1, float m2, float range) {
     long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
-    long n = (long)hp * wp;
+    long n = (long)rows * wp;
     if (i >= n) return;
-    int y = (int)(i / wp), x = (int)(i % wp);
-    int sy = min(y, h - 1), sx = min(x, w - 1);
+    int y = gy0 + (int)(i / wp), x = (int)(i % wp);
+    int sy = max(0, min(y, h - 1)), sx = min(x, w - 1);
     long src = (long)sy * w + sx, plane = (long)h * w;
     out[i * 3 + 0] = (in[src] - m0) * range;
     out[i * 3 + 1] = (in[plane + src] - m1) * range;
@@ -25,8 +27,8 @@ __global__ void k_pre(const float* __restrict__ in, float* __restrict__ out, int
 void launch_pre(const float* in, float* out, const Plan& p, const float mean[3], float img_range,
                 cudaStream_t st) {
     long n = p.tokens();
-    k_pre<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(in, out, p.h, p.w, p.hp, p.wp, mean[0], mean[1],
-                                                       mean[2], img_range);
+    k_pre<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(in, out, p.h, p.w, p.rows, p.wp, p.gy0(), mean[0],
+                                                       mean[1], mean[2], img_range);
     HAT_CUDA(cudaGetLastError());
     count_launch();
 }
@@ -37,7 +39,7 @@ void launch_pre(const float* in, float* out, const Plan& p, const float mean[3],
 // once, and this kernel adds each pixel's nine neighbours' taps. One thread per pixel.
 template <int CMAX>
 __global__ void k_tapsum_gelu(const float* __restrict__ taps, int ldt, const float* __restrict__ bias, Dst out,
-                              int ldo, int cout, int hp, int wp) {
+                              int ldo, int cout, int hp, int wp, int ylo, int yhi) {
     const long p = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (p >= (long)hp * wp) return;
     const int y = (int)(p / wp), x = (int)(p - (long)y * wp);
@@ -47,7 +49,7 @@ __global__ void k_tapsum_gelu(const float* __restrict__ taps, int ldt, const flo
 #pragma unroll
     for (int tap = 0; tap < 9; ++tap) {
         const int yy = y + tap / 3 - 1, xx = x + tap % 3 - 1;
-        if (yy < 0 || yy >= hp || xx < 0 || xx >= wp) continue;
+        if (yy < ylo || yy >= yhi || xx < 0 || xx >= wp) continue;
         const float* row = taps + ((long)yy * wp + xx) * ldt + tap * cout;
 #pragma unroll
         for (int co = 0; co < CMAX; ++co)
@@ -62,10 +64,27 @@ __global__ void k_tapsum_gelu(const float* __restrict__ taps, int ldt, const flo
 }
 
 void launch_tapsum_gelu(const float* taps, int ldt, const float* bias, Dst out, int ldo, int cout, int hp, int wp,
-                        cudaStream_t st) {
+                        int ylo, int yhi, cudaStream_t st) {
     if (cout > 8 || ldo > 8 || ldt < 9 * cout) throw Error(1, "tapsum: at most 8 output channels");
     const long n = (long)hp * wp;
-    k_tapsum_gelu<8><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(taps, ldt, bias, out, ldo, cout, hp, wp);
+    k_tapsum_gelu<8><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(taps, ldt, bias, out, ldo, cout, hp, wp, ylo, yhi);
+    HAT_CUDA(cudaGetLastError());
+    count_launch();
+}
+
+// ---------------------------------------------------------------- channel sums
+// sum[c] = the `rows` partial rows [rows][c] added in row order (a strip's part of the
+// channel-attention pool, before the sum over strips).
+__global__ void k_rowsum(const float* __restrict__ partial, long rows, int c, float* __restrict__ sum) {
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < c; j += gridDim.x * blockDim.x) {
+        float s = 0.f;
+        for (long r = 0; r < rows; ++r) s += partial[r * c + j];
+        sum[j] = s;
+    }
+}
+
+void launch_rowsum(const float* partial, long rows, int c, float* sum, cudaStream_t st) {
+    k_rowsum<<<(c + 127) / 128, 128, 0, st>>>(partial, rows, c, sum);
     HAT_CUDA(cudaGetLastError());
     count_launch();
 }

@@ -153,6 +153,7 @@ struct UmmaArgs {
     int stages;
     // conv geometry (MODE 1): plane H x W, channel chunks per tap, patch tiles along x
     int H, W, cchunks, tx;
+    int ty0;         // conv: first 8-row tile row computed
     long mtiles, ntiles;
     Dst y;
     int ldo;         // row stride of the output plane (channels), for plain stores
@@ -167,7 +168,7 @@ __device__ __forceinline__ void tile_row(const UmmaArgs& g, long mt, int trow, l
         m = mt * 128 + trow;
         valid = m < g.M;
     } else {
-        const int py = (int)(mt / g.tx) * 8 + trow / 16, px = (int)(mt % g.tx) * 16 + trow % 16;
+        const int py = (g.ty0 + (int)(mt / g.tx)) * 8 + trow / 16, px = (int)(mt % g.tx) * 16 + trow % 16;
         m = (long)py * g.W + px;
         valid = py < g.H;
     }
@@ -343,7 +344,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         if (TERMS == 3) tma_2d(sAl(s), &tmAl, kel, (int)(mt * 128), &full[s]);
                     } else {
                         const int tap = kb / g.cchunks, cc = kb - tap * g.cchunks;
-                        const int py = (int)(mt / g.tx), px = (int)(mt % g.tx);
+                        const int py = g.ty0 + (int)(mt / g.tx), px = (int)(mt % g.tx);
                         const int c0 = cc * (g.ckb / 4), x0 = px * 16 + tap % 3 - 1, y0 = py * 8 + tap / 3 - 1;
                         tma_3d(sAh(s), &tmAh, c0, x0, y0, &full[s]);
                         if (TERMS == 3) tma_3d(sAl(s), &tmAl, c0, x0, y0, &full[s]);
@@ -422,7 +423,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 m = mt * 128 + row;
                 valid = m < g.M;
             } else {
-                py = (int)(mt / g.tx) * 8 + row / 16;
+                py = (g.ty0 + (int)(mt / g.tx)) * 8 + row / 16;
                 px = (int)(mt % g.tx) * 16 + row % 16;
                 m = (long)py * g.W + px;
                 valid = py < g.H;
@@ -479,12 +480,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     if (e.planar_out) {
                         const int wid = MODE == 0 ? 1 : g.W;
                         const int yy = (int)(m / wid), xx = (int)(m % wid);
-                        const bool inside = yy < e.oh && xx < e.ow;
+                        const bool inside = yy + e.oy0 >= 0 && yy + e.oy0 < e.oh && xx < e.ow;
 #pragma unroll
                         for (int j = 0; j < 16; ++j) {
                             const int n = n0 + c0 + j;
                             if (inside && n < g.N)
-                                g.y.hi[((long)n * e.oh + yy) * e.ow + xx] =
+                                g.y.hi[((long)n * e.oh + yy + e.oy0) * e.ow + xx] =
                                     v[j] / e.img_range + (n == 0 ? e.mean[0] : n == 1 ? e.mean[1] : e.mean[2]);
                         }
                     } else if (e.shuffle) {
@@ -726,7 +727,10 @@ long umma_conv3x3(int mode, Opnd x, const GemmW& w, Dst y, int hgt, int wid, con
     g.H = hgt;
     g.W = wid;
     g.tx = wid / 16;
-    g.mtiles = (long)(hgt / 8) * g.tx;
+    const int ylo = e.y_hi > 0 ? e.y_lo : 0, yhi = e.y_hi > 0 ? e.y_hi : hgt;
+    if (ylo % 8 || yhi % 8 || ylo < 0 || yhi > hgt || ylo >= yhi) throw Error(1, "umma_conv3x3: bad output row range");
+    g.ty0 = ylo / 8;
+    g.mtiles = (long)((yhi - ylo) / 8) * g.tx;
     g.ntiles = g.mtiles * g.ntn;
     if (three)
         launch_k<1, 3>(tah, tal, tbh, tbl, g, e, st);

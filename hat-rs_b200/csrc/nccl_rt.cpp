@@ -1,0 +1,111 @@
+// NCCL bound at run time with dlopen (see nccl_rt.h).
+#include "nccl_rt.h"
+
+#include <dlfcn.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+
+#ifndef HAT_NCCL_LIB
+#define HAT_NCCL_LIB "libnccl.so.2"
+#endif
+
+namespace hat {
+
+namespace {
+
+struct Api {
+    ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*group_start)() = nullptr;
+    ncclResult_t (*group_end)() = nullptr;
+    ncclResult_t (*send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                               cudaStream_t) = nullptr;
+    const char* (*error_string)(ncclResult_t) = nullptr;
+};
+
+template <class F>
+void bind(void* lib, const char* name, F& fn) {
+    fn = reinterpret_cast<F>(dlsym(lib, name));
+    if (!fn) throw Error(3, std::string("nccl: symbol ") + name + " not found");
+}
+
+const Api& api() {
+    static Api a;
+    static std::once_flag once;
+    static std::string failure;
+    std::call_once(once, [] {
+        // The copy the process already loaded (torch's), else the search path, else the
+        // path recorded at build time.
+        void* lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+        if (!lib) lib = dlopen("libnccl.so.2", RTLD_NOW);
+        if (!lib) lib = dlopen(HAT_NCCL_LIB, RTLD_NOW);
+        if (!lib) {
+            failure = std::string("nccl: cannot open libnccl.so.2 (") + (dlerror() ? dlerror() : "?") + ")";
+            return;
+        }
+        try {
+            bind(lib, "ncclGetUniqueId", a.get_unique_id);
+            bind(lib, "ncclCommInitRank", a.comm_init_rank);
+            bind(lib, "ncclCommDestroy", a.comm_destroy);
+            bind(lib, "ncclGroupStart", a.group_start);
+            bind(lib, "ncclGroupEnd", a.group_end);
+            bind(lib, "ncclSend", a.send);
+            bind(lib, "ncclRecv", a.recv);
+            bind(lib, "ncclAllReduce", a.all_reduce);
+            bind(lib, "ncclGetErrorString", a.error_string);
+        } catch (const Error& e) {
+            failure = e.what();
+        }
+    });
+    if (!failure.empty()) throw Error(3, failure);
+    return a;
+}
+
+void check(ncclResult_t r, const char* what) {
+    if (r != ncclSuccess) throw Error(3, std::string("nccl: ") + what + " failed: " + api().error_string(r));
+}
+
+}  // namespace
+
+void nccl_unique_id(void* out, size_t len) {
+    if (len < sizeof(ncclUniqueId)) throw Error(1, "nccl: the unique id needs 128 bytes");
+    ncclUniqueId id;
+    check(api().get_unique_id(&id), "ncclGetUniqueId");
+    memcpy(out, &id, sizeof id);
+}
+
+Comm::Comm(int rank, int n, const void* id, size_t idlen, int device) : rank_(rank), n_(n) {
+    if (n < 1 || rank < 0 || rank >= n) throw Error(1, "nccl: bad rank / size");
+    if (!id || idlen < sizeof(ncclUniqueId)) throw Error(1, "nccl: the unique id needs 128 bytes");
+    ncclUniqueId uid;
+    memcpy(&uid, id, sizeof uid);
+    HAT_CUDA(cudaSetDevice(device));
+    check(api().comm_init_rank(&comm_, n, uid, rank), "ncclCommInitRank");
+}
+
+Comm::~Comm() {
+    if (comm_) api().comm_destroy(comm_);
+}
+
+void Comm::group_start() { check(api().group_start(), "ncclGroupStart"); }
+void Comm::group_end() { check(api().group_end(), "ncclGroupEnd"); }
+
+void Comm::send(const float* buf, size_t count, int peer, cudaStream_t st) {
+    check(api().send(buf, count, ncclFloat32, peer, comm_, st), "ncclSend");
+}
+
+void Comm::recv(float* buf, size_t count, int peer, cudaStream_t st) {
+    check(api().recv(buf, count, ncclFloat32, peer, comm_, st), "ncclRecv");
+}
+
+void Comm::allreduce_sum(float* buf, size_t count, cudaStream_t st) {
+    check(api().all_reduce(buf, buf, count, ncclFloat32, ncclSum, comm_, st), "ncclAllReduce");
+}
+
+}  // namespace hat

@@ -1,0 +1,36 @@
+// NCCL for the strip-sharded pass: the library is opened at run time (the process
+// already has it loaded when torch.distributed runs NCCL), so libhat_b200 itself has no
+// link dependency on it. Only the calls the halo exchange and the channel-sum
+// all-reduce use are bound.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <string>
+
+namespace hat {
+
+// A communicator over `n` ranks, one GPU each, created collectively from one unique id.
+class Comm {
+public:
+    Comm(int rank, int n, const void* id, size_t idlen, int device);
+    ~Comm();
+    int rank() const { return rank_; }
+    int size() const { return n_; }
+    // Inside group(): the calls are matched per peer in the order they are posted.
+    void group_start();
+    void group_end();
+    void send(const float* buf, size_t count, int peer, cudaStream_t st);
+    void recv(float* buf, size_t count, int peer, cudaStream_t st);
+    void allreduce_sum(float* buf, size_t count, cudaStream_t st);
+
+private:
+    int rank_, n_;
+    ncclComm_t comm_ = nullptr;
+};
+
+// ncclGetUniqueId into `out` (at least sizeof(ncclUniqueId) = 128 bytes).
+void nccl_unique_id(void* out, size_t len);
+
+}  // namespace hat

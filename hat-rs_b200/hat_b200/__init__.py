@@ -72,6 +72,9 @@ SIGNATURES = {
     "hat_b200_window_attention": (_I, [_I, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "hat_b200_overlap_attention": (_I, [_I, _P, _P, _P, _I, _I, _I, _I, _P]),
     "hat_b200_linear_noalloc": (_I, [_I, _P, _P, _P, _P, _I, _I, _I, _P, _C, _S]),
+    "hat_b200_strip_rows": (_I, [_I, _I, _I, ctypes.POINTER(_I), ctypes.POINTER(_I)]),
+    "hat_b200_nccl_unique_id": (_I, [_P, _S, _C, _S]),
+    "hat_b200_attach_strip": (_I, [_P, _I, _I, _P, _S, _C, _S]),
     "hat_b200_launch_count": (ctypes.c_uint64, [_P]),
     "hat_b200_profile": (_I, [_P, _I, _I, _C, _S, _C, _S]),
 }
@@ -186,6 +189,12 @@ class B200:
                                              ctypes.c_void_p(d_out), ctypes.c_void_p(stream), e,
                                              len(e)), e)
 
+    def attach_strip(self, rank: int, nranks: int, uid: bytes) -> None:
+        """Shard every later pass over `nranks` GPUs by row strips (collective: all ranks
+        call it with the same NCCL unique id); each pass then writes this rank's rows."""
+        e = _err()
+        _check(lib().hat_b200_attach_strip(self._h, rank, nranks, uid, len(uid), e, len(e)), e)
+
     def footprint_bytes(self, h: int, w: int) -> int:
         return int(lib().hat_b200_footprint_bytes(self._h, h, w))
 
@@ -209,6 +218,22 @@ def linear(mode, x, w, b, y, m, n, k, stream=0):
     rc = lib().hat_b200_linear(mode, x, w, b, y, m, n, k, stream)
     if rc:
         raise HatError(rc, "linear launch failed")
+
+
+def strip_rows(height: int, nranks: int, rank: int):
+    """Padded rows [r0, r1) of rank `rank`'s strip (window-aligned, as equal as possible)."""
+    r0, r1 = _I(), _I()
+    rc = lib().hat_b200_strip_rows(height, nranks, rank, ctypes.byref(r0), ctypes.byref(r1))
+    if rc:
+        raise HatError(rc, f"no strip plan for {height} rows over {nranks} ranks")
+    return r0.value, r1.value
+
+
+def nccl_unique_id() -> bytes:
+    """An NCCL unique id for hat_b200_attach_strip (made on one rank, shared with all)."""
+    buf, e = ctypes.create_string_buffer(128), _err()
+    _check(lib().hat_b200_nccl_unique_id(buf, 128, e, len(e)), e)
+    return buf.raw
 
 
 def linear_noalloc(mode, x, w, b, y, m, n, k, stream=0):

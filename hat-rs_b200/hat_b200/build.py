@@ -25,6 +25,21 @@ FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", 
          "--expt-relaxed-constexpr", "-I", str(INC), "-I", str(SRC)]
 
 
+def _nccl_dirs():
+    """nccl.h and libnccl.so.2 of the NCCL wheel torch uses (strip sharding binds NCCL at
+    run time; the header gives the types, the path is the last place it looks)."""
+    try:
+        import nvidia.nccl as nc
+        root = Path(list(nc.__path__)[0])
+    except Exception:
+        root = Path("/usr")
+    return root / "include", root / "lib" / "libnccl.so.2"
+
+
+_NCCL_INC, _NCCL_LIB = _nccl_dirs()
+FLAGS += ["-I", str(_NCCL_INC), f'-DHAT_NCCL_LIB="{_NCCL_LIB}"']
+
+
 def _sources():
     return sorted([p for p in SRC.iterdir() if p.suffix in (".cu", ".cpp")])
 
@@ -60,7 +75,7 @@ def build(verbose: bool = False) -> Path:
     newest = max(o.stat().st_mtime for o in objs)
     if LIB.exists() and LIB.stat().st_mtime >= newest:
         return LIB
-    cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-cudart", "static"]
+    cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-cudart", "static", "-ldl"]
     if verbose:
         print(" ".join(cmd), file=sys.stderr)
     r = subprocess.run(cmd, capture_output=True, text=True)

@@ -133,6 +133,28 @@ HAT_B200_API int hat_b200_window_attention(int mode, const float* qkv, const flo
 HAT_B200_API int hat_b200_overlap_attention(int mode, const float* qkv, const float* table, float* out,
                                int hp, int wp, int c, int heads, void* stream);
 
+/* Strip sharding of one large image over several GPUs (no counterpart in the reference,
+ * which runs on one device). Padded rows are split into window-aligned strips
+ * as equal as the 16-row windows allow (the first (hp/16) % nranks ranks take one window
+ * row more); this writes rank `rank`'s padded rows [*r0, *r1) for an image `height`
+ * rows high. No device needed. */
+HAT_B200_API int hat_b200_strip_rows(int height, int nranks, int rank, int* r0, int* r1);
+
+/* ncclGetUniqueId into `id` (idlen >= 128): rank 0 makes it, every rank passes the same
+ * bytes to hat_b200_attach_strip. */
+HAT_B200_API int hat_b200_nccl_unique_id(void* id, size_t idlen, char* err, size_t errlen);
+
+/* Joins the handle to an NCCL communicator of `nranks` ranks (collective: every rank calls
+ * it with the same id, one handle per GPU). From then on each forward computes only this
+ * rank's row strip of the image: the input is the whole image on every rank, the output
+ * buffer is the whole output and only this rank's rows of it are written (output rows
+ * [scale*r0, scale*r1) cropped to the image). Halo rows are exchanged with the
+ * neighbouring ranks before every layer that reads across the strip edge, and the
+ * channel-attention means are summed over ranks; the result equals the unsharded pass up
+ * to the order of those sums. Needs the tensor-core modes. */
+HAT_B200_API int hat_b200_attach_strip(hat_b200* h, int rank, int nranks, const void* id, size_t idlen, char* err,
+                                       size_t errlen);
+
 /* hat_b200_linear without device allocation. No counterpart in the reference: it is for
  * callers that may not allocate device memory on this path (device memory already
  * reserved by another allocator, latency-critical loops, callers that must know the
