@@ -7,7 +7,11 @@ Metric: output Mpix/s (BASELINE.json `metric`). One process per GPU; for N > 1 e
 rank runs its own image (the batch is split per GPU, no collective on the data path),
 so scaling is weak.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+`--shard strip` measures the other multi-GPU mode instead:
+ONE HAT-L x4 1024x1024 image split into window-aligned row strips over the N GPUs, with
+NCCL halo exchange between neighbours; scaling is strong (the same image at every N).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--shard batch|strip]
 
 `value`: K timed steps of `hat_b200_forward_device` with the input already in HBM, each
 step timed with CUDA events on the launching stream, L2 flushed between steps; the max
@@ -33,13 +37,32 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "hat-rs_b200"))
 sys.path.insert(0, str(ROOT))
 
-VARIANT, SCALE, H, W = "hat-s", 4, 512, 512
-WEIGHT_SEED, CFG_ID = 2024, 2
-METRIC = "output Mpix/s, HAT-S x4 512x512 input (fp32-parity mode)"
-REF_GPU_MPIXS = 8.6  # seconds, README.md:18 of the reference (HAT-S x4 512x512, GPU, hardware unstated)
-BASELINE_MPIXS = (H * SCALE) * (W * SCALE) / 1e6 / REF_GPU_MPIXS
-# Algorithmic FLOPs of HAT-S x4 per padded input pixel (QK^T and PV counted once).
-FLOPS_PER_PIX = 26.67e6
+# The two workloads: (variant, scale, H, W, config id, algorithmic FLOPs per padded input
+# pixel with QK^T and PV counted once).
+WORKLOADS = {
+    "batch": ("hat-s", 4, 512, 512, 2, 26.67e6),
+    "strip": ("hat-l", 4, 1024, 1024, 4, 99.12e6),
+}
+VARIANT, SCALE, H, W, CFG_ID, FLOPS_PER_PIX = WORKLOADS["batch"]
+WEIGHT_SEED = 2024
+REF_GPU_S = 8.6  # seconds, README.md:18 of the reference (HAT-S x4 512x512, GPU, hardware unstated)
+
+
+def select_workload(shard: str):
+    global VARIANT, SCALE, H, W, CFG_ID, FLOPS_PER_PIX
+    VARIANT, SCALE, H, W, CFG_ID, FLOPS_PER_PIX = WORKLOADS[shard]
+
+
+def metric_name(mode: str = "parity") -> str:
+    return f"output Mpix/s, {VARIANT.upper()} x{SCALE} {H}x{W} input (fp32-{mode} mode)" if mode == "parity" \
+        else f"output Mpix/s, {VARIANT.upper()} x{SCALE} {H}x{W} input ({mode} mode)"
+
+
+def baseline_mpixs():
+    """The reference's published number for this metric, when there is one."""
+    if (VARIANT, SCALE, H, W) == ("hat-s", 4, 512, 512):
+        return (H * SCALE) * (W * SCALE) / 1e6 / REF_GPU_S
+    return None
 # DRAM bytes (read + write) per launch of a kernel kind at this workload, from one ncu
 # capture (dram__bytes_read.sum + dram__bytes_write.sum); profiles/ holds the capture's
 # summary and command. Kinds without a capture report null.
@@ -143,10 +166,10 @@ def run_reference(args):
     value = mpix / t
     cores = os.cpu_count()
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "Mpix/s", "n_gpus": ws,
+        "impl": "reference", "metric": metric_name(), "value": value, "unit": "Mpix/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-        "config": {"workload": f"HAT-S x4 {crop}x{crop} crop of the 512x512 image per step (CPU)",
+        "config": {"workload": f"{VARIANT.upper()} x{SCALE} {crop}x{crop} crop of the {H}x{W} image per step (CPU)",
                    "variant": VARIANT, "scale": SCALE},
         "cpu_baseline": {"value": value, "unit": "Mpix/s", "cores": cores, "kind": "port",
                          "sample": f"numpy/OpenBLAS float32 restatement of the reference forward "
@@ -177,7 +200,16 @@ def run_ours(args):
     ck = make_checkpoint(tmp)
     mode = hat_b200.MODE_FAST if args.mode == "fast" else hat_b200.MODE_PARITY
     be = hat_b200.B200(ck, device=local, mode=mode, use_graph=True)
-    img = synth.image(H, W, CFG_ID * 1000 + rank)
+    strip = args.shard == "strip"
+    if strip and ws > 1:
+        # One NCCL communicator for the library's halo exchange; rank 0 makes its id.
+        uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+        if rank == 0:
+            uid.copy_(torch.frombuffer(bytearray(hat_b200.nccl_unique_id()), dtype=torch.uint8))
+        dist.broadcast(uid, 0)
+        be.attach_strip(rank, ws, bytes(uid.cpu().numpy().tobytes()))
+    # Batch: every rank its own image. Strip: every rank the same image, its own rows.
+    img = synth.image(H, W, CFG_ID * 1000 + (0 if strip else rank))
     # A dedicated stream: the library's kernels run on it and the timing events are
     # recorded on it (torch's default stream is the legacy NULL stream).
     st = torch.cuda.Stream()
@@ -215,8 +247,13 @@ def run_ours(args):
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         t_dev = float(tt.item())
     out_mpix = (H * SCALE) * (W * SCALE) / 1e6
-    value = ws * args.steps * out_mpix / t_dev
+    images = 1 if strip else ws  # images the whole job finishes per step
+    value = images * args.steps * out_mpix / t_dev
 
+    d2h_rows = H * SCALE
+    if strip and ws > 1:
+        r0, r1 = hat_b200.strip_rows(H, ws, rank)
+        d2h_rows = min(r1 * SCALE, H * SCALE) - r0 * SCALE
     # e2e: the public host entry point from pinned host memory, wall clock around it.
     h_in = torch.from_numpy(img).pin_memory()
     h_out = torch.empty((3, H * SCALE, W * SCALE)).pin_memory()
@@ -238,11 +275,12 @@ def run_ours(args):
         tt = torch.tensor([t_e2e], device="cuda")
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         t_e2e = float(tt.item())
-    e2e = ws * args.steps * out_mpix / t_e2e
+    e2e = images * args.steps * out_mpix / t_e2e
 
     # Roofline of the dominant kernel, from an event-timed eager pass on this stream.
     prof = be.profile(H, W)
-    top_kind, top = max(prof.items(), key=lambda kv: kv[1]["ms"])
+    top_kind, top = max(((k, v) for k, v in prof.items() if v["flops"] > 0 or v["bytes"] > 0),
+                        key=lambda kv: kv[1]["ms"])
     hbm, tf, src = peaks()
     total_ms = sum(v["ms"] for v in prof.values())
     if top["flops"] > 0:
@@ -260,7 +298,7 @@ def run_ours(args):
         roof = {"kernel": top_kind, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                 "frac": achieved / hbm, "traffic": None, "peak_source": f"{src} HBM copy",
                 "share_of_pass": top["ms"] / total_ms, "launches": top["launches"]}
-    if top_kind in NCU_TRAFFIC_BYTES:
+    if top_kind in NCU_TRAFFIC_BYTES and not strip and (VARIANT, H, W) == ("hat-s", 512, 512):
         roof["traffic"] = NCU_TRAFFIC_BYTES[top_kind]
         roof["alg_bytes_per_launch"] = top["bytes"] / max(top["launches"], 1)
     cpu = None
@@ -271,23 +309,31 @@ def run_ours(args):
                          f"crop of the workload image, one forward, {dt:.1f} s"}
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": "Mpix/s", "n_gpus": ws, "steps": args.steps,
-            "warmup": max(args.warmup, 3), "ms_per_step": t_dev / args.steps * 1e3,
-            "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": value / BASELINE_MPIXS, "dtype": "fp32" if mode == 0 else "tf32",
+            "metric": metric_name(args.mode), "value": value, "unit": "Mpix/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": t_dev / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "strong" if strip else "weak",
+            "vs_baseline": value / baseline_mpixs() if baseline_mpixs() else None,
+            "dtype": "fp32" if mode == 0 else "tf32",
             "data": "synthetic",
-            "config": {"workload": "HAT-S x4, one 512x512 image per GPU (configs[1])",
-                       "variant": VARIANT, "scale": SCALE, "h": H, "w": W, "images_per_gpu": 1,
-                       "mode": args.mode, "parallelism": f"dp{ws} (independent images)",
+            "config": {"workload": (f"{VARIANT.upper()} x{SCALE}, one {H}x{W} image split into row strips over "
+                                    f"{ws} GPU(s) (configs[3])") if strip else
+                                   f"{VARIANT.upper()} x{SCALE}, one {H}x{W} image per GPU (configs[1])",
+                       "variant": VARIANT, "scale": SCALE, "h": H, "w": W,
+                       "images_per_gpu": (1.0 / ws) if strip else 1,
+                       "mode": args.mode,
+                       "parallelism": (f"strip{ws} (row strips, NCCL halo exchange)" if strip
+                                       else f"dp{ws} (independent images)"),
                        "l2": "256 MB buffer written between timed steps (> 126 MB L2)"},
+            # per rank: the whole input image in, this rank's output rows out (all of them
+            # unless strip-sharded)
             "e2e": {"value": e2e, "unit": "Mpix/s", "h2d_bytes_per_step": 3 * H * W * 4,
-                    "d2h_bytes_per_step": 3 * H * SCALE * W * SCALE * 4},
+                    "d2h_bytes_per_step": 3 * d2h_rows * W * SCALE * 4},
             "gpu_launches": launches,
             "roofline": roof,
             "cpu_baseline": cpu,
             "clocks": clk,
             "kernel_ms_per_pass": {k: round(v["ms"], 3) for k, v in sorted(prof.items())},
-            "alg_tflops_per_s": FLOPS_PER_PIX * H * W / (t_dev / args.steps) / 1e12,
+            "alg_tflops_per_s": images * FLOPS_PER_PIX * H * W / (t_dev / args.steps) / 1e12,
         }
         print(json.dumps(line), flush=True)
     be.close()
@@ -305,7 +351,9 @@ def main():
     ap.add_argument("--mode", default="parity", choices=["parity", "fast"])
     ap.add_argument("--ref-crop", type=int, default=96)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--shard", default="batch", choices=["batch", "strip"])
     args = ap.parse_args()
+    select_workload(args.shard)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)
