@@ -8,6 +8,7 @@
 #include "../../include/hat_b200.h"
 #include "engine.h"
 #include "nccl_rt.h"
+#include "tile.h"
 
 using namespace hat;
 
@@ -157,6 +158,44 @@ int hat_b200_profile(hat_b200* h, int height, int width, char* json, size_t json
     return guarded(err, errlen, [&] {
         std::string j = h->eng->profile(height, width);
         set_err(json, jsonlen, j);
+    });
+}
+
+int hat_b200_forward_tiled(hat_b200* h, int height, int width, const float* in, float* out, int tile, int margin,
+                           hat_b200_tiling* info, char* err, size_t errlen) {
+    if (!h || !in || !out) {
+        set_err(err, errlen, "hat_b200_forward_tiled: null handle or buffer");
+        return HAT_B200_EINVAL;
+    }
+    return guarded(err, errlen, [&] {
+        if (h->eng->sharded()) throw Error(1, "tiling: the handle is strip-sharded");
+        Tiling t = tile_forward(*h->eng, height, width, in, out, tile, margin);
+        if (info) {
+            info->tile = t.tile;
+            info->margin = t.margin;
+            info->scale = t.scale;
+            info->tiles = t.tiles;
+            info->largest_h = t.largest_h;
+            info->largest_w = t.largest_w;
+        }
+    });
+}
+
+int hat_b200_auto_tile(int height, int width, int window, uint64_t budget_bytes, uint64_t per_pixel_floats,
+                       uint64_t constant_floats, int margin, int* tile) {
+    if (height <= 0 || width <= 0 || window <= 0 || margin < 0 || !tile) return HAT_B200_EINVAL;
+    auto t = auto_tile(height, width, window, budget_bytes, per_pixel_floats, constant_floats, margin);
+    if (!t) return HAT_B200_ENOMEM;
+    *tile = *t;
+    return HAT_B200_OK;
+}
+
+int hat_b200_gpu_auto_tile(const hat_b200* h, int height, int width, int* tile, char* err, size_t errlen) {
+    if (!h || !tile) return HAT_B200_EINVAL;
+    return guarded(err, errlen, [&] {
+        auto t = gpu_auto_tile(*h->eng, height, width);
+        if (!t) throw Error(4, "one window does not fit the device's free memory");
+        *tile = *t;
     });
 }
 

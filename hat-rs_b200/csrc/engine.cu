@@ -284,6 +284,7 @@ void Engine::attach_strip(int rank, int n, const void* id, size_t idlen) {
         HAT_CUDA(cudaStreamSynchronize(stream_));
         cudaFree(arena_);
         arena_ = nullptr;
+        arena_floats_ = 0;
     }
     have_plan_ = false;
     comm_.reset(new Comm(rank, n, id, idlen, device_));
@@ -361,7 +362,7 @@ void Engine::check_memory(int h, int w) const {
     HAT_CUDA(cudaSetDevice(device_));
     HAT_CUDA(cudaMemGetInfo(&fr, &tot));
     // The engine's current arena is released before a new plan allocates, so it counts.
-    double avail = (double)fr + (have_plan_ ? (double)sizes_.total() * sizeof(float) : 0.0);
+    double avail = (double)fr + (arena_ ? (double)arena_floats_ * sizeof(float) : 0.0);
     if (need > avail) {
         std::ostringstream o;
         o << "not enough video memory for a " << w << "x" << h << " pass on the GPU\n"
@@ -388,19 +389,26 @@ void Engine::check_device_error() {
 void Engine::ensure_plan(int h, int w) {
     Plan p = plan_for(h, w);
     if (have_plan_ && p == plan_) return;
-    check_memory(h, w);
+    Sizes s = Sizes::of(wt_, p);
     if (graph_) {
         cudaGraphExecDestroy(graph_);
         graph_ = nullptr;
     }
-    if (arena_) {
+    if (arena_ && (size_t)s.total() <= arena_floats_) {
+        // A plan no larger than the arena (a smaller tile, say) is carved out of it.
         HAT_CUDA(cudaStreamSynchronize(stream_));
-        cudaFree(arena_);
-        arena_ = nullptr;
-        have_plan_ = false;
+    } else {
+        check_memory(h, w);
+        if (arena_) {
+            HAT_CUDA(cudaStreamSynchronize(stream_));
+            cudaFree(arena_);
+            arena_ = nullptr;
+            arena_floats_ = 0;
+            have_plan_ = false;
+        }
+        HAT_CUDA(cudaMalloc(&arena_, (size_t)s.total() * sizeof(float)));
+        arena_floats_ = (size_t)s.total();
     }
-    Sizes s = Sizes::of(wt_, p);
-    HAT_CUDA(cudaMalloc(&arena_, (size_t)s.total() * sizeof(float)));
     HAT_CUDA(cudaMemsetAsync(arena_, 0, (size_t)s.total() * sizeof(float), stream_));
     a_.reset(new Acts);
     float* q = arena_;

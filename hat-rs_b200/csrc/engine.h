@@ -109,6 +109,7 @@ private:
     bool have_plan_ = false;
     Sizes sizes_;
     float* arena_ = nullptr;
+    size_t arena_floats_ = 0;  // capacity of the arena (plans no larger reuse it)
     std::unique_ptr<Acts> a_;
     cudaGraphExec_t graph_ = nullptr;
     int eager_runs_ = 0;

@@ -73,6 +73,10 @@ SIGNATURES = {
     "hat_b200_overlap_attention": (_I, [_I, _P, _P, _P, _I, _I, _I, _I, _P]),
     "hat_b200_linear_noalloc": (_I, [_I, _P, _P, _P, _P, _I, _I, _I, _P, _C, _S]),
     "hat_b200_strip_rows": (_I, [_I, _I, _I, ctypes.POINTER(_I), ctypes.POINTER(_I)]),
+    "hat_b200_forward_tiled": (_I, [_P, _I, _I, _P, _P, _I, _I, _P, _C, _S]),
+    "hat_b200_auto_tile": (_I, [_I, _I, _I, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, _I,
+                                ctypes.POINTER(_I)]),
+    "hat_b200_gpu_auto_tile": (_I, [_P, _I, _I, ctypes.POINTER(_I), _C, _S]),
     "hat_b200_nccl_unique_id": (_I, [_P, _S, _C, _S]),
     "hat_b200_attach_strip": (_I, [_P, _I, _I, _P, _S, _C, _S]),
     "hat_b200_launch_count": (ctypes.c_uint64, [_P]),
@@ -189,6 +193,21 @@ class B200:
                                              ctypes.c_void_p(d_out), ctypes.c_void_p(stream), e,
                                              len(e)), e)
 
+    def forward_tiled(self, h: int, w: int, image: np.ndarray, tile: int, margin: int):
+        """tile::forward: `--tile` / `--mem` cores with a margin of context; returns
+        (planar output, tiling info dict)."""
+        x = np.ascontiguousarray(image, dtype=np.float32).reshape(3, h, w)
+        out = np.empty((3, h * self.scale, w * self.scale), np.float32)
+        info, e = Tiling(), _err()
+        _check(lib().hat_b200_forward_tiled(self._h, h, w, _ptr(x), _ptr(out), tile, margin, ctypes.byref(info),
+                                            e, len(e)), e)
+        return out, info.as_dict()
+
+    def gpu_auto_tile(self, h: int, w: int) -> int:
+        t, e = _I(), _err()
+        _check(lib().hat_b200_gpu_auto_tile(self._h, h, w, ctypes.byref(t), e, len(e)), e)
+        return t.value
+
     def attach_strip(self, rank: int, nranks: int, uid: bytes) -> None:
         """Shard every later pass over `nranks` GPUs by row strips (collective: all ranks
         call it with the same NCCL unique id); each pass then writes this rank's rows."""
@@ -218,6 +237,26 @@ def linear(mode, x, w, b, y, m, n, k, stream=0):
     rc = lib().hat_b200_linear(mode, x, w, b, y, m, n, k, stream)
     if rc:
         raise HatError(rc, "linear launch failed")
+
+
+class Tiling(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in ("tile", "margin", "scale", "tiles", "largest_h", "largest_w")]
+
+    def as_dict(self):
+        return {n: getattr(self, n) for n, _ in self._fields_}
+
+
+def auto_tile(h: int, w: int, win: int, budget_bytes: int, per_pixel_floats: int, constant_floats: int,
+              margin: int):
+    """tile::auto_tile: the core side for a memory budget, or None when one window does not fit."""
+    t = _I()
+    rc = lib().hat_b200_auto_tile(h, w, win, budget_bytes, per_pixel_floats, constant_floats, margin,
+                                  ctypes.byref(t))
+    if rc == E_NOMEM:
+        return None
+    if rc:
+        raise HatError(rc, "auto_tile: bad arguments")
+    return t.value
 
 
 def strip_rows(height: int, nranks: int, rank: int):

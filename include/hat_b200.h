@@ -133,6 +133,35 @@ HAT_B200_API int hat_b200_window_attention(int mode, const float* qkv, const flo
 HAT_B200_API int hat_b200_overlap_attention(int mode, const float* qkv, const float* table, float* out,
                                int hp, int wp, int c, int heads, void* stream);
 
+/* What a tiled pass did (src/tile.rs:29-43): the core side and margin used (window
+ * multiples), the scale, the number of tiles and the largest sub-image a forward ran on. */
+typedef struct hat_b200_tiling {
+    int tile, margin, scale, tiles, largest_h, largest_w;
+} hat_b200_tiling;
+
+/* tile::forward (src/tile.rs:47-105), the `--tile` / `--mem` path: the image is cut into
+ * window-aligned `tile`-pixel cores (rounded up to the window), each run as its own pass
+ * on the core plus `margin` pixels of context (rounded up to the window, clamped to the
+ * image, edge-replicated beyond it), and the cores are copied into `out` without
+ * blending. Host buffers as hat_b200_forward; `info` may be NULL. The CLI's margin is two
+ * windows (src/main.rs:303-305). Not available on a strip-sharded handle. */
+HAT_B200_API int hat_b200_forward_tiled(hat_b200* h, int height, int width, const float* in, float* out, int tile,
+                                        int margin, hat_b200_tiling* info, char* err, size_t errlen);
+
+/* tile::auto_tile (src/tile.rs:147-184): the largest window-multiple core whose
+ * sub-image (core + 2 * margin on a side) fits `budget_bytes` at `per_pixel_floats` floats
+ * per pixel plus `constant_floats`, capped at the image. Returns HAT_B200_ENOMEM when not
+ * even one window fits. No device needed. For `--mem`, per_pixel_floats is
+ * hat_b200_footprint_bytes / 4 divided by the padded pixel count, and constant 0. */
+HAT_B200_API int hat_b200_auto_tile(int height, int width, int window, uint64_t budget_bytes,
+                                    uint64_t per_pixel_floats, uint64_t constant_floats, int margin, int* tile);
+
+/* gpu_auto_tile (src/main.rs:107-140): the tile when neither --tile nor --mem is given,
+ * halving from the larger image side until the memory guard admits a pass of that size
+ * on the handle's device; *tile >= the larger side means the whole image fits. */
+HAT_B200_API int hat_b200_gpu_auto_tile(const hat_b200* h, int height, int width, int* tile, char* err,
+                                        size_t errlen);
+
 /* Strip sharding of one large image over several GPUs (no counterpart in the reference,
  * which runs on one device). Padded rows are split into window-aligned strips
  * as equal as the 16-row windows allow (the first (hp/16) % nranks ranks take one window
