@@ -455,6 +455,15 @@ void Engine::mlp(const std::string& p, float* x, Dst out) {
     const int c = wt_.embed, hid = wt_.mlp_ratio * c;
     mark("layernorm", 0, 8.0 * P * c);
     launch_layernorm(x, W(p + ".norm2.weight"), W(p + ".norm2.bias"), D(a_->n1, a_->n1lo), P, c, stream_);
+    const GemmW& w1 = G(p + ".mlp.fc1.weight");
+    const GemmW& w2 = G(p + ".mlp.fc2.weight");
+    if (!simt_only_ && umma_mlp_ok(w1, w2)) {
+        // fc1 + GELU + fc2 + residual in one launch, the hidden plane never written out.
+        mark("mlp.fused", 4.0 * P * hid * c, 4.0 * P * (2 * c + c));
+        umma_mlp(mode_, O(a_->n1, a_->n1lo), w1, W(p + ".mlp.fc1.bias"), w2, W(p + ".mlp.fc2.bias"), x, out, P,
+                 derr_, stream_);
+        return;
+    }
     Epi e1;
     e1.bias = W(p + ".mlp.fc1.bias");
     e1.act = ACT_GELU;

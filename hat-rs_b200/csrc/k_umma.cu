@@ -571,6 +571,315 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
 }
 
+// ------------------------------------------------------------------ fused MLP
+// The HAB / OCAB MLP in one launch (hat_arch.py:252-263 with the residual of :309):
+//
+//   out = res + b2 + W2 . GELU(W1 . n + b1)        n: the LayerNorm output, split hi/lo
+//
+// per 128-row tile. The hidden activations never leave the SM: the hidden width runs in
+// chunks of MLP_HC = 96 columns; each chunk's fc1 accumulator (96 TMEM columns) is read
+// by the epilogue warps, which add b1, apply GELU, split the result into tf32 hi/lo and
+// write it back into TMEM, where it is the A operand of that chunk's fc2 products
+// (`tcgen05.mma` with A in tensor memory), accumulated into the tile's fc2 accumulator.
+// The tile's last chunk done, the epilogue adds b2 and the residual and stores, like the
+// GEMM's plain-store epilogue. TMEM columns: fc2 accumulator [0, CP), fc1 chunk
+// [CP, CP+96), hidden hi [CP+96, CP+192), hidden lo [CP+192, CP+288).
+//
+// Order of the MMA issuer per tile (each fc1 chunk needs the previous chunk's
+// accumulator read; each fc2 chunk needs that chunk's hidden values written):
+//   fc1(0); for h: { fc1(h+1) if any; fc2(h) }
+// and the TMA producer loads the operands in exactly that order through the same ring.
+constexpr int MLP_HC = 96;
+
+struct MlpArgs {
+    int C, HID, NCH, CP, KB1, stages;
+    long mtiles;
+    const float* b1;  // [HID]
+    UmmaArgs st;      // the final store's geometry (N = C, BN = CP, one column tile)
+};
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+        ::"r"(taddr), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+          "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+          "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+          "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+          "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+          "r"(__float_as_uint(v[15]))
+        : "memory");
+}
+__device__ __forceinline__ void mma_tf32_ts(uint32_t dtmem, uint32_t atmem, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n}\n"
+        ::"r"(dtmem), "r"(atmem), "l"(b), "r"(idesc), "r"(acc));
+}
+
+template <int TERMS>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    k_mlp(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
+          const __grid_constant__ CUtensorMap tmW1h, const __grid_constant__ CUtensorMap tmW1l,
+          const __grid_constant__ CUtensorMap tmW2h, const __grid_constant__ CUtensorMap tmW2l, const MlpArgs g,
+          const Epi e) {
+    extern __shared__ __align__(1024) uint8_t smraw[];
+    __shared__ uint64_t full[6], empty[6], d1_full, d1_free, h_full, h_empty, d2_full, d2_free, drain;
+    __shared__ uint32_t tmem_slot;
+    __shared__ volatile int abort_flag;
+    __shared__ float stg[EPI_WARPS][32][17];
+    __shared__ float no_colsum[256];
+
+    uint8_t* sm = (uint8_t*)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
+    const int S = g.stages;
+    const uint32_t A_B = 128 * 128, W1_B = MLP_HC * 128, W2_B = (uint32_t)g.CP * 128;
+    const uint32_t st_bytes = max(2 * A_B + 2 * W1_B, 2 * W2_B);
+    int* gerr = g.st.err;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(&d1_full, 1);
+        mbar_init(&d1_free, 32 * EPI_WARPS);
+        mbar_init(&h_full, 32 * EPI_WARPS);
+        mbar_init(&h_empty, 1);
+        mbar_init(&d2_full, 1);
+        mbar_init(&d2_free, 32 * EPI_WARPS);
+        mbar_init(&drain, 1);
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(&tmem_slot)));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    const uint32_t T_D2 = 0, T_D1 = (uint32_t)g.CP, T_HH = T_D1 + MLP_HC, T_HL = T_HH + MLP_HC;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            uint32_t it = 0;
+            bool ok = true;
+            auto stage = [&](uint32_t bytes) -> int {
+                const int s = (int)(it % S);
+                if (!mbar_wait(&empty[s], ((it / S) & 1) ^ 1, &abort_flag, gerr, 21)) return -1;
+                mbar_expect_tx(&full[s], bytes);
+                return s;
+            };
+            auto load_fc1 = [&](long t, int h) {
+                for (int kb = 0; kb < g.KB1 && ok; ++kb, ++it) {
+                    const int s = stage(TERMS == 3 ? 2 * A_B + 2 * W1_B : A_B + W1_B);
+                    if (s < 0) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* b = sm + s * st_bytes;
+                    tma_2d(b, &tmAh, kb * 32, (int)(t * 128), &full[s]);
+                    if (TERMS == 3) tma_2d(b + A_B, &tmAl, kb * 32, (int)(t * 128), &full[s]);
+                    tma_2d(b + 2 * A_B, &tmW1h, kb * 32, h * MLP_HC, &full[s]);
+                    if (TERMS == 3) tma_2d(b + 2 * A_B + W1_B, &tmW1l, kb * 32, h * MLP_HC, &full[s]);
+                }
+            };
+            auto load_fc2 = [&](int h) {
+                for (int kb = 0; kb < MLP_HC / 32 && ok; ++kb, ++it) {
+                    const int s = stage(TERMS == 3 ? 2 * W2_B : W2_B);
+                    if (s < 0) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* b = sm + s * st_bytes;
+                    tma_2d(b, &tmW2h, h * MLP_HC + kb * 32, 0, &full[s]);
+                    if (TERMS == 3) tma_2d(b + W2_B, &tmW2l, h * MLP_HC + kb * 32, 0, &full[s]);
+                }
+            };
+            for (long t = blockIdx.x; t < g.mtiles && ok && !abort_flag; t += gridDim.x) {
+                load_fc1(t, 0);
+                for (int h = 0; h < g.NCH && ok; ++h) {
+                    if (h + 1 < g.NCH) load_fc1(t, h + 1);
+                    load_fc2(h);
+                }
+            }
+            if (abort_flag) {
+                for (uint32_t j = (it > (uint32_t)S ? it - S : 0); j < it; ++j) mbar_wait_quiet(&full[j % S], (j / S) & 1);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            uint32_t it = 0, qn = 0, tl = 0;  // ring position, next fc1 chunk, local tile
+            const uint32_t id1 = idesc_tf32(128, MLP_HC), id2 = idesc_tf32(128, g.CP);
+            bool ok = true;
+            auto fc1 = [&]() {
+                // D1 free: the epilogue has read the previous chunk's accumulator.
+                if (!mbar_wait(&d1_free, (qn & 1) ^ 1, &abort_flag, gerr, 22)) {
+                    ok = false;
+                    return;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem + T_D1;
+                for (int kb = 0; kb < g.KB1; ++kb, ++it) {
+                    const int s = (int)(it % S);
+                    if (!mbar_wait(&full[s], (it / S) & 1, &abort_flag, gerr, 23)) {
+                        ok = false;
+                        return;
+                    }
+                    tc_fence_after();
+                    const uint32_t ah = smem_u32(sm + s * st_bytes), al = ah + A_B;
+                    const uint32_t bh = ah + 2 * A_B, bl = bh + W1_B;
+#pragma unroll 1
+                    for (int k = 0; k < 4; ++k) {
+                        const uint32_t off = k * 32, acc0 = (kb | k) ? 1u : 0u;
+                        if (TERMS == 3) {
+                            mma_tf32(d, smem_desc(al + off, 128), smem_desc(bh + off, 128), id1, acc0);
+                            mma_tf32(d, smem_desc(ah + off, 128), smem_desc(bl + off, 128), id1, 1u);
+                            mma_tf32(d, smem_desc(ah + off, 128), smem_desc(bh + off, 128), id1, 1u);
+                        } else {
+                            mma_tf32(d, smem_desc(ah + off, 128), smem_desc(bh + off, 128), id1, acc0);
+                        }
+                    }
+                    mma_commit(&empty[s]);
+                }
+                mma_commit(&d1_full);
+                ++qn;
+            };
+            for (long t = blockIdx.x; t < g.mtiles && ok && !abort_flag; t += gridDim.x, ++tl) {
+                const uint32_t q0 = qn;
+                fc1();
+                for (int h = 0; h < g.NCH && ok; ++h) {
+                    const uint32_t q = q0 + h;
+                    if (h + 1 < g.NCH) {
+                        fc1();
+                        if (!ok) break;
+                    }
+                    // This chunk's hidden values written; for the tile's first chunk, the
+                    // previous tile's fc2 accumulator read.
+                    if (!mbar_wait(&h_full, q & 1, &abort_flag, gerr, 24)) {
+                        ok = false;
+                        break;
+                    }
+                    if (h == 0 && !mbar_wait(&d2_free, (tl & 1) ^ 1, &abort_flag, gerr, 25)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d = tmem + T_D2;
+                    for (int kb = 0; kb < MLP_HC / 32; ++kb, ++it) {
+                        const int s = (int)(it % S);
+                        if (!mbar_wait(&full[s], (it / S) & 1, &abort_flag, gerr, 26)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t bh = smem_u32(sm + s * st_bytes), bl = bh + W2_B;
+#pragma unroll 1
+                        for (int k = 0; k < 4; ++k) {
+                            const uint32_t col = (uint32_t)(kb * 32 + k * 8), off = k * 32;
+                            const uint32_t acc0 = (h | kb | k) ? 1u : 0u;
+                            if (TERMS == 3) {
+                                mma_tf32_ts(d, tmem + T_HL + col, smem_desc(bh + off, 128), id2, acc0);
+                                mma_tf32_ts(d, tmem + T_HH + col, smem_desc(bl + off, 128), id2, 1u);
+                                mma_tf32_ts(d, tmem + T_HH + col, smem_desc(bh + off, 128), id2, 1u);
+                            } else {
+                                mma_tf32_ts(d, tmem + T_HH + col, smem_desc(bh + off, 128), id2, acc0);
+                            }
+                        }
+                        mma_commit(&empty[s]);
+                    }
+                    if (!ok) break;
+                    mma_commit(&h_empty);
+                }
+                if (!ok) break;
+                mma_commit(&d2_full);
+            }
+            mma_commit(&drain);
+            mbar_wait_quiet(&drain, 0);
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int q4 = warp & 3;
+        const int row = q4 * 32 + lane;
+        const int ew = warp - 2;
+        const int half = ew >> 2;
+        const uint32_t lanes = (uint32_t)(q4 * 32) << 16;
+        uint32_t qc = 0, tl = 0;
+        for (long t = blockIdx.x; t < g.mtiles; t += gridDim.x, ++tl) {
+            if (__any_sync(0xffffffffu, abort_flag != 0)) break;
+            bool ok = true;
+            for (int h = 0; h < g.NCH; ++h, ++qc) {
+                const bool got = mbar_wait(&d1_full, qc & 1, &abort_flag, gerr, 27);
+                if (!__all_sync(0xffffffffu, got)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                // This warp's 48 columns of the chunk.
+                float v[48];
+                tmem_ld16(tmem + lanes + T_D1 + half * 48, v);
+                tmem_ld16(tmem + lanes + T_D1 + half * 48 + 16, v + 16);
+                tmem_ld16(tmem + lanes + T_D1 + half * 48 + 32, v + 32);
+                tc_fence_before();
+                mbar_arrive(&d1_free);
+                const int nb = h * MLP_HC + half * 48;
+#pragma unroll
+                for (int j = 0; j < 48; ++j) {
+                    const float b = nb + j < g.HID ? __ldg(g.b1 + nb + j) : 0.f;
+                    const float x = v[j] + b;
+                    v[j] = 0.5f * x * (1.f + erff(x * 0.70710678118654752f));
+                }
+                // The hidden buffer is free once the previous chunk's fc2 has run.
+                const bool freed = mbar_wait(&h_empty, (qc & 1) ^ 1, &abort_flag, gerr, 28);
+                if (!__all_sync(0xffffffffu, freed)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int g16 = 0; g16 < 3; ++g16) {
+                    float hi[16], lo[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        if (TERMS == 3) {
+                            split_tf32(v[16 * g16 + j], hi[j], lo[j]);
+                        } else {
+                            hi[j] = tf32_rna(v[16 * g16 + j]);
+                            lo[j] = 0.f;
+                        }
+                    }
+                    tmem_st16(tmem + lanes + T_HH + half * 48 + 16 * g16, hi);
+                    if (TERMS == 3) tmem_st16(tmem + lanes + T_HL + half * 48 + 16 * g16, lo);
+                }
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                tc_fence_before();
+                mbar_arrive(&h_full);
+            }
+            if (!ok) break;
+            const bool got = mbar_wait(&d2_full, tl & 1, &abort_flag, gerr, 29);
+            if (!__all_sync(0xffffffffu, got)) break;
+            tc_fence_after();
+            const long m = t * 128 + row;
+            const bool valid = m < g.st.M;
+#pragma unroll 1
+            for (int c0 = 16 * half; c0 < g.CP; c0 += 32)
+                epi_chunk16<0>(g.st, e, tmem + lanes + T_D2, 0, c0, t, q4, lane, valid, stg[ew], no_colsum);
+            tc_fence_before();
+            mbar_arrive(&d2_free);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+    }
+}
+
 // ------------------------------------------------------------------ host side
 
 // cuTensorMapEncodeTiled, fetched from the driver through the runtime so the library
@@ -737,6 +1046,84 @@ long umma_conv3x3(int mode, Opnd x, const GemmW& w, Dst y, int hgt, int wid, con
     else
         launch_k<1, 1>(tah, tal, tbh, tbl, g, e, st);
     return colsum_rows(g);
+}
+
+}  // namespace hat
+
+namespace hat {
+
+bool umma_mlp_ok(const GemmW& w1, const GemmW& w2) {
+    return w1.umma && w2.umma && !w1.conv && !w2.conv && w2.n == w1.k && w2.k == w1.n && w1.n_pad == w2.k_pad &&
+           w1.n_pad % MLP_HC == 0 && w2.n_pad % 16 == 0 && w2.n_pad + 3 * MLP_HC <= 512 && w1.k % 4 == 0;
+}
+
+long umma_mlp(int mode, Opnd x, const GemmW& w1, const float* b1, const GemmW& w2, const float* b2, const float* res,
+              Dst y, long m, int* err, cudaStream_t st) {
+    if (!umma_mlp_ok(w1, w2)) throw Error(1, "umma_mlp: weights not in the fused-MLP layout");
+    const bool three = mode == 0;
+    if (three && !x.lo) throw Error(1, "umma_mlp: fp32-parity mode needs a split operand");
+    const int C = w1.k;
+    uint64_t adims[2] = {(uint64_t)C, (uint64_t)m};
+    uint64_t astr[1] = {(uint64_t)C * 4};
+    uint32_t abox[2] = {32, 128};
+    CUtensorMap tah = make_map(x.hi, 2, adims, astr, abox, 128);
+    CUtensorMap tal = make_map(three ? x.lo : x.hi, 2, adims, astr, abox, 128);
+    uint64_t d1[2] = {(uint64_t)w1.k_pad, (uint64_t)w1.n_pad};
+    uint64_t s1[1] = {(uint64_t)w1.k_pad * 4};
+    uint32_t b1box[2] = {32, (uint32_t)MLP_HC};
+    CUtensorMap t1h = make_map(w1.hi, 2, d1, s1, b1box, 128);
+    CUtensorMap t1l = make_map(three ? w1.lo : w1.hi, 2, d1, s1, b1box, 128);
+    uint64_t d2[2] = {(uint64_t)w2.k_pad, (uint64_t)w2.n_pad};
+    uint64_t s2[1] = {(uint64_t)w2.k_pad * 4};
+    uint32_t b2box[2] = {32, (uint32_t)w2.n_pad};
+    CUtensorMap t2h = make_map(w2.hi, 2, d2, s2, b2box, 128);
+    CUtensorMap t2l = make_map(three ? w2.lo : w2.hi, 2, d2, s2, b2box, 128);
+
+    MlpArgs g{};
+    g.C = C;
+    g.HID = w1.n;
+    g.NCH = w1.n_pad / MLP_HC;
+    g.CP = w2.n_pad;
+    g.KB1 = w1.k_pad / 32;
+    g.mtiles = (m + 127) / 128;
+    g.b1 = b1;
+    const long st_bytes = std::max(2L * 128 * 128 + 2L * MLP_HC * 128, 2L * g.CP * 128);
+    g.stages = (int)std::max(2L, std::min(6L, (SMEM_CAP - 1024) / st_bytes));
+    UmmaArgs& u = g.st;
+    u.M = m;
+    u.N = C;
+    u.BN = g.CP;
+    u.ntn = 1;
+    u.y = y;
+    u.ldo = C;
+    u.nstore = C;
+    u.err = err;
+    u.mtiles = g.mtiles;
+    u.ntiles = g.mtiles;
+    Epi e;
+    e.bias = b2;
+    e.res = res;
+    if (C % 4) throw Error(1, "umma_mlp: the width must be a multiple of 4");
+    const size_t smem = (size_t)g.stages * st_bytes + 1024;
+    static unsigned configured[2] = {0, 0};
+    int dev = 0;
+    HAT_CUDA(cudaGetDevice(&dev));
+    const int which = three ? 0 : 1;
+    if (!(configured[which] & (1u << dev))) {
+        if (three)
+            HAT_CUDA(cudaFuncSetAttribute(k_mlp<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_CAP));
+        else
+            HAT_CUDA(cudaFuncSetAttribute(k_mlp<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_CAP));
+        configured[which] |= 1u << dev;
+    }
+    const long grid = std::min<long>(g.mtiles, num_sms());
+    if (three)
+        k_mlp<3><<<(unsigned)grid, NTHREADS, smem, st>>>(tah, tal, t1h, t1l, t2h, t2l, g, e);
+    else
+        k_mlp<1><<<(unsigned)grid, NTHREADS, smem, st>>>(tah, tal, t1h, t1l, t2h, t2l, g, e);
+    HAT_CUDA(cudaGetLastError());
+    count_launch();
+    return 0;
 }
 
 }  // namespace hat

@@ -47,6 +47,14 @@ long umma_linear(int mode, Opnd x, const GemmW& w, Dst y, long m, const Epi& e, 
 long umma_conv3x3(int mode, Opnd x, const GemmW& w, Dst y, int hgt, int wid, const Epi& e, int* err,
                   cudaStream_t st);
 
+// The HAB / OCAB MLP fused into one tensor-core launch: y = res + b2 + w2 . GELU(w1 . x + b1),
+// the hidden activations kept on chip (k_umma.cu, k_mlp). `umma_mlp_ok` says whether the
+// two weights' tensor-core layouts allow it (hidden width a multiple of 96 after padding,
+// output width at most 224); `res` may alias `y.hi`.
+bool umma_mlp_ok(const GemmW& w1, const GemmW& w2);
+long umma_mlp(int mode, Opnd x, const GemmW& w1, const float* b1, const GemmW& w2, const float* b2, const float* res,
+              Dst y, long m, int* err, cudaStream_t st);
+
 // CUDA-core launchers (read hi + lo when the operand is split); same return value.
 long simt_linear(Opnd x, const GemmW& w, Dst y, long m, const Epi& e, cudaStream_t st);
 long simt_conv3x3(Opnd x, const GemmW& w, Dst y, int hgt, int wid, const Epi& e, cudaStream_t st);
