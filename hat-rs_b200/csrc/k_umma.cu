@@ -590,6 +590,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 //   fc1(0); for h: { fc1(h+1) if any; fc2(h) }
 // and the TMA producer loads the operands in exactly that order through the same ring.
 constexpr int MLP_HC = 96;
+constexpr int MLP_MAXH = 768;  // the largest padded hidden width the fused MLP takes
 
 struct MlpArgs {
     int C, HID, NCH, CP, KB1, stages;
@@ -627,10 +628,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     __shared__ volatile int abort_flag;
     __shared__ float stg[EPI_WARPS][32][17];
     __shared__ float no_colsum[256];
+    __shared__ float b1s[MLP_MAXH];  // fc1 bias, zero past HID (read by every chunk)
 
     uint8_t* sm = (uint8_t*)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
     const int S = g.stages;
     const uint32_t A_B = 128 * 128, W1_B = MLP_HC * 128, W2_B = (uint32_t)g.CP * 128;
+    for (int i = threadIdx.x; i < MLP_MAXH; i += NTHREADS) b1s[i] = i < g.HID ? g.b1[i] : 0.f;
     const uint32_t st_bytes = max(2 * A_B + 2 * W1_B, 2 * W2_B);
     int* gerr = g.st.err;
 
@@ -827,8 +830,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const int nb = h * MLP_HC + half * 48;
 #pragma unroll
                 for (int j = 0; j < 48; ++j) {
-                    const float b = nb + j < g.HID ? __ldg(g.b1 + nb + j) : 0.f;
-                    const float x = v[j] + b;
+                    const float x = v[j] + b1s[nb + j];
                     v[j] = 0.5f * x * (1.f + erff(x * 0.70710678118654752f));
                 }
                 // The hidden buffer is free once the previous chunk's fc2 has run.
@@ -1054,7 +1056,8 @@ namespace hat {
 
 bool umma_mlp_ok(const GemmW& w1, const GemmW& w2) {
     return w1.umma && w2.umma && !w1.conv && !w2.conv && w2.n == w1.k && w2.k == w1.n && w1.n_pad == w2.k_pad &&
-           w1.n_pad % MLP_HC == 0 && w2.n_pad % 16 == 0 && w2.n_pad + 3 * MLP_HC <= 512 && w1.k % 4 == 0;
+           w1.n_pad % MLP_HC == 0 && w1.n_pad <= MLP_MAXH && w2.n_pad % 16 == 0 && w2.n_pad + 3 * MLP_HC <= 512 &&
+           w1.k % 4 == 0;
 }
 
 long umma_mlp(int mode, Opnd x, const GemmW& w1, const float* b1, const GemmW& w2, const float* b2, const float* res,
