@@ -381,6 +381,9 @@ void Engine::check_device_error() {
     HAT_CUDA(cudaStreamSynchronize(stream_));
     if (v) {
         HAT_CUDA(cudaMemsetAsync(derr_, 0, sizeof(int), stream_));
+        if (v == 20)
+            throw Error(3, "gpu: an attention operand (q, k or v) reached fp16's range (|x| >= 65504), which the "
+                           "tensor-core split cannot carry (code 20); the pass's output is invalid");
         throw Error(3, "gpu: a tensor-core kernel gave up waiting on its pipeline (code " + std::to_string(v) +
                            "); the pass's output is invalid");
     }

@@ -8,18 +8,26 @@
 //
 // Work item = (window, head, half of the window's 256 queries); 128 query rows per
 // item, keys streamed in blocks of 32 (8 blocks for 256 keys, 18 for 576). Every
-// operand is split into tf32 hi/lo halves, and both products use the 3-term split
-// (A_lo.B_hi + A_hi.B_lo + A_hi.B_hi) in fp32-parity mode; fast mode issues the single
-// A_hi.B_hi.
+// operand is split into fp16 hi/lo halves (hi = fp16(x), lo = fp16(x - hi): 22
+// significant bits, the same as a tf32 pair), and both products use the 3-term split
+// (A_lo.B_hi + A_hi.B_lo + A_hi.B_hi) of `tcgen05.mma.kind::f16` with fp32 accumulation
+// in fp32-parity mode; fast mode issues the single A_hi.B_hi. A kind::f16 MMA takes 16
+// elements of K for the cost of 8 in kind::tf32, so QK^T (head dim 24 or 30, padded to
+// 32) is 2 k-steps and PV over a 32-key block 2 k-steps. Values below fp16's normal
+// range keep an absolute error of at most 2^-25 per element; |q|, |k|, |v| of 65504 or
+// more would overflow, so the loaders check the range and stop the kernel with an
+// error code instead.
 //
-// Softmax: P is written back into tensor memory (P_hi over the block's S columns, P_lo
-// beside it) and the PV product reads its A operand from there. O accumulates in tensor
-// memory across the item's key blocks. Each row keeps a reference max m: P = exp(S - m)
-// with the row sum l accumulated against the same m, so O / l is exact whatever m is.
-// m is the first block's max and moves only when a later block's max exceeds it by more
-// than RESCALE_LOG2 (in log2 units, so every P stays below 2^RESCALE_LOG2); then the
-// row's O in tensor memory and l are scaled by exp(m_old - m_new) first. With
-// RESCALE_LOG2 = 8 that is rare, so O is read once per item, not once per key block.
+// Softmax: P is written back into tensor memory as packed fp16 pairs (P_hi in the first
+// 16 of the block's 32 S columns, P_lo in the other 16) and the PV product reads its A
+// operand from there. O accumulates in tensor memory across the item's key blocks. Each
+// row keeps a reference max m: P = exp(S - m) with the row sum l accumulated against the
+// same m, so O / l is exact whatever m is. m is the first block's max and moves only
+// when a later block's max exceeds it by more than RESCALE_LOG2 (in log2 units, so every
+// P stays below 2^RESCALE_LOG2); then the row's O in tensor memory and l are scaled by
+// exp(m_old - m_new) first. With RESCALE_LOG2 = 8 that is rare, so O is read once per
+// item, not once per key block. P and l carry a factor 2^P_SHIFT (P below 2^14), which
+// keeps more of P's split above fp16's subnormals and cancels in O / l.
 //
 // The window partition, the cyclic roll, the nn.Unfold of the keys with its zero
 // padding, the relative-position bias gather and the shift mask are address
@@ -31,6 +39,8 @@
 // (TMEM lane quarters 1,2,3,0), 5-8 loaders (gather, scale, split, swizzled stores).
 // Every mbarrier wait is bounded; on expiry the kernel records an error code, all roles
 // leave, and TMEM is released.
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 
 namespace hat {
@@ -42,8 +52,10 @@ constexpr int KBLK = 32;     // keys per block
 constexpr int MT = 128;      // query rows per work item
 constexpr int KVS = 4;       // K/V pipeline stages
 constexpr int TSTRIDE = 48;  // shared bias-table row stride (floats)
-constexpr int TMEM_COLS = 256;
+constexpr int TMEM_COLS = 128;
 constexpr float RESCALE_LOG2 = 8.f;
+constexpr float P_SHIFT = 6.f;
+constexpr float F16_LIMIT = 65504.f;  // the largest finite fp16
 constexpr long long WAIT_CYCLES_A = 4000000000ll;
 
 __device__ __forceinline__ uint32_t su(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -95,21 +107,31 @@ __device__ __forceinline__ uint64_t mdesc(uint32_t saddr, int rowbytes, uint32_t
     d |= (uint64_t)(rowbytes == 128 ? 2 : 6) << 61;
     return d;
 }
-// kind::tf32, f32 accumulate, M = 128, both operands K-major.
-__host__ __device__ constexpr uint32_t idesc_a(int n) {
-    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+// kind::f16 with fp16 A and B (format 0), f32 accumulate, M = 128, both operands K-major.
+__host__ __device__ constexpr uint32_t idesc_h(int n) {
+    return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
 // D (tmem) (+)= A (smem) . B (smem)
 __device__ __forceinline__ void mma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
     asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n"
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
         ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(acc));
 }
-// D (tmem) (+)= A (tmem: lane = row, column = k) . B (smem)
+// D (tmem) (+)= A (tmem: lane = row, column j = the fp16 pair k = 2j, 2j+1) . B (smem)
 __device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
     asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n}\n"
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n"
         ::"r"(d), "r"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+// fp16 pair (a in the low half, b in the high half) as one 32-bit word.
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+// x = hi + lo in fp16 (round to nearest both times); returns hi, lo through the pair.
+__device__ __forceinline__ void split_h(float x, float& hi, float& lo) {
+    hi = __half2float(__float2half_rn(x));
+    lo = x - hi;
 }
 __device__ __forceinline__ void commit(uint64_t* b) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su(b))
@@ -147,12 +169,18 @@ __device__ __forceinline__ void tst32(uint32_t taddr, const float* v) {
           "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
         : "memory");
 }
+__device__ __forceinline__ void tst16(uint32_t taddr, const uint32_t* r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+          "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
 __device__ __forceinline__ void tst_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// Byte offset of element (row, c), c < 32, in a SWIZZLE_128B tile of 128-byte rows.
-__device__ __forceinline__ uint32_t off_sw128(int row, int c) {
-    return row * 128 + ((((c >> 2) ^ row) & 7) << 4) + (c & 3) * 4;
-}
+// Byte offset of the 16-byte chunk q (0 or 1) of row `row` in a SWIZZLE_32B tile of
+// 32-byte rows (16 fp16 values of K per row).
+__device__ __forceinline__ uint32_t off_sw32(int row, int q) { return row * 32 + (((q ^ (row >> 2)) & 1) << 4); }
 
 __device__ __forceinline__ int band3(int v, int n, int shift) { return v < n - 16 ? 0 : (v < n - shift ? 1 : 2); }
 
@@ -176,21 +204,21 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
     k_attn_tc(const float* __restrict__ qkv, const float* __restrict__ table, Dst out, const AttnGeom gm, int c,
               int heads, float scale, long items, int* err) {
     const int wp = gm.wp;
-    constexpr int KS = (D + 7) / 8;                 // k-steps of the QK^T product
+    constexpr int KH = (D + 15) / 16;               // k-steps of the QK^T product (16 fp16 each)
     constexpr int NK = OCA ? 576 : 256;             // keys per window
     constexpr int NBLK = NK / KBLK;
     constexpr int TR = OCA ? 39 : 31;               // bias-table rows (and columns)
     constexpr int TW = OCA ? 39 : 31;               // the checkpoint table's row length
-    constexpr uint32_t Q_BYTES = KS * 4096;         // 128 rows x 32 B per k-step
-    constexpr uint32_t K_BYTES = KS * 1024;         // 32 rows x 32 B per k-step
-    constexpr uint32_t V_BYTES = 4096;              // V^T: 32 features x 128 B (32 keys)
+    constexpr uint32_t Q_BYTES = KH * 4096;         // 128 rows x 32 B per k-step
+    constexpr uint32_t K_BYTES = KH * 1024;         // 32 keys x 32 B per k-step
+    constexpr uint32_t V_BYTES = 2 * 1024;          // V^T: 32 features x 32 B per 16-key k-step
     constexpr uint32_t KV_BYTES = 2 * K_BYTES + 2 * V_BYTES;
     constexpr uint32_t OFF_KV = 2 * Q_BYTES;
     constexpr uint32_t OFF_TAB = OFF_KV + KVS * KV_BYTES;
     constexpr uint32_t OFF_KOFF = OFF_TAB + TR * TSTRIDE * 4;
-    // TMEM columns: S / P_hi blocks at 0 and 32, P_lo at 64 and 96, O (per item parity)
-    // at 128 and 160.
-    constexpr uint32_t T_PLO = 64, T_O = 128;
+    // TMEM columns: S blocks at 0 and 32 (fp32); once read, a block's first 16 columns
+    // hold P_hi and the next 16 P_lo (fp16 pairs); O (per item parity) at 64 and 96.
+    constexpr uint32_t T_PLO = 16, T_O = 64;
 
     extern __shared__ __align__(1024) uint8_t raw[];
     uint8_t* sm = (uint8_t*)(((uintptr_t)raw + 1023) & ~(uintptr_t)1023);
@@ -246,7 +274,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
     if (warp == 0) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            const uint32_t id_s = idesc_a(32), id_o = idesc_a(32);
+            const uint32_t id_s = idesc_h(32), id_o = idesc_h(32);
             const uint32_t qh = su(sm), ql = su(sm + Q_BYTES);
             long g = 0;  // global key-block counter
             uint32_t ti = 0;
@@ -263,7 +291,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
                     const uint32_t kb = su(sm + OFF_KV + kvs * KV_BYTES);
                     const uint32_t d = tmem + s * 32;
 #pragma unroll
-                    for (int k = 0; k < KS; ++k) {
+                    for (int k = 0; k < KH; ++k) {
                         const uint64_t aH = mdesc(qh + k * 4096, 32, 256), aL = mdesc(ql + k * 4096, 32, 256);
                         const uint64_t bH = mdesc(kb + k * 1024, 32, 256), bL = mdesc(kb + K_BYTES + k * 1024, 32, 256);
                         if (TERMS == 3) {
@@ -298,10 +326,10 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
                     tcf_after();
                     const int kvs = (int)(gb % KVS);
                     const uint32_t vb = su(sm + OFF_KV + kvs * KV_BYTES + 2 * K_BYTES);
-                    const uint32_t ph = tmem + s * 32, pl = tmem + T_PLO + s * 32;
+                    const uint32_t ph = tmem + s * 32, pl = ph + T_PLO;
 #pragma unroll
-                    for (int k = 0; k < KBLK / 8; ++k) {
-                        const uint64_t bH = mdesc(vb + k * 32, 128, 1024), bL = mdesc(vb + V_BYTES + k * 32, 128, 1024);
+                    for (int k = 0; k < KBLK / 16; ++k) {
+                        const uint64_t bH = mdesc(vb + k * 1024, 32, 256), bL = mdesc(vb + V_BYTES + k * 1024, 32, 256);
                         const uint32_t acc = (j | k) ? 1u : 0u;
                         if (TERMS == 3) {
                             mma_ts(od, pl + k * 8, bH, id_o, acc);
@@ -400,20 +428,22 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
                     m = bmax;
                     l *= a;
                 }
+                // P (times 2^P_SHIFT) as fp16 hi/lo pairs over the block's S columns.
                 float psum = 0.f;
-                float pl[32];
+                uint32_t ph[16], pl[16];
+                const float mo = m - P_SHIFT;
 #pragma unroll
-                for (int k = 0; k < 32; ++k) {
-                    const float p = exp2f(sv[k] - m);
-                    psum += p;
-                    if (TERMS == 3) {
-                        split_tf32(p, sv[k], pl[k]);
-                    } else {
-                        sv[k] = tf32_rna(p);
-                    }
+                for (int k = 0; k < 32; k += 2) {
+                    const float p0 = exp2f(sv[k] - mo), p1 = exp2f(sv[k + 1] - mo);
+                    psum += p0 + p1;
+                    float h0, l0, h1, l1;
+                    split_h(p0, h0, l0);
+                    split_h(p1, h1, l1);
+                    ph[k >> 1] = pack_h2(h0, h1);
+                    pl[k >> 1] = pack_h2(l0, l1);
                 }
-                tst32(tmem + trow + s * 32, sv);
-                if (TERMS == 3) tst32(tmem + trow + T_PLO + s * 32, pl);
+                tst16(tmem + trow + s * 32, ph);
+                if (TERMS == 3) tst16(tmem + trow + s * 32 + T_PLO, pl);
                 l += psum;
                 if (j > 0) {
                     // PV of the previous block has finished (this also keeps every
@@ -464,11 +494,12 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
         }
     } else {
         // ------------------------------------------------------------ loaders
-        // Warps 5-6 load K: lane = key, warp = column half [0,16) / [16,32); each 4-column
-        // chunk is one 16-byte store into the K-major SW32 tiles. Warps 7-8 load V: a
-        // thread owns a 4-key x 4-feature block, transposes it in registers and writes
-        // four 16-byte rows of V^T (K-major SW128: one row of 32 keys per feature). Loads
-        // for the next key block are issued before waiting for a free stage.
+        // Warps 5-6 load K: lane = key, warp = k-step (columns [0,16) / [16,32)); each
+        // 8-column chunk is one 16-byte store of fp16 into the K-major SW32 tiles. Warps
+        // 7-8 load V: a thread owns a 4-key x 4-feature block, transposes it in registers
+        // and writes four 8-byte pieces of V^T rows (K-major SW32, one 32-byte row of 16
+        // keys per feature and k-step). Loads for the next key block are issued before
+        // waiting for a free stage. A value of fp16's range or beyond records error 20.
         constexpr int VW = (D % 4 == 0) ? 4 : 2;  // vector width that keeps the row alignment
         const int t = threadIdx.x - 160;           // 0..127
         const int lw = warp - 5;                   // 0..3
@@ -478,6 +509,22 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
         long g = 0;
         uint32_t ti = 0;
         float buf[16];
+        bool range_ok = true;
+        // fp16 hi/lo of 8 values as four packed words each (element 2i in the low half).
+        auto split8 = [&](const float* x, uint4& hi, uint4& lo) {
+            uint32_t h[4], l[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float h0, l0, h1, l1;
+                range_ok &= !(fabsf(x[2 * i]) >= F16_LIMIT) && !(fabsf(x[2 * i + 1]) >= F16_LIMIT);
+                split_h(x[2 * i], h0, l0);
+                split_h(x[2 * i + 1], h1, l1);
+                h[i] = pack_h2(h0, h1);
+                l[i] = pack_h2(l0, l1);
+            }
+            hi = make_uint4(h[0], h[1], h[2], h[3]);
+            lo = make_uint4(l[0], l[1], l[2], l[3]);
+        };
         auto key_pos = [&](int wy, int wx, int kk, bool& inside) -> long {
             inside = true;
             if (OCA) {
@@ -540,21 +587,20 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
                     OCA ? (long)(gm.oy + wy * 16 + qy) * wp + wx * 16 + qx
                         : (long)((gm.oy + wy * 16 + qy + gm.sy) % gm.rows) * wp + (wx * 16 + qx + gm.sx) % wp;
                 const float* src = qkv + qpos * c3 + (long)head * D;
-                float qv[KS * 8];
+                float qv[KH * 16];
                 load_cols(src, 0, true, qv, 16);
-                if (KS * 8 > 16) load_cols(src, 16, true, qv + 16, KS * 8 - 16);
+                if (KH > 1) load_cols(src, 16, true, qv + 16, 16);
+#pragma unroll
+                for (int i = 0; i < KH * 16; ++i) qv[i] *= scale;
                 const bool got = bar_wait(&q_empty, (ti & 1) ^ 1, &abort_flag, err, 17);
                 if (!__all_sync(0xffffffffu, got)) break;
 #pragma unroll
-                for (int c4 = 0; c4 < KS * 2; ++c4) {
-                    float4 h, lo;
-                    split_tf32(qv[4 * c4] * scale, h.x, lo.x);
-                    split_tf32(qv[4 * c4 + 1] * scale, h.y, lo.y);
-                    split_tf32(qv[4 * c4 + 2] * scale, h.z, lo.z);
-                    split_tf32(qv[4 * c4 + 3] * scale, h.w, lo.w);
-                    const uint32_t o = (c4 >> 1) * 4096 + t * 32 + ((((c4 & 1) ^ (t >> 2)) & 1) << 4);
-                    *reinterpret_cast<float4*>(sm + o) = h;
-                    if (TERMS == 3) *reinterpret_cast<float4*>(sm + Q_BYTES + o) = lo;
+                for (int c8 = 0; c8 < KH * 2; ++c8) {
+                    uint4 h, lo;
+                    split8(qv + 8 * c8, h, lo);
+                    const uint32_t o = (c8 >> 1) * 4096 + off_sw32(t, c8 & 1);
+                    *reinterpret_cast<uint4*>(sm + o) = h;
+                    if (TERMS == 3) *reinterpret_cast<uint4*>(sm + Q_BYTES + o) = lo;
                 }
                 fence_async();
                 bar_arrive(&q_full);
@@ -570,32 +616,34 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
                 }
                 uint8_t* kvb = sm + OFF_KV + s * KV_BYTES;
                 if (!is_v) {
+                    if (lw < KH) {
 #pragma unroll
-                    for (int c4 = 0; c4 < 4; ++c4) {
-                        const int cc = col0 + 4 * c4;
-                        if (cc < KS * 8) {
-                            float4 h, lo;
-                            split_tf32(buf[4 * c4], h.x, lo.x);
-                            split_tf32(buf[4 * c4 + 1], h.y, lo.y);
-                            split_tf32(buf[4 * c4 + 2], h.z, lo.z);
-                            split_tf32(buf[4 * c4 + 3], h.w, lo.w);
-                            const uint32_t o = (cc >> 3) * 1024 + kk0 * 32 + (((((cc >> 2) & 1) ^ (kk0 >> 2)) & 1) << 4);
-                            *reinterpret_cast<float4*>(kvb + o) = h;
-                            if (TERMS == 3) *reinterpret_cast<float4*>(kvb + K_BYTES + o) = lo;
+                        for (int q = 0; q < 2; ++q) {
+                            uint4 h, lo;
+                            split8(buf + 8 * q, h, lo);
+                            const uint32_t o = lw * 1024 + off_sw32(kk0, q);
+                            *reinterpret_cast<uint4*>(kvb + o) = h;
+                            if (TERMS == 3) *reinterpret_cast<uint4*>(kvb + K_BYTES + o) = lo;
                         }
                     }
                 } else {
 #pragma unroll
                     for (int f = 0; f < 4; ++f) {
                         const int n = col0 + f;  // feature = row of V^T
-                        float4 h, lo;
-                        split_tf32(buf[f], h.x, lo.x);
-                        split_tf32(buf[4 + f], h.y, lo.y);
-                        split_tf32(buf[8 + f], h.z, lo.z);
-                        split_tf32(buf[12 + f], h.w, lo.w);
-                        const uint32_t o = 2 * K_BYTES + off_sw128(n, kk0);
-                        *reinterpret_cast<float4*>(kvb + o) = h;
-                        if (TERMS == 3) *reinterpret_cast<float4*>(kvb + V_BYTES + o) = lo;
+                        const float x[4] = {buf[f], buf[4 + f], buf[8 + f], buf[12 + f]};
+                        uint32_t h[2], l[2];
+#pragma unroll
+                        for (int i = 0; i < 2; ++i) {
+                            float h0, l0, h1, l1;
+                            range_ok &= !(fabsf(x[2 * i]) >= F16_LIMIT) && !(fabsf(x[2 * i + 1]) >= F16_LIMIT);
+                            split_h(x[2 * i], h0, l0);
+                            split_h(x[2 * i + 1], h1, l1);
+                            h[i] = pack_h2(h0, h1);
+                            l[i] = pack_h2(l0, l1);
+                        }
+                        const uint32_t o = 2 * K_BYTES + (kk0 >> 4) * 1024 + off_sw32(n, (kk0 >> 3) & 1) + (kk0 & 7) * 2;
+                        *reinterpret_cast<uint2*>(kvb + o) = make_uint2(h[0], h[1]);
+                        if (TERMS == 3) *reinterpret_cast<uint2*>(kvb + V_BYTES + o) = make_uint2(l[0], l[1]);
                     }
                 }
                 fence_async();
@@ -605,6 +653,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
             if (!ok) break;
             g += NBLK;
         }
+        if (!range_ok) atomicCAS(err, 0, 20);
     }
 
     tcf_before();
@@ -619,10 +668,10 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
 template <int D, bool OCA, int TERMS>
 static void run_tc(const float* qkv, const float* table, Dst out, const Plan& p, int c, int heads, int shift, int* err,
                    cudaStream_t st) {
-    constexpr int KS = (D + 7) / 8;
+    constexpr int KH = (D + 15) / 16;
     constexpr int TR = OCA ? 39 : 31;
     constexpr size_t bytes =
-        2 * KS * 4096 + KVS * (2 * KS * 1024 + 2 * 4096) + TR * TSTRIDE * 4 + (OCA ? 576 * 4 : 0) + 1024;
+        2 * KH * 4096 + KVS * (2 * KH * 1024 + 2 * 2048) + TR * TSTRIDE * 4 + (OCA ? 576 * 4 : 0) + 1024;
     static unsigned configured = 0;
     int dev = 0;
     HAT_CUDA(cudaGetDevice(&dev));
