@@ -3,6 +3,9 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#ifdef __CUDACC__
+#include <cuda_fp16.h>
+#endif
 #include <cstdint>
 #include <cstdio>
 #include <stdexcept>
@@ -77,18 +80,40 @@ struct Plan {
 
 // ---------------------------------------------------------------- operands
 // A GEMM operand plane. In fp32-parity mode every plane a tensor-core GEMM reads is
-// stored pre-split by the kernel that produces it: `hi` holds the value rounded to
-// tf32 and `lo` the rounded remainder (see split_tf32), so hi + lo carries the fp32
-// value to 2^-22 and the GEMM needs no conversion pass. `lo == nullptr` marks a plain
-// fp32 plane (fast mode, the CUDA-core path, and planes read only by CUDA-core code).
+// stored pre-split by the kernel that produces it, so the GEMM needs no conversion
+// pass. Two split kinds:
+//  * `h16`: `hi` and `lo` are fp16 arrays (element i at byte 2i, behind the float
+//    pointers): hi = fp16(x), lo = fp16(x - hi), 22 significant bits, read by
+//    kind::f16 MMAs. Values under fp16's normal range keep an absolute error of at
+//    most 2^-25; |x| >= 65504 does not fit and is reported through `err` (code 21).
+//  * otherwise: fp32 arrays, hi = x rounded to tf32 and lo the rounded remainder (see
+//    split_tf32), hi + lo within 2^-22 |x| of x, read by kind::tf32 MMAs.
+// `lo == nullptr` marks a plain fp32 plane (fast mode, the CUDA-core path, and planes
+// read only by CUDA-core code).
 struct Opnd {
     const float* hi = nullptr;
     const float* lo = nullptr;
+    bool h16 = false;
 };
 struct Dst {
     float* hi = nullptr;
     float* lo = nullptr;
+    bool h16 = false;
+    int* err = nullptr;  // h16: set to 21 when a value is beyond fp16's range
 };
+// The plane starting `i` elements further on (2 bytes per element for an h16 split).
+inline Opnd opnd_at(Opnd o, long i) {
+    if (o.lo && o.h16)
+        return Opnd{reinterpret_cast<const float*>(reinterpret_cast<const char*>(o.hi) + 2 * i),
+                    reinterpret_cast<const float*>(reinterpret_cast<const char*>(o.lo) + 2 * i), true};
+    return Opnd{o.hi + i, o.lo ? o.lo + i : nullptr, false};
+}
+inline Dst dst_at(Dst d, long i) {
+    if (d.lo && d.h16)
+        return Dst{reinterpret_cast<float*>(reinterpret_cast<char*>(d.hi) + 2 * i),
+                   reinterpret_cast<float*>(reinterpret_cast<char*>(d.lo) + 2 * i), true, d.err};
+    return Dst{d.hi + i, d.lo ? d.lo + i : nullptr, false, d.err};
+}
 
 #ifdef __CUDACC__
 // x = hi + lo with hi = x rounded to the nearest tf32 value and lo = (x - hi) rounded
@@ -104,9 +129,29 @@ __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
     hi = tf32_rna(x);
     lo = tf32_rna(x - hi);
 }
+// fp16 split: hi = fp16(x) and lo = fp16(x - hi), both rounded to nearest.
+__device__ __forceinline__ void split_h16(float x, __half& hi, __half& lo) {
+    hi = __float2half_rn(x);
+    lo = __float2half_rn(x - __half2float(hi));
+}
+// The same for a pair, packed (a in the low half): what kind::f16 operands hold.
+__device__ __forceinline__ void split_h16x2(float a, float b, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(a, b);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(a - hf.x, b - hf.y);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+__device__ __forceinline__ bool beyond_h16(float v) { return fabsf(v) >= 65504.f; }
 // Store v at index i of a destination plane, split when it has a lo half.
 __device__ __forceinline__ void put(const Dst& d, long i, float v) {
-    if (d.lo) {
+    if (d.lo && d.h16) {
+        __half h, l;
+        split_h16(v, h, l);
+        reinterpret_cast<__half*>(d.hi)[i] = h;
+        reinterpret_cast<__half*>(d.lo)[i] = l;
+        if (beyond_h16(v) && d.err) atomicCAS(d.err, 0, 21);
+    } else if (d.lo) {
         float h, l;
         split_tf32(v, h, l);
         d.hi[i] = h;
@@ -115,8 +160,17 @@ __device__ __forceinline__ void put(const Dst& d, long i, float v) {
         d.hi[i] = v;
     }
 }
+// i a multiple of 4.
 __device__ __forceinline__ void put4(const Dst& d, long i, float4 v) {
-    if (d.lo) {
+    if (d.lo && d.h16) {
+        uint2 h, l;
+        split_h16x2(v.x, v.y, h.x, l.x);
+        split_h16x2(v.z, v.w, h.y, l.y);
+        *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(d.hi) + i) = h;
+        *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(d.lo) + i) = l;
+        if ((beyond_h16(v.x) || beyond_h16(v.y) || beyond_h16(v.z) || beyond_h16(v.w)) && d.err)
+            atomicCAS(d.err, 0, 21);
+    } else if (d.lo) {
         float4 h, l;
         split_tf32(v.x, h.x, l.x);
         split_tf32(v.y, h.y, l.y);
@@ -129,7 +183,12 @@ __device__ __forceinline__ void put4(const Dst& d, long i, float4 v) {
     }
 }
 // The fp32 value of element i of an operand plane.
-__device__ __forceinline__ float get(const Opnd& o, long i) { return o.lo ? o.hi[i] + o.lo[i] : o.hi[i]; }
+__device__ __forceinline__ float get(const Opnd& o, long i) {
+    if (o.lo && o.h16)
+        return __half2float(reinterpret_cast<const __half*>(o.hi)[i]) +
+               __half2float(reinterpret_cast<const __half*>(o.lo)[i]);
+    return o.lo ? o.hi[i] + o.lo[i] : o.hi[i];
+}
 #endif
 
 // ---------------------------------------------------------------- epilogues
@@ -196,7 +255,7 @@ void launch_overlap_attention(int mode, bool simt, const float* qkv, const float
 // The second half of a 3x3 conv computed as a per-tap linear: `taps` is the [hp][wp][ldt]
 // plane of Y[p][tap*cout + co] = sum_ci w[co][ci][tap] x[p][ci] (tap = ky*3 + kx), and
 // out[p][co] = gelu(bias[co] + sum_tap Y[p + (ky-1, kx-1)][tap*cout + co]) with zero
-// padding; channels cout..ldo-1 of `out` are written as zeros. cout <= 8.
+// padding; channels cout..ldo-1 of `out` are written as zeros. cout <= 8, ldo <= 16.
 void launch_tapsum_gelu(const float* taps, int ldt, const float* bias, Dst out, int ldo, int cout, int hp, int wp,
                         int ylo, int yhi, cudaStream_t st);
 // Rows [ylo, yhi) of the plane are data; the taps of rows outside are the conv's zero padding.

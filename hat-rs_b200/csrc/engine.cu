@@ -6,6 +6,7 @@
 #include "engine.h"
 
 #include <algorithm>
+#include <cmath>
 
 #include "nccl_rt.h"
 #include <cstring>
@@ -142,6 +143,18 @@ Engine::Engine(const std::string& path, int device, int mode, bool use_graph, bo
     const int cmid_stride = Sizes::of(wt_, Plan::make(16, 16, wt_.window)).cmid_stride;
     tap_cab_ = 9 * wt_.compressed <= 64;
     tap_ld_ = (9 * wt_.compressed + 3) / 4 * 4;
+    h16_ = split() && wt_.embed % 8 == 0;
+    // fp16 stride of the middle plane: 16 (one 32-byte k-step) or a multiple of 8; it
+    // fits in the buffer's cmid_stride floats (cmid_stride >= max(compressed, 8)).
+    cmid_ld_ = !h16_ ? cmid_stride : wt_.compressed <= 16 ? 16 : (wt_.compressed + 7) / 8 * 8;
+    if (2 * cmid_ld_ > 4 * cmid_stride && h16_) throw Error(3, "gpu: the CAB's middle plane is too narrow");
+    // h16 weights: the factor that puts the largest |w| of each weight near 2^14.
+    auto h16_scale = [&](const std::string& name, const TensorInfo& ti) {
+        const float* w = wt_.st.f32(name);
+        float mx = 0.f;
+        for (size_t i = 0, n = (size_t)ti.numel(); i < n; ++i) mx = std::max(mx, std::fabs(w[i]));
+        return 1.f / h16_weight_factor(mx);
+    };
     auto is_cab1 = [](const std::string& n) { return n.find("conv_block.cab.0.weight") != std::string::npos; };
     size_t total = 0;
     std::vector<std::string> names;
@@ -154,15 +167,17 @@ Engine::Engine(const std::string& path, int device, int mode, bool use_graph, bo
             const auto& s = kv.second.shape;
             if (s.size() == 4) {
                 const bool cab2 = kv.first.find("conv_block.cab.2.weight") != std::string::npos;
-                plan_gemm_w(g, (int)s[0], (int)s[1], true, cab2 ? cmid_stride : (int)s[1]);
+                plan_gemm_w(g, (int)s[0], (int)s[1], true, cab2 ? cmid_ld_ : (int)s[1], h16_);
             } else {
-                plan_gemm_w(g, (int)s[0], (int)s[1], false, 0);
+                plan_gemm_w(g, (int)s[0], (int)s[1], false, 0, h16_);
             }
+            if (g.h16) g.scale = h16_scale(kv.first, kv.second);
             gw_[kv.first] = g;
             total += (gemm_w_floats(g) + 64) / 64 * 64 + 192;
             if (tap_cab_ && is_cab1(kv.first)) {
                 GemmW t;
-                plan_gemm_w(t, 9 * (int)s[0], (int)s[1], false, 0);
+                plan_gemm_w(t, 9 * (int)s[0], (int)s[1], false, 0, h16_);
+                t.scale = g.scale;  // the same values, reordered
                 gw_[kv.first + "#taps"] = t;
                 total += ((size_t)t.n * t.k + 63) / 64 * 64 + (gemm_w_floats(t) + 64) / 64 * 64 + 192;
             }
@@ -290,11 +305,12 @@ void Engine::attach_strip(int rank, int n, const void* id, size_t idlen) {
     comm_.reset(new Comm(rank, n, id, idlen, device_));
 }
 
-void Engine::exchange(float* plane, int ch, int res, int n) {
+void Engine::exchange(float* plane, int ch, int res, int n) { exchange_rows(plane, (long)plan_.wp * res * ch, res, n); }
+
+void Engine::exchange_rows(float* plane, long rowf, int res, int n) {
     if (!comm_) return;
     const Plan& p = plan_;
     if (n > p.halo * res) throw Error(1, "exchange: more rows than the halo holds");
-    const long rowf = (long)p.wp * res * ch;
     const int top = p.halo * res, bot = (p.halo + p.own()) * res;  // first own row, first bottom-halo row
     const int N = comm_->size(), r = comm_->rank();
     const int up = (r - 1 + N) % N, down = (r + 1) % N;
@@ -309,6 +325,13 @@ void Engine::exchange(float* plane, int ch, int res, int n) {
 }
 
 void Engine::exchange(Dst d, int ch, int res, int n) {
+    if (d.lo && d.h16) {
+        // fp16 rows: half the floats (wp is a multiple of 16, so rows stay whole floats)
+        const long rowf = (long)plan_.wp * res * ch / 2;
+        exchange_rows(d.hi, rowf, res, n);
+        exchange_rows(d.lo, rowf, res, n);
+        return;
+    }
     exchange(d.hi, ch, res, n);
     if (d.lo) exchange(d.lo, ch, res, n);
 }
@@ -322,7 +345,7 @@ long Engine::conv_res(const std::string& wname, Opnd x, int xch, Dst y, int ych,
         if (p.r1 == p.hp) hi = (p.halo + p.own()) * res;  // below the image
     }
     const long xoff = (long)lo * wid * xch;
-    Opnd xv{x.hi + xoff, x.lo ? x.lo + xoff : nullptr};
+    Opnd xv = opnd_at(x, xoff);
     long yoff = 0;
     if (e.planar_out)
         e.oy0 += p.gy0() * res + lo;  // padded output row of view row 0
@@ -330,7 +353,7 @@ long Engine::conv_res(const std::string& wname, Opnd x, int xch, Dst y, int ych,
         yoff = (long)lo * e.shuffle * wid * e.shuffle * ych;
     else
         yoff = (long)lo * wid * ych;
-    Dst yv{y.hi + yoff, y.lo ? y.lo + yoff : nullptr};
+    Dst yv = dst_at(y, yoff);
     if (e.res) e.res += yoff;
     if (e.cx) e.cx += yoff;
     if (p.strip() && !all_rows) {
@@ -384,6 +407,9 @@ void Engine::check_device_error() {
         if (v == 20)
             throw Error(3, "gpu: an attention operand (q, k or v) reached fp16's range (|x| >= 65504), which the "
                            "tensor-core split cannot carry (code 20); the pass's output is invalid");
+        if (v == 21)
+            throw Error(3, "gpu: an activation reached fp16's range (|x| >= 65504), which the fp16 operand split "
+                           "cannot carry (code 21); the pass's output is invalid");
         throw Error(3, "gpu: a tensor-core kernel gave up waiting on its pipeline (code " + std::to_string(v) +
                            "); the pass's output is invalid");
     }
@@ -494,7 +520,7 @@ void Engine::hab(int stage, int blk, const float* in, float* out) {
     Epi ec1;
     ec1.bias = W(cb + ".0.bias");
     ec1.act = ACT_GELU;
-    ec1.ldo = sizes_.cmid_stride;
+    ec1.ldo = cmid_ld_;
     mark("conv.cab1", 18.0 * P * c * cc, 4.0 * P * (c + cc));
     if (tap_cab_) {
         // Per-tap partial outputs into the (not yet used) qkv buffer, then the tap sum.
@@ -504,17 +530,17 @@ void Engine::hab(int stage, int blk, const float* in, float* out) {
         // Rows beyond the image (a strip's halo at the top or bottom edge) are padding.
         const int ylo = plan_.strip() && plan_.r0 == 0 ? plan_.halo : 0;
         const int yhi = plan_.strip() && plan_.r1 == plan_.hp ? plan_.halo + plan_.own() : plan_.rows;
-        launch_tapsum_gelu(a_->qkv, tap_ld_, W(cb + ".0.bias"), D(a_->cmid, a_->cmidlo), sizes_.cmid_stride, cc,
+        launch_tapsum_gelu(a_->qkv, tap_ld_, W(cb + ".0.bias"), D(a_->cmid, a_->cmidlo), cmid_ld_, cc,
                            plan_.rows, plan_.wp, ylo, yhi, stream_);
     } else {
         // Every row: the second conv reads one row past the strip's own rows.
-        conv_res(cb + ".0.weight", O(a_->n1, a_->n1lo), c, D(a_->cmid, a_->cmidlo), sizes_.cmid_stride, 1, true, ec1);
+        conv_res(cb + ".0.weight", O(a_->n1, a_->n1lo), c, D(a_->cmid, a_->cmidlo), cmid_ld_, 1, true, ec1);
     }
     Epi ec2;
     ec2.bias = W(cb + ".2.bias");
     ec2.colsum = a_->chsum;
     mark("conv.cab2", 18.0 * P * c * cc, 4.0 * P * (c + cc));
-    long rows = conv_res(cb + ".2.weight", O(a_->cmid, a_->cmidlo), sizes_.cmid_stride, Dst{a_->convx, nullptr}, c, 1,
+    long rows = conv_res(cb + ".2.weight", O(a_->cmid, a_->cmidlo), cmid_ld_, Dst{a_->convx, nullptr}, c, 1,
                          false, ec2);
     mark("ca_gate", 0, 4.0 * rows * c);
     // The pool averages over the whole padded plane (src/gpu.rs:435); sharded, the

@@ -84,11 +84,15 @@ private:
     const GemmW& G(const std::string& name) const;
     long linear(const std::string& wname, Opnd x, Dst y, const Epi& e);
     long conv(const std::string& wname, Opnd x, Dst y, int hgt, int wid, const Epi& e);
-    // Operand planes: split into tf32 hi/lo halves when the tensor cores run in
-    // fp32-parity mode, plain fp32 otherwise.
+    // Operand planes: split into hi/lo halves when the tensor cores run in fp32-parity
+    // mode (fp16 pairs when `h16_`, tf32 pairs otherwise), plain fp32 otherwise.
     bool split() const { return mode_ == 0 && !simt_only_; }
-    Dst D(float* hi, float* lo) const { return Dst{hi, split() ? lo : nullptr}; }
-    Opnd O(const float* hi, const float* lo) const { return Opnd{hi, split() ? lo : nullptr}; }
+    Dst D(float* hi, float* lo) const {
+        return split() ? Dst{hi, lo, h16_, derr_} : Dst{hi, nullptr, false, nullptr};
+    }
+    Opnd O(const float* hi, const float* lo) const { return split() ? Opnd{hi, lo, h16_} : Opnd{hi, nullptr, false}; }
+    // Halo rows of a plane of `rowf` floats per row at `res` times the base resolution.
+    void exchange_rows(float* plane, long rowf, int res, int n);
 
     Weights wt_;
     // The CAB's first conv as a per-tap linear + tap sum when its output is narrow
@@ -96,6 +100,12 @@ private:
     // times. tap_ld_ is the row stride of the per-tap plane (it borrows the qkv buffer).
     bool tap_cab_ = false;
     int tap_ld_ = 0;
+    // fp16 split planes (kind::f16 GEMMs): parity mode with a width of a multiple of 8,
+    // so every split plane's rows are whole 16-byte units. cmid_ld_: the CAB's middle
+    // plane's channel stride in elements (16 or a multiple of 8 as fp16; the buffer's
+    // own stride as tf32 pairs or fp32).
+    bool h16_ = false;
+    int cmid_ld_ = 0;
     int device_ = 0, mode_ = 0;
     std::unique_ptr<Comm> comm_;
     bool use_graph_ = true, simt_only_ = false;

@@ -7,6 +7,15 @@
 namespace hat {
 
 __device__ __forceinline__ float4 ld4o(const Opnd& o, long i) {
+    if (o.lo && o.h16) {
+        const uint2 h = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(o.hi) + i);
+        const uint2 l = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(o.lo) + i);
+        const float2 h0 = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
+        const float2 h1 = __half22float2(*reinterpret_cast<const __half2*>(&h.y));
+        const float2 l0 = __half22float2(*reinterpret_cast<const __half2*>(&l.x));
+        const float2 l1 = __half22float2(*reinterpret_cast<const __half2*>(&l.y));
+        return make_float4(h0.x + l0.x, h0.y + l0.y, h1.x + l1.x, h1.y + l1.y);
+    }
     float4 v = *reinterpret_cast<const float4*>(o.hi + i);
     if (o.lo) {
         const float4 l = *reinterpret_cast<const float4*>(o.lo + i);

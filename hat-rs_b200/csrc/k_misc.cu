@@ -55,17 +55,19 @@ __global__ void k_tapsum_gelu(const float* __restrict__ taps, int ldt, const flo
         for (int co = 0; co < CMAX; ++co)
             if (co < cout) acc[co] += row[co];
     }
+    // channels cout..ldo-1 (ldo <= 2 * CMAX) are written as zeros
 #pragma unroll
-    for (int co = 0; co < CMAX; ++co) {
+    for (int co = 0; co < 2 * CMAX; ++co) {
         if (co >= ldo) break;
-        const float v = co < cout ? 0.5f * acc[co] * (1.f + erff(acc[co] * 0.70710678118654752f)) : 0.f;
+        const float a = co < CMAX ? acc[co < CMAX ? co : 0] : 0.f;
+        const float v = co < cout ? 0.5f * a * (1.f + erff(a * 0.70710678118654752f)) : 0.f;
         put(out, p * ldo + co, v);
     }
 }
 
 void launch_tapsum_gelu(const float* taps, int ldt, const float* bias, Dst out, int ldo, int cout, int hp, int wp,
                         int ylo, int yhi, cudaStream_t st) {
-    if (cout > 8 || ldo > 8 || ldt < 9 * cout) throw Error(1, "tapsum: at most 8 output channels");
+    if (cout > 8 || ldo > 16 || ldt < 9 * cout) throw Error(1, "tapsum: at most 8 output channels (16 stored)");
     const long n = (long)hp * wp;
     k_tapsum_gelu<8><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(taps, ldt, bias, out, ldo, cout, hp, wp, ylo, yhi);
     HAT_CUDA(cudaGetLastError());

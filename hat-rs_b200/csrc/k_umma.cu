@@ -1,5 +1,6 @@
-// Tensor-core GEMM for sm_100a: tcgen05.mma (kind::tf32) with the accumulator in
-// tensor memory, operands staged in shared memory by TMA, one persistent CTA per SM.
+// Tensor-core GEMM for sm_100a: tcgen05.mma (kind::f16 or kind::tf32) with the
+// accumulator in tensor memory, operands staged in shared memory by TMA, one persistent
+// CTA per SM.
 //
 //   D[m][n] = sum_k A[m][k] * B[n][k]       A: activations, B: weights (both K-major)
 //
@@ -8,13 +9,16 @@
 // K loop runs over (tap, 32-channel chunk) and TMA's zero fill outside the plane is
 // the conv's zero padding.
 //
-// fp32 parity ("3xTF32"): every operand x arrives split into x_hi = x rounded to the
-// nearest tf32 value and x_lo = (x - x_hi) rounded to tf32 (the weights are split once
-// at upload; every activation plane a GEMM reads is written split by the kernel that
-// produces it), and
+// fp32 parity: every operand x arrives split into x_hi + x_lo (the weights are split
+// once at upload; every activation plane a GEMM reads is written split by the kernel
+// that produces it), and
 //   A.B ~= A_hi.B_hi + A_hi.B_lo + A_lo.B_hi,
-// which drops only A_lo.B_lo (relative 2^-22). FAST mode issues the single A_hi.B_hi.
-// The epilogue can write its own output split the same way for the next GEMM.
+// which drops only A_lo.B_lo (relative 2^-22). The split is fp16 pairs (H16: kind::f16,
+// 16 elements of K per MMA, 2 bytes each) or tf32 pairs (kind::tf32, 8 elements of 4
+// bytes); either way one MMA k-step is 32 bytes of each operand row, so the shared
+// memory layout is the same. H16 weights carry a power-of-two factor that the epilogue
+// takes out (`ascale`). FAST mode issues the single A_hi.B_hi on tf32. The epilogue can
+// write its own output split the same way for the next GEMM.
 //
 // Warp roles (320 threads): 0 TMA producer, 1 MMA issuer + TMEM owner, 2-9 epilogue
 // (TMEM -> registers -> fused epilogue -> global). Two epilogue warps share each TMEM
@@ -111,14 +115,34 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, int rowbytes) {
     d |= (uint64_t)(rowbytes == 128 ? 2 : 6) << 61;      // swizzle mode
     return d;
 }
-// Instruction descriptor of kind::tf32: f32 accumulate, tf32 A and B, both K-major.
+// Instruction descriptor: f32 accumulate, both operands K-major; A/B format 2 (tf32)
+// for kind::tf32, 0 (fp16) for kind::f16.
 __host__ __device__ constexpr uint32_t idesc_tf32(int m, int n) {
     return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+__host__ __device__ constexpr uint32_t idesc_f16(int m, int n) {
+    return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+template <bool H16>
+__host__ __device__ constexpr uint32_t idesc_k(int m, int n) {
+    return H16 ? idesc_f16(m, n) : idesc_tf32(m, n);
 }
 __device__ __forceinline__ void mma_tf32(uint32_t dtmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
     asm volatile(
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n"
         ::"r"(dtmem), "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void mma_f16(uint32_t dtmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
+        ::"r"(dtmem), "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+template <bool H16>
+__device__ __forceinline__ void mma_k(uint32_t dtmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    if (H16)
+        mma_f16(dtmem, a, b, idesc, acc);
+    else
+        mma_tf32(dtmem, a, b, idesc, acc);
 }
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -149,7 +173,9 @@ struct UmmaArgs {
     long M;          // rows (tokens / pixels)
     int N, BN, ntn;  // output columns, columns per tile, tiles along N
     int KB;          // k-blocks per tile
-    int ckb;         // bytes of K per k-block row: 128 (32 fp32) or 32 (8 fp32)
+    int ckb;         // bytes of K per k-block row: 128 or 32
+    int klast;       // MMA k-steps of a tile's last k-block (linear) / a tap's last chunk (conv)
+    float ascale;    // the accumulator's factor (h16 weights: 2^-e; else 1)
     int stages;
     // conv geometry (MODE 1): plane H x W, channel chunks per tap, patch tiles along x
     int H, W, cchunks, tx;
@@ -214,6 +240,8 @@ __device__ __forceinline__ void epi_chunk16(const UmmaArgs& g, const Epi& e, uin
 
     float v[16];
     tmem_ld16(taddr + c0, v);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] *= g.ascale;
     if (e.bias) {
         if (nb + 16 <= g.N) {
 #pragma unroll
@@ -275,7 +303,7 @@ __device__ __forceinline__ void epi_chunk16(const UmmaArgs& g, const Epi& e, uin
     __syncwarp();
 }
 
-template <int MODE, int TERMS, int EK>
+template <int MODE, int TERMS, int EK, bool H16>
 __global__ void __launch_bounds__(NTHREADS, 1)
     k_umma(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
            const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl, const UmmaArgs g,
@@ -338,14 +366,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     const int s = it % S;
                     if (!mbar_wait(&empty[s], ((it / S) & 1) ^ 1, &abort_flag, g.err, 1)) break;
                     mbar_expect_tx(&full[s], tx);
-                    const int kel = kb * (g.ckb / 4);  // K offset in elements
+                    constexpr int ES = H16 ? 2 : 4;      // bytes per element
+                    const int kel = kb * (g.ckb / ES);  // K offset in elements
                     if (MODE == 0) {
                         tma_2d(sAh(s), &tmAh, kel, (int)(mt * 128), &full[s]);
                         if (TERMS == 3) tma_2d(sAl(s), &tmAl, kel, (int)(mt * 128), &full[s]);
                     } else {
                         const int tap = kb / g.cchunks, cc = kb - tap * g.cchunks;
                         const int py = g.ty0 + (int)(mt / g.tx), px = (int)(mt % g.tx);
-                        const int c0 = cc * (g.ckb / 4), x0 = px * 16 + tap % 3 - 1, y0 = py * 8 + tap / 3 - 1;
+                        const int c0 = cc * (g.ckb / ES), x0 = px * 16 + tap % 3 - 1, y0 = py * 8 + tap / 3 - 1;
                         tma_3d(sAh(s), &tmAh, c0, x0, y0, &full[s]);
                         if (TERMS == 3) tma_3d(sAl(s), &tmAl, c0, x0, y0, &full[s]);
                     }
@@ -362,8 +391,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
             uint32_t it = 0, tl = 0;
-            const uint32_t idesc = idesc_tf32(128, g.BN);
-            const int ksteps = g.ckb / 32;  // MMA k = 8 tf32 = 32 bytes
+            const uint32_t idesc = idesc_k<H16>(128, g.BN);
+            const int ksteps = g.ckb / 32;  // one MMA k-step = 32 bytes (8 tf32 or 16 fp16)
             for (long t = blockIdx.x; t < ntiles && !abort_flag; t += gridDim.x, ++tl) {
                 const int a = tl & 1;
                 if (!mbar_wait(&acc_empty[a], ((tl >> 1) & 1) ^ 1, &abort_flag, g.err, 2)) break;
@@ -379,17 +408,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     tc_fence_after();
                     const uint32_t ah = smem_u32(sAh(s)), al = smem_u32(sAl(s));
                     const uint32_t bh = smem_u32(sBh(s)), bl = smem_u32(sBl(s));
+                    // k-steps past K (the last k-block of a row / of a tap) are skipped
+                    const bool last = MODE == 0 ? kb == g.KB - 1 : (kb % g.cchunks) == g.cchunks - 1;
+                    const int kst = last ? g.klast : ksteps;
 #pragma unroll 1
-                    for (int k = 0; k < ksteps; ++k) {
+                    for (int k = 0; k < kst; ++k) {
                         const uint32_t off = k * 32;
                         const uint32_t acc0 = (kb | k) ? 1u : 0u;
                         if (TERMS == 3) {
                             // small terms first, so they are added while the sum is small
-                            mma_tf32(d, smem_desc(al + off, g.ckb), smem_desc(bh + off, g.ckb), idesc, acc0);
-                            mma_tf32(d, smem_desc(ah + off, g.ckb), smem_desc(bl + off, g.ckb), idesc, 1u);
-                            mma_tf32(d, smem_desc(ah + off, g.ckb), smem_desc(bh + off, g.ckb), idesc, 1u);
+                            mma_k<H16>(d, smem_desc(al + off, g.ckb), smem_desc(bh + off, g.ckb), idesc, acc0);
+                            mma_k<H16>(d, smem_desc(ah + off, g.ckb), smem_desc(bl + off, g.ckb), idesc, 1u);
+                            mma_k<H16>(d, smem_desc(ah + off, g.ckb), smem_desc(bh + off, g.ckb), idesc, 1u);
                         } else {
-                            mma_tf32(d, smem_desc(ah + off, g.ckb), smem_desc(bh + off, g.ckb), idesc, acc0);
+                            mma_k<H16>(d, smem_desc(ah + off, g.ckb), smem_desc(bh + off, g.ckb), idesc, acc0);
                         }
                     }
                     mma_commit(&empty[s]);
@@ -440,7 +472,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     tmem_ld16(taddr + c0, v);
                     tmem_ld16(taddr + c0 + 16, v + 16);
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] = epi_act(v[j] + (e.bias ? e.bias[n0 + c0 + j] : 0.f), e.act);
+                    for (int j = 0; j < 32; ++j)
+                        v[j] = epi_act(v[j] * g.ascale + (e.bias ? e.bias[n0 + c0 + j] : 0.f), e.act);
                     if (valid) {
                         const int cb = (n0 + c0) / 4;
 #pragma unroll
@@ -470,7 +503,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     const int n = n0 + c0 + j;
-                    v[j] = n < g.N ? epi_act(v[j] + (e.bias ? e.bias[n] : 0.f), e.act) : 0.f;
+                    v[j] = n < g.N ? epi_act(v[j] * g.ascale + (e.bias ? e.bias[n] : 0.f), e.act) : 0.f;
                 }
                 // Every loop over v[] is fully unrolled with guards rather than breaks,
                 // so v stays in registers (a dynamically indexed v would live in local
@@ -578,12 +611,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 //
 // per 128-row tile. The hidden activations never leave the SM: the hidden width runs in
 // chunks of MLP_HC = 96 columns; each chunk's fc1 accumulator (96 TMEM columns) is read
-// by the epilogue warps, which add b1, apply GELU, split the result into tf32 hi/lo and
-// write it back into TMEM, where it is the A operand of that chunk's fc2 products
-// (`tcgen05.mma` with A in tensor memory), accumulated into the tile's fc2 accumulator.
-// The tile's last chunk done, the epilogue adds b2 and the residual and stores, like the
-// GEMM's plain-store epilogue. TMEM columns: fc2 accumulator [0, CP), fc1 chunk
-// [CP, CP+96), hidden hi [CP+96, CP+192), hidden lo [CP+192, CP+288).
+// by the epilogue warps, which add b1, apply GELU, split the result into hi/lo (fp16
+// pairs, packed two to a column, for H16; tf32 otherwise) and write it back into TMEM,
+// where it is the A operand of that chunk's fc2 products (`tcgen05.mma` with A in
+// tensor memory), accumulated into the tile's fc2 accumulator. The tile's last chunk
+// done, the epilogue adds b2 and the residual and stores, like the GEMM's plain-store
+// epilogue. TMEM columns: fc2 accumulator [0, CP), fc1 chunk [CP, CP+96), hidden hi
+// [CP+96, CP+96+HW), hidden lo [CP+96+HW, CP+96+2HW), HW = 48 (H16) or 96.
 //
 // Order of the MMA issuer per tile (each fc1 chunk needs the previous chunk's
 // accumulator read; each fc2 chunk needs that chunk's hidden values written):
@@ -594,6 +628,8 @@ constexpr int MLP_MAXH = 768;  // the largest padded hidden width the fused MLP 
 
 struct MlpArgs {
     int C, HID, NCH, CP, KB1, stages;
+    int klast1;       // MMA k-steps of fc1's last k-block
+    float s1;         // fc1 accumulator factor (H16 weight scale; fc2's is st.ascale)
     long mtiles;
     const float* b1;  // [HID]
     UmmaArgs st;      // the final store's geometry (N = C, BN = CP, one column tile)
@@ -615,8 +651,26 @@ __device__ __forceinline__ void mma_tf32_ts(uint32_t dtmem, uint32_t atmem, uint
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n}\n"
         ::"r"(dtmem), "r"(atmem), "l"(b), "r"(idesc), "r"(acc));
 }
+// A in tensor memory as fp16 pairs: column j holds k = 2j (low half) and 2j + 1.
+__device__ __forceinline__ void mma_f16_ts(uint32_t dtmem, uint32_t atmem, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n"
+        ::"r"(dtmem), "r"(atmem), "l"(b), "r"(idesc), "r"(acc));
+}
+template <bool H16>
+__device__ __forceinline__ void mma_k_ts(uint32_t dtmem, uint32_t atmem, uint64_t b, uint32_t idesc, uint32_t acc) {
+    if (H16)
+        mma_f16_ts(dtmem, atmem, b, idesc, acc);
+    else
+        mma_tf32_ts(dtmem, atmem, b, idesc, acc);
+}
+__device__ __forceinline__ void tmem_st8u(uint32_t taddr, const uint32_t* r) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+                 "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+}
 
-template <int TERMS>
+template <int TERMS, bool H16>
 __global__ void __launch_bounds__(NTHREADS, 1)
     k_mlp(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
           const __grid_constant__ CUtensorMap tmW1h, const __grid_constant__ CUtensorMap tmW1l,
@@ -661,7 +715,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_slot;
-    const uint32_t T_D2 = 0, T_D1 = (uint32_t)g.CP, T_HH = T_D1 + MLP_HC, T_HL = T_HH + MLP_HC;
+    constexpr uint32_t HW = H16 ? MLP_HC / 2 : MLP_HC;  // TMEM columns of one hidden half (hi or lo)
+    constexpr int KEL = H16 ? 64 : 32;                   // K elements per 128-byte k-block row
+    constexpr int NKB2 = (MLP_HC + KEL - 1) / KEL;       // fc2 k-blocks per hidden chunk
+    const uint32_t T_D2 = 0, T_D1 = (uint32_t)g.CP, T_HH = T_D1 + MLP_HC, T_HL = T_HH + HW;
 
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
@@ -682,22 +739,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         break;
                     }
                     uint8_t* b = sm + s * st_bytes;
-                    tma_2d(b, &tmAh, kb * 32, (int)(t * 128), &full[s]);
-                    if (TERMS == 3) tma_2d(b + A_B, &tmAl, kb * 32, (int)(t * 128), &full[s]);
-                    tma_2d(b + 2 * A_B, &tmW1h, kb * 32, h * MLP_HC, &full[s]);
-                    if (TERMS == 3) tma_2d(b + 2 * A_B + W1_B, &tmW1l, kb * 32, h * MLP_HC, &full[s]);
+                    tma_2d(b, &tmAh, kb * KEL, (int)(t * 128), &full[s]);
+                    if (TERMS == 3) tma_2d(b + A_B, &tmAl, kb * KEL, (int)(t * 128), &full[s]);
+                    tma_2d(b + 2 * A_B, &tmW1h, kb * KEL, h * MLP_HC, &full[s]);
+                    if (TERMS == 3) tma_2d(b + 2 * A_B + W1_B, &tmW1l, kb * KEL, h * MLP_HC, &full[s]);
                 }
             };
             auto load_fc2 = [&](int h) {
-                for (int kb = 0; kb < MLP_HC / 32 && ok; ++kb, ++it) {
+                for (int kb = 0; kb < NKB2 && ok; ++kb, ++it) {
                     const int s = stage(TERMS == 3 ? 2 * W2_B : W2_B);
                     if (s < 0) {
                         ok = false;
                         break;
                     }
                     uint8_t* b = sm + s * st_bytes;
-                    tma_2d(b, &tmW2h, h * MLP_HC + kb * 32, 0, &full[s]);
-                    if (TERMS == 3) tma_2d(b + W2_B, &tmW2l, h * MLP_HC + kb * 32, 0, &full[s]);
+                    tma_2d(b, &tmW2h, h * MLP_HC + kb * KEL, 0, &full[s]);
+                    if (TERMS == 3) tma_2d(b + W2_B, &tmW2l, h * MLP_HC + kb * KEL, 0, &full[s]);
                 }
             };
             for (long t = blockIdx.x; t < g.mtiles && ok && !abort_flag; t += gridDim.x) {
@@ -715,7 +772,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
             uint32_t it = 0, qn = 0, tl = 0;  // ring position, next fc1 chunk, local tile
-            const uint32_t id1 = idesc_tf32(128, MLP_HC), id2 = idesc_tf32(128, g.CP);
+            const uint32_t id1 = idesc_k<H16>(128, MLP_HC), id2 = idesc_k<H16>(128, g.CP);
             bool ok = true;
             auto fc1 = [&]() {
                 // D1 free: the epilogue has read the previous chunk's accumulator.
@@ -734,15 +791,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     tc_fence_after();
                     const uint32_t ah = smem_u32(sm + s * st_bytes), al = ah + A_B;
                     const uint32_t bh = ah + 2 * A_B, bl = bh + W1_B;
+                    const int kst = kb == g.KB1 - 1 ? g.klast1 : 4;
 #pragma unroll 1
-                    for (int k = 0; k < 4; ++k) {
+                    for (int k = 0; k < kst; ++k) {
                         const uint32_t off = k * 32, acc0 = (kb | k) ? 1u : 0u;
                         if (TERMS == 3) {
-                            mma_tf32(d, smem_desc(al + off, 128), smem_desc(bh + off, 128), id1, acc0);
-                            mma_tf32(d, smem_desc(ah + off, 128), smem_desc(bl + off, 128), id1, 1u);
-                            mma_tf32(d, smem_desc(ah + off, 128), smem_desc(bh + off, 128), id1, 1u);
+                            mma_k<H16>(d, smem_desc(al + off, 128), smem_desc(bh + off, 128), id1, acc0);
+                            mma_k<H16>(d, smem_desc(ah + off, 128), smem_desc(bl + off, 128), id1, 1u);
+                            mma_k<H16>(d, smem_desc(ah + off, 128), smem_desc(bh + off, 128), id1, 1u);
                         } else {
-                            mma_tf32(d, smem_desc(ah + off, 128), smem_desc(bh + off, 128), id1, acc0);
+                            mma_k<H16>(d, smem_desc(ah + off, 128), smem_desc(bh + off, 128), id1, acc0);
                         }
                     }
                     mma_commit(&empty[s]);
@@ -771,7 +829,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     }
                     tc_fence_after();
                     const uint32_t d = tmem + T_D2;
-                    for (int kb = 0; kb < MLP_HC / 32; ++kb, ++it) {
+                    for (int kb = 0; kb < NKB2; ++kb, ++it) {
                         const int s = (int)(it % S);
                         if (!mbar_wait(&full[s], (it / S) & 1, &abort_flag, gerr, 26)) {
                             ok = false;
@@ -779,16 +837,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         }
                         tc_fence_after();
                         const uint32_t bh = smem_u32(sm + s * st_bytes), bl = bh + W2_B;
+                        // k-steps of this k-block inside the chunk (H16: 64 + 32 of 96)
+                        const int kst = (MLP_HC - kb * KEL) / (KEL / 4) < 4 ? (MLP_HC - kb * KEL) / (KEL / 4) : 4;
 #pragma unroll 1
-                        for (int k = 0; k < 4; ++k) {
-                            const uint32_t col = (uint32_t)(kb * 32 + k * 8), off = k * 32;
+                        for (int k = 0; k < kst; ++k) {
+                            // TMEM column of this k-step's A: one per element (tf32), one per pair (fp16)
+                            const uint32_t col = H16 ? (uint32_t)((kb * KEL + k * 16) / 2) : (uint32_t)(kb * 32 + k * 8);
+                            const uint32_t off = k * 32;
                             const uint32_t acc0 = (h | kb | k) ? 1u : 0u;
                             if (TERMS == 3) {
-                                mma_tf32_ts(d, tmem + T_HL + col, smem_desc(bh + off, 128), id2, acc0);
-                                mma_tf32_ts(d, tmem + T_HH + col, smem_desc(bl + off, 128), id2, 1u);
-                                mma_tf32_ts(d, tmem + T_HH + col, smem_desc(bh + off, 128), id2, 1u);
+                                mma_k_ts<H16>(d, tmem + T_HL + col, smem_desc(bh + off, 128), id2, acc0);
+                                mma_k_ts<H16>(d, tmem + T_HH + col, smem_desc(bl + off, 128), id2, 1u);
+                                mma_k_ts<H16>(d, tmem + T_HH + col, smem_desc(bh + off, 128), id2, 1u);
                             } else {
-                                mma_tf32_ts(d, tmem + T_HH + col, smem_desc(bh + off, 128), id2, acc0);
+                                mma_k_ts<H16>(d, tmem + T_HH + col, smem_desc(bh + off, 128), id2, acc0);
                             }
                         }
                         mma_commit(&empty[s]);
@@ -830,7 +892,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const int nb = h * MLP_HC + half * 48;
 #pragma unroll
                 for (int j = 0; j < 48; ++j) {
-                    const float x = v[j] + b1s[nb + j];
+                    const float x = v[j] * g.s1 + b1s[nb + j];
                     v[j] = 0.5f * x * (1.f + erff(x * 0.70710678118654752f));
                 }
                 // The hidden buffer is free once the previous chunk's fc2 has run.
@@ -840,20 +902,35 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     break;
                 }
                 tc_fence_after();
+                if (H16) {
+                    // 48 values -> 24 packed pairs of hi and of lo (columns half*24 ..)
+                    uint32_t hp[24], lp[24];
 #pragma unroll
-                for (int g16 = 0; g16 < 3; ++g16) {
-                    float hi[16], lo[16];
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        if (TERMS == 3) {
-                            split_tf32(v[16 * g16 + j], hi[j], lo[j]);
-                        } else {
-                            hi[j] = tf32_rna(v[16 * g16 + j]);
-                            lo[j] = 0.f;
-                        }
+                    for (int j = 0; j < 24; ++j) split_h16x2(v[2 * j], v[2 * j + 1], hp[j], lp[j]);
+                    tmem_st8u(tmem + lanes + T_HH + half * 24, hp);
+                    tmem_st8u(tmem + lanes + T_HH + half * 24 + 8, hp + 8);
+                    tmem_st8u(tmem + lanes + T_HH + half * 24 + 16, hp + 16);
+                    if (TERMS == 3) {
+                        tmem_st8u(tmem + lanes + T_HL + half * 24, lp);
+                        tmem_st8u(tmem + lanes + T_HL + half * 24 + 8, lp + 8);
+                        tmem_st8u(tmem + lanes + T_HL + half * 24 + 16, lp + 16);
                     }
-                    tmem_st16(tmem + lanes + T_HH + half * 48 + 16 * g16, hi);
-                    if (TERMS == 3) tmem_st16(tmem + lanes + T_HL + half * 48 + 16 * g16, lo);
+                } else {
+#pragma unroll
+                    for (int g16 = 0; g16 < 3; ++g16) {
+                        float hi[16], lo[16];
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            if (TERMS == 3) {
+                                split_tf32(v[16 * g16 + j], hi[j], lo[j]);
+                            } else {
+                                hi[j] = tf32_rna(v[16 * g16 + j]);
+                                lo[j] = 0.f;
+                            }
+                        }
+                        tmem_st16(tmem + lanes + T_HH + half * 48 + 16 * g16, hi);
+                        if (TERMS == 3) tmem_st16(tmem + lanes + T_HL + half * 48 + 16 * g16, lo);
+                    }
                 }
                 asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                 tc_fence_before();
@@ -903,10 +980,11 @@ static EncodeTiledFn encode_fn() {
 }
 
 static CUtensorMap make_map(const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
-                            const uint32_t* box, int rowbytes) {
+                            const uint32_t* box, int rowbytes, bool h16 = false) {
     CUtensorMap m;
     uint32_t es[5] = {1, 1, 1, 1, 1};
-    CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank, const_cast<void*>(base), dims,
+    CUresult r = encode_fn()(&m, h16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank,
+                             const_cast<void*>(base), dims,
                              strides_bytes, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
                              rowbytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_32B,
                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -927,7 +1005,7 @@ static int num_sms() {
 // tile (3 x 68 KB) still fit.
 static const long SMEM_CAP = 232448 - 22528;
 
-template <int MODE, int TERMS, int EK>
+template <int MODE, int TERMS, int EK, bool H16>
 static void launch_ek(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh, const CUtensorMap& bl,
                       const UmmaArgs& g, const Epi& e, cudaStream_t st) {
     const size_t smem = (size_t)g.stages * (2 * 128 * g.ckb + 2 * g.BN * g.ckb) + 1024;
@@ -935,13 +1013,13 @@ static void launch_ek(const CUtensorMap& ah, const CUtensorMap& al, const CUtens
     int dev = 0;
     HAT_CUDA(cudaGetDevice(&dev));
     if (!(configured & (1u << dev))) {
-        HAT_CUDA(cudaFuncSetAttribute(k_umma<MODE, TERMS, EK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        HAT_CUDA(cudaFuncSetAttribute(k_umma<MODE, TERMS, EK, H16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)SMEM_CAP));
         configured |= 1u << dev;
     }
     const long grid = std::min<long>(g.ntiles, num_sms());
     if (e.colsum && g.N > 256) throw Error(1, "umma: channel sums are limited to 256 columns");
-    k_umma<MODE, TERMS, EK><<<(unsigned)grid, NTHREADS, smem, st>>>(ah, al, bh, bl, g, e);
+    k_umma<MODE, TERMS, EK, H16><<<(unsigned)grid, NTHREADS, smem, st>>>(ah, al, bh, bl, g, e);
     HAT_CUDA(cudaGetLastError());
     count_launch();
 }
@@ -955,14 +1033,25 @@ static int pick_ek(const UmmaArgs& g, const Epi& e) {
     return EK_GENERIC;
 }
 
-template <int MODE, int TERMS>
+template <int MODE, int TERMS, bool H16>
 static void launch_k(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh, const CUtensorMap& bl,
                      const UmmaArgs& g, const Epi& e, cudaStream_t st) {
     switch (pick_ek(g, e)) {
-        case EK_STORE: launch_ek<MODE, TERMS, EK_STORE>(ah, al, bh, bl, g, e, st); break;
-        case EK_SHUF2: launch_ek<MODE, TERMS, EK_SHUF2>(ah, al, bh, bl, g, e, st); break;
-        default: launch_ek<MODE, TERMS, EK_GENERIC>(ah, al, bh, bl, g, e, st); break;
+        case EK_STORE: launch_ek<MODE, TERMS, EK_STORE, H16>(ah, al, bh, bl, g, e, st); break;
+        case EK_SHUF2: launch_ek<MODE, TERMS, EK_SHUF2, H16>(ah, al, bh, bl, g, e, st); break;
+        default: launch_ek<MODE, TERMS, EK_GENERIC, H16>(ah, al, bh, bl, g, e, st); break;
     }
+}
+// parity on fp16 pairs, parity on tf32 pairs, or fast (tf32, one term)
+template <int MODE>
+static void launch_mode(bool three, bool h16, const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh,
+                        const CUtensorMap& bl, const UmmaArgs& g, const Epi& e, cudaStream_t st) {
+    if (three && h16)
+        launch_k<MODE, 3, true>(ah, al, bh, bl, g, e, st);
+    else if (three)
+        launch_k<MODE, 3, false>(ah, al, bh, bl, g, e, st);
+    else
+        launch_k<MODE, 1, false>(ah, al, bh, bl, g, e, st);
 }
 
 static long colsum_rows(const UmmaArgs& g) { return std::min<long>(g.ntiles, num_sms()) * 4; }
@@ -987,51 +1076,57 @@ long umma_linear(int mode, Opnd x, const GemmW& w, Dst y, long m, const Epi& e, 
     const int ckb = 128;
     const bool three = mode == 0;
     if (three && !x.lo) throw Error(1, "umma_linear: fp32-parity mode needs a split operand");
+    const bool h16 = three && w.h16;
+    if (three && x.h16 != w.h16) throw Error(1, "umma_linear: operand and weight split kinds differ");
+    const int es = h16 ? 2 : 4, kel = ckb / es, kstep = 32 / es;  // elements per k-block / k-step
     uint64_t adims[2] = {(uint64_t)w.k, (uint64_t)m};
-    uint64_t astr[1] = {(uint64_t)w.k * 4};
-    uint32_t abox[2] = {32, 128};
-    CUtensorMap tah = make_map(x.hi, 2, adims, astr, abox, ckb);
-    CUtensorMap tal = make_map(three ? x.lo : x.hi, 2, adims, astr, abox, ckb);
+    uint64_t astr[1] = {(uint64_t)w.k * es};
+    uint32_t abox[2] = {(uint32_t)kel, 128};
+    CUtensorMap tah = make_map(x.hi, 2, adims, astr, abox, ckb, h16);
+    CUtensorMap tal = make_map(three ? x.lo : x.hi, 2, adims, astr, abox, ckb, h16);
     uint64_t bdims[2] = {(uint64_t)w.k_pad, (uint64_t)w.n_pad};
-    uint64_t bstr[1] = {(uint64_t)w.k_pad * 4};
-    uint32_t bbox[2] = {32, (uint32_t)w.bn};
-    CUtensorMap tbh = make_map(w.hi, 2, bdims, bstr, bbox, ckb);
-    CUtensorMap tbl = make_map(three ? w.lo : w.hi, 2, bdims, bstr, bbox, ckb);
+    uint64_t bstr[1] = {(uint64_t)w.k_pad * es};
+    uint32_t bbox[2] = {(uint32_t)kel, (uint32_t)w.bn};
+    CUtensorMap tbh = make_map(w.hi, 2, bdims, bstr, bbox, ckb, h16);
+    CUtensorMap tbl = make_map(three ? w.lo : w.hi, 2, bdims, bstr, bbox, ckb, h16);
     UmmaArgs g{};
     fill_common(g, w, y, e, err);
     g.M = m;
-    g.KB = w.k_pad / 32;
+    g.KB = (w.k + kel - 1) / kel;  // k-blocks holding real K (the rest of k_pad is zeros)
+    g.klast = (w.k - (g.KB - 1) * kel + kstep - 1) / kstep;
+    g.ascale = h16 ? w.scale : 1.f;
     g.ckb = ckb;
     g.stages = pick_stages(w.bn, ckb);
     g.mtiles = (m + 127) / 128;
     g.ntiles = g.mtiles * g.ntn;
-    if (three)
-        launch_k<0, 3>(tah, tal, tbh, tbl, g, e, st);
-    else
-        launch_k<0, 1>(tah, tal, tbh, tbl, g, e, st);
+    launch_mode<0>(three, h16, tah, tal, tbh, tbl, g, e, st);
     return colsum_rows(g);  // colsum: one partial row per (CTA, epilogue warp)
 }
 
 long umma_conv3x3(int mode, Opnd x, const GemmW& w, Dst y, int hgt, int wid, const Epi& e, int* err,
                   cudaStream_t st) {
-    const int ckb = w.cinp == 8 ? 32 : 128;
-    const int cke = ckb / 4;
     const bool three = mode == 0;
     if (three && !x.lo) throw Error(1, "umma_conv3x3: fp32-parity mode needs a split operand");
+    const bool h16 = three && w.h16;
+    if (three && x.h16 != w.h16) throw Error(1, "umma_conv3x3: operand and weight split kinds differ");
+    const int ckb = w.ckb;
+    const int es = h16 ? 2 : 4, cke = ckb / es, kstep = 32 / es;  // channels per chunk / per k-step
     uint64_t adims[3] = {(uint64_t)w.cin_plane, (uint64_t)wid, (uint64_t)hgt};
-    uint64_t astr[2] = {(uint64_t)w.cin_plane * 4, (uint64_t)wid * w.cin_plane * 4};
+    uint64_t astr[2] = {(uint64_t)w.cin_plane * es, (uint64_t)wid * w.cin_plane * es};
     uint32_t abox[3] = {(uint32_t)cke, 16, 8};
-    CUtensorMap tah = make_map(x.hi, 3, adims, astr, abox, ckb);
-    CUtensorMap tal = make_map(three ? x.lo : x.hi, 3, adims, astr, abox, ckb);
+    CUtensorMap tah = make_map(x.hi, 3, adims, astr, abox, ckb, h16);
+    CUtensorMap tal = make_map(three ? x.lo : x.hi, 3, adims, astr, abox, ckb, h16);
     uint64_t bdims[2] = {(uint64_t)w.k_pad, (uint64_t)w.n_pad};
-    uint64_t bstr[1] = {(uint64_t)w.k_pad * 4};
+    uint64_t bstr[1] = {(uint64_t)w.k_pad * es};
     uint32_t bbox[2] = {(uint32_t)cke, (uint32_t)w.bn};
-    CUtensorMap tbh = make_map(w.hi, 2, bdims, bstr, bbox, ckb);
-    CUtensorMap tbl = make_map(three ? w.lo : w.hi, 2, bdims, bstr, bbox, ckb);
+    CUtensorMap tbh = make_map(w.hi, 2, bdims, bstr, bbox, ckb, h16);
+    CUtensorMap tbl = make_map(three ? w.lo : w.hi, 2, bdims, bstr, bbox, ckb, h16);
     UmmaArgs g{};
     fill_common(g, w, y, e, err);
     g.M = (long)hgt * wid;
-    g.cchunks = w.cinp / cke;
+    g.cchunks = (w.cin + cke - 1) / cke;  // chunks holding real channels (cinp - cin are zeros)
+    g.klast = (w.cin - (g.cchunks - 1) * cke + kstep - 1) / kstep;
+    g.ascale = h16 ? w.scale : 1.f;
     g.KB = 9 * g.cchunks;
     g.ckb = ckb;
     g.stages = pick_stages(w.bn, ckb);
@@ -1043,10 +1138,7 @@ long umma_conv3x3(int mode, Opnd x, const GemmW& w, Dst y, int hgt, int wid, con
     g.ty0 = ylo / 8;
     g.mtiles = (long)((yhi - ylo) / 8) * g.tx;
     g.ntiles = g.mtiles * g.ntn;
-    if (three)
-        launch_k<1, 3>(tah, tal, tbh, tbl, g, e, st);
-    else
-        launch_k<1, 1>(tah, tal, tbh, tbl, g, e, st);
+    launch_mode<1>(three, h16, tah, tal, tbh, tbl, g, e, st);
     return colsum_rows(g);
 }
 
@@ -1055,9 +1147,9 @@ long umma_conv3x3(int mode, Opnd x, const GemmW& w, Dst y, int hgt, int wid, con
 namespace hat {
 
 bool umma_mlp_ok(const GemmW& w1, const GemmW& w2) {
-    return w1.umma && w2.umma && !w1.conv && !w2.conv && w2.n == w1.k && w2.k == w1.n && w1.n_pad == w2.k_pad &&
-           w1.n_pad % MLP_HC == 0 && w1.n_pad <= MLP_MAXH && w2.n_pad % 16 == 0 && w2.n_pad + 3 * MLP_HC <= 512 &&
-           w1.k % 4 == 0;
+    return w1.umma && w2.umma && !w1.conv && !w2.conv && w1.h16 == w2.h16 && w2.n == w1.k && w2.k == w1.n &&
+           w1.n_pad % MLP_HC == 0 && w2.k_pad >= w1.n_pad && w1.n_pad <= MLP_MAXH &&
+           w2.n_pad % 16 == 0 && w2.n_pad + 3 * MLP_HC <= 512 && w1.k % (w1.h16 ? 8 : 4) == 0;
 }
 
 long umma_mlp(int mode, Opnd x, const GemmW& w1, const float* b1, const GemmW& w2, const float* b2, const float* res,
@@ -1065,29 +1157,34 @@ long umma_mlp(int mode, Opnd x, const GemmW& w1, const float* b1, const GemmW& w
     if (!umma_mlp_ok(w1, w2)) throw Error(1, "umma_mlp: weights not in the fused-MLP layout");
     const bool three = mode == 0;
     if (three && !x.lo) throw Error(1, "umma_mlp: fp32-parity mode needs a split operand");
+    const bool h16 = three && w1.h16;
+    if (three && x.h16 != w1.h16) throw Error(1, "umma_mlp: operand and weight split kinds differ");
+    const int es = h16 ? 2 : 4, kel = 128 / es, kstep = 32 / es;
     const int C = w1.k;
     uint64_t adims[2] = {(uint64_t)C, (uint64_t)m};
-    uint64_t astr[1] = {(uint64_t)C * 4};
-    uint32_t abox[2] = {32, 128};
-    CUtensorMap tah = make_map(x.hi, 2, adims, astr, abox, 128);
-    CUtensorMap tal = make_map(three ? x.lo : x.hi, 2, adims, astr, abox, 128);
+    uint64_t astr[1] = {(uint64_t)C * es};
+    uint32_t abox[2] = {(uint32_t)kel, 128};
+    CUtensorMap tah = make_map(x.hi, 2, adims, astr, abox, 128, h16);
+    CUtensorMap tal = make_map(three ? x.lo : x.hi, 2, adims, astr, abox, 128, h16);
     uint64_t d1[2] = {(uint64_t)w1.k_pad, (uint64_t)w1.n_pad};
-    uint64_t s1[1] = {(uint64_t)w1.k_pad * 4};
-    uint32_t b1box[2] = {32, (uint32_t)MLP_HC};
-    CUtensorMap t1h = make_map(w1.hi, 2, d1, s1, b1box, 128);
-    CUtensorMap t1l = make_map(three ? w1.lo : w1.hi, 2, d1, s1, b1box, 128);
+    uint64_t s1[1] = {(uint64_t)w1.k_pad * es};
+    uint32_t b1box[2] = {(uint32_t)kel, (uint32_t)MLP_HC};
+    CUtensorMap t1h = make_map(w1.hi, 2, d1, s1, b1box, 128, h16);
+    CUtensorMap t1l = make_map(three ? w1.lo : w1.hi, 2, d1, s1, b1box, 128, h16);
     uint64_t d2[2] = {(uint64_t)w2.k_pad, (uint64_t)w2.n_pad};
-    uint64_t s2[1] = {(uint64_t)w2.k_pad * 4};
-    uint32_t b2box[2] = {32, (uint32_t)w2.n_pad};
-    CUtensorMap t2h = make_map(w2.hi, 2, d2, s2, b2box, 128);
-    CUtensorMap t2l = make_map(three ? w2.lo : w2.hi, 2, d2, s2, b2box, 128);
+    uint64_t s2[1] = {(uint64_t)w2.k_pad * es};
+    uint32_t b2box[2] = {(uint32_t)kel, (uint32_t)w2.n_pad};
+    CUtensorMap t2h = make_map(w2.hi, 2, d2, s2, b2box, 128, h16);
+    CUtensorMap t2l = make_map(three ? w2.lo : w2.hi, 2, d2, s2, b2box, 128, h16);
 
     MlpArgs g{};
     g.C = C;
     g.HID = w1.n;
     g.NCH = w1.n_pad / MLP_HC;
     g.CP = w2.n_pad;
-    g.KB1 = w1.k_pad / 32;
+    g.KB1 = (C + kel - 1) / kel;
+    g.klast1 = (C - (g.KB1 - 1) * kel + kstep - 1) / kstep;
+    g.s1 = h16 ? w1.scale : 1.f;
     g.mtiles = (m + 127) / 128;
     g.b1 = b1;
     const long st_bytes = std::max(2L * 128 * 128 + 2L * MLP_HC * 128, 2L * g.CP * 128);
@@ -1103,27 +1200,23 @@ long umma_mlp(int mode, Opnd x, const GemmW& w1, const float* b1, const GemmW& w
     u.err = err;
     u.mtiles = g.mtiles;
     u.ntiles = g.mtiles;
+    u.ascale = h16 ? w2.scale : 1.f;
     Epi e;
     e.bias = b2;
     e.res = res;
     if (C % 4) throw Error(1, "umma_mlp: the width must be a multiple of 4");
     const size_t smem = (size_t)g.stages * st_bytes + 1024;
-    static unsigned configured[2] = {0, 0};
+    static unsigned configured[3] = {0, 0, 0};
     int dev = 0;
     HAT_CUDA(cudaGetDevice(&dev));
-    const int which = three ? 0 : 1;
+    const int which = h16 ? 2 : three ? 0 : 1;
+    auto kern = h16 ? k_mlp<3, true> : three ? k_mlp<3, false> : k_mlp<1, false>;
     if (!(configured[which] & (1u << dev))) {
-        if (three)
-            HAT_CUDA(cudaFuncSetAttribute(k_mlp<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_CAP));
-        else
-            HAT_CUDA(cudaFuncSetAttribute(k_mlp<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_CAP));
+        HAT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_CAP));
         configured[which] |= 1u << dev;
     }
     const long grid = std::min<long>(g.mtiles, num_sms());
-    if (three)
-        k_mlp<3><<<(unsigned)grid, NTHREADS, smem, st>>>(tah, tal, t1h, t1l, t2h, t2l, g, e);
-    else
-        k_mlp<1><<<(unsigned)grid, NTHREADS, smem, st>>>(tah, tal, t1h, t1l, t2h, t2l, g, e);
+    kern<<<(unsigned)grid, NTHREADS, smem, st>>>(tah, tal, t1h, t1l, t2h, t2l, g, e);
     HAT_CUDA(cudaGetLastError());
     count_launch();
     return 0;

@@ -9,8 +9,11 @@ namespace hat {
 // A Linear or 3x3 Conv2d weight in the layouts the kernels read.
 //  * `simt`: linear [n][k]; conv [n][9][cin] (tap-major K).
 //  * `hi`/`lo`: the tensor-core B operand [n_pad][k_pad], K-major, zero padded, split
-//    so that hi is exactly representable in tf32 and hi + lo is the fp32 weight. For a
-//    conv, K = 9 taps x `cinp` channels (cinp = 8, or a multiple of 32).
+//    the way the operand planes it multiplies are (see Opnd): tf32 pairs, or (`h16`)
+//    fp16 pairs of the weight times 2^e, with e chosen so that the largest |w| lands in
+//    [2^14, 2^15) and `scale` = 2^-e undoing it in the epilogue (a power of two: exact).
+//    For a conv, K = 9 taps x `cinp` channels, `cinp` a multiple of the channel chunk
+//    one k-block of a tap covers (`ckb` bytes: 128, or 32 for narrow inputs).
 struct GemmW {
     const float* simt = nullptr;
     const float* hi = nullptr;
@@ -20,8 +23,11 @@ struct GemmW {
     int cin = 0;            // conv input channels
     int cin_plane = 0;      // channel stride of the conv's input plane (>= cin)
     int cinp = 0;           // conv channels per tap in the tensor-core K layout
+    int ckb = 128;          // bytes of K per k-block row
     int bn = 0, n_pad = 0, k_pad = 0;
     bool umma = false;      // tensor-core layout present
+    bool h16 = false;       // fp16 split (kind::f16) rather than tf32 (kind::tf32)
+    float scale = 1.f;      // h16: the accumulator's factor (2^-e)
 };
 
 
@@ -35,13 +41,16 @@ inline int umma_bn(int n) {
 
 // Device-side weight preparation (k_prep.cu). `w` is the PyTorch layout on the device;
 // the outputs are allocated by the caller with the sizes `plan_gemm_w` sets.
-void plan_gemm_w(GemmW& g, int n, int k_or_cin, bool conv, int cin_plane);
+void plan_gemm_w(GemmW& g, int n, int k_or_cin, bool conv, int cin_plane, bool h16 = false);
+// The power of two 2^e that puts max|w| in [2^14, 2^15) (1 for an all-zero weight).
+float h16_weight_factor(float max_abs);
 size_t gemm_w_floats(const GemmW& g);  // simt + hi + lo floats
 void launch_prep_gemm_w(const float* w, float* simt, float* hi, float* lo, const GemmW& g, cudaStream_t st);
 // [cout][cin][3][3] conv weights -> the per-tap linear [9*cout][cin] (row tap*cout + co).
 void launch_prep_taps(const float* w, float* out, int cout, int cin, cudaStream_t st);
 
-// Tensor-core launchers (`x.lo` required in parity mode); return the number of
+// Tensor-core launchers (`x.lo` required in parity mode, split the same way as the
+// weight: `x.h16 == w.h16`); return the number of
 // channel-sum partial rows written when `e.colsum` is set.
 long umma_linear(int mode, Opnd x, const GemmW& w, Dst y, long m, const Epi& e, int* err, cudaStream_t st);
 long umma_conv3x3(int mode, Opnd x, const GemmW& w, Dst y, int hgt, int wid, const Epi& e, int* err,
