@@ -27,7 +27,9 @@
 // P stays below 2^RESCALE_LOG2); then the row's O in tensor memory and l are scaled by
 // exp(m_old - m_new) first. With RESCALE_LOG2 = 8 that is rare, so O is read once per
 // item, not once per key block. P and l carry a factor 2^P_SHIFT (P below 2^14), which
-// keeps more of P's split above fp16's subnormals and cancels in O / l.
+// keeps more of P's split above fp16's subnormals and cancels in O / l. S, the bias
+// table and the shift mask are in log2 units (q is scaled by scale * log2(e)), so P is
+// one ex2 per key.
 //
 // The window partition, the cyclic roll, the nn.Unfold of the keys with its zero
 // padding, the relative-position bias gather and the shift mask are address
@@ -123,16 +125,14 @@ __device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a, uint64_t b, uint3
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n"
         ::"r"(d), "r"(a), "l"(b), "r"(idesc), "r"(acc));
 }
-// fp16 pair (a in the low half, b in the high half) as one 32-bit word.
-__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
-    __half2 h = __floats2half2_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&h);
+// 2^x by the PTX ex2.approx instruction (relative error about 2^-22; subnormal results
+// flush to zero, which P never needs).
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
-// x = hi + lo in fp16 (round to nearest both times); returns hi, lo through the pair.
-__device__ __forceinline__ void split_h(float x, float& hi, float& lo) {
-    hi = __half2float(__float2half_rn(x));
-    lo = x - hi;
-}
+constexpr float L2E = 1.4426950408889634f;  // log2(e): S, the bias and the mask in log2 units
 __device__ __forceinline__ void commit(uint64_t* b) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su(b))
                  : "memory");
@@ -240,7 +240,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
         const int r = i / TR, s = i - r * TR;
         int src = OCA ? (r - 22) * TW + (s - 22) : r * TW + s;
         if (src < 0) src += TR * TW;
-        tab[r * TSTRIDE + s] = table[(long)src * heads + head];
+        tab[r * TSTRIDE + s] = table[(long)src * heads + head] * L2E;
     }
     if (OCA)
         for (int i = threadIdx.x; i < NK; i += TC_THREADS) koff[i] = (i / 24) * TSTRIDE + (i % 24);
@@ -352,7 +352,6 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
         const int q4 = warp & 3;
         const int row = q4 * 32 + lane;
         const uint32_t trow = (uint32_t)(q4 * 32) << 16;
-        constexpr float L2E = 1.4426950408889634f;
         constexpr int VW = (D % 4 == 0) ? 4 : 2;
         long g = 0;
         uint32_t ti = 0;
@@ -413,18 +412,17 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
                         v = sv[k] + trow_sa[-((k >> 4) * TSTRIDE + (k & 15))];
                         if (masked) {
                             const uint32_t mr = (k >> 4) ? mrow1 : mrow0;
-                            if ((mr >> (k & 15)) & 1u) v += -100.f;
+                            if ((mr >> (k & 15)) & 1u) v += -100.f * L2E;
                         }
                     }
-                    sv[k] = v * L2E;  // log2 units from here on
+                    sv[k] = v;  // log2 units: q carries scale * log2(e), the table log2(e)
                     bmax = fmaxf(bmax, v);
                 }
-                bmax *= L2E;
                 // The row's reference max moves only on a large jump (first block: set).
                 const bool need = j == 0 || bmax > m + RESCALE_LOG2;
                 float a = 1.f;
                 if (need) {
-                    a = j == 0 ? 0.f : exp2f(m - bmax);
+                    a = j == 0 ? 0.f : ex2(m - bmax);
                     m = bmax;
                     l *= a;
                 }
@@ -434,13 +432,9 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
                 const float mo = m - P_SHIFT;
 #pragma unroll
                 for (int k = 0; k < 32; k += 2) {
-                    const float p0 = exp2f(sv[k] - mo), p1 = exp2f(sv[k + 1] - mo);
+                    const float p0 = ex2(sv[k] - mo), p1 = ex2(sv[k + 1] - mo);
                     psum += p0 + p1;
-                    float h0, l0, h1, l1;
-                    split_h(p0, h0, l0);
-                    split_h(p1, h1, l1);
-                    ph[k >> 1] = pack_h2(h0, h1);
-                    pl[k >> 1] = pack_h2(l0, l1);
+                    split_h16x2(p0, p1, ph[k >> 1], pl[k >> 1]);
                 }
                 tst16(tmem + trow + s * 32, ph);
                 if (TERMS == 3) tst16(tmem + trow + s * 32 + T_PLO, pl);
@@ -515,12 +509,8 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
             uint32_t h[4], l[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                float h0, l0, h1, l1;
                 range_ok &= !(fabsf(x[2 * i]) >= F16_LIMIT) && !(fabsf(x[2 * i + 1]) >= F16_LIMIT);
-                split_h(x[2 * i], h0, l0);
-                split_h(x[2 * i + 1], h1, l1);
-                h[i] = pack_h2(h0, h1);
-                l[i] = pack_h2(l0, l1);
+                split_h16x2(x[2 * i], x[2 * i + 1], h[i], l[i]);
             }
             hi = make_uint4(h[0], h[1], h[2], h[3]);
             lo = make_uint4(l[0], l[1], l[2], l[3]);
@@ -591,7 +581,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
                 load_cols(src, 0, true, qv, 16);
                 if (KH > 1) load_cols(src, 16, true, qv + 16, 16);
 #pragma unroll
-                for (int i = 0; i < KH * 16; ++i) qv[i] *= scale;
+                for (int i = 0; i < KH * 16; ++i) qv[i] *= scale * L2E;
                 const bool got = bar_wait(&q_empty, (ti & 1) ^ 1, &abort_flag, err, 17);
                 if (!__all_sync(0xffffffffu, got)) break;
 #pragma unroll
@@ -634,12 +624,8 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
                         uint32_t h[2], l[2];
 #pragma unroll
                         for (int i = 0; i < 2; ++i) {
-                            float h0, l0, h1, l1;
                             range_ok &= !(fabsf(x[2 * i]) >= F16_LIMIT) && !(fabsf(x[2 * i + 1]) >= F16_LIMIT);
-                            split_h(x[2 * i], h0, l0);
-                            split_h(x[2 * i + 1], h1, l1);
-                            h[i] = pack_h2(h0, h1);
-                            l[i] = pack_h2(l0, l1);
+                            split_h16x2(x[2 * i], x[2 * i + 1], h[i], l[i]);
                         }
                         const uint32_t o = 2 * K_BYTES + (kk0 >> 4) * 1024 + off_sw32(n, (kk0 >> 3) & 1) + (kk0 & 7) * 2;
                         *reinterpret_cast<uint2*>(kvb + o) = make_uint2(h[0], h[1]);
