@@ -213,7 +213,7 @@ enum { EK_STORE = 0, EK_SHUF2 = 1, EK_GENERIC = 2 };
 // row's 16 columns, and the residual loads and (split) stores are 64-byte row segments.
 template <int MODE>
 __device__ __forceinline__ void epi_chunk16(const UmmaArgs& g, const Epi& e, uint32_t taddr, int n0, int c0,
-                                            long mt, int q, int lane, bool valid_own, float (*stg)[17],
+                                            long mt, int q, int lane, bool valid_own, float (*stg)[16],
                                             float* cacc) {
     const int nb = n0 + c0;
     // Phase-2 geometry and the residual loads first, so their latency overlaps the TMEM
@@ -237,27 +237,31 @@ __device__ __forceinline__ void epi_chunk16(const UmmaArgs& g, const Epi& e, uin
     }
     float4 gt = make_float4(0.f, 0.f, 0.f, 0.f);
     if (e.cx && n < g.nstore) gt = *reinterpret_cast<const float4*>(e.gate + n);
-
-    float v[16];
-    tmem_ld16(taddr + c0, v);
+    // The chunk's bias, also loaded before the TMEM load so its latency overlaps it.
+    float bv[16];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) v[j] *= g.ascale;
+    for (int j = 0; j < 16; ++j) bv[j] = 0.f;
     if (e.bias) {
         if (nb + 16 <= g.N) {
 #pragma unroll
             for (int j4 = 0; j4 < 4; ++j4) {
                 const float4 b = __ldg(reinterpret_cast<const float4*>(e.bias + nb) + j4);
-                v[4 * j4] += b.x;
-                v[4 * j4 + 1] += b.y;
-                v[4 * j4 + 2] += b.z;
-                v[4 * j4 + 3] += b.w;
+                bv[4 * j4] = b.x;
+                bv[4 * j4 + 1] = b.y;
+                bv[4 * j4 + 2] = b.z;
+                bv[4 * j4 + 3] = b.w;
             }
         } else {
 #pragma unroll
             for (int j = 0; j < 16; ++j)
-                if (nb + j < g.N) v[j] += __ldg(e.bias + nb + j);
+                if (nb + j < g.N) bv[j] = __ldg(e.bias + nb + j);
         }
     }
+
+    float v[16];
+    tmem_ld16(taddr + c0, v);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = v[j] * g.ascale + bv[j];
     if (e.act == ACT_GELU) {
 #pragma unroll
         for (int j = 0; j < 16; ++j) v[j] = 0.5f * v[j] * (1.f + erff(v[j] * 0.70710678118654752f));
@@ -279,14 +283,19 @@ __device__ __forceinline__ void epi_chunk16(const UmmaArgs& g, const Epi& e, uin
             if (lane == 0 && nb + j < g.N) cacc[nb + j] += s;
         }
     }
+    // Staging tile rows of 16 floats, the four 16-byte chunks of row r rotated by
+    // (r >> 1) & 3: both the row-per-lane stores here and the 4-lanes-per-row loads
+    // below are free of bank conflicts.
 #pragma unroll
-    for (int j = 0; j < 16; ++j) stg[lane][j] = v[j];
+    for (int q = 0; q < 4; ++q)
+        *reinterpret_cast<float4*>(&stg[lane][4 * (q ^ ((lane >> 1) & 3))]) =
+            make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
     __syncwarp();
 #pragma unroll
     for (int it = 0; it < 4; ++it) {
         if (!ok[it]) continue;
         const int r = it * 8 + lr;
-        float4 o = make_float4(stg[r][lc], stg[r][lc + 1], stg[r][lc + 2], stg[r][lc + 3]);
+        float4 o = *reinterpret_cast<const float4*>(&stg[r][4 * ((lc >> 2) ^ ((r >> 1) & 3))]);
         if (e.cx) {
             o.x = (rs[it].x + o.x) + (cx[it].x * gt.x) * e.cscale;
             o.y = (rs[it].y + o.y) + (cx[it].y * gt.y) * e.cscale;
@@ -316,8 +325,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // every tile this CTA owns (in its fixed tile order), written once at the end. The
     // quarter's two epilogue warps own disjoint columns.
     __shared__ float colacc[4][256];
-    // Per epilogue warp: a 32 x 16 staging tile (padded) for the coalesced store.
-    __shared__ float stg[EPI_WARPS][32][17];
+    // Per epilogue warp: a 32 x 16 staging tile (swizzled) for the coalesced store.
+    __shared__ __align__(16) float stg[EPI_WARPS][32][16];
 
     uint8_t* sm = (uint8_t*)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
     const int S = g.stages;
@@ -468,12 +477,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 // each of the 4 sub-pixels: two float4 stores per sub-pixel.
                 const int cout = g.N / 4;
                 for (int c0 = 32 * half; c0 < g.BN; c0 += 64) {
+                    float bv[32];  // bias first, so its latency overlaps the TMEM loads
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) bv[j] = e.bias ? __ldg(e.bias + n0 + c0 + j) : 0.f;
                     float v[32];
                     tmem_ld16(taddr + c0, v);
                     tmem_ld16(taddr + c0 + 16, v + 16);
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        v[j] = epi_act(v[j] * g.ascale + (e.bias ? e.bias[n0 + c0 + j] : 0.f), e.act);
+                    for (int j = 0; j < 32; ++j) v[j] = epi_act(v[j] * g.ascale + bv[j], e.act);
                     if (valid) {
                         const int cb = (n0 + c0) / 4;
 #pragma unroll
@@ -680,7 +691,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     __shared__ uint64_t full[6], empty[6], d1_full, d1_free, h_full, h_empty, d2_full, d2_free, drain;
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int abort_flag;
-    __shared__ float stg[EPI_WARPS][32][17];
+    __shared__ __align__(16) float stg[EPI_WARPS][32][16];
     __shared__ float no_colsum[256];
     __shared__ float b1s[MLP_MAXH];  // fc1 bias, zero past HID (read by every chunk)
 
