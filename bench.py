@@ -66,7 +66,7 @@ def baseline_mpixs():
 # DRAM bytes (read + write) per launch of a kernel kind at this workload, from one ncu
 # capture (dram__bytes_read.sum + dram__bytes_write.sum); profiles/ holds the capture's
 # summary and command. Kinds without a capture report null.
-NCU_TRAFFIC_BYTES = {"attn.window": 720.8e6}  # profiles/k_attn_tc_window_hats_x4_512.md
+NCU_TRAFFIC_BYTES = {"attn.window": 583.4e6}  # profiles/k_attn_tc_window_hats_x4_512.md
 
 
 def peaks():
@@ -285,13 +285,19 @@ def run_ours(args):
     total_ms = sum(v["ms"] for v in prof.values())
     if top["flops"] > 0:
         achieved = top["flops"] / (top["ms"] / 1e3) / 1e12
-        # Parity mode issues every product as 3 TF32 MMAs, and the TF32 pipe runs at half
-        # the bf16 rate: tf32_pipe_frac is the tensor pipe's own utilisation.
-        terms = 3 if mode == hat_b200.MODE_PARITY else 1
+        # Parity mode issues every product as 3 MMAs: fp16 pairs (kind::f16, the bf16 rate)
+        # when the width is a multiple of 8, else tf32 pairs (kind::tf32, half that rate);
+        # fast mode one tf32 MMA. pipe_frac is the tensor pipe's own utilisation.
+        parity = mode == hat_b200.MODE_PARITY
+        from hat_b200 import checkpoint as ck_mod
+        h16 = parity and ck_mod.VARIANTS[VARIANT]["embed_dim"] % 8 == 0
+        terms = 3 if parity else 1
+        pipe_peak = tf if h16 else tf / 2
         roof = {"kernel": top_kind, "bound": "tensor", "achieved": achieved, "peak": tf,
                 "unit": "TFLOP/s", "frac": achieved / tf, "traffic": None,
                 "peak_source": f"{src} bf16 dense (MEASURED_PEAKS.json)",
-                "tf32_pipe_frac": terms * achieved / (tf / 2),
+                "pipe_frac": terms * achieved / pipe_peak,
+                "pipe_kind": "f16" if h16 else "tf32",
                 "share_of_pass": top["ms"] / total_ms, "launches": top["launches"]}
     else:
         achieved = top["bytes"] / (top["ms"] / 1e3) / 1e9
