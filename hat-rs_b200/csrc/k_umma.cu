@@ -206,15 +206,38 @@ __device__ __forceinline__ void tile_row(const UmmaArgs& g, long mt, int trow, l
 // everything else (planar output, other shuffle factors, odd strides).
 enum { EK_STORE = 0, EK_SHUF2 = 1, EK_GENERIC = 2 };
 
+// The bias of columns nb .. nb+15 (zeros past N or without a bias).
+__device__ __forceinline__ void load_bias16(const UmmaArgs& g, const Epi& e, int nb, float* bv) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) bv[j] = 0.f;
+    if (e.bias) {
+        if (nb + 16 <= g.N) {
+#pragma unroll
+            for (int j4 = 0; j4 < 4; ++j4) {
+                const float4 b = __ldg(reinterpret_cast<const float4*>(e.bias + nb) + j4);
+                bv[4 * j4] = b.x;
+                bv[4 * j4 + 1] = b.y;
+                bv[4 * j4 + 2] = b.z;
+                bv[4 * j4 + 3] = b.w;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (nb + j < g.N) bv[j] = __ldg(e.bias + nb + j);
+        }
+    }
+}
+
 // One 16-column chunk of an epilogue warp's 32 rows with a plain (possibly residual)
 // store. Phase 1: each thread holds its own row's accumulators (TMEM lane = row), adds
 // bias and activation, contributes the channel sums, and parks the values in the
 // warp's staging tile. Phase 2: the warp re-reads the tile so that four lanes cover one
 // row's 16 columns, and the residual loads and (split) stores are 64-byte row segments.
+// `bv` is the chunk's bias, loaded by the caller a chunk ahead.
 template <int MODE>
 __device__ __forceinline__ void epi_chunk16(const UmmaArgs& g, const Epi& e, uint32_t taddr, int n0, int c0,
                                             long mt, int q, int lane, bool valid_own, float (*stg)[16],
-                                            float* cacc) {
+                                            float* cacc, const float* bv) {
     const int nb = n0 + c0;
     // Phase-2 geometry and the residual loads first, so their latency overlaps the TMEM
     // load and the register work of phase 1.
@@ -237,27 +260,6 @@ __device__ __forceinline__ void epi_chunk16(const UmmaArgs& g, const Epi& e, uin
     }
     float4 gt = make_float4(0.f, 0.f, 0.f, 0.f);
     if (e.cx && n < g.nstore) gt = *reinterpret_cast<const float4*>(e.gate + n);
-    // The chunk's bias, also loaded before the TMEM load so its latency overlaps it.
-    float bv[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) bv[j] = 0.f;
-    if (e.bias) {
-        if (nb + 16 <= g.N) {
-#pragma unroll
-            for (int j4 = 0; j4 < 4; ++j4) {
-                const float4 b = __ldg(reinterpret_cast<const float4*>(e.bias + nb) + j4);
-                bv[4 * j4] = b.x;
-                bv[4 * j4 + 1] = b.y;
-                bv[4 * j4 + 2] = b.z;
-                bv[4 * j4 + 3] = b.w;
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-                if (nb + j < g.N) bv[j] = __ldg(e.bias + nb + j);
-        }
-    }
-
     float v[16];
     tmem_ld16(taddr + c0, v);
 #pragma unroll
@@ -501,9 +503,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 continue;
             }
             if (EK == EK_STORE) {
+                // each chunk's bias is loaded while the chunk before it is processed
+                float bcur[16], bnext[16];
+                load_bias16(g, e, n0 + 16 * half, bcur);
 #pragma unroll 1
-                for (int c0 = 16 * half; c0 < g.BN; c0 += 32)
-                    epi_chunk16<MODE>(g, e, taddr, n0, c0, mt, q, lane, valid, stg[ew], colacc[q]);
+                for (int c0 = 16 * half; c0 < g.BN; c0 += 32) {
+                    if (c0 + 32 < g.BN) load_bias16(g, e, n0 + c0 + 32, bnext);
+                    epi_chunk16<MODE>(g, e, taddr, n0, c0, mt, q, lane, valid, stg[ew], colacc[q], bcur);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) bcur[j] = bnext[j];
+                }
                 tc_fence_before();
                 mbar_arrive(&acc_empty[a]);
                 continue;
@@ -953,9 +962,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             tc_fence_after();
             const long m = t * 128 + row;
             const bool valid = m < g.st.M;
+            float bcur[16], bnext[16];
+            load_bias16(g.st, e, 16 * half, bcur);
 #pragma unroll 1
-            for (int c0 = 16 * half; c0 < g.CP; c0 += 32)
-                epi_chunk16<0>(g.st, e, tmem + lanes + T_D2, 0, c0, t, q4, lane, valid, stg[ew], no_colsum);
+            for (int c0 = 16 * half; c0 < g.CP; c0 += 32) {
+                if (c0 + 32 < g.CP) load_bias16(g.st, e, c0 + 32, bnext);
+                epi_chunk16<0>(g.st, e, tmem + lanes + T_D2, 0, c0, t, q4, lane, valid, stg[ew], no_colsum, bcur);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) bcur[j] = bnext[j];
+            }
             tc_fence_before();
             mbar_arrive(&d2_free);
         }
