@@ -129,8 +129,53 @@ __global__ void k_layernorm(const float* __restrict__ x, const float* __restrict
     }
 }
 
+
+// Half a warp per token: lanes 0-15 one token, 16-31 the next; lane l holds channels
+// l, l+16, ... (MAXV of them), so each load instruction covers 64 bytes of each token.
+template <int MAXV>
+__global__ void k_layernorm16(const float* __restrict__ x, const float* __restrict__ g,
+                              const float* __restrict__ b, Dst y, long m, int c) {
+    const int lane = threadIdx.x & 31, hl = lane & 15;
+    const long row = ((long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * 2 + (lane >> 4);
+    const bool live = row < m;
+    const float* xr = x + (live ? row : 0) * c;
+    float v[MAXV];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        const int ch = i * 16 + hl;
+        v[i] = live && ch < c ? xr[ch] : 0.f;
+        s += v[i];
+    }
+#pragma unroll
+    for (int o = 8; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float mean = s / (float)c;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        const int ch = i * 16 + hl;
+        const float d = ch < c ? v[i] - mean : 0.f;
+        q += d * d;
+    }
+#pragma unroll
+    for (int o = 8; o; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    const float rstd = 1.f / sqrtf(q / (float)c + 1e-5f);
+    if (!live) return;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        const int ch = i * 16 + hl;
+        if (ch < c) put(y, row * c + ch, (v[i] - mean) * rstd * g[ch] + b[ch]);
+    }
+}
+
 void launch_layernorm(const float* x, const float* g, const float* b, Dst y, long m, int c, cudaStream_t st) {
     if (c > 256) throw Error(1, "layernorm: c > 256 is not supported");
+    if (c <= 144) {
+        k_layernorm16<9><<<(unsigned)((m + 15) / 16), 256, 0, st>>>(x, g, b, y, m, c);
+        HAT_CUDA(cudaGetLastError());
+        count_launch();
+        return;
+    }
     unsigned grid = (unsigned)((m + 7) / 8);
     if (c <= 160)
         k_layernorm<5><<<grid, 256, 0, st>>>(x, g, b, y, m, c);

@@ -160,6 +160,23 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Bulk tensor stores from shared memory (the epilogue's staging tiles).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
+                 ::"l"((uint64_t)map), "r"(c0), "r"(c1), "r"(smem_u32(src))
+                 : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int c1, int c2) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];"
+                 ::"l"((uint64_t)map), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(src))
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// the staging tile may be written again (the stores in flight have read it)
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// every store issued has completed
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 __device__ __forceinline__ float epi_act(float v, int act) {
     if (act == ACT_GELU) return 0.5f * v * (1.f + erff(v * 0.70710678118654752f));
     if (act == ACT_LEAKY) return v > 0.f ? v : 0.01f * v;
@@ -184,6 +201,7 @@ struct UmmaArgs {
     Dst y;
     int ldo;         // row stride of the output plane (channels), for plain stores
     int nstore;      // columns stored (<= ldo)
+    int tma_st;      // 1: plain fp32 stores by TMA from the staging tiles (the output's tensor map)
     int* err;
 };
 
@@ -202,9 +220,10 @@ __device__ __forceinline__ void tile_row(const UmmaArgs& g, long mt, int trow, l
 
 // Epilogue kinds, one kernel instantiation each so a kernel carries only its own store
 // path (the instruction footprint of all of them together thrashed the instruction
-// cache): EK_STORE plain/residual stores, EK_SHUF2 PixelShuffle(2) stores, EK_GENERIC
-// everything else (planar output, other shuffle factors, odd strides).
-enum { EK_STORE = 0, EK_SHUF2 = 1, EK_GENERIC = 2 };
+// cache): EK_STORE plain/residual stores, EK_TMA plain fp32 stores without a residual by
+// TMA, EK_SHUF2 PixelShuffle(2) stores, EK_GENERIC everything else (planar output, other
+// shuffle factors, odd strides).
+enum { EK_STORE = 0, EK_SHUF2 = 1, EK_GENERIC = 2, EK_TMA = 3 };
 
 // The bias of columns nb .. nb+15 (zeros past N or without a bias).
 __device__ __forceinline__ void load_bias16(const UmmaArgs& g, const Epi& e, int nb, float* bv) {
@@ -234,11 +253,88 @@ __device__ __forceinline__ void load_bias16(const UmmaArgs& g, const Epi& e, int
 // warp's staging tile. Phase 2: the warp re-reads the tile so that four lanes cover one
 // row's 16 columns, and the residual loads and (split) stores are 64-byte row segments.
 // `bv` is the chunk's bias, loaded by the caller a chunk ahead.
-template <int MODE>
+template <int MODE, bool TMA>
 __device__ __forceinline__ void epi_chunk16(const UmmaArgs& g, const Epi& e, uint32_t taddr, int n0, int c0,
                                             long mt, int q, int lane, bool valid_own, float (*stg)[16],
-                                            float* cacc, const float* bv) {
+                                            float* cacc, const float* bv, const CUtensorMap* tmy) {
     const int nb = n0 + c0;
+    if (TMA) {
+        // fp32 output by TMA: each lane finishes its own row (residual loaded row-wise),
+        // parks it in the staging tile in the 64-byte-swizzle layout of the output's
+        // tensor map, and one lane stores the 32 x 16 tile.
+        long m;
+        bool vrow;
+        tile_row<MODE>(g, mt, q * 32 + lane, m, vrow);
+        float4 r4[4], c4[4], g4[4];
+#pragma unroll
+        for (int j4 = 0; j4 < 4; ++j4) {
+            const bool in = vrow && nb + 4 * j4 < g.nstore;
+            r4[j4] = make_float4(0.f, 0.f, 0.f, 0.f);
+            c4[j4] = r4[j4];
+            g4[j4] = r4[j4];
+            if (in && e.res) r4[j4] = *reinterpret_cast<const float4*>(e.res + m * g.ldo + nb + 4 * j4);
+            if (in && e.cx) {
+                c4[j4] = *reinterpret_cast<const float4*>(e.cx + m * g.ldo + nb + 4 * j4);
+                g4[j4] = *reinterpret_cast<const float4*>(e.gate + nb + 4 * j4);
+            }
+        }
+        float v[16];
+        tmem_ld16(taddr + c0, v);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = v[j] * g.ascale + bv[j];
+        if (e.act == ACT_GELU) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = 0.5f * v[j] * (1.f + erff(v[j] * 0.70710678118654752f));
+        } else if (e.act == ACT_LEAKY) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = v[j] > 0.f ? v[j] : 0.01f * v[j];
+        }
+        if (nb + 16 > g.N) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (nb + j >= g.N) v[j] = 0.f;
+        }
+        if (e.colsum) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                float sm = valid_own ? v[j] : 0.f;
+#pragma unroll
+                for (int o = 16; o; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+                if (lane == 0 && nb + j < g.N) cacc[nb + j] += sm;
+            }
+        }
+        float o[16];
+#pragma unroll
+        for (int j4 = 0; j4 < 4; ++j4) {
+            const float rr[4] = {r4[j4].x, r4[j4].y, r4[j4].z, r4[j4].w};
+            const float cc[4] = {c4[j4].x, c4[j4].y, c4[j4].z, c4[j4].w};
+            const float gg[4] = {g4[j4].x, g4[j4].y, g4[j4].z, g4[j4].w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int j = 4 * j4 + u;
+                o[j] = e.cx ? (rr[u] + v[j]) + (cc[u] * gg[u]) * e.cscale : (e.res ? rr[u] + v[j] : v[j]);
+            }
+        }
+        // the previous chunk's store has read the tile
+        if (lane == 0) bulk_wait_read();
+        __syncwarp();
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq)
+            *reinterpret_cast<float4*>(&stg[lane][4 * (qq ^ ((lane >> 1) & 3))]) =
+                make_float4(o[4 * qq], o[4 * qq + 1], o[4 * qq + 2], o[4 * qq + 3]);
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+            if (MODE == 0) {
+                tma_store_2d(tmy, &stg[0][0], nb, (int)(mt * 128 + q * 32));
+            } else {
+                const int py = (g.ty0 + (int)(mt / g.tx)) * 8 + 2 * q, px = (int)(mt % g.tx) * 16;
+                tma_store_3d(tmy, &stg[0][0], nb, px, py);
+            }
+            bulk_commit();
+        }
+        return;
+    }
     // Phase-2 geometry and the residual loads first, so their latency overlaps the TMEM
     // load and the register work of phase 1.
     const int lr = lane >> 2, lc = (lane & 3) * 4;
@@ -318,7 +414,7 @@ template <int MODE, int TERMS, int EK, bool H16>
 __global__ void __launch_bounds__(NTHREADS, 1)
     k_umma(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
            const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl, const UmmaArgs g,
-           const Epi e) {
+           const Epi e, const __grid_constant__ CUtensorMap tmY) {
     extern __shared__ __align__(1024) uint8_t smraw[];
     __shared__ uint64_t full[6], empty[6], acc_full[2], acc_empty[2], drain;
     __shared__ uint32_t tmem_slot;
@@ -327,8 +423,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // every tile this CTA owns (in its fixed tile order), written once at the end. The
     // quarter's two epilogue warps own disjoint columns.
     __shared__ float colacc[4][256];
-    // Per epilogue warp: a 32 x 16 staging tile (swizzled) for the coalesced store.
-    __shared__ __align__(16) float stg[EPI_WARPS][32][16];
+    // Per epilogue warp: a 32 x 16 staging tile (swizzled) for the coalesced store; the
+    // rotation is the 64-byte swizzle of the TMA store path, whose pattern needs the
+    // tiles 512-byte aligned.
+    __shared__ __align__(1024) float stg[EPI_WARPS][32][16];
 
     uint8_t* sm = (uint8_t*)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
     const int S = g.stages;
@@ -502,14 +600,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 mbar_arrive(&acc_empty[a]);
                 continue;
             }
-            if (EK == EK_STORE) {
+            if (EK == EK_STORE || EK == EK_TMA) {
                 // each chunk's bias is loaded while the chunk before it is processed
                 float bcur[16], bnext[16];
                 load_bias16(g, e, n0 + 16 * half, bcur);
 #pragma unroll 1
                 for (int c0 = 16 * half; c0 < g.BN; c0 += 32) {
                     if (c0 + 32 < g.BN) load_bias16(g, e, n0 + c0 + 32, bnext);
-                    epi_chunk16<MODE>(g, e, taddr, n0, c0, mt, q, lane, valid, stg[ew], colacc[q], bcur);
+                    epi_chunk16<MODE, EK == EK_TMA>(g, e, taddr, n0, c0, mt, q, lane, valid, stg[ew], colacc[q], bcur,
+                                                    &tmY);
 #pragma unroll
                     for (int j = 0; j < 16; ++j) bcur[j] = bnext[j];
                 }
@@ -615,6 +714,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
     }
 
+    // The epilogue's bulk stores complete before the CTA (and its staging tiles) go away.
+    if (EK == EK_TMA && warp >= 2 && lane == 0) bulk_wait_all();
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
@@ -700,7 +801,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     __shared__ uint64_t full[6], empty[6], d1_full, d1_free, h_full, h_empty, d2_full, d2_free, drain;
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int abort_flag;
-    __shared__ __align__(16) float stg[EPI_WARPS][32][16];
+    __shared__ __align__(1024) float stg[EPI_WARPS][32][16];
     __shared__ float no_colsum[256];
     __shared__ float b1s[MLP_MAXH];  // fc1 bias, zero past HID (read by every chunk)
 
@@ -967,7 +1068,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll 1
             for (int c0 = 16 * half; c0 < g.CP; c0 += 32) {
                 if (c0 + 32 < g.CP) load_bias16(g.st, e, c0 + 32, bnext);
-                epi_chunk16<0>(g.st, e, tmem + lanes + T_D2, 0, c0, t, q4, lane, valid, stg[ew], no_colsum, bcur);
+                epi_chunk16<0, false>(g.st, e, tmem + lanes + T_D2, 0, c0, t, q4, lane, valid, stg[ew], no_colsum,
+                                      bcur, nullptr);
 #pragma unroll
                 for (int j = 0; j < 16; ++j) bcur[j] = bnext[j];
             }
@@ -1012,7 +1114,9 @@ static CUtensorMap make_map(const void* base, int rank, const uint64_t* dims, co
     CUresult r = encode_fn()(&m, h16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank,
                              const_cast<void*>(base), dims,
                              strides_bytes, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                             rowbytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_32B,
+                             rowbytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                             : rowbytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                              : CU_TENSOR_MAP_SWIZZLE_32B,
                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) throw Error(3, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
     return m;
@@ -1033,7 +1137,7 @@ static const long SMEM_CAP = 232448 - 22528;
 
 template <int MODE, int TERMS, int EK, bool H16>
 static void launch_ek(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh, const CUtensorMap& bl,
-                      const UmmaArgs& g, const Epi& e, cudaStream_t st) {
+                      const UmmaArgs& g, const Epi& e, const CUtensorMap& ty, cudaStream_t st) {
     const size_t smem = (size_t)g.stages * (2 * 128 * g.ckb + 2 * g.BN * g.ckb) + 1024;
     static unsigned configured = 0;
     int dev = 0;
@@ -1045,7 +1149,7 @@ static void launch_ek(const CUtensorMap& ah, const CUtensorMap& al, const CUtens
     }
     const long grid = std::min<long>(g.ntiles, num_sms());
     if (e.colsum && g.N > 256) throw Error(1, "umma: channel sums are limited to 256 columns");
-    k_umma<MODE, TERMS, EK, H16><<<(unsigned)grid, NTHREADS, smem, st>>>(ah, al, bh, bl, g, e);
+    k_umma<MODE, TERMS, EK, H16><<<(unsigned)grid, NTHREADS, smem, st>>>(ah, al, bh, bl, g, e, ty);
     HAT_CUDA(cudaGetLastError());
     count_launch();
 }
@@ -1059,13 +1163,42 @@ static int pick_ek(const UmmaArgs& g, const Epi& e) {
     return EK_GENERIC;
 }
 
+// The output's tensor map for the TMA-store epilogue (plain fp32 stores of EK_STORE without
+// a residual), or false when the launch keeps the lanes' own stores. MODE 0: [M][ldo] rows; MODE 1: the
+// [H][W][ldo] plane, a lane quarter's 32 rows being 2 pixel rows of 16.
+template <int MODE>
+static bool store_map(const UmmaArgs& g, const Epi& e, CUtensorMap& ty) {
+    // Residual epilogues keep the lanes' stores: their residual loads are coalesced there
+    // (row-wise loads for the TMA path measured slower than what the stores saved).
+    if (pick_ek(g, e) != EK_STORE || g.y.lo || e.res || e.cx || (reinterpret_cast<uintptr_t>(g.y.hi) & 15) ||
+        g.ldo % 4 || g.nstore < 16)
+        return false;
+    if (MODE == 0) {
+        if (g.M < 32) return false;
+        uint64_t dims[2] = {(uint64_t)g.nstore, (uint64_t)g.M};
+        uint64_t str[1] = {(uint64_t)g.ldo * 4};
+        uint32_t box[2] = {16, 32};
+        ty = make_map(g.y.hi, 2, dims, str, box, 64);
+    } else {
+        if (g.H < 2 || g.W < 16) return false;
+        uint64_t dims[3] = {(uint64_t)g.nstore, (uint64_t)g.W, (uint64_t)g.H};
+        uint64_t str[2] = {(uint64_t)g.ldo * 4, (uint64_t)g.W * g.ldo * 4};
+        uint32_t box[3] = {16, 16, 2};
+        ty = make_map(g.y.hi, 3, dims, str, box, 64);
+    }
+    return true;
+}
+
 template <int MODE, int TERMS, bool H16>
 static void launch_k(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh, const CUtensorMap& bl,
-                     const UmmaArgs& g, const Epi& e, cudaStream_t st) {
-    switch (pick_ek(g, e)) {
-        case EK_STORE: launch_ek<MODE, TERMS, EK_STORE, H16>(ah, al, bh, bl, g, e, st); break;
-        case EK_SHUF2: launch_ek<MODE, TERMS, EK_SHUF2, H16>(ah, al, bh, bl, g, e, st); break;
-        default: launch_ek<MODE, TERMS, EK_GENERIC, H16>(ah, al, bh, bl, g, e, st); break;
+                     UmmaArgs g, const Epi& e, cudaStream_t st) {
+    CUtensorMap ty = ah;  // unused unless the TMA-store epilogue runs
+    g.tma_st = store_map<MODE>(g, e, ty) ? 1 : 0;
+    switch (g.tma_st ? (int)EK_TMA : pick_ek(g, e)) {
+        case EK_TMA: launch_ek<MODE, TERMS, EK_TMA, H16>(ah, al, bh, bl, g, e, ty, st); break;
+        case EK_STORE: launch_ek<MODE, TERMS, EK_STORE, H16>(ah, al, bh, bl, g, e, ty, st); break;
+        case EK_SHUF2: launch_ek<MODE, TERMS, EK_SHUF2, H16>(ah, al, bh, bl, g, e, ty, st); break;
+        default: launch_ek<MODE, TERMS, EK_GENERIC, H16>(ah, al, bh, bl, g, e, ty, st); break;
     }
 }
 // parity on fp16 pairs, parity on tf32 pairs, or fast (tf32, one term)
@@ -1241,6 +1374,7 @@ long umma_mlp(int mode, Opnd x, const GemmW& w1, const float* b1, const GemmW& w
         HAT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_CAP));
         configured[which] |= 1u << dev;
     }
+    u.tma_st = 0;  // the final store keeps the lanes' own stores (a residual or a split output)
     const long grid = std::min<long>(g.mtiles, num_sms());
     kern<<<(unsigned)grid, NTHREADS, smem, st>>>(tah, tal, t1h, t1l, t2h, t2l, g, e);
     HAT_CUDA(cudaGetLastError());
