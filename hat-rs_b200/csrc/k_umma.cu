@@ -220,10 +220,10 @@ __device__ __forceinline__ void tile_row(const UmmaArgs& g, long mt, int trow, l
 
 // Epilogue kinds, one kernel instantiation each so a kernel carries only its own store
 // path (the instruction footprint of all of them together thrashed the instruction
-// cache): EK_STORE plain/residual stores, EK_TMA plain fp32 stores without a residual by
-// TMA, EK_SHUF2 PixelShuffle(2) stores, EK_GENERIC everything else (planar output, other
-// shuffle factors, odd strides).
-enum { EK_STORE = 0, EK_SHUF2 = 1, EK_GENERIC = 2, EK_TMA = 3 };
+// cache): EK_STORE plain/residual stores by the lanes, EK_TMA plain fp32 stores without a
+// residual by TMA, EK_TMA_RES fp32 stores with a residual by TMA, EK_SHUF2 PixelShuffle(2)
+// stores, EK_GENERIC everything else (planar output, other shuffle factors, odd strides).
+enum { EK_STORE = 0, EK_SHUF2 = 1, EK_GENERIC = 2, EK_TMA = 3, EK_TMA_RES = 4 };
 
 // The bias of columns nb .. nb+15 (zeros past N or without a bias).
 __device__ __forceinline__ void load_bias16(const UmmaArgs& g, const Epi& e, int nb, float* bv) {
@@ -253,12 +253,14 @@ __device__ __forceinline__ void load_bias16(const UmmaArgs& g, const Epi& e, int
 // warp's staging tile. Phase 2: the warp re-reads the tile so that four lanes cover one
 // row's 16 columns, and the residual loads and (split) stores are 64-byte row segments.
 // `bv` is the chunk's bias, loaded by the caller a chunk ahead.
-template <int MODE, bool TMA>
+// SK, how the chunk leaves: 0 the lanes' own stores (phase 2); 1 by TMA straight from
+// phase 1 (no residual); 2 by TMA after phase 2 has added the residual in place.
+template <int MODE, int SK>
 __device__ __forceinline__ void epi_chunk16(const UmmaArgs& g, const Epi& e, uint32_t taddr, int n0, int c0,
                                             long mt, int q, int lane, bool valid_own, float (*stg)[16],
                                             float* cacc, const float* bv, const CUtensorMap* tmy) {
     const int nb = n0 + c0;
-    if (TMA) {
+    if (SK == 1) {
         // fp32 output by TMA: each lane finishes its own row (residual loaded row-wise),
         // parks it in the staging tile in the 64-byte-swizzle layout of the output's
         // tensor map, and one lane stores the 32 x 16 tile.
@@ -384,6 +386,11 @@ __device__ __forceinline__ void epi_chunk16(const UmmaArgs& g, const Epi& e, uin
     // Staging tile rows of 16 floats, the four 16-byte chunks of row r rotated by
     // (r >> 1) & 3: both the row-per-lane stores here and the 4-lanes-per-row loads
     // below are free of bank conflicts.
+    if (SK == 2) {
+        // the previous chunk's store has read the tile
+        if (lane == 0) bulk_wait_read();
+        __syncwarp();
+    }
 #pragma unroll
     for (int q = 0; q < 4; ++q)
         *reinterpret_cast<float4*>(&stg[lane][4 * (q ^ ((lane >> 1) & 3))]) =
@@ -405,7 +412,24 @@ __device__ __forceinline__ void epi_chunk16(const UmmaArgs& g, const Epi& e, uin
             o.z = rs[it].z + o.z;
             o.w = rs[it].w + o.w;
         }
-        put4(g.y, base[it], o);
+        if (SK == 2)
+            *reinterpret_cast<float4*>(&stg[r][4 * ((lc >> 2) ^ ((r >> 1) & 3))]) = o;  // back in place
+        else
+            put4(g.y, base[it], o);
+    }
+    if (SK == 2) {
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+            if (MODE == 0) {
+                tma_store_2d(tmy, &stg[0][0], nb, (int)(mt * 128 + q * 32));
+            } else {
+                const int py = (g.ty0 + (int)(mt / g.tx)) * 8 + 2 * q, px = (int)(mt % g.tx) * 16;
+                tma_store_3d(tmy, &stg[0][0], nb, px, py);
+            }
+            bulk_commit();
+        }
+        return;
     }
     __syncwarp();
 }
@@ -600,15 +624,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 mbar_arrive(&acc_empty[a]);
                 continue;
             }
-            if (EK == EK_STORE || EK == EK_TMA) {
+            if (EK == EK_STORE || EK == EK_TMA || EK == EK_TMA_RES) {
                 // each chunk's bias is loaded while the chunk before it is processed
                 float bcur[16], bnext[16];
                 load_bias16(g, e, n0 + 16 * half, bcur);
 #pragma unroll 1
                 for (int c0 = 16 * half; c0 < g.BN; c0 += 32) {
                     if (c0 + 32 < g.BN) load_bias16(g, e, n0 + c0 + 32, bnext);
-                    epi_chunk16<MODE, EK == EK_TMA>(g, e, taddr, n0, c0, mt, q, lane, valid, stg[ew], colacc[q], bcur,
-                                                    &tmY);
+                    epi_chunk16<MODE, EK == EK_TMA ? 1 : EK == EK_TMA_RES ? 2 : 0>(g, e, taddr, n0, c0, mt, q, lane,
+                                                                                   valid, stg[ew], colacc[q], bcur, &tmY);
 #pragma unroll
                     for (int j = 0; j < 16; ++j) bcur[j] = bnext[j];
                 }
@@ -715,7 +739,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
 
     // The epilogue's bulk stores complete before the CTA (and its staging tiles) go away.
-    if (EK == EK_TMA && warp >= 2 && lane == 0) bulk_wait_all();
+    if ((EK == EK_TMA || EK == EK_TMA_RES) && warp >= 2 && lane == 0) bulk_wait_all();
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
@@ -791,12 +815,12 @@ __device__ __forceinline__ void tmem_st8u(uint32_t taddr, const uint32_t* r) {
                  : "memory");
 }
 
-template <int TERMS, bool H16>
+template <int TERMS, bool H16, int SK>
 __global__ void __launch_bounds__(NTHREADS, 1)
     k_mlp(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
           const __grid_constant__ CUtensorMap tmW1h, const __grid_constant__ CUtensorMap tmW1l,
           const __grid_constant__ CUtensorMap tmW2h, const __grid_constant__ CUtensorMap tmW2l, const MlpArgs g,
-          const Epi e) {
+          const Epi e, const __grid_constant__ CUtensorMap tmY) {
     extern __shared__ __align__(1024) uint8_t smraw[];
     __shared__ uint64_t full[6], empty[6], d1_full, d1_free, h_full, h_empty, d2_full, d2_free, drain;
     __shared__ uint32_t tmem_slot;
@@ -1068,8 +1092,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll 1
             for (int c0 = 16 * half; c0 < g.CP; c0 += 32) {
                 if (c0 + 32 < g.CP) load_bias16(g.st, e, c0 + 32, bnext);
-                epi_chunk16<0, false>(g.st, e, tmem + lanes + T_D2, 0, c0, t, q4, lane, valid, stg[ew], no_colsum,
-                                      bcur, nullptr);
+                epi_chunk16<0, SK>(g.st, e, tmem + lanes + T_D2, 0, c0, t, q4, lane, valid, stg[ew], no_colsum, bcur,
+                                   &tmY);
 #pragma unroll
                 for (int j = 0; j < 16; ++j) bcur[j] = bnext[j];
             }
@@ -1078,6 +1102,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
     }
 
+    if (SK != 0 && warp >= 2 && lane == 0) bulk_wait_all();
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
@@ -1163,39 +1188,44 @@ static int pick_ek(const UmmaArgs& g, const Epi& e) {
     return EK_GENERIC;
 }
 
-// The output's tensor map for the TMA-store epilogue (plain fp32 stores of EK_STORE without
-// a residual), or false when the launch keeps the lanes' own stores. MODE 0: [M][ldo] rows; MODE 1: the
-// [H][W][ldo] plane, a lane quarter's 32 rows being 2 pixel rows of 16.
+// The output's tensor map for the TMA-store epilogues (plain fp32 stores of EK_STORE) and
+// the epilogue kind that goes with it: EK_TMA without a residual, EK_TMA_RES with one (the
+// residual is added in the staging tile, where its loads are coalesced), or EK_STORE when
+// the launch keeps the lanes' own stores. MODE 0: [M][ldo] rows; MODE 1: the [H][W][ldo]
+// plane, a lane quarter's 32 rows being 2 pixel rows of 16.
 template <int MODE>
-static bool store_map(const UmmaArgs& g, const Epi& e, CUtensorMap& ty) {
-    // Residual epilogues keep the lanes' stores: their residual loads are coalesced there
-    // (row-wise loads for the TMA path measured slower than what the stores saved).
-    if (pick_ek(g, e) != EK_STORE || g.y.lo || e.res || e.cx || (reinterpret_cast<uintptr_t>(g.y.hi) & 15) ||
-        g.ldo % 4 || g.nstore < 16)
-        return false;
+static int store_map(const UmmaArgs& g, const Epi& e, CUtensorMap& ty, bool mlp = false) {
+    if (pick_ek(g, e) != EK_STORE || g.y.lo || (reinterpret_cast<uintptr_t>(g.y.hi) & 15) || g.ldo % 4 ||
+        g.nstore < 16)
+        return EK_STORE;
     if (MODE == 0) {
-        if (g.M < 32) return false;
+        if (g.M < 32) return EK_STORE;
         uint64_t dims[2] = {(uint64_t)g.nstore, (uint64_t)g.M};
         uint64_t str[1] = {(uint64_t)g.ldo * 4};
         uint32_t box[2] = {16, 32};
         ty = make_map(g.y.hi, 2, dims, str, box, 64);
     } else {
-        if (g.H < 2 || g.W < 16) return false;
+        if (g.H < 2 || g.W < 16) return EK_STORE;
         uint64_t dims[3] = {(uint64_t)g.nstore, (uint64_t)g.W, (uint64_t)g.H};
         uint64_t str[2] = {(uint64_t)g.ldo * 4, (uint64_t)g.W * g.ldo * 4};
         uint32_t box[3] = {16, 16, 2};
         ty = make_map(g.y.hi, 3, dims, str, box, 64);
     }
-    return true;
+    // With a residual only the linears gain (measured: proj faster; the fused MLP and the
+    // residual convs slower than with the lanes' stores).
+    if (e.res || e.cx) return MODE == 0 && !mlp ? EK_TMA_RES : EK_STORE;
+    return EK_TMA;
 }
 
 template <int MODE, int TERMS, bool H16>
 static void launch_k(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh, const CUtensorMap& bl,
                      UmmaArgs g, const Epi& e, cudaStream_t st) {
-    CUtensorMap ty = ah;  // unused unless the TMA-store epilogue runs
-    g.tma_st = store_map<MODE>(g, e, ty) ? 1 : 0;
-    switch (g.tma_st ? (int)EK_TMA : pick_ek(g, e)) {
+    CUtensorMap ty = ah;  // unused unless a TMA-store epilogue runs
+    const int sk = store_map<MODE>(g, e, ty);
+    g.tma_st = sk != EK_STORE;
+    switch (sk != EK_STORE ? sk : pick_ek(g, e)) {
         case EK_TMA: launch_ek<MODE, TERMS, EK_TMA, H16>(ah, al, bh, bl, g, e, ty, st); break;
+        case EK_TMA_RES: launch_ek<MODE, TERMS, EK_TMA_RES, H16>(ah, al, bh, bl, g, e, ty, st); break;
         case EK_STORE: launch_ek<MODE, TERMS, EK_STORE, H16>(ah, al, bh, bl, g, e, ty, st); break;
         case EK_SHUF2: launch_ek<MODE, TERMS, EK_SHUF2, H16>(ah, al, bh, bl, g, e, ty, st); break;
         default: launch_ek<MODE, TERMS, EK_GENERIC, H16>(ah, al, bh, bl, g, e, ty, st); break;
@@ -1365,18 +1395,26 @@ long umma_mlp(int mode, Opnd x, const GemmW& w1, const float* b1, const GemmW& w
     e.res = res;
     if (C % 4) throw Error(1, "umma_mlp: the width must be a multiple of 4");
     const size_t smem = (size_t)g.stages * st_bytes + 1024;
-    static unsigned configured[3] = {0, 0, 0};
+    CUtensorMap ty = tah;  // the output's tensor map when the final store goes by TMA
+    const int sk = store_map<0>(u, e, ty, true);
+    u.tma_st = sk != EK_STORE;
+    const int skx = sk == EK_TMA ? 1 : sk == EK_TMA_RES ? 2 : 0;
+    static unsigned configured[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
     int dev = 0;
     HAT_CUDA(cudaGetDevice(&dev));
-    const int which = h16 ? 2 : three ? 0 : 1;
-    auto kern = h16 ? k_mlp<3, true> : three ? k_mlp<3, false> : k_mlp<1, false>;
+    const int which = (h16 ? 2 : three ? 0 : 1) * 3 + skx;
+    using KFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, MlpArgs, Epi,
+                         CUtensorMap);
+    const KFn table[9] = {k_mlp<3, false, 0>, k_mlp<3, false, 1>, k_mlp<3, false, 2>,
+                          k_mlp<1, false, 0>, k_mlp<1, false, 1>, k_mlp<1, false, 2>,
+                          k_mlp<3, true, 0>,  k_mlp<3, true, 1>,  k_mlp<3, true, 2>};
+    const KFn kern = table[which];
     if (!(configured[which] & (1u << dev))) {
         HAT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_CAP));
         configured[which] |= 1u << dev;
     }
-    u.tma_st = 0;  // the final store keeps the lanes' own stores (a residual or a split output)
     const long grid = std::min<long>(g.mtiles, num_sms());
-    kern<<<(unsigned)grid, NTHREADS, smem, st>>>(tah, tal, t1h, t1l, t2h, t2l, g, e);
+    kern<<<(unsigned)grid, NTHREADS, smem, st>>>(tah, tal, t1h, t1l, t2h, t2l, g, e, ty);
     HAT_CUDA(cudaGetLastError());
     count_launch();
     return 0;
