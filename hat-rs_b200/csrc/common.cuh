@@ -222,6 +222,13 @@ struct Epi {
     // row); the input plane is still read over its full height, so rows next to the range
     // are real data, not padding. The CUDA-core conv ignores this and computes every row.
     int y_lo = 0, y_hi = 0;
+    // The qkv linear of a HAB in fp16 parity mode writes its output straight in the layout
+    // the window attention copies from (fp16 hi/lo pairs, M tokens, c = N / 3): q|k hi
+    // [M][2c], q|k lo [M][2c], v^T hi [c][M], v^T lo [c][M], one after the other from
+    // `qkv_split`, columns below `qcols` (q) multiplied by `qscale`.
+    float* qkv_split = nullptr;
+    float qscale = 1.f;
+    int qcols = 0;
 };
 
 // ---------------------------------------------------------------- kernels (launchers)
@@ -245,8 +252,9 @@ void launch_split(const float* x, float* hi, float* lo, long n, cudaStream_t st)
 
 // Window attention of one HAB over the [hp][wp][3c] qkv plane (hat_arch.py:165-196):
 // the tensor-core kernel (mode: parity / fast), or the CUDA-core one when `simt`.
+// `pre`: the qkv buffer holds the qkv linear's attention layout (Epi::qkv_split).
 void launch_window_attention(int mode, bool simt, const float* qkv, const float* table, Dst out, const Plan& p,
-                             int c, int heads, int shift, int* err, cudaStream_t st);
+                             int c, int heads, int shift, int* err, cudaStream_t st, bool pre = false);
 
 // OCAB attention over the [hp][wp][3c] qkv plane (hat_arch.py:392-438).
 void launch_overlap_attention(int mode, bool simt, const float* qkv, const float* table, Dst out, const Plan& p,

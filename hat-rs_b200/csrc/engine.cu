@@ -71,16 +71,16 @@ void launch_overlap_attention_simt(const float* qkv, const float* table, Dst out
                                    cudaStream_t st);
 
 void launch_attention_tc(int mode, bool oca, const float* qkv, const float* table, Dst out, const Plan& p, int c,
-                         int heads, int shift, int* err, cudaStream_t st);
+                         int heads, int shift, int* err, cudaStream_t st, bool pre = false);
 
 // The tensor-core kernel in parity and fast modes; the CUDA-core one for the debug path.
 void launch_window_attention(int mode, bool simt, const float* qkv, const float* table, Dst out, const Plan& p, int c,
-                             int heads, int shift, int* err, cudaStream_t st) {
-    if (simt && p.strip()) throw Error(1, "attention: strips need the tensor-core kernel");
+                             int heads, int shift, int* err, cudaStream_t st, bool pre) {
+    if (simt && (p.strip() || pre)) throw Error(1, "attention: strips and the pre-split layout need the tensor-core kernel");
     if (simt)
         launch_window_attention_simt(qkv, table, out, p, c, heads, shift, st);
     else
-        launch_attention_tc(mode, false, qkv, table, out, p, c, heads, shift, err, st);
+        launch_attention_tc(mode, false, qkv, table, out, p, c, heads, shift, err, st, pre);
 }
 
 void launch_overlap_attention(int mode, bool simt, const float* qkv, const float* table, Dst out, const Plan& p, int c,
@@ -556,15 +556,23 @@ void Engine::hab(int stage, int blk, const float* in, float* out) {
     launch_ca_gate(pooled, rows, inv_count, W(cb + ".3.attention.1.weight"), W(cb + ".3.attention.1.bias"),
                    W(cb + ".3.attention.3.weight"), W(cb + ".3.attention.3.bias"), a_->gate, c, wt_.squeezed,
                    stream_);
-    // Attention on the normed plane; odd blocks are shifted by win/2 with the mask.
+    // Attention on the normed plane; odd blocks are shifted by win/2 with the mask. With fp16
+    // operand pairs and head dim 24, the qkv linear writes q (pre-scaled by scale * log2(e)),
+    // k and v^T as the pairs the attention kernel copies (Epi::qkv_split).
     Epi eq;
     eq.bias = W(p + ".attn.qkv.bias");
+    const bool pre = h16_ && c / wt_.heads == 24 && c % wt_.heads == 0 && G(p + ".attn.qkv.weight").umma;
+    if (pre) {
+        eq.qkv_split = a_->qkv;
+        eq.qscale = 1.f / sqrtf(24.f) * 1.4426950408889634f;
+        eq.qcols = c;
+    }
     mark("linear.qkv", 6.0 * P * c * c, 16.0 * P * c);
     linear(p + ".attn.qkv.weight", O(a_->n1, a_->n1lo), Dst{a_->qkv, nullptr}, eq);
     const int shift = blk % 2 ? plan_.shift : 0;
     mark("attn.window", 4.0 * P * 256 * c, 16.0 * P * c);
     launch_window_attention(mode_, simt_only_, a_->qkv, W(p + ".attn.relative_position_bias_table"),
-                            D(a_->attn, a_->attnlo), plan_, c, wt_.heads, shift, derr_, stream_);
+                            D(a_->attn, a_->attnlo), plan_, c, wt_.heads, shift, derr_, stream_, pre);
     // proj, then `(shortcut + attn) + conv_x * conv_scale` in the epilogue.
     Epi ep;
     ep.bias = W(p + ".attn.proj.bias");

@@ -198,8 +198,11 @@ struct AttnGeom {
     int rows, wp, nwy, oy, sy, sx, ghp, yr0, gy0, olo, ohi, mshift;
 };
 
-// D: head dim (24 or 30); OCA: overlapping attention; TERMS: 3 (parity) or 1 (fast).
-template <int D, bool OCA, int TERMS>
+// D: head dim (24 or 30); OCA: overlapping attention; TERMS: 3 (parity) or 1 (fast);
+// PRE: q, k and v arrive as fp16 pairs in the qkv linear's attention layout (q|k hi and lo
+// [P][2c], v^T hi and lo [c][P], q already scaled by scale * log2(e); see Epi::qkv_split),
+// so the loaders only copy 16-byte pieces (window attention, D = 24, parity mode).
+template <int D, bool OCA, int TERMS, bool PRE>
 __global__ void __launch_bounds__(TC_THREADS, 2)
     k_attn_tc(const float* __restrict__ qkv, const float* __restrict__ table, Dst out, const AttnGeom gm, int c,
               int heads, float scale, long items, int* err) {
@@ -265,6 +268,23 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su(&tmem_slot)),
                      "n"(TMEM_COLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    if (PRE) {
+        // The head dim's padding (24 -> 32) is never copied: zero it once. Q and K: the second
+        // 16-byte piece of k-step 1 of every row; V^T: feature rows 24..31.
+        const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+        for (int i = threadIdx.x; i < 2 * MT; i += TC_THREADS)
+            *reinterpret_cast<uint4*>(sm + (i / MT) * Q_BYTES + 4096 + off_sw32(i % MT, 1)) = z;
+        for (int i = threadIdx.x; i < KVS * 2 * KBLK; i += TC_THREADS) {
+            const int st = i / (2 * KBLK), lo = (i / KBLK) & 1, key = i % KBLK;
+            *reinterpret_cast<uint4*>(sm + OFF_KV + st * KV_BYTES + lo * K_BYTES + 1024 + off_sw32(key, 1)) = z;
+        }
+        for (int i = threadIdx.x; i < KVS * 2 * 8 * 4; i += TC_THREADS) {
+            const int st = i / 64, lo = (i / 32) & 1, f = 24 + ((i / 4) & 7), ks = (i / 2) & 1, pc = i & 1;
+            *reinterpret_cast<uint4*>(sm + OFF_KV + st * KV_BYTES + 2 * K_BYTES + lo * V_BYTES + ks * 1024 +
+                                      off_sw32(f, pc)) = z;
+        }
+        fence_async();
     }
     tcf_before();
     __syncthreads();
@@ -486,6 +506,84 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
             }
             g += NBLK;
         }
+    } else if constexpr (PRE) {
+        // ------------------------------------------------------------ loaders (copies)
+        // Per item, Q: 128 rows x 3 pieces of 8 dims x (hi, lo) = 6 copies a thread; per key
+        // block, K: 32 keys x 3 x 2 and V^T: 24 features x 4 pieces of 8 keys x 2 = 3 copies a
+        // thread. A key block is two window rows, and each 8-key piece of V^T is contiguous
+        // in the plane (the roll moves windows by 8 columns, so pieces never wrap).
+        static_assert(D == 24 && !OCA && TERMS == 3, "the copy loaders are for parity window attention, D = 24");
+        const int t = threadIdx.x - 160;  // 0..127
+        const long P = (long)gm.rows * wp, c2 = 2L * c;
+        const __half* qkh = reinterpret_cast<const __half*>(qkv);
+        const __half* qkl = qkh + P * c2;
+        const __half* vth = qkl + P * c2;
+        const __half* vtl = vth + (long)c * P;
+        auto pos = [&](int wy, int wx, int y, int x) -> long {
+            return (long)((gm.oy + wy * 16 + y + gm.sy) % gm.rows) * wp + (wx * 16 + x + gm.sx) % wp;
+        };
+        long g = 0;
+        uint32_t ti = 0;
+        for (long w = blockIdx.x; w < items; w += gridDim.x, ++ti) {
+            if (__any_sync(0xffffffffu, abort_flag != 0)) break;
+            const long rest = w / heads;
+            const int win = (int)(rest >> 1), mtile = (int)(rest & 1);
+            const int wy = win / nx, wx = win - wy * nx;
+            {
+                uint4 qv[6];
+                uint32_t qd[6];
+#pragma unroll
+                for (int u = 0; u < 6; ++u) {
+                    const int cid = t + 128 * u, row = cid / 6, part = cid % 6, lo = part / 3, ch = part % 3;
+                    const int qi = mtile * MT + row;
+                    const long qpos = pos(wy, wx, qi >> 4, qi & 15);
+                    qv[u] = *reinterpret_cast<const uint4*>((lo ? qkl : qkh) + qpos * c2 + head * D + 8 * ch);
+                    qd[u] = lo * Q_BYTES + (ch >> 1) * 4096 + off_sw32(row, ch & 1);
+                }
+                const bool got = bar_wait(&q_empty, (ti & 1) ^ 1, &abort_flag, err, 17);
+                if (!__all_sync(0xffffffffu, got)) break;
+#pragma unroll
+                for (int u = 0; u < 6; ++u) *reinterpret_cast<uint4*>(sm + qd[u]) = qv[u];
+                fence_async();
+                bar_arrive(&q_full);
+            }
+            bool ok = true;
+            for (int j = 0; j < NBLK; ++j) {
+                const long gb = g + j;
+                const int s = (int)(gb % KVS);
+                uint4 cv[3];
+                uint32_t dst[3];
+#pragma unroll
+                for (int u = 0; u < 3; ++u) {
+                    const int cid = t + 128 * u;  // 0..383
+                    if (cid < 192) {
+                        const int key = cid / 6, part = cid % 6, lo = part / 3, ch = part % 3;
+                        const int kk = j * KBLK + key;
+                        const long kpos = pos(wy, wx, kk >> 4, kk & 15);
+                        cv[u] = *reinterpret_cast<const uint4*>((lo ? qkl : qkh) + kpos * c2 + c + head * D + 8 * ch);
+                        dst[u] = lo * K_BYTES + (ch >> 1) * 1024 + off_sw32(key, ch & 1);
+                    } else {
+                        const int v2 = cid - 192, f = v2 >> 3, part = v2 & 7, lo = part >> 2;
+                        const int ks = (part >> 1) & 1, pc = part & 1;  // key row 2j + ks, keys 8 pc ..
+                        const long kpos = pos(wy, wx, 2 * j + ks, 8 * pc);
+                        cv[u] = *reinterpret_cast<const uint4*>((lo ? vtl : vth) + (long)(head * D + f) * P + kpos);
+                        dst[u] = 2 * K_BYTES + lo * V_BYTES + ks * 1024 + off_sw32(f, pc);
+                    }
+                }
+                const bool got = bar_wait(&kv_empty[s], (uint32_t)(((gb / KVS) & 1) ^ 1), &abort_flag, err, 18);
+                if (!__all_sync(0xffffffffu, got)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* kvb = sm + OFF_KV + s * KV_BYTES;
+#pragma unroll
+                for (int u = 0; u < 3; ++u) *reinterpret_cast<uint4*>(kvb + dst[u]) = cv[u];
+                fence_async();
+                bar_arrive(&kv_full[s]);
+            }
+            if (!ok) break;
+            g += NBLK;
+        }
     } else {
         // ------------------------------------------------------------ loaders
         // Warps 5-6 load K: lane = key, warp = k-step (columns [0,16) / [16,32)); each
@@ -651,7 +749,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
     }
 }
 
-template <int D, bool OCA, int TERMS>
+template <int D, bool OCA, int TERMS, bool PRE = false>
 static void run_tc(const float* qkv, const float* table, Dst out, const Plan& p, int c, int heads, int shift, int* err,
                    cudaStream_t st) {
     constexpr int KH = (D + 15) / 16;
@@ -662,7 +760,8 @@ static void run_tc(const float* qkv, const float* table, Dst out, const Plan& p,
     int dev = 0;
     HAT_CUDA(cudaGetDevice(&dev));
     if (!(configured & (1u << dev))) {
-        HAT_CUDA(cudaFuncSetAttribute(k_attn_tc<D, OCA, TERMS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+        HAT_CUDA(cudaFuncSetAttribute(k_attn_tc<D, OCA, TERMS, PRE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)bytes));
         configured |= 1u << dev;
     }
     // The windows of this launch (see AttnGeom).
@@ -697,18 +796,24 @@ static void run_tc(const float* qkv, const float* table, Dst out, const Plan& p,
     // Two CTAs per SM; a multiple of the head count, so every CTA keeps one head (and
     // one bias table).
     long grid = std::min<long>(items, (long)(2 * sms / heads) * heads);
-    k_attn_tc<D, OCA, TERMS><<<(unsigned)grid, TC_THREADS, bytes, st>>>(qkv, table, out, gm, c, heads,
-                                                                        1.f / sqrtf((float)D), items, err);
+    k_attn_tc<D, OCA, TERMS, PRE><<<(unsigned)grid, TC_THREADS, bytes, st>>>(qkv, table, out, gm, c, heads,
+                                                                             1.f / sqrtf((float)D), items, err);
     HAT_CUDA(cudaGetLastError());
     count_launch();
 }
 
 void launch_attention_tc(int mode, bool oca, const float* qkv, const float* table, Dst out, const Plan& p, int c,
-                         int heads, int shift, int* err, cudaStream_t st) {
+                         int heads, int shift, int* err, cudaStream_t st, bool pre) {
     if (p.win != 16 || p.owin != 24) throw Error(1, "attention: the kernels are built for window 16 / overlap window 24");
     if (heads <= 0 || c % heads) throw Error(1, "attention: c is not divisible by heads");
     const int d = c / heads;
     const bool three = mode == 0;
+    if (pre) {
+        if (oca || d != 24 || !three || c % 8 || p.tokens() % 8)
+            throw Error(1, "attention: the pre-split qkv layout is for parity window attention with head dim 24");
+        run_tc<24, false, 3, true>(qkv, table, out, p, c, heads, shift, err, st);
+        return;
+    }
 #define HAT_ATTN_CASE(DD, O)                                                                 \
     if (d == DD && oca == O) {                                                               \
         if (three)                                                                           \

@@ -140,6 +140,7 @@ long gemm_linear(const GemmCtx& c, Opnd x, const GemmW& w, Dst y, long m, const 
     if (x.lo && x.h16 != w.h16) throw Error(1, "gemm: operand and weight split kinds differ");
     if (!c.simt_only && w.umma && ok && !e.planar_out && !e.shuffle)
         return umma_linear(c.mode, x, w, y, m, e, c.err, st);
+    if (e.qkv_split) throw Error(1, "gemm: the qkv attention layout needs the tensor-core linear");
     return simt_linear(x, w, y, m, e, st);
 }
 

@@ -222,8 +222,15 @@ __device__ __forceinline__ void tile_row(const UmmaArgs& g, long mt, int trow, l
 // path (the instruction footprint of all of them together thrashed the instruction
 // cache): EK_STORE plain/residual stores by the lanes, EK_TMA plain fp32 stores without a
 // residual by TMA, EK_TMA_RES fp32 stores with a residual by TMA, EK_SHUF2 PixelShuffle(2)
-// stores, EK_GENERIC everything else (planar output, other shuffle factors, odd strides).
-enum { EK_STORE = 0, EK_SHUF2 = 1, EK_GENERIC = 2, EK_TMA = 3, EK_TMA_RES = 4 };
+// stores, EK_GENERIC everything else (planar output, other shuffle factors, odd strides),
+// EK_QKV the qkv linear's attention layout.
+enum { EK_STORE = 0, EK_SHUF2 = 1, EK_GENERIC = 2, EK_TMA = 3, EK_TMA_RES = 4, EK_QKV = 5 };
+
+// The four output maps of EK_QKV (see Epi::qkv_split): q|k hi and lo (SW32 boxes of 16 x
+// 32), v^T hi and lo (unswizzled boxes of 32 tokens x 16 features).
+struct __align__(64) QkvMaps {
+    CUtensorMap qkh, qkl, vth, vtl;
+};
 
 // The bias of columns nb .. nb+15 (zeros past N or without a bias).
 __device__ __forceinline__ void load_bias16(const UmmaArgs& g, const Epi& e, int nb, float* bv) {
@@ -254,12 +261,72 @@ __device__ __forceinline__ void load_bias16(const UmmaArgs& g, const Epi& e, int
 // row's 16 columns, and the residual loads and (split) stores are 64-byte row segments.
 // `bv` is the chunk's bias, loaded by the caller a chunk ahead.
 // SK, how the chunk leaves: 0 the lanes' own stores (phase 2); 1 by TMA straight from
-// phase 1 (no residual); 2 by TMA after phase 2 has added the residual in place.
+// phase 1 (no residual); 2 by TMA after phase 2 has added the residual in place; 3 the
+// qkv attention layout (fp16 pairs by TMA; v transposed), see Epi::qkv_split.
 template <int MODE, int SK>
 __device__ __forceinline__ void epi_chunk16(const UmmaArgs& g, const Epi& e, uint32_t taddr, int n0, int c0,
                                             long mt, int q, int lane, bool valid_own, float (*stg)[16],
-                                            float* cacc, const float* bv, const CUtensorMap* tmy) {
+                                            float* cacc, const float* bv, const CUtensorMap* tmy,
+                                            const QkvMaps* qm = nullptr) {
     const int nb = n0 + c0;
+    if (SK == 3) {
+        float v[16];
+        tmem_ld16(taddr + c0, v);
+        const float qs = nb < e.qcols ? e.qscale : 1.f;
+        bool big = false;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            v[j] = (v[j] * g.ascale + bv[j]) * qs;
+            big |= beyond_h16(v[j]);
+        }
+        if (big) atomicCAS(g.err, 0, 21);
+        const int row0 = (int)(mt * 128 + q * 32);
+        const int c2 = 2 * (g.N / 3);  // q|k columns
+        __half* th = reinterpret_cast<__half*>(&stg[0][0]);
+        __half* tl = th + 512;  // two 1 KB tiles
+        // the previous chunk's stores have read the tiles
+        if (lane == 0) bulk_wait_read();
+        __syncwarp();
+        if (nb < c2) {
+            // q / k: this lane's row, 16 values as two 16-byte chunks per tile (32-byte rows,
+            // the chunk index flipped by (row >> 2) & 1: the 32-byte swizzle of the map)
+            uint32_t hp[8], lp[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) split_h16x2(v[2 * i], v[2 * i + 1], hp[i], lp[i]);
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                const int off = lane * 32 + (((c ^ (lane >> 2)) & 1) << 4);
+                *reinterpret_cast<uint4*>(reinterpret_cast<char*>(th) + off) =
+                    make_uint4(hp[4 * c], hp[4 * c + 1], hp[4 * c + 2], hp[4 * c + 3]);
+                *reinterpret_cast<uint4*>(reinterpret_cast<char*>(tl) + off) =
+                    make_uint4(lp[4 * c], lp[4 * c + 1], lp[4 * c + 2], lp[4 * c + 3]);
+            }
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_2d(&qm->qkh, th, nb, row0);
+                tma_store_2d(&qm->qkl, tl, nb, row0);
+                bulk_commit();
+            }
+        } else {
+            // v, transposed: tile [16 features][32 tokens], token = lane
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                __half h, l;
+                split_h16(v[j], h, l);
+                th[j * 32 + lane] = h;
+                tl[j * 32 + lane] = l;
+            }
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_2d(&qm->vth, th, row0, nb - c2);
+                tma_store_2d(&qm->vtl, tl, row0, nb - c2);
+                bulk_commit();
+            }
+        }
+        return;
+    }
     if (SK == 1) {
         // fp32 output by TMA: each lane finishes its own row (residual loaded row-wise),
         // parks it in the staging tile in the 64-byte-swizzle layout of the output's
@@ -438,7 +505,7 @@ template <int MODE, int TERMS, int EK, bool H16>
 __global__ void __launch_bounds__(NTHREADS, 1)
     k_umma(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
            const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl, const UmmaArgs g,
-           const Epi e, const __grid_constant__ CUtensorMap tmY) {
+           const Epi e, const __grid_constant__ CUtensorMap tmY, const __grid_constant__ QkvMaps qm) {
     extern __shared__ __align__(1024) uint8_t smraw[];
     __shared__ uint64_t full[6], empty[6], acc_full[2], acc_empty[2], drain;
     __shared__ uint32_t tmem_slot;
@@ -624,15 +691,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 mbar_arrive(&acc_empty[a]);
                 continue;
             }
-            if (EK == EK_STORE || EK == EK_TMA || EK == EK_TMA_RES) {
+            if (EK == EK_STORE || EK == EK_TMA || EK == EK_TMA_RES || EK == EK_QKV) {
                 // each chunk's bias is loaded while the chunk before it is processed
                 float bcur[16], bnext[16];
                 load_bias16(g, e, n0 + 16 * half, bcur);
 #pragma unroll 1
                 for (int c0 = 16 * half; c0 < g.BN; c0 += 32) {
                     if (c0 + 32 < g.BN) load_bias16(g, e, n0 + c0 + 32, bnext);
-                    epi_chunk16<MODE, EK == EK_TMA ? 1 : EK == EK_TMA_RES ? 2 : 0>(g, e, taddr, n0, c0, mt, q, lane,
-                                                                                   valid, stg[ew], colacc[q], bcur, &tmY);
+                    epi_chunk16<MODE, EK == EK_TMA ? 1 : EK == EK_TMA_RES ? 2 : EK == EK_QKV ? 3 : 0>(
+                        g, e, taddr, n0, c0, mt, q, lane, valid, stg[ew], colacc[q], bcur, &tmY, &qm);
 #pragma unroll
                     for (int j = 0; j < 16; ++j) bcur[j] = bnext[j];
                 }
@@ -739,7 +806,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
 
     // The epilogue's bulk stores complete before the CTA (and its staging tiles) go away.
-    if ((EK == EK_TMA || EK == EK_TMA_RES) && warp >= 2 && lane == 0) bulk_wait_all();
+    if ((EK == EK_TMA || EK == EK_TMA_RES || EK == EK_QKV) && warp >= 2 && lane == 0) bulk_wait_all();
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
@@ -1139,9 +1206,10 @@ static CUtensorMap make_map(const void* base, int rank, const uint64_t* dims, co
     CUresult r = encode_fn()(&m, h16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank,
                              const_cast<void*>(base), dims,
                              strides_bytes, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                             rowbytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                             rowbytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
                              : rowbytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
-                                              : CU_TENSOR_MAP_SWIZZLE_32B,
+                             : rowbytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                              : CU_TENSOR_MAP_SWIZZLE_NONE,
                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) throw Error(3, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
     return m;
@@ -1162,7 +1230,7 @@ static const long SMEM_CAP = 232448 - 22528;
 
 template <int MODE, int TERMS, int EK, bool H16>
 static void launch_ek(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh, const CUtensorMap& bl,
-                      const UmmaArgs& g, const Epi& e, const CUtensorMap& ty, cudaStream_t st) {
+                      const UmmaArgs& g, const Epi& e, const CUtensorMap& ty, const QkvMaps& qm, cudaStream_t st) {
     const size_t smem = (size_t)g.stages * (2 * 128 * g.ckb + 2 * g.BN * g.ckb) + 1024;
     static unsigned configured = 0;
     int dev = 0;
@@ -1174,7 +1242,7 @@ static void launch_ek(const CUtensorMap& ah, const CUtensorMap& al, const CUtens
     }
     const long grid = std::min<long>(g.ntiles, num_sms());
     if (e.colsum && g.N > 256) throw Error(1, "umma: channel sums are limited to 256 columns");
-    k_umma<MODE, TERMS, EK, H16><<<(unsigned)grid, NTHREADS, smem, st>>>(ah, al, bh, bl, g, e, ty);
+    k_umma<MODE, TERMS, EK, H16><<<(unsigned)grid, NTHREADS, smem, st>>>(ah, al, bh, bl, g, e, ty, qm);
     HAT_CUDA(cudaGetLastError());
     count_launch();
 }
@@ -1221,14 +1289,39 @@ template <int MODE, int TERMS, bool H16>
 static void launch_k(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh, const CUtensorMap& bl,
                      UmmaArgs g, const Epi& e, cudaStream_t st) {
     CUtensorMap ty = ah;  // unused unless a TMA-store epilogue runs
+    QkvMaps qm{ah, ah, ah, ah};
+    if constexpr (MODE == 0 && TERMS == 3 && H16) {
+      if (e.qkv_split) {
+        // the qkv attention layout (see Epi::qkv_split)
+        const int c = g.N / 3;
+        if (g.N % 48 || g.M % 8 || (reinterpret_cast<uintptr_t>(e.qkv_split) & 15))
+            throw Error(1, "umma_linear: the qkv attention layout needs N a multiple of 48 and M of 8");
+        const __half* qkh = reinterpret_cast<const __half*>(e.qkv_split);
+        const __half* qkl = qkh + g.M * 2 * c;
+        const __half* vth = qkl + g.M * 2 * c;
+        const __half* vtl = vth + (long)c * g.M;
+        uint64_t dqk[2] = {(uint64_t)(2 * c), (uint64_t)g.M}, sqk[1] = {(uint64_t)(2 * c) * 2};
+        uint32_t bqk[2] = {16, 32};
+        qm.qkh = make_map(qkh, 2, dqk, sqk, bqk, 32, true);
+        qm.qkl = make_map(qkl, 2, dqk, sqk, bqk, 32, true);
+        uint64_t dvt[2] = {(uint64_t)g.M, (uint64_t)c}, svt[1] = {(uint64_t)g.M * 2};
+        uint32_t bvt[2] = {32, 16};
+        qm.vth = make_map(vth, 2, dvt, svt, bvt, 0, true);
+        qm.vtl = make_map(vtl, 2, dvt, svt, bvt, 0, true);
+        g.tma_st = 1;
+        launch_ek<MODE, TERMS, EK_QKV, H16>(ah, al, bh, bl, g, e, ty, qm, st);
+        return;
+      }
+    }
+    if (e.qkv_split) throw Error(1, "umma_linear: the qkv attention layout is for fp16 parity mode");
     const int sk = store_map<MODE>(g, e, ty);
     g.tma_st = sk != EK_STORE;
     switch (sk != EK_STORE ? sk : pick_ek(g, e)) {
-        case EK_TMA: launch_ek<MODE, TERMS, EK_TMA, H16>(ah, al, bh, bl, g, e, ty, st); break;
-        case EK_TMA_RES: launch_ek<MODE, TERMS, EK_TMA_RES, H16>(ah, al, bh, bl, g, e, ty, st); break;
-        case EK_STORE: launch_ek<MODE, TERMS, EK_STORE, H16>(ah, al, bh, bl, g, e, ty, st); break;
-        case EK_SHUF2: launch_ek<MODE, TERMS, EK_SHUF2, H16>(ah, al, bh, bl, g, e, ty, st); break;
-        default: launch_ek<MODE, TERMS, EK_GENERIC, H16>(ah, al, bh, bl, g, e, ty, st); break;
+        case EK_TMA: launch_ek<MODE, TERMS, EK_TMA, H16>(ah, al, bh, bl, g, e, ty, qm, st); break;
+        case EK_TMA_RES: launch_ek<MODE, TERMS, EK_TMA_RES, H16>(ah, al, bh, bl, g, e, ty, qm, st); break;
+        case EK_STORE: launch_ek<MODE, TERMS, EK_STORE, H16>(ah, al, bh, bl, g, e, ty, qm, st); break;
+        case EK_SHUF2: launch_ek<MODE, TERMS, EK_SHUF2, H16>(ah, al, bh, bl, g, e, ty, qm, st); break;
+        default: launch_ek<MODE, TERMS, EK_GENERIC, H16>(ah, al, bh, bl, g, e, ty, qm, st); break;
     }
 }
 // parity on fp16 pairs, parity on tf32 pairs, or fast (tf32, one term)
