@@ -258,7 +258,7 @@ void launch_window_attention(int mode, bool simt, const float* qkv, const float*
 
 // OCAB attention over the [hp][wp][3c] qkv plane (hat_arch.py:392-438).
 void launch_overlap_attention(int mode, bool simt, const float* qkv, const float* table, Dst out, const Plan& p,
-                              int c, int heads, int* err, cudaStream_t st);
+                              int c, int heads, int* err, cudaStream_t st, bool pre = false);
 
 // The second half of a 3x3 conv computed as a per-tap linear: `taps` is the [hp][wp][ldt]
 // plane of Y[p][tap*cout + co] = sum_ci w[co][ci][tap] x[p][ci] (tap = ky*3 + kx), and

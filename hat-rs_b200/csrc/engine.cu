@@ -84,12 +84,12 @@ void launch_window_attention(int mode, bool simt, const float* qkv, const float*
 }
 
 void launch_overlap_attention(int mode, bool simt, const float* qkv, const float* table, Dst out, const Plan& p, int c,
-                              int heads, int* err, cudaStream_t st) {
-    if (simt && p.strip()) throw Error(1, "attention: strips need the tensor-core kernel");
+                              int heads, int* err, cudaStream_t st, bool pre) {
+    if (simt && (p.strip() || pre)) throw Error(1, "attention: strips and the pre-split layout need the tensor-core kernel");
     if (simt)
         launch_overlap_attention_simt(qkv, table, out, p, c, heads, st);
     else
-        launch_attention_tc(mode, true, qkv, table, out, p, c, heads, 0, err, st);
+        launch_attention_tc(mode, true, qkv, table, out, p, c, heads, 0, err, st, pre);
 }
 
 // ------------------------------------------------------------------ engine
@@ -596,11 +596,17 @@ void Engine::ocab(int stage, const float* in, float* out) {
     launch_layernorm(in, W(p + ".norm1.weight"), W(p + ".norm1.bias"), D(a_->n1, a_->n1lo), P, c, stream_);
     Epi eq;
     eq.bias = W(p + ".qkv.bias");
+    const bool pre = h16_ && c / wt_.heads == 24 && c % wt_.heads == 0 && G(p + ".qkv.weight").umma;
+    if (pre) {  // as in the HAB: q, k and v^T written as the attention kernel's fp16 pairs
+        eq.qkv_split = a_->qkv;
+        eq.qscale = 1.f / sqrtf(24.f) * 1.4426950408889634f;
+        eq.qcols = c;
+    }
     mark("linear.qkv", 6.0 * P * c * c, 16.0 * P * c);
     linear(p + ".qkv.weight", O(a_->n1, a_->n1lo), Dst{a_->qkv, nullptr}, eq);
     mark("attn.overlap", 4.0 * P * 576 * c, 16.0 * P * c);
     launch_overlap_attention(mode_, simt_only_, a_->qkv, W(p + ".relative_position_bias_table"),
-                             D(a_->attn, a_->attnlo), plan_, c, wt_.heads, derr_, stream_);
+                             D(a_->attn, a_->attnlo), plan_, c, wt_.heads, derr_, stream_, pre);
     Epi ep;
     ep.bias = W(p + ".proj.bias");
     ep.res = in;

@@ -508,11 +508,14 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
         }
     } else if constexpr (PRE) {
         // ------------------------------------------------------------ loaders (copies)
-        // Per item, Q: 128 rows x 3 pieces of 8 dims x (hi, lo) = 6 copies a thread; per key
-        // block, K: 32 keys x 3 x 2 and V^T: 24 features x 4 pieces of 8 keys x 2 = 3 copies a
-        // thread. A key block is two window rows, and each 8-key piece of V^T is contiguous
-        // in the plane (the roll moves windows by 8 columns, so pieces never wrap).
-        static_assert(D == 24 && !OCA && TERMS == 3, "the copy loaders are for parity window attention, D = 24");
+        // Per item, Q: 128 rows x 3 pieces of 8 dims x (hi, lo) = 6 copies a thread. Per key
+        // block, K: 32 keys x 3 x 2 16-byte copies, and V^T: SA, 24 features x 4 pieces of 8
+        // keys x 2 (a key block is two window rows, and each 8-key piece is contiguous in
+        // the plane: the roll moves windows by 8 columns, so pieces never wrap); OCAB, 24
+        // features x 8 pieces of 4 keys x 2 8-byte copies (the key window starts 4 columns
+        // left of the query window). OCAB keys outside the image are zeros, a whole piece at
+        // a time (the image edges fall on multiples of 4).
+        static_assert(D == 24 && TERMS == 3, "the copy loaders are for parity attention, D = 24");
         const int t = threadIdx.x - 160;  // 0..127
         const long P = (long)gm.rows * wp, c2 = 2L * c;
         const __half* qkh = reinterpret_cast<const __half*>(qkv);
@@ -521,6 +524,12 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
         const __half* vtl = vth + (long)c * P;
         auto pos = [&](int wy, int wx, int y, int x) -> long {
             return (long)((gm.oy + wy * 16 + y + gm.sy) % gm.rows) * wp + (wx * 16 + x + gm.sx) % wp;
+        };
+        // OCAB key (ky, kx) of window (wy, wx): its plane index, or -1 outside the image
+        auto okey = [&](int wy, int wx, int ky, int kx) -> long {
+            const int Y = gm.oy + wy * 16 - 4 + ky, X = wx * 16 - 4 + kx;
+            const bool in = Y >= 0 && Y < gm.rows && gm.gy0 + Y >= 0 && gm.gy0 + Y < gm.ghp && X >= 0 && X < wp;
+            return in ? (long)Y * wp + X : -1;
         };
         long g = 0;
         uint32_t ti = 0;
@@ -536,7 +545,8 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
                 for (int u = 0; u < 6; ++u) {
                     const int cid = t + 128 * u, row = cid / 6, part = cid % 6, lo = part / 3, ch = part % 3;
                     const int qi = mtile * MT + row;
-                    const long qpos = pos(wy, wx, qi >> 4, qi & 15);
+                    const long qpos = OCA ? (long)(gm.oy + wy * 16 + (qi >> 4)) * wp + wx * 16 + (qi & 15)
+                                          : pos(wy, wx, qi >> 4, qi & 15);
                     qv[u] = *reinterpret_cast<const uint4*>((lo ? qkl : qkh) + qpos * c2 + head * D + 8 * ch);
                     qd[u] = lo * Q_BYTES + (ch >> 1) * 4096 + off_sw32(row, ch & 1);
                 }
@@ -551,23 +561,43 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
             for (int j = 0; j < NBLK; ++j) {
                 const long gb = g + j;
                 const int s = (int)(gb % KVS);
-                uint4 cv[3];
-                uint32_t dst[3];
+                constexpr int NCP = OCA ? 5 : 3;  // copies a thread: 192 K + 384 (OCAB) or 192 V^T
+                constexpr int NCOPY = OCA ? 576 : 384;
+                uint4 cv[NCP];
+                uint32_t dst[NCP];
+                bool wide[NCP];
 #pragma unroll
-                for (int u = 0; u < 3; ++u) {
-                    const int cid = t + 128 * u;  // 0..383
+                for (int u = 0; u < NCP; ++u) {
+                    const int cid = t + 128 * u;
+                    cv[u] = make_uint4(0u, 0u, 0u, 0u);
+                    dst[u] = 0xffffffffu;
+                    wide[u] = true;
+                    if (cid >= NCOPY) continue;
                     if (cid < 192) {
                         const int key = cid / 6, part = cid % 6, lo = part / 3, ch = part % 3;
                         const int kk = j * KBLK + key;
-                        const long kpos = pos(wy, wx, kk >> 4, kk & 15);
-                        cv[u] = *reinterpret_cast<const uint4*>((lo ? qkl : qkh) + kpos * c2 + c + head * D + 8 * ch);
+                        const long kpos = OCA ? okey(wy, wx, kk / 24, kk % 24) : pos(wy, wx, kk >> 4, kk & 15);
+                        if (kpos >= 0)
+                            cv[u] = *reinterpret_cast<const uint4*>((lo ? qkl : qkh) + kpos * c2 + c + head * D + 8 * ch);
                         dst[u] = lo * K_BYTES + (ch >> 1) * 1024 + off_sw32(key, ch & 1);
-                    } else {
+                    } else if (!OCA) {
                         const int v2 = cid - 192, f = v2 >> 3, part = v2 & 7, lo = part >> 2;
                         const int ks = (part >> 1) & 1, pc = part & 1;  // key row 2j + ks, keys 8 pc ..
                         const long kpos = pos(wy, wx, 2 * j + ks, 8 * pc);
                         cv[u] = *reinterpret_cast<const uint4*>((lo ? vtl : vth) + (long)(head * D + f) * P + kpos);
                         dst[u] = 2 * K_BYTES + lo * V_BYTES + ks * 1024 + off_sw32(f, pc);
+                    } else {
+                        const int v2 = cid - 192, f = v2 >> 4, part = v2 & 15, lo = part >> 3, pc4 = part & 7;
+                        const int kb = 4 * pc4, kk = j * KBLK + kb;  // 4 keys kb .. kb+3 of the block
+                        const long kpos = okey(wy, wx, kk / 24, kk % 24);
+                        if (kpos >= 0) {
+                            const uint2 x2 =
+                                *reinterpret_cast<const uint2*>((lo ? vtl : vth) + (long)(head * D + f) * P + kpos);
+                            cv[u].x = x2.x;
+                            cv[u].y = x2.y;
+                        }
+                        wide[u] = false;
+                        dst[u] = 2 * K_BYTES + lo * V_BYTES + (kb >> 4) * 1024 + off_sw32(f, (kb >> 3) & 1) + (kb & 7) * 2;
                     }
                 }
                 const bool got = bar_wait(&kv_empty[s], (uint32_t)(((gb / KVS) & 1) ^ 1), &abort_flag, err, 18);
@@ -577,7 +607,13 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
                 }
                 uint8_t* kvb = sm + OFF_KV + s * KV_BYTES;
 #pragma unroll
-                for (int u = 0; u < 3; ++u) *reinterpret_cast<uint4*>(kvb + dst[u]) = cv[u];
+                for (int u = 0; u < NCP; ++u) {
+                    if (dst[u] == 0xffffffffu) continue;
+                    if (wide[u])
+                        *reinterpret_cast<uint4*>(kvb + dst[u]) = cv[u];
+                    else
+                        *reinterpret_cast<uint2*>(kvb + dst[u]) = make_uint2(cv[u].x, cv[u].y);
+                }
                 fence_async();
                 bar_arrive(&kv_full[s]);
             }
@@ -809,9 +845,12 @@ void launch_attention_tc(int mode, bool oca, const float* qkv, const float* tabl
     const int d = c / heads;
     const bool three = mode == 0;
     if (pre) {
-        if (oca || d != 24 || !three || c % 8 || p.tokens() % 8)
-            throw Error(1, "attention: the pre-split qkv layout is for parity window attention with head dim 24");
-        run_tc<24, false, 3, true>(qkv, table, out, p, c, heads, shift, err, st);
+        if (d != 24 || !three || c % 8 || p.tokens() % 8)
+            throw Error(1, "attention: the pre-split qkv layout is for parity attention with head dim 24");
+        if (oca)
+            run_tc<24, true, 3, true>(qkv, table, out, p, c, heads, shift, err, st);
+        else
+            run_tc<24, false, 3, true>(qkv, table, out, p, c, heads, shift, err, st);
         return;
     }
 #define HAT_ATTN_CASE(DD, O)                                                                 \
