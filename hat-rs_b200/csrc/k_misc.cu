@@ -46,14 +46,51 @@ __global__ void k_tapsum_gelu(const float* __restrict__ taps, int ldt, const flo
     float acc[CMAX];
 #pragma unroll
     for (int co = 0; co < CMAX; ++co) acc[co] = co < cout ? bias[co] : 0.f;
+    const bool pairs = cout % 2 == 0 && ldt % 2 == 0;  // 8-byte loads of two channels
 #pragma unroll
     for (int tap = 0; tap < 9; ++tap) {
         const int yy = y + tap / 3 - 1, xx = x + tap % 3 - 1;
         if (yy < ylo || yy >= yhi || xx < 0 || xx >= wp) continue;
         const float* row = taps + ((long)yy * wp + xx) * ldt + tap * cout;
+        if (pairs) {
 #pragma unroll
-        for (int co = 0; co < CMAX; ++co)
-            if (co < cout) acc[co] += row[co];
+            for (int co = 0; co < CMAX; co += 2)
+                if (co < cout) {
+                    const float2 t2 = *reinterpret_cast<const float2*>(row + co);
+                    acc[co] += t2.x;
+                    acc[co + 1] += t2.y;
+                }
+        } else {
+#pragma unroll
+            for (int co = 0; co < CMAX; ++co)
+                if (co < cout) acc[co] += row[co];
+        }
+    }
+    if (out.lo && out.h16 && ldo == 2 * CMAX) {
+        // an fp16 pair plane of 2 * CMAX channels: the pixel's channels as 16-byte stores
+        uint32_t hw[CMAX], lw[CMAX];
+        bool big = false;
+#pragma unroll
+        for (int i = 0; i < CMAX; ++i) {
+            float v2[2];
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                const int co = 2 * i + k;
+                const float a = co < CMAX ? acc[co < CMAX ? co : 0] : 0.f;
+                v2[k] = co < cout ? 0.5f * a * (1.f + erff(a * 0.70710678118654752f)) : 0.f;
+                big |= beyond_h16(v2[k]);
+            }
+            split_h16x2(v2[0], v2[1], hw[i], lw[i]);
+        }
+        if (big && out.err) atomicCAS(out.err, 0, 21);
+        uint4* dh = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(out.hi) + p * ldo);
+        uint4* dl = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(out.lo) + p * ldo);
+#pragma unroll
+        for (int i = 0; i < CMAX / 4; ++i) {
+            dh[i] = make_uint4(hw[4 * i], hw[4 * i + 1], hw[4 * i + 2], hw[4 * i + 3]);
+            dl[i] = make_uint4(lw[4 * i], lw[4 * i + 1], lw[4 * i + 2], lw[4 * i + 3]);
+        }
+        return;
     }
     // channels cout..ldo-1 (ldo <= 2 * CMAX) are written as zeros
 #pragma unroll
