@@ -37,8 +37,10 @@
 // rows 48 floats apart, which puts the two half-warps (two query rows of the window)
 // on disjoint banks.
 //
-// Warp roles (288 threads, two CTAs per SM): 0 MMA issuer + TMEM owner, 1-4 softmax
-// (TMEM lane quarters 1,2,3,0), 5-8 loaders (gather, scale, split, swizzled stores).
+// Warp roles: 0 MMA issuer + TMEM owner, 1-4 softmax (TMEM lane quarters 1,2,3,0), then the
+// loaders: 4 warps (gathering, splitting loaders, or copies on the pre-split layout for the
+// OCAB; 288 threads, two CTAs per SM) or, for the window attention on the pre-split layout,
+// 2 warps of 16-byte copies (224 threads, three CTAs per SM).
 // Every mbarrier wait is bounded; on expiry the kernel records an error code, all roles
 // leave, and TMEM is released.
 #include <cuda_fp16.h>
@@ -49,7 +51,16 @@ namespace hat {
 
 namespace {
 
-constexpr int TC_THREADS = 288;
+// SLIM (window attention on the pre-split layout): two copying loader warps, 224 threads,
+// three CTAs per SM (80 registers a thread). Otherwise four loader warps, 288 threads, two
+// CTAs per SM (96 registers). Measured: the slim shape is faster for the window attention;
+// the OCAB kernel spills at 80 registers and keeps the wide one.
+template <bool SLIM>
+struct AttnShape {
+    static constexpr int loaders = SLIM ? 2 : 4;        // loader warps
+    static constexpr int threads = 160 + 32 * loaders;  // + MMA warp + 4 softmax warps
+    static constexpr int ctas = SLIM ? 3 : 2;           // CTAs per SM
+};
 constexpr int KBLK = 32;     // keys per block
 constexpr int MT = 128;      // query rows per work item
 constexpr int KVS = 4;       // K/V pipeline stages
@@ -203,7 +214,7 @@ struct AttnGeom {
 // [P][2c], v^T hi and lo [c][P], q already scaled by scale * log2(e); see Epi::qkv_split),
 // so the loaders only copy 16-byte pieces (window attention, D = 24, parity mode).
 template <int D, bool OCA, int TERMS, bool PRE>
-__global__ void __launch_bounds__(TC_THREADS, 2)
+__global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE && !OCA>::ctas)
     k_attn_tc(const float* __restrict__ qkv, const float* __restrict__ table, Dst out, const AttnGeom gm, int c,
               int heads, float scale, long items, int* err) {
     const int wp = gm.wp;
@@ -239,19 +250,20 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
     // Bias table of this head, rows TSTRIDE apart. SA: tab[r][s] = table[r*31 + s], the
     // bias of (qy - ky + 15, qx - kx + 15). OCAB: tab[r][s] is the bias of key - query
     // offset (r - 22, s - 22), i.e. table[((r - 22)*39 + (s - 22)) mod 1521].
-    for (int i = threadIdx.x; i < TR * TR; i += TC_THREADS) {
+    constexpr int NT = AttnShape<PRE && !OCA>::threads, NLT = 32 * AttnShape<PRE && !OCA>::loaders;
+    for (int i = threadIdx.x; i < TR * TR; i += NT) {
         const int r = i / TR, s = i - r * TR;
         int src = OCA ? (r - 22) * TW + (s - 22) : r * TW + s;
         if (src < 0) src += TR * TW;
         tab[r * TSTRIDE + s] = table[(long)src * heads + head] * L2E;
     }
     if (OCA)
-        for (int i = threadIdx.x; i < NK; i += TC_THREADS) koff[i] = (i / 24) * TSTRIDE + (i % 24);
+        for (int i = threadIdx.x; i < NK; i += NT) koff[i] = (i / 24) * TSTRIDE + (i % 24);
     if (threadIdx.x == 0) {
-        bar_init(&q_full, 128);
+        bar_init(&q_full, NLT);
         bar_init(&q_empty, 1);
         for (int s = 0; s < KVS; ++s) {
-            bar_init(&kv_full[s], 128);
+            bar_init(&kv_full[s], NLT);
             bar_init(&kv_empty[s], 1);
         }
         for (int s = 0; s < 2; ++s) {
@@ -273,13 +285,13 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
         // The head dim's padding (24 -> 32) is never copied: zero it once. Q and K: the second
         // 16-byte piece of k-step 1 of every row; V^T: feature rows 24..31.
         const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-        for (int i = threadIdx.x; i < 2 * MT; i += TC_THREADS)
+        for (int i = threadIdx.x; i < 2 * MT; i += NT)
             *reinterpret_cast<uint4*>(sm + (i / MT) * Q_BYTES + 4096 + off_sw32(i % MT, 1)) = z;
-        for (int i = threadIdx.x; i < KVS * 2 * KBLK; i += TC_THREADS) {
+        for (int i = threadIdx.x; i < KVS * 2 * KBLK; i += NT) {
             const int st = i / (2 * KBLK), lo = (i / KBLK) & 1, key = i % KBLK;
             *reinterpret_cast<uint4*>(sm + OFF_KV + st * KV_BYTES + lo * K_BYTES + 1024 + off_sw32(key, 1)) = z;
         }
-        for (int i = threadIdx.x; i < KVS * 2 * 8 * 4; i += TC_THREADS) {
+        for (int i = threadIdx.x; i < KVS * 2 * 8 * 4; i += NT) {
             const int st = i / 64, lo = (i / 32) & 1, f = 24 + ((i / 4) & 7), ks = (i / 2) & 1, pc = i & 1;
             *reinterpret_cast<uint4*>(sm + OFF_KV + st * KV_BYTES + 2 * K_BYTES + lo * V_BYTES + ks * 1024 +
                                       off_sw32(f, pc)) = z;
@@ -516,8 +528,9 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
         // left of the query window). OCAB keys outside the image are zeros, a whole piece at
         // a time (the image edges fall on multiples of 4).
         static_assert(D == 24 && TERMS == 3, "the copy loaders are for parity attention, D = 24");
-        const int t = threadIdx.x - 160;  // 0..127
+        const int t = threadIdx.x - 160;  // 0..NLT-1
         const long P = (long)gm.rows * wp, c2 = 2L * c;
+        constexpr int R = 6;  // copies in flight a thread (registers), rounds of R
         const __half* qkh = reinterpret_cast<const __half*>(qkv);
         const __half* qkl = qkh + P * c2;
         const __half* vth = qkl + P * c2;
@@ -539,21 +552,29 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
             const int win = (int)(rest >> 1), mtile = (int)(rest & 1);
             const int wy = win / nx, wx = win - wy * nx;
             {
-                uint4 qv[6];
-                uint32_t qd[6];
+                // Q: 768 copies, R at a time per thread (the first round issued before the wait)
+                bool got = true;
+#pragma unroll 1
+                for (int r0 = 0; r0 < 768; r0 += R * NLT) {
+                    uint4 qv[R];
+                    uint32_t qd[R];
 #pragma unroll
-                for (int u = 0; u < 6; ++u) {
-                    const int cid = t + 128 * u, row = cid / 6, part = cid % 6, lo = part / 3, ch = part % 3;
-                    const int qi = mtile * MT + row;
-                    const long qpos = OCA ? (long)(gm.oy + wy * 16 + (qi >> 4)) * wp + wx * 16 + (qi & 15)
-                                          : pos(wy, wx, qi >> 4, qi & 15);
-                    qv[u] = *reinterpret_cast<const uint4*>((lo ? qkl : qkh) + qpos * c2 + head * D + 8 * ch);
-                    qd[u] = lo * Q_BYTES + (ch >> 1) * 4096 + off_sw32(row, ch & 1);
+                    for (int u = 0; u < R; ++u) {
+                        const int cid = r0 + t + NLT * u, row = cid / 6, part = cid % 6, lo = part / 3, ch = part % 3;
+                        const int qi = mtile * MT + row;
+                        const long qpos = OCA ? (long)(gm.oy + wy * 16 + (qi >> 4)) * wp + wx * 16 + (qi & 15)
+                                              : pos(wy, wx, qi >> 4, qi & 15);
+                        qv[u] = *reinterpret_cast<const uint4*>((lo ? qkl : qkh) + qpos * c2 + head * D + 8 * ch);
+                        qd[u] = lo * Q_BYTES + (ch >> 1) * 4096 + off_sw32(row, ch & 1);
+                    }
+                    if (r0 == 0) {
+                        got = bar_wait(&q_empty, (ti & 1) ^ 1, &abort_flag, err, 17);
+                        if (!__all_sync(0xffffffffu, got)) break;
+                    }
+#pragma unroll
+                    for (int u = 0; u < R; ++u) *reinterpret_cast<uint4*>(sm + qd[u]) = qv[u];
                 }
-                const bool got = bar_wait(&q_empty, (ti & 1) ^ 1, &abort_flag, err, 17);
                 if (!__all_sync(0xffffffffu, got)) break;
-#pragma unroll
-                for (int u = 0; u < 6; ++u) *reinterpret_cast<uint4*>(sm + qd[u]) = qv[u];
                 fence_async();
                 bar_arrive(&q_full);
             }
@@ -561,14 +582,17 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
             for (int j = 0; j < NBLK; ++j) {
                 const long gb = g + j;
                 const int s = (int)(gb % KVS);
-                constexpr int NCP = OCA ? 5 : 3;  // copies a thread: 192 K + 384 (OCAB) or 192 V^T
-                constexpr int NCOPY = OCA ? 576 : 384;
-                uint4 cv[NCP];
-                uint32_t dst[NCP];
-                bool wide[NCP];
+                constexpr int NCOPY = OCA ? 576 : 384;  // 192 K + 384 (OCAB) or 192 V^T copies
+                bool got = true;
+                uint8_t* kvb = sm + OFF_KV + s * KV_BYTES;
+#pragma unroll 1
+                for (int r0 = 0; r0 < NCOPY; r0 += R * NLT) {
+                uint4 cv[R];
+                uint32_t dst[R];
+                bool wide[R];
 #pragma unroll
-                for (int u = 0; u < NCP; ++u) {
-                    const int cid = t + 128 * u;
+                for (int u = 0; u < R; ++u) {
+                    const int cid = r0 + t + NLT * u;
                     cv[u] = make_uint4(0u, 0u, 0u, 0u);
                     dst[u] = 0xffffffffu;
                     wide[u] = true;
@@ -600,19 +624,22 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
                         dst[u] = 2 * K_BYTES + lo * V_BYTES + (kb >> 4) * 1024 + off_sw32(f, (kb >> 3) & 1) + (kb & 7) * 2;
                     }
                 }
-                const bool got = bar_wait(&kv_empty[s], (uint32_t)(((gb / KVS) & 1) ^ 1), &abort_flag, err, 18);
-                if (!__all_sync(0xffffffffu, got)) {
-                    ok = false;
-                    break;
+                if (r0 == 0) {
+                    got = bar_wait(&kv_empty[s], (uint32_t)(((gb / KVS) & 1) ^ 1), &abort_flag, err, 18);
+                    if (!__all_sync(0xffffffffu, got)) break;
                 }
-                uint8_t* kvb = sm + OFF_KV + s * KV_BYTES;
 #pragma unroll
-                for (int u = 0; u < NCP; ++u) {
+                for (int u = 0; u < R; ++u) {
                     if (dst[u] == 0xffffffffu) continue;
                     if (wide[u])
                         *reinterpret_cast<uint4*>(kvb + dst[u]) = cv[u];
                     else
                         *reinterpret_cast<uint2*>(kvb + dst[u]) = make_uint2(cv[u].x, cv[u].y);
+                }
+                }
+                if (!__all_sync(0xffffffffu, got)) {
+                    ok = false;
+                    break;
                 }
                 fence_async();
                 bar_arrive(&kv_full[s]);
@@ -829,10 +856,11 @@ static void run_tc(const float* qkv, const float* table, Dst out, const Plan& p,
     const long items = (long)gm.nwy * p.nx() * heads * 2;
     int sms = 0;
     HAT_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    // Two CTAs per SM; a multiple of the head count, so every CTA keeps one head (and
-    // one bias table).
-    long grid = std::min<long>(items, (long)(2 * sms / heads) * heads);
-    k_attn_tc<D, OCA, TERMS, PRE><<<(unsigned)grid, TC_THREADS, bytes, st>>>(qkv, table, out, gm, c, heads,
+    // AttnShape::ctas CTAs per SM; a multiple of the head count, so every CTA keeps one head
+    // (and one bias table).
+    using Shape = AttnShape<PRE && !OCA>;
+    long grid = std::min<long>(items, (long)(Shape::ctas * sms / heads) * heads);
+    k_attn_tc<D, OCA, TERMS, PRE><<<(unsigned)grid, Shape::threads, bytes, st>>>(qkv, table, out, gm, c, heads,
                                                                              1.f / sqrtf((float)D), items, err);
     HAT_CUDA(cudaGetLastError());
     count_launch();
