@@ -177,6 +177,33 @@ __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.w
 // every store issued has completed
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// Column sums of a warp's 32 x 16 values (lane = row, x[j] = column j; x is consumed): a
+// transpose-and-add butterfly of 16 shuffles (8 + 4 + 2 + 1 + 1). Returns the sum over the
+// 32 rows of column `col`, which the lane pair (l, l ^ 1) share.
+__device__ __forceinline__ float colsum16(float* x, int lane, int& col) {
+    const int h1 = (lane >> 4) & 1, h2 = (lane >> 3) & 1, h3 = (lane >> 2) & 1, h4 = (lane >> 1) & 1;
+    float a8[8], a4[4], a2[2];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float keep = h1 ? x[8 + i] : x[i], give = h1 ? x[i] : x[8 + i];
+        a8[i] = keep + __shfl_xor_sync(0xffffffffu, give, 16);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float keep = h2 ? a8[4 + i] : a8[i], give = h2 ? a8[i] : a8[4 + i];
+        a4[i] = keep + __shfl_xor_sync(0xffffffffu, give, 8);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const float keep = h3 ? a4[2 + i] : a4[i], give = h3 ? a4[i] : a4[2 + i];
+        a2[i] = keep + __shfl_xor_sync(0xffffffffu, give, 4);
+    }
+    const float keep = h4 ? a2[1] : a2[0], give = h4 ? a2[0] : a2[1];
+    const float a1 = keep + __shfl_xor_sync(0xffffffffu, give, 2);
+    col = 8 * h1 + 4 * h2 + 2 * h3 + h4;
+    return a1 + __shfl_xor_sync(0xffffffffu, a1, 1);
+}
+
 __device__ __forceinline__ float epi_act(float v, int act) {
     if (act == ACT_GELU) return 0.5f * v * (1.f + erff(v * 0.70710678118654752f));
     if (act == ACT_LEAKY) return v > 0.f ? v : 0.01f * v;
@@ -364,13 +391,12 @@ __device__ __forceinline__ void epi_chunk16(const UmmaArgs& g, const Epi& e, uin
                 if (nb + j >= g.N) v[j] = 0.f;
         }
         if (e.colsum) {
+            float x[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                float sm = valid_own ? v[j] : 0.f;
-#pragma unroll
-                for (int o = 16; o; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
-                if (lane == 0 && nb + j < g.N) cacc[nb + j] += sm;
-            }
+            for (int j = 0; j < 16; ++j) x[j] = valid_own ? v[j] : 0.f;
+            int col;
+            const float sm = colsum16(x, lane, col);
+            if (!(lane & 1) && nb + col < g.N) cacc[nb + col] += sm;
         }
         float o[16];
 #pragma unroll
@@ -442,13 +468,12 @@ __device__ __forceinline__ void epi_chunk16(const UmmaArgs& g, const Epi& e, uin
             if (nb + j >= g.N) v[j] = 0.f;
     }
     if (e.colsum) {
+        float x[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            float s = valid_own ? v[j] : 0.f;
-#pragma unroll
-            for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-            if (lane == 0 && nb + j < g.N) cacc[nb + j] += s;
-        }
+        for (int j = 0; j < 16; ++j) x[j] = valid_own ? v[j] : 0.f;
+        int col;
+        const float sm = colsum16(x, lane, col);
+        if (!(lane & 1) && nb + col < g.N) cacc[nb + col] += sm;
     }
     // Staging tile rows of 16 floats, the four 16-byte chunks of row r rotated by
     // (r >> 1) & 3: both the row-per-lane stores here and the 4-lanes-per-row loads
@@ -784,14 +809,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 if (e.colsum) {
                     // Column sums of this warp's 32 rows, reduced in a fixed order and
                     // accumulated per warp across this CTA's tiles.
+                    float x[16];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        float s = valid ? v[j] : 0.f;
-#pragma unroll
-                        for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-                        const int n = n0 + c0 + j;
-                        if (lane == 0 && n < g.N) colacc[q][n] += s;
-                    }
+                    for (int j = 0; j < 16; ++j) x[j] = valid ? v[j] : 0.f;
+                    int col;
+                    const float sm = colsum16(x, lane, col);
+                    const int n = n0 + c0 + col;
+                    if (!(lane & 1) && n < g.N) colacc[q][n] += sm;
                 }
             }
             tc_fence_before();
