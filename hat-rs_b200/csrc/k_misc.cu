@@ -77,7 +77,7 @@ __global__ void k_tapsum_gelu(const float* __restrict__ taps, int ldt, const flo
             for (int k = 0; k < 2; ++k) {
                 const int co = 2 * i + k;
                 const float a = co < CMAX ? acc[co < CMAX ? co : 0] : 0.f;
-                v2[k] = co < cout ? 0.5f * a * (1.f + erff(a * 0.70710678118654752f)) : 0.f;
+                v2[k] = co < cout ? gelu_fast(a) : 0.f;
                 big |= beyond_h16(v2[k]);
             }
             split_h16x2(v2[0], v2[1], hw[i], lw[i]);
@@ -97,7 +97,7 @@ __global__ void k_tapsum_gelu(const float* __restrict__ taps, int ldt, const flo
     for (int co = 0; co < 2 * CMAX; ++co) {
         if (co >= ldo) break;
         const float a = co < CMAX ? acc[co < CMAX ? co : 0] : 0.f;
-        const float v = co < cout ? 0.5f * a * (1.f + erff(a * 0.70710678118654752f)) : 0.f;
+        const float v = co < cout ? gelu_fast(a) : 0.f;
         put(out, p * ldo + co, v);
     }
 }

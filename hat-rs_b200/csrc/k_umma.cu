@@ -205,7 +205,7 @@ __device__ __forceinline__ float colsum16(float* x, int lane, int& col) {
 }
 
 __device__ __forceinline__ float epi_act(float v, int act) {
-    if (act == ACT_GELU) return 0.5f * v * (1.f + erff(v * 0.70710678118654752f));
+    if (act == ACT_GELU) return gelu_fast(v);
     if (act == ACT_LEAKY) return v > 0.f ? v : 0.01f * v;
     return v;
 }
@@ -380,7 +380,7 @@ __device__ __forceinline__ void epi_chunk16(const UmmaArgs& g, const Epi& e, uin
         for (int j = 0; j < 16; ++j) v[j] = v[j] * g.ascale + bv[j];
         if (e.act == ACT_GELU) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = 0.5f * v[j] * (1.f + erff(v[j] * 0.70710678118654752f));
+            for (int j = 0; j < 16; ++j) v[j] = gelu_fast(v[j]);
         } else if (e.act == ACT_LEAKY) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] = v[j] > 0.f ? v[j] : 0.01f * v[j];
@@ -457,7 +457,7 @@ __device__ __forceinline__ void epi_chunk16(const UmmaArgs& g, const Epi& e, uin
     for (int j = 0; j < 16; ++j) v[j] = v[j] * g.ascale + bv[j];
     if (e.act == ACT_GELU) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = 0.5f * v[j] * (1.f + erff(v[j] * 0.70710678118654752f));
+        for (int j = 0; j < 16; ++j) v[j] = gelu_fast(v[j]);
     } else if (e.act == ACT_LEAKY) {
 #pragma unroll
         for (int j = 0; j < 16; ++j) v[j] = v[j] > 0.f ? v[j] : 0.01f * v[j];
@@ -1129,7 +1129,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
                 for (int j = 0; j < 48; ++j) {
                     const float x = v[j] * g.s1 + b1s[nb + j];
-                    v[j] = 0.5f * x * (1.f + erff(x * 0.70710678118654752f));
+                    v[j] = gelu_fast(x);
                 }
                 // The hidden buffer is free once the previous chunk's fc2 has run.
                 const bool freed = mbar_wait(&h_empty, (qc & 1) ^ 1, &abort_flag, gerr, 28);

@@ -204,6 +204,28 @@ void run_all(Log& log) {
     }
 }
 
+__global__ void k_gelu_probe(float* out, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = gelu_fast(-10.f + 20.f * (float)i / (float)(n - 1));
+}
+
+// The GELU the tensor-core epilogues use (gelu_fast, erf after Abramowitz & Stegun 7.1.26)
+// against the exact GELU in double precision over [-10, 10].
+void gelu_check(Log& log) {
+    const int n = 1 << 20;
+    Dev d((size_t)n);
+    k_gelu_probe<<<(n + 255) / 256, 256>>>(d.p, n);
+    HAT_CUDA(cudaGetLastError());
+    HAT_CUDA(cudaDeviceSynchronize());
+    const std::vector<float> got = d.get((size_t)n);
+    std::vector<double> ref((size_t)n);
+    for (int i = 0; i < n; ++i) {
+        const double x = (double)(-10.f + 20.f * (float)i / (float)(n - 1));
+        ref[i] = 0.5 * x * (1.0 + std::erf(x / std::sqrt(2.0)));
+    }
+    log.check("gelu (erf after A&S 7.1.26) on [-10, 10]", maxdiff(got, ref), 1e-6);
+}
+
 }  // namespace
 
 extern "C" int hat_b200_selftest(int device, char* log_out, size_t loglen) {
@@ -212,6 +234,7 @@ extern "C" int hat_b200_selftest(int device, char* log_out, size_t loglen) {
     try {
         HAT_CUDA(cudaSetDevice(device));
         run_all(log);
+        gelu_check(log);
         if (log.fails) rc = HAT_B200_ESELFTEST;
     } catch (const std::exception& e) {
         log.s += std::string("selftest aborted: ") + e.what() + "\n";
