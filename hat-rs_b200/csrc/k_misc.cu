@@ -205,8 +205,165 @@ __global__ void k_layernorm16(const float* __restrict__ x, const float* __restri
     }
 }
 
+// The fp16-pair LayerNorm by bulk copies: a persistent CTA moves tiles of LN_TOK tokens with
+// one asynchronous bulk load each (double-buffered, completion on an mbarrier), normalises
+// them from shared memory with half a warp per token, and writes the tile's hi and lo rows
+// with two bulk stores. Few instructions and many bytes in flight per SM. c a multiple of 8
+// and at most 144 (9 channels a lane). Waits are bounded; on expiry error 30 is recorded and
+// the CTA stops.
+constexpr int LN_TOK = 64;
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__global__ void __launch_bounds__(256) k_layernorm_bulk(const float* __restrict__ x, const float* __restrict__ g,
+                                                        const float* __restrict__ b, Dst y, long m, int c,
+                                                        int* err) {
+    extern __shared__ __align__(128) uint8_t lsm[];
+    __shared__ __align__(8) uint64_t full[2];
+    float* in0 = reinterpret_cast<float*>(lsm);
+    const int tile_f = LN_TOK * c;  // floats of one input tile
+    __half* oh = reinterpret_cast<__half*>(lsm + 2 * tile_f * 4);
+    __half* ol = oh + tile_f;
+    const int lane = threadIdx.x & 31, hl = lane & 15, slot = threadIdx.x >> 4;  // 16 tokens a round
+    const long ntiles = (m + LN_TOK - 1) / LN_TOK;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 2; ++i)
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&full[i])));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    auto issue = [&](long t, int buf) {
+        const long rows = min((long)LN_TOK, m - t * LN_TOK);
+        const uint32_t bytes = (uint32_t)(rows * c * 4);
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(&full[buf])),
+                     "r"(bytes) : "memory");
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                     ::"r"(smem_addr(in0 + buf * tile_f)), "l"(x + t * LN_TOK * c), "r"(bytes),
+                     "r"(smem_addr(&full[buf]))
+                     : "memory");
+    };
+    float gg[9], bb[9];
+#pragma unroll
+    for (int k = 0; k < 9; ++k) {
+        const int ch = hl + 16 * k;
+        gg[k] = ch < c ? g[ch] : 0.f;
+        bb[k] = ch < c ? b[ch] : 0.f;
+    }
+    if (threadIdx.x == 0 && (long)blockIdx.x < ntiles) issue(blockIdx.x, 0);
+    bool big = false;
+    uint32_t i = 0;
+    for (long t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+        const int buf = i & 1;
+        if (threadIdx.x == 0 && t + gridDim.x < ntiles) issue(t + gridDim.x, buf ^ 1);
+        // this tile's rows have landed
+        {
+            uint32_t ok = 0;
+            const long long t0 = clock64();
+            while (!ok) {
+                asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+                             " selp.u32 %0, 1, 0, p;\n}\n"
+                             : "=r"(ok) : "r"(smem_addr(&full[buf])), "r"((i >> 1) & 1) : "memory");
+                if (!ok && clock64() - t0 > 4000000000ll) break;
+            }
+            if (!__syncthreads_and(ok)) {
+                if (threadIdx.x == 0) {
+                    atomicCAS(err, 0, 30);
+                    // let the loads in flight (this tile's and the next one's) land first
+                    for (int k = 0; k < 2; ++k) {
+                        const int bf = buf ^ k;
+                        const uint32_t par = ((i + k) >> 1) & 1;
+                        uint32_t done = 0;
+                        const long long t1 = clock64();
+                        while (!done && clock64() - t1 < 4000000000ll)
+                            asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+                                         " selp.u32 %0, 1, 0, p;\n}\n"
+                                         : "=r"(done) : "r"(smem_addr(&full[bf])), "r"(par) : "memory");
+                    }
+                }
+                break;
+            }
+        }
+        // the previous tile's stores have read the output rows
+        if (threadIdx.x == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+        __syncthreads();
+        const long rows = min((long)LN_TOK, m - t * LN_TOK);
+        const float* tin = in0 + buf * tile_f;
+#pragma unroll 1
+        for (int r = 0; r < LN_TOK; r += 16) {
+            const int tok = r + slot;
+            const bool live = tok < rows;
+            float v[9];
+            float s = 0.f;
+#pragma unroll
+            for (int k = 0; k < 9; ++k) {
+                const int ch = hl + 16 * k;
+                v[k] = live && ch < c ? tin[tok * c + ch] : 0.f;
+                s += v[k];
+            }
+#pragma unroll
+            for (int o = 8; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            const float mean = s / (float)c;
+            float q = 0.f;
+#pragma unroll
+            for (int k = 0; k < 9; ++k) {
+                const int ch = hl + 16 * k;
+                const float d = ch < c ? v[k] - mean : 0.f;
+                q += d * d;
+            }
+#pragma unroll
+            for (int o = 8; o; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+            const float rstd = 1.f / sqrtf(q / (float)c + 1e-5f);
+            if (live) {
+#pragma unroll
+                for (int k = 0; k < 9; ++k) {
+                    const int ch = hl + 16 * k;
+                    if (ch < c) {
+                        const float o = (v[k] - mean) * rstd * gg[k] + bb[k];
+                        __half h, l;
+                        split_h16(o, h, l);
+                        oh[tok * c + ch] = h;
+                        ol[tok * c + ch] = l;
+                        big |= beyond_h16(o);
+                    }
+                }
+            }
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const uint32_t bytes = (uint32_t)(rows * c * 2);
+            asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+                         ::"l"(reinterpret_cast<__half*>(y.hi) + t * LN_TOK * c), "r"(smem_addr(oh)), "r"(bytes)
+                         : "memory");
+            asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+                         ::"l"(reinterpret_cast<__half*>(y.lo) + t * LN_TOK * c), "r"(smem_addr(ol)), "r"(bytes)
+                         : "memory");
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
+    }
+    if (big && y.err) atomicCAS(y.err, 0, 21);
+    if (threadIdx.x == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 void launch_layernorm(const float* x, const float* g, const float* b, Dst y, long m, int c, cudaStream_t st) {
     if (c > 256) throw Error(1, "layernorm: c > 256 is not supported");
+    int* err = y.err;  // the engine's device error word (timeouts, fp16 range)
+    if (y.lo && y.h16 && err && c % 8 == 0 && c <= 144 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+        (reinterpret_cast<uintptr_t>(y.hi) & 15) == 0 && (reinterpret_cast<uintptr_t>(y.lo) & 15) == 0) {
+        const size_t smem = (size_t)LN_TOK * c * (2 * 4 + 2 * 2);
+        static unsigned configured = 0;
+        int dev = 0, sms = 0;
+        HAT_CUDA(cudaGetDevice(&dev));
+        HAT_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        if (!(configured & (1u << dev))) {
+            HAT_CUDA(cudaFuncSetAttribute(k_layernorm_bulk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            configured |= 1u << dev;
+        }
+        const long ntiles = (m + LN_TOK - 1) / LN_TOK;
+        const long grid = std::min<long>(ntiles, 2L * sms);
+        k_layernorm_bulk<<<(unsigned)grid, 256, smem, st>>>(x, g, b, y, m, c, err);
+        HAT_CUDA(cudaGetLastError());
+        count_launch();
+        return;
+    }
     if (c <= 144) {
         k_layernorm16<9><<<(unsigned)((m + 15) / 16), 256, 0, st>>>(x, g, b, y, m, c);
         HAT_CUDA(cudaGetLastError());
