@@ -906,17 +906,24 @@ __device__ __forceinline__ void tmem_st8u(uint32_t taddr, const uint32_t* r) {
                  : "memory");
 }
 
+// SK as for epi_chunk16 (0, 1, 2), or MLP_RT: the producer warp loads the tile's residual
+// rows by TMA into a shared-memory tile ([CP/16 chunks][128 rows][16], 64-byte swizzle)
+// while the hidden chunks run; the final epilogue adds fc2 + bias into that tile in place
+// and stores it by TMA, so no global load sits on the epilogue's critical path.
+constexpr int MLP_RT = 4;
 template <int TERMS, bool H16, int SK>
 __global__ void __launch_bounds__(NTHREADS, 1)
     k_mlp(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
           const __grid_constant__ CUtensorMap tmW1h, const __grid_constant__ CUtensorMap tmW1l,
           const __grid_constant__ CUtensorMap tmW2h, const __grid_constant__ CUtensorMap tmW2l, const MlpArgs g,
-          const Epi e, const __grid_constant__ CUtensorMap tmY) {
+          const Epi e, const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmR) {
+    constexpr bool RT = SK == MLP_RT;
     extern __shared__ __align__(1024) uint8_t smraw[];
     __shared__ uint64_t full[6], empty[6], d1_full, d1_free, h_full, h_empty, d2_full, d2_free, drain;
+    __shared__ uint64_t res_full, res_empty;
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int abort_flag;
-    __shared__ __align__(1024) float stg[EPI_WARPS][32][16];
+    __shared__ __align__(1024) float stg[RT ? 1 : EPI_WARPS][32][16];
     __shared__ float no_colsum[256];
     __shared__ float b1s[MLP_MAXH];  // fc1 bias, zero past HID (read by every chunk)
 
@@ -925,6 +932,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const uint32_t A_B = 128 * 128, W1_B = MLP_HC * 128, W2_B = (uint32_t)g.CP * 128;
     for (int i = threadIdx.x; i < MLP_MAXH; i += NTHREADS) b1s[i] = i < g.HID ? g.b1[i] : 0.f;
     const uint32_t st_bytes = max(2 * A_B + 2 * W1_B, 2 * W2_B);
+    float* rtile = reinterpret_cast<float*>(sm + S * st_bytes);  // MLP_RT: the residual / output tile
     int* gerr = g.st.err;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -940,6 +948,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         mbar_init(&d2_full, 1);
         mbar_init(&d2_free, 32 * EPI_WARPS);
         mbar_init(&drain, 1);
+        mbar_init(&res_full, 1);
+        mbar_init(&res_empty, EPI_WARPS);
         abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -993,15 +1003,31 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     if (TERMS == 3) tma_2d(b + W2_B, &tmW2l, h * MLP_HC + kb * KEL, 0, &full[s]);
                 }
             };
+            uint32_t rn = 0;  // residual tiles issued
+            auto load_res = [&](long t) {
+                // the previous tile's output stores have read the tile
+                if (!mbar_wait(&res_empty, (rn & 1) ^ 1, &abort_flag, gerr, 31)) {
+                    ok = false;
+                    return;
+                }
+                mbar_expect_tx(&res_full, (uint32_t)g.CP * 512);
+                for (int c = 0; c < g.CP / 16; ++c) tma_2d(rtile + c * 2048, &tmR, c * 16, (int)(t * 128), &res_full);
+                ++rn;
+            };
             for (long t = blockIdx.x; t < g.mtiles && ok && !abort_flag; t += gridDim.x) {
                 load_fc1(t, 0);
                 for (int h = 0; h < g.NCH && ok; ++h) {
                     if (h + 1 < g.NCH) load_fc1(t, h + 1);
                     load_fc2(h);
+                    // Issued once the tile's first chunk is under way: by then the epilogue
+                    // has finished the previous tile, so the wait above does not hold up
+                    // the weight loads.
+                    if (RT && h == 0 && ok) load_res(t);
                 }
             }
             if (abort_flag) {
                 for (uint32_t j = (it > (uint32_t)S ? it - S : 0); j < it; ++j) mbar_wait_quiet(&full[j % S], (j / S) & 1);
+                if (RT && rn) mbar_wait_quiet(&res_full, (rn - 1) & 1);
             }
         }
     } else if (warp == 1) {
@@ -1176,20 +1202,60 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const bool got = mbar_wait(&d2_full, tl & 1, &abort_flag, gerr, 29);
             if (!__all_sync(0xffffffffu, got)) break;
             tc_fence_after();
-            const long m = t * 128 + row;
-            const bool valid = m < g.st.M;
-            float bcur[16], bnext[16];
-            load_bias16(g.st, e, 16 * half, bcur);
+            if constexpr (RT) {
+                const bool rg = mbar_wait(&res_full, tl & 1, &abort_flag, gerr, 32);
+                if (!__all_sync(0xffffffffu, rg)) break;
+                const int sw = (lane >> 1) & 3;  // this row's 16-byte chunk rotation (64-byte swizzle)
+                float bcur[16], bnext[16];
+                load_bias16(g.st, e, 16 * half, bcur);
 #pragma unroll 1
-            for (int c0 = 16 * half; c0 < g.CP; c0 += 32) {
-                if (c0 + 32 < g.CP) load_bias16(g.st, e, c0 + 32, bnext);
-                epi_chunk16<0, SK>(g.st, e, tmem + lanes + T_D2, 0, c0, t, q4, lane, valid, stg[ew], no_colsum, bcur,
-                                   &tmY);
+                for (int c0 = 16 * half; c0 < g.CP; c0 += 32) {
+                    if (c0 + 32 < g.CP) load_bias16(g.st, e, c0 + 32, bnext);
+                    float v[16];
+                    tmem_ld16(tmem + lanes + T_D2 + c0, v);
+                    float* tile = rtile + (c0 >> 4) * 2048 + q4 * 512;  // this warp's 32 rows of the chunk
 #pragma unroll
-                for (int j = 0; j < 16; ++j) bcur[j] = bnext[j];
+                    for (int qq = 0; qq < 4; ++qq) {
+                        float4* p = reinterpret_cast<float4*>(tile + lane * 16 + 4 * (qq ^ sw));
+                        float4 r = *p;
+                        r.x = r.x + (v[4 * qq] * g.st.ascale + bcur[4 * qq]);
+                        r.y = r.y + (v[4 * qq + 1] * g.st.ascale + bcur[4 * qq + 1]);
+                        r.z = r.z + (v[4 * qq + 2] * g.st.ascale + bcur[4 * qq + 2]);
+                        r.w = r.w + (v[4 * qq + 3] * g.st.ascale + bcur[4 * qq + 3]);
+                        *p = r;
+                    }
+                    fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&tmY, tile, c0, (int)(t * 128 + q4 * 32));
+                        bulk_commit();
+                    }
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) bcur[j] = bnext[j];
+                }
+                tc_fence_before();
+                mbar_arrive(&d2_free);
+                if (lane == 0) {
+                    bulk_wait_read();
+                    mbar_arrive(&res_empty);
+                }
+                __syncwarp();
+            } else {
+                const long m = t * 128 + row;
+                const bool valid = m < g.st.M;
+                float bcur[16], bnext[16];
+                load_bias16(g.st, e, 16 * half, bcur);
+#pragma unroll 1
+                for (int c0 = 16 * half; c0 < g.CP; c0 += 32) {
+                    if (c0 + 32 < g.CP) load_bias16(g.st, e, c0 + 32, bnext);
+                    epi_chunk16<0, SK>(g.st, e, tmem + lanes + T_D2, 0, c0, t, q4, lane, valid, stg[ew], no_colsum,
+                                       bcur, &tmY);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) bcur[j] = bnext[j];
+                }
+                tc_fence_before();
+                mbar_arrive(&d2_free);
             }
-            tc_fence_before();
-            mbar_arrive(&d2_free);
         }
     }
 
@@ -1495,6 +1561,14 @@ long umma_mlp(int mode, Opnd x, const GemmW& w1, const float* b1, const GemmW& w
     g.b1 = b1;
     const long st_bytes = std::max(2L * 128 * 128 + 2L * MLP_HC * 128, 2L * g.CP * 128);
     g.stages = (int)std::max(2L, std::min(6L, (SMEM_CAP - 1024) / st_bytes));
+    // The residual-tile epilogue (MLP_RT): an fp32 output with a residual, both 16-byte
+    // aligned, whole 128-row tiles of the tensor maps, and two pipeline stages beside the
+    // CP x 128 fp32 tile.
+    const long rt_bytes = (long)g.CP * 512;
+    const bool rt = res && !y.lo && !y.h16 && !(reinterpret_cast<uintptr_t>(y.hi) & 15) &&
+                    !(reinterpret_cast<uintptr_t>(res) & 15) && C % 4 == 0 && C >= 16 && m >= 128 &&
+                    g.CP % 16 == 0 && 2 * st_bytes + rt_bytes + 1024 <= SMEM_CAP;
+    if (rt) g.stages = 2;
     UmmaArgs& u = g.st;
     u.M = m;
     u.N = C;
@@ -1511,27 +1585,39 @@ long umma_mlp(int mode, Opnd x, const GemmW& w1, const float* b1, const GemmW& w
     e.bias = b2;
     e.res = res;
     if (C % 4) throw Error(1, "umma_mlp: the width must be a multiple of 4");
-    const size_t smem = (size_t)g.stages * st_bytes + 1024;
+    const size_t smem = (size_t)g.stages * st_bytes + (rt ? rt_bytes : 0) + 1024;
     CUtensorMap ty = tah;  // the output's tensor map when the final store goes by TMA
-    const int sk = store_map<0>(u, e, ty, true);
-    u.tma_st = sk != EK_STORE;
-    const int skx = sk == EK_TMA ? 1 : sk == EK_TMA_RES ? 2 : 0;
-    static unsigned configured[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
+    CUtensorMap tr = tah;  // MLP_RT: the residual's
+    int skx;
+    if (rt) {
+        uint64_t dims[2] = {(uint64_t)C, (uint64_t)m};
+        uint64_t str[1] = {(uint64_t)C * 4};
+        uint32_t ybox[2] = {16, 32}, rbox[2] = {16, 128};
+        ty = make_map(y.hi, 2, dims, str, ybox, 64);
+        tr = make_map(res, 2, dims, str, rbox, 64);
+        u.tma_st = true;
+        skx = 3;
+    } else {
+        const int sk = store_map<0>(u, e, ty, true);
+        u.tma_st = sk != EK_STORE;
+        skx = sk == EK_TMA ? 1 : sk == EK_TMA_RES ? 2 : 0;
+    }
+    static unsigned configured[12] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
     int dev = 0;
     HAT_CUDA(cudaGetDevice(&dev));
-    const int which = (h16 ? 2 : three ? 0 : 1) * 3 + skx;
+    const int which = (h16 ? 2 : three ? 0 : 1) * 4 + skx;
     using KFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, MlpArgs, Epi,
-                         CUtensorMap);
-    const KFn table[9] = {k_mlp<3, false, 0>, k_mlp<3, false, 1>, k_mlp<3, false, 2>,
-                          k_mlp<1, false, 0>, k_mlp<1, false, 1>, k_mlp<1, false, 2>,
-                          k_mlp<3, true, 0>,  k_mlp<3, true, 1>,  k_mlp<3, true, 2>};
+                         CUtensorMap, CUtensorMap);
+    const KFn table[12] = {k_mlp<3, false, 0>, k_mlp<3, false, 1>, k_mlp<3, false, 2>, k_mlp<3, false, MLP_RT>,
+                           k_mlp<1, false, 0>, k_mlp<1, false, 1>, k_mlp<1, false, 2>, k_mlp<1, false, MLP_RT>,
+                           k_mlp<3, true, 0>,  k_mlp<3, true, 1>,  k_mlp<3, true, 2>,  k_mlp<3, true, MLP_RT>};
     const KFn kern = table[which];
     if (!(configured[which] & (1u << dev))) {
         HAT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_CAP));
         configured[which] |= 1u << dev;
     }
     const long grid = std::min<long>(g.mtiles, num_sms());
-    kern<<<(unsigned)grid, NTHREADS, smem, st>>>(tah, tal, t1h, t1l, t2h, t2l, g, e, ty);
+    kern<<<(unsigned)grid, NTHREADS, smem, st>>>(tah, tal, t1h, t1l, t2h, t2l, g, e, ty, tr);
     HAT_CUDA(cudaGetLastError());
     count_launch();
     return 0;
