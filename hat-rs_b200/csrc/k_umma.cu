@@ -250,8 +250,16 @@ __device__ __forceinline__ void tile_row(const UmmaArgs& g, long mt, int trow, l
 // cache): EK_STORE plain/residual stores by the lanes, EK_TMA plain fp32 stores without a
 // residual by TMA, EK_TMA_RES fp32 stores with a residual by TMA, EK_SHUF2 PixelShuffle(2)
 // stores, EK_GENERIC everything else (planar output, other shuffle factors, odd strides),
-// EK_QKV the qkv linear's attention layout.
-enum { EK_STORE = 0, EK_SHUF2 = 1, EK_GENERIC = 2, EK_TMA = 3, EK_TMA_RES = 4, EK_QKV = 5 };
+// EK_QKV the qkv linear's attention layout, EK_RING fp32 stores with a residual (and the
+// CAB term) whose inputs a second producer lane streams by TMA (below).
+enum { EK_STORE = 0, EK_SHUF2 = 1, EK_GENERIC = 2, EK_TMA = 3, EK_TMA_RES = 4, EK_QKV = 5, EK_RING = 6 };
+
+// EK_RING: the residual (and the CAB output) of each 16-column chunk of a tile, all 128
+// rows, are loaded by TMA into one of RING_SLOTS shared-memory slots ([128][16] fp32 each,
+// 64-byte swizzle) ahead of the epilogue; the epilogue adds the accumulator into the
+// slot in place and stores it from there by TMA. The slot maps travel in QkvMaps:
+// qkh = the residual, qkl = the CAB output.
+constexpr int RING_SLOTS = 4;
 
 // The four output maps of EK_QKV (see Epi::qkv_split): q|k hi and lo (SW32 boxes of 16 x
 // 32), v^T hi and lo (unswizzled boxes of 32 tokens x 16 features).
@@ -533,8 +541,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
            const Epi e, const __grid_constant__ CUtensorMap tmY, const __grid_constant__ QkvMaps qm) {
     extern __shared__ __align__(1024) uint8_t smraw[];
     __shared__ uint64_t full[6], empty[6], acc_full[2], acc_empty[2], drain;
+    __shared__ uint64_t rfull[RING_SLOTS], rempty[RING_SLOTS];
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int abort_flag;
+    constexpr bool RING = EK == EK_RING;
     // The channel-attention pool: per TMEM lane quarter, column sums accumulated over
     // every tile this CTA owns (in its fixed tile order), written once at the end. The
     // quarter's two epilogue warps own disjoint columns.
@@ -553,9 +563,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     auto sAl = [&](int s) { return sm + s * st_bytes + a_bytes; };
     auto sBh = [&](int s) { return sm + s * st_bytes + 2 * a_bytes; };
     auto sBl = [&](int s) { return sm + s * st_bytes + 2 * a_bytes + b_bytes; };
+    // EK_RING: the slots after the stages (each the residual chunk, then the CAB chunk),
+    // then the CAB gate
+    float* ring = reinterpret_cast<float*>(sm + ((S * st_bytes + 1023) & ~1023u));
+    const int rstride = e.cx ? 4096 : 2048;  // floats per slot
+    float* gsm = ring + RING_SLOTS * rstride;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int i = threadIdx.x; i < 4 * 256; i += NTHREADS) (&colacc[0][0])[i] = 0.f;
+    if (RING && e.cx)
+        for (int i = threadIdx.x; i < g.BN * g.ntn; i += NTHREADS) gsm[i] = i < g.N ? e.gate[i] : 0.f;
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
@@ -566,6 +583,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             mbar_init(&acc_empty[a], 32 * EPI_WARPS);
         }
         mbar_init(&drain, 1);
+        for (int r = 0; r < RING_SLOTS; ++r) {
+            mbar_init(&rfull[r], 1);
+            mbar_init(&rempty[r], 4);  // the four lane-quarter warps of the chunk's half
+        }
         abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -610,6 +631,30 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (abort_flag) {
                 // Let the copies already issued land before the CTA can exit.
                 for (uint32_t j = (it > (uint32_t)S ? it - S : 0); j < it; ++j) mbar_wait_quiet(&full[j % S], (j / S) & 1);
+            }
+        } else if (RING && lane == 1) {
+            // the residual stream: chunk k of this CTA's tile sequence into slot k % RING_SLOTS
+            uint32_t k = 0;
+            const uint32_t tx = e.cx ? 16384u : 8192u;
+            const int nc = g.BN / 16;
+            bool ok = true;
+            for (long t = blockIdx.x; t < ntiles && ok && !abort_flag; t += gridDim.x) {
+                const int row0 = (int)(t / g.ntn * 128), n0 = (int)(t % g.ntn) * g.BN;
+                for (int c = 0; c < nc; ++c, ++k) {
+                    const int s = (int)(k % RING_SLOTS);
+                    if (!mbar_wait(&rempty[s], ((k / RING_SLOTS) & 1) ^ 1, &abort_flag, g.err, 6)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(&rfull[s], tx);
+                    float* slot = ring + s * rstride;
+                    tma_2d(slot, &qm.qkh, n0 + 16 * c, row0, &rfull[s]);
+                    if (e.cx) tma_2d(slot + 2048, &qm.qkl, n0 + 16 * c, row0, &rfull[s]);
+                }
+            }
+            if (abort_flag) {
+                for (uint32_t j = (k > (uint32_t)RING_SLOTS ? k - RING_SLOTS : 0); j < k; ++j)
+                    mbar_wait_quiet(&rfull[j % RING_SLOTS], (j / RING_SLOTS) & 1);
             }
         }
     } else if (warp == 1) {
@@ -687,6 +732,77 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             const int n0 = nt * g.BN;
             const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + a * 256;
+            if constexpr (RING) {
+                // Each lane finishes its own row in the slot (64-byte swizzle: the 16-byte
+                // piece qq of row r sits at qq ^ ((r >> 1) & 3)), then one lane stores the
+                // warp's 32 rows. A slot is released once the store has read it.
+                const int sw = (lane >> 1) & 3;
+                const int nc = g.BN / 16;
+                float bcur[16], bnext[16];
+                load_bias16(g, e, n0 + 16 * half, bcur);
+                int pend = -1;
+                bool rok = true;
+#pragma unroll 1
+                for (int c0 = 16 * half; c0 < g.BN; c0 += 32) {
+                    if (c0 + 32 < g.BN) load_bias16(g, e, n0 + c0 + 32, bnext);
+                    const uint32_t k = tl * nc + (c0 >> 4);
+                    const int s = (int)(k % RING_SLOTS);
+                    const bool in = mbar_wait(&rfull[s], (k / RING_SLOTS) & 1, &abort_flag, g.err, 7);
+                    if (!__all_sync(0xffffffffu, in)) {
+                        rok = false;
+                        break;
+                    }
+                    float v[16];
+                    tmem_ld16(taddr + c0, v);
+                    float* rt = ring + s * rstride + q * 512;  // this warp's 32 rows of the chunk
+#pragma unroll
+                    for (int qq = 0; qq < 4; ++qq) {
+                        float4* p = reinterpret_cast<float4*>(rt + lane * 16 + 4 * (qq ^ sw));
+                        float4 r = *p;
+                        const float o0 = v[4 * qq] * g.ascale + bcur[4 * qq];
+                        const float o1 = v[4 * qq + 1] * g.ascale + bcur[4 * qq + 1];
+                        const float o2 = v[4 * qq + 2] * g.ascale + bcur[4 * qq + 2];
+                        const float o3 = v[4 * qq + 3] * g.ascale + bcur[4 * qq + 3];
+                        if (e.cx) {
+                            const float4 cx = *reinterpret_cast<const float4*>(rt + 2048 + lane * 16 + 4 * (qq ^ sw));
+                            const float4 gt = *reinterpret_cast<const float4*>(gsm + n0 + c0 + 4 * qq);
+                            r.x = (r.x + o0) + (cx.x * gt.x) * e.cscale;
+                            r.y = (r.y + o1) + (cx.y * gt.y) * e.cscale;
+                            r.z = (r.z + o2) + (cx.z * gt.z) * e.cscale;
+                            r.w = (r.w + o3) + (cx.w * gt.w) * e.cscale;
+                        } else {
+                            r.x = r.x + o0;
+                            r.y = r.y + o1;
+                            r.z = r.z + o2;
+                            r.w = r.w + o3;
+                        }
+                        *p = r;
+                    }
+                    fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&tmY, rt, n0 + c0, (int)(mt * 128 + q * 32));
+                        bulk_commit();
+                        if (pend >= 0) {
+                            // the previous chunk's store has read its slot
+                            asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+                            mbar_arrive(&rempty[pend]);
+                        }
+                    }
+                    pend = s;
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) bcur[j] = bnext[j];
+                }
+                if (lane == 0 && pend >= 0) {
+                    bulk_wait_read();
+                    mbar_arrive(&rempty[pend]);
+                }
+                __syncwarp();
+                tc_fence_before();
+                mbar_arrive(&acc_empty[a]);
+                if (!rok) break;
+                continue;
+            }
             if (EK == EK_SHUF2) {
                 // PixelShuffle(2) store: channel n = 4c + 2i + j goes to channel c of output
                 // pixel (2y + i, 2x + j). 32 columns give 8 consecutive output channels for
@@ -830,7 +946,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
 
     // The epilogue's bulk stores complete before the CTA (and its staging tiles) go away.
-    if ((EK == EK_TMA || EK == EK_TMA_RES || EK == EK_QKV) && warp >= 2 && lane == 0) bulk_wait_all();
+    if ((EK == EK_TMA || EK == EK_TMA_RES || EK == EK_QKV || EK == EK_RING) && warp >= 2 && lane == 0) bulk_wait_all();
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
@@ -1318,10 +1434,17 @@ static int num_sms() {
 // tile (3 x 68 KB) still fit.
 static const long SMEM_CAP = 232448 - 22528;
 
+// EK_RING: the stages, rounded to 1 KB, then the slots and the gate.
+static size_t ring_smem(const UmmaArgs& g, const Epi& e) {
+    const size_t st = ((size_t)g.stages * (2 * 128 * g.ckb + 2 * g.BN * g.ckb) + 1023) & ~(size_t)1023;
+    return st + (size_t)RING_SLOTS * (e.cx ? 16384 : 8192) + (e.cx ? 4 * (size_t)g.BN * g.ntn : 0) + 1024;
+}
+
 template <int MODE, int TERMS, int EK, bool H16>
 static void launch_ek(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh, const CUtensorMap& bl,
                       const UmmaArgs& g, const Epi& e, const CUtensorMap& ty, const QkvMaps& qm, cudaStream_t st) {
-    const size_t smem = (size_t)g.stages * (2 * 128 * g.ckb + 2 * g.BN * g.ckb) + 1024;
+    size_t smem = (size_t)g.stages * (2 * 128 * g.ckb + 2 * g.BN * g.ckb) + 1024;
+    if (EK == EK_RING) smem = ring_smem(g, e);
     static unsigned configured = 0;
     int dev = 0;
     HAT_CUDA(cudaGetDevice(&dev));
@@ -1404,6 +1527,31 @@ static void launch_k(const CUtensorMap& ah, const CUtensorMap& al, const CUtenso
       }
     }
     if (e.qkv_split) throw Error(1, "umma_linear: the qkv attention layout is for fp16 parity mode");
+    if constexpr (MODE == 0) {
+        // A linear with a residual and a plain fp32 output: the residual stream by TMA.
+        auto al16 = [](const void* p) { return !(reinterpret_cast<uintptr_t>(p) & 15); };
+        const bool ring = e.res && !e.colsum && e.act == ACT_NONE && pick_ek(g, e) == EK_STORE && !g.y.lo &&
+                          !g.y.h16 && al16(g.y.hi) && al16(e.res) && g.ldo % 4 == 0 && g.nstore >= 16 &&
+                          g.M >= 128 && g.BN % 16 == 0 && (!e.cx || (al16(e.cx) && e.gate));
+        if (ring) {
+            UmmaArgs gr = g;
+            const long per = 2L * 128 * g.ckb + 2L * g.BN * g.ckb;
+            const long extra = (long)RING_SLOTS * (e.cx ? 16384 : 8192) + (e.cx ? 4L * g.BN * g.ntn : 0) + 2048;
+            gr.stages = (int)std::min<long>(g.stages, (SMEM_CAP - extra) / per);
+            if (gr.stages >= 2) {
+                uint64_t dims[2] = {(uint64_t)g.nstore, (uint64_t)g.M};
+                uint64_t str[1] = {(uint64_t)g.ldo * 4};
+                uint32_t ybox[2] = {16, 32}, rbox[2] = {16, 128};
+                ty = make_map(g.y.hi, 2, dims, str, ybox, 64);
+                qm.qkh = make_map(e.res, 2, dims, str, rbox, 64);
+                if (e.cx) qm.qkl = make_map(e.cx, 2, dims, str, rbox, 64);
+                gr.tma_st = 1;
+                if (ring_smem(gr, e) > (size_t)SMEM_CAP) throw Error(1, "umma_linear: residual ring does not fit");
+                launch_ek<MODE, TERMS, EK_RING, H16>(ah, al, bh, bl, gr, e, ty, qm, st);
+                return;
+            }
+        }
+    }
     const int sk = store_map<MODE>(g, e, ty);
     g.tma_st = sk != EK_STORE;
     switch (sk != EK_STORE ? sk : pick_ek(g, e)) {
