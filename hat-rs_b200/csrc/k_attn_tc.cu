@@ -138,6 +138,12 @@ __device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a, uint64_t b, uint3
 }
 // 2^x by the PTX ex2.approx instruction (relative error about 2^-22; subnormal results
 // flush to zero, which P never needs).
+// max of three (sm_100's three-input max)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
 __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -434,7 +440,6 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
                     mrow1 = b1 == 0 ? cm[0] : (b1 == 1 ? cm[1] : cm[2]);
                 }
                 const float* trow_sa = tab + (A0 - 2 * TSTRIDE * j);  // SA: minus (k>>4)*48 + (k&15)
-                float bmax = -INFINITY;
 #pragma unroll
                 for (int k = 0; k < 32; ++k) {
                     float v;
@@ -448,8 +453,11 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
                         }
                     }
                     sv[k] = v;  // log2 units: q carries scale * log2(e), the table log2(e)
-                    bmax = fmaxf(bmax, v);
                 }
+                // the block max: 16 three-input maxes
+                float bmax = fmaxf(sv[0], sv[1]);
+#pragma unroll
+                for (int k = 2; k < 32; k += 2) bmax = fmax3(bmax, sv[k], sv[k + 1]);
                 // The row's reference max moves only on a large jump (first block: set).
                 const bool need = j == 0 || bmax > m + RESCALE_LOG2;
                 float a = 1.f;
@@ -507,7 +515,23 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
             const long qpos = (long)qrow * wp + (OCA ? wx * 16 + qx : (wx * 16 + qx + gm.sx) % wp);
             const long ob = qpos * c + (long)head * D;
             if (qrow >= gm.olo && qrow < gm.ohi) {  // rows outside [olo, ohi) are a neighbour's
-                if (VW == 4) {
+                if (D % 8 == 0 && c % 8 == 0 && out.lo && out.h16) {
+                    // fp16 pairs, 16 bytes (8 features) a store, one range check
+                    bool big = false;
+#pragma unroll
+                    for (int i = 0; i < D; i += 8) {
+                        uint4 h, lo;
+                        split_h16x2(ov[i] * inv, ov[i + 1] * inv, h.x, lo.x);
+                        split_h16x2(ov[i + 2] * inv, ov[i + 3] * inv, h.y, lo.y);
+                        split_h16x2(ov[i + 4] * inv, ov[i + 5] * inv, h.z, lo.z);
+                        split_h16x2(ov[i + 6] * inv, ov[i + 7] * inv, h.w, lo.w);
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) big |= beyond_h16(ov[i + u] * inv);
+                        *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(out.hi) + ob + i) = h;
+                        *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(out.lo) + ob + i) = lo;
+                    }
+                    if (big && out.err) atomicCAS(out.err, 0, 21);
+                } else if (VW == 4) {
 #pragma unroll
                     for (int i = 0; i < D; i += 4)
                         put4(out, ob + i, make_float4(ov[i] * inv, ov[i + 1] * inv, ov[i + 2] * inv, ov[i + 3] * inv));
