@@ -261,6 +261,16 @@ enum { EK_STORE = 0, EK_SHUF2 = 1, EK_GENERIC = 2, EK_TMA = 3, EK_TMA_RES = 4, E
 // qkh = the residual, qkl = the CAB output.
 constexpr int RING_SLOTS = 4;
 
+// Epilogue warps of a k_umma kind. The qkv linear, whose attention-layout epilogue is its
+// bound, runs three warps per TMEM lane quarter, each taking every third 16-column chunk;
+// the other kinds two.
+constexpr int umma_epi_warps(int MODE, int EK) { return MODE == 0 && EK == EK_QKV ? 12 : 8; }
+// Warps ahead of the epilogue: the TMA producer, the MMA issuer and, for EK_RING, the
+// residual stream's producer (a warp of its own: two lanes of one warp spinning on
+// different barriers can starve each other).
+constexpr int umma_lead_warps(int EK) { return EK == EK_RING ? 3 : 2; }
+constexpr int umma_threads(int MODE, int EK) { return 32 * (umma_lead_warps(EK) + umma_epi_warps(MODE, EK)); }
+
 // The four output maps of EK_QKV (see Epi::qkv_split): q|k hi and lo (SW32 boxes of 16 x
 // 32), v^T hi and lo (unswizzled boxes of 32 tokens x 16 features).
 struct __align__(64) QkvMaps {
@@ -535,10 +545,12 @@ __device__ __forceinline__ void epi_chunk16(const UmmaArgs& g, const Epi& e, uin
 }
 
 template <int MODE, int TERMS, int EK, bool H16>
-__global__ void __launch_bounds__(NTHREADS, 1)
+__global__ void __launch_bounds__(umma_threads(MODE, EK), 1)
     k_umma(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
            const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl, const UmmaArgs g,
            const Epi e, const __grid_constant__ CUtensorMap tmY, const __grid_constant__ QkvMaps qm) {
+    constexpr int EW = umma_epi_warps(MODE, EK), LEAD = umma_lead_warps(EK), NT = umma_threads(MODE, EK);
+    constexpr int PARTS = EW / 4;
     extern __shared__ __align__(1024) uint8_t smraw[];
     __shared__ uint64_t full[6], empty[6], acc_full[2], acc_empty[2], drain;
     __shared__ uint64_t rfull[RING_SLOTS], rempty[RING_SLOTS];
@@ -548,11 +560,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // The channel-attention pool: per TMEM lane quarter, column sums accumulated over
     // every tile this CTA owns (in its fixed tile order), written once at the end. The
     // quarter's two epilogue warps own disjoint columns.
-    __shared__ float colacc[4][256];
+    constexpr int CA = (EK == EK_QKV || EK == EK_RING) ? 1 : 256;  // kinds without channel sums
+    __shared__ float colacc[4][CA];
     // Per epilogue warp: a 32 x 16 staging tile (swizzled) for the coalesced store; the
     // rotation is the 64-byte swizzle of the TMA store path, whose pattern needs the
     // tiles 512-byte aligned.
-    __shared__ __align__(1024) float stg[EPI_WARPS][32][16];
+    __shared__ __align__(1024) float stg[EK == EK_RING ? 1 : EW][32][16];
 
     uint8_t* sm = (uint8_t*)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
     const int S = g.stages;
@@ -570,9 +583,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     float* gsm = ring + RING_SLOTS * rstride;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int i = threadIdx.x; i < 4 * 256; i += NTHREADS) (&colacc[0][0])[i] = 0.f;
+    for (int i = threadIdx.x; i < 4 * CA; i += NT) (&colacc[0][0])[i] = 0.f;
     if (RING && e.cx)
-        for (int i = threadIdx.x; i < g.BN * g.ntn; i += NTHREADS) gsm[i] = i < g.N ? e.gate[i] : 0.f;
+        for (int i = threadIdx.x; i < g.BN * g.ntn; i += NT) gsm[i] = i < g.N ? e.gate[i] : 0.f;
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
@@ -580,12 +593,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&acc_full[a], 1);
-            mbar_init(&acc_empty[a], 32 * EPI_WARPS);
+            mbar_init(&acc_empty[a], 32 * EW);
         }
         mbar_init(&drain, 1);
         for (int r = 0; r < RING_SLOTS; ++r) {
             mbar_init(&rfull[r], 1);
-            mbar_init(&rempty[r], 4);  // the four lane-quarter warps of the chunk's half
+            mbar_init(&rempty[r], 4);  // the four lane-quarter warps that take the chunk
         }
         abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -632,7 +645,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 // Let the copies already issued land before the CTA can exit.
                 for (uint32_t j = (it > (uint32_t)S ? it - S : 0); j < it; ++j) mbar_wait_quiet(&full[j % S], (j / S) & 1);
             }
-        } else if (RING && lane == 1) {
+        }
+    } else if (RING && warp == 2) {
+        if (lane == 0) {
             // the residual stream: chunk k of this CTA's tile sequence into slot k % RING_SLOTS
             uint32_t k = 0;
             const uint32_t tx = e.cx ? 16384u : 8192u;
@@ -707,8 +722,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // ------------------------------------------------------------ epilogue
         const int q = warp & 3;          // TMEM lane quarter this warp may read
         const int row = q * 32 + lane;   // tile row of this thread
-        const int ew = warp - 2;         // 0..7 within the epilogue group
-        const int half = ew >> 2;        // which of the quarter's alternate chunks
+        const int ew = warp - LEAD;      // 0..EW-1 within the epilogue group
+        const int part = ew >> 2;        // which of the quarter's PARTS interleaved chunk sets
         uint32_t tl = 0;
         for (long t = blockIdx.x; t < ntiles; t += gridDim.x, ++tl) {
             if (__any_sync(0xffffffffu, abort_flag != 0)) break;
@@ -739,12 +754,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const int sw = (lane >> 1) & 3;
                 const int nc = g.BN / 16;
                 float bcur[16], bnext[16];
-                load_bias16(g, e, n0 + 16 * half, bcur);
+                load_bias16(g, e, n0 + 16 * part, bcur);
                 int pend = -1;
                 bool rok = true;
 #pragma unroll 1
-                for (int c0 = 16 * half; c0 < g.BN; c0 += 32) {
-                    if (c0 + 32 < g.BN) load_bias16(g, e, n0 + c0 + 32, bnext);
+                for (int c0 = 16 * part; c0 < g.BN; c0 += 16 * PARTS) {
+                    if (c0 + 16 * PARTS < g.BN) load_bias16(g, e, n0 + c0 + 16 * PARTS, bnext);
                     const uint32_t k = tl * nc + (c0 >> 4);
                     const int s = (int)(k % RING_SLOTS);
                     const bool in = mbar_wait(&rfull[s], (k / RING_SLOTS) & 1, &abort_flag, g.err, 7);
@@ -808,7 +823,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 // pixel (2y + i, 2x + j). 32 columns give 8 consecutive output channels for
                 // each of the 4 sub-pixels: two float4 stores per sub-pixel.
                 const int cout = g.N / 4;
-                for (int c0 = 32 * half; c0 < g.BN; c0 += 64) {
+                for (int c0 = 32 * part; c0 < g.BN; c0 += 32 * PARTS) {
                     float bv[32];  // bias first, so its latency overlaps the TMEM loads
 #pragma unroll
                     for (int j = 0; j < 32; ++j) bv[j] = e.bias ? __ldg(e.bias + n0 + c0 + j) : 0.f;
@@ -835,10 +850,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (EK == EK_STORE || EK == EK_TMA || EK == EK_TMA_RES || EK == EK_QKV) {
                 // each chunk's bias is loaded while the chunk before it is processed
                 float bcur[16], bnext[16];
-                load_bias16(g, e, n0 + 16 * half, bcur);
+                load_bias16(g, e, n0 + 16 * part, bcur);
 #pragma unroll 1
-                for (int c0 = 16 * half; c0 < g.BN; c0 += 32) {
-                    if (c0 + 32 < g.BN) load_bias16(g, e, n0 + c0 + 32, bnext);
+                for (int c0 = 16 * part; c0 < g.BN; c0 += 16 * PARTS) {
+                    if (c0 + 16 * PARTS < g.BN) load_bias16(g, e, n0 + c0 + 16 * PARTS, bnext);
                     epi_chunk16<MODE, EK == EK_TMA ? 1 : EK == EK_TMA_RES ? 2 : EK == EK_QKV ? 3 : 0>(
                         g, e, taddr, n0, c0, mt, q, lane, valid, stg[ew], colacc[q], bcur, &tmY, &qm);
 #pragma unroll
@@ -848,7 +863,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 mbar_arrive(&acc_empty[a]);
                 continue;
             }
-            for (int c0 = 16 * half; c0 < g.BN; c0 += 32) {
+            for (int c0 = 16 * part; c0 < g.BN; c0 += 16 * PARTS) {
                 float v[16];
                 tmem_ld16(taddr + c0, v);
 #pragma unroll
@@ -941,12 +956,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             __syncwarp();
             // Each warp writes the columns it owns (its chunk parity within a tile).
             for (int n = lane; n < g.N; n += 32)
-                if ((((n % g.BN) >> 4) & 1) == half) e.colsum[((long)blockIdx.x * 4 + q) * g.N + n] = colacc[q][n];
+                if (((n % g.BN) >> 4) % PARTS == part) e.colsum[((long)blockIdx.x * 4 + q) * g.N + n] = colacc[q][n];
         }
     }
 
     // The epilogue's bulk stores complete before the CTA (and its staging tiles) go away.
-    if ((EK == EK_TMA || EK == EK_TMA_RES || EK == EK_QKV || EK == EK_RING) && warp >= 2 && lane == 0) bulk_wait_all();
+    if ((EK == EK_TMA || EK == EK_TMA_RES || EK == EK_QKV || EK == EK_RING) && warp >= LEAD && lane == 0) bulk_wait_all();
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
@@ -1440,22 +1455,39 @@ static size_t ring_smem(const UmmaArgs& g, const Epi& e) {
     return st + (size_t)RING_SLOTS * (e.cx ? 16384 : 8192) + (e.cx ? 4 * (size_t)g.BN * g.ntn : 0) + 1024;
 }
 
+// The dynamic shared memory a k_umma instantiation may take: the 227 KB a CTA can have,
+// less its static shared memory (staging tiles and channel sums vary with the kind).
 template <int MODE, int TERMS, int EK, bool H16>
-static void launch_ek(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh, const CUtensorMap& bl,
-                      const UmmaArgs& g, const Epi& e, const CUtensorMap& ty, const QkvMaps& qm, cudaStream_t st) {
-    size_t smem = (size_t)g.stages * (2 * 128 * g.ckb + 2 * g.BN * g.ckb) + 1024;
-    if (EK == EK_RING) smem = ring_smem(g, e);
-    static unsigned configured = 0;
+static long umma_smem_cap() {
+    static long cap[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     int dev = 0;
     HAT_CUDA(cudaGetDevice(&dev));
-    if (!(configured & (1u << dev))) {
+    if (!cap[dev & 7]) {
+        cudaFuncAttributes fa;
+        HAT_CUDA(cudaFuncGetAttributes(&fa, k_umma<MODE, TERMS, EK, H16>));
+        cap[dev & 7] = 232448 - (long)fa.sharedSizeBytes;
         HAT_CUDA(cudaFuncSetAttribute(k_umma<MODE, TERMS, EK, H16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)SMEM_CAP));
-        configured |= 1u << dev;
+                                      (int)cap[dev & 7]));
     }
+    return cap[dev & 7];
+}
+
+template <int MODE, int TERMS, int EK, bool H16>
+static void launch_ek(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh, const CUtensorMap& bl,
+                      const UmmaArgs& g0, const Epi& e, const CUtensorMap& ty, const QkvMaps& qm, cudaStream_t st) {
+    const long cap = umma_smem_cap<MODE, TERMS, EK, H16>();
+    UmmaArgs g = g0;
+    const long per = 2L * 128 * g.ckb + 2L * g.BN * g.ckb;
+    const long extra = EK == EK_RING ? (long)ring_smem(g, e) - (long)g.stages * per : 1024;
+    g.stages = (int)std::min<long>(g.stages, (cap - extra) / per);
+    if (g.stages < 1 || (EK == EK_RING && g.stages < 2))
+        throw Error(1, "umma: the pipeline stages do not fit in shared memory");
+    const size_t smem = EK == EK_RING ? ring_smem(g, e) : (size_t)g.stages * per + 1024;
     const long grid = std::min<long>(g.ntiles, num_sms());
-    if (e.colsum && g.N > 256) throw Error(1, "umma: channel sums are limited to 256 columns");
-    k_umma<MODE, TERMS, EK, H16><<<(unsigned)grid, NTHREADS, smem, st>>>(ah, al, bh, bl, g, e, ty, qm);
+    if (e.colsum && (g.N > 256 || EK == EK_QKV || EK == EK_RING))
+        throw Error(1, "umma: channel sums are limited to 256 columns of the plain epilogues");
+    constexpr int NT = umma_threads(MODE, EK);
+    k_umma<MODE, TERMS, EK, H16><<<(unsigned)grid, NT, smem, st>>>(ah, al, bh, bl, g, e, ty, qm);
     HAT_CUDA(cudaGetLastError());
     count_launch();
 }
@@ -1537,7 +1569,8 @@ static void launch_k(const CUtensorMap& ah, const CUtensorMap& al, const CUtenso
             UmmaArgs gr = g;
             const long per = 2L * 128 * g.ckb + 2L * g.BN * g.ckb;
             const long extra = (long)RING_SLOTS * (e.cx ? 16384 : 8192) + (e.cx ? 4L * g.BN * g.ntn : 0) + 2048;
-            gr.stages = (int)std::min<long>(g.stages, (SMEM_CAP - extra) / per);
+            const long cap = umma_smem_cap<MODE, TERMS, EK_RING, H16>();
+            gr.stages = (int)std::min<long>(g.stages, (cap - extra) / per);
             if (gr.stages >= 2) {
                 uint64_t dims[2] = {(uint64_t)g.nstore, (uint64_t)g.M};
                 uint64_t str[1] = {(uint64_t)g.ldo * 4};
@@ -1546,7 +1579,7 @@ static void launch_k(const CUtensorMap& ah, const CUtensorMap& al, const CUtenso
                 qm.qkh = make_map(e.res, 2, dims, str, rbox, 64);
                 if (e.cx) qm.qkl = make_map(e.cx, 2, dims, str, rbox, 64);
                 gr.tma_st = 1;
-                if (ring_smem(gr, e) > (size_t)SMEM_CAP) throw Error(1, "umma_linear: residual ring does not fit");
+                if (ring_smem(gr, e) > (size_t)cap) throw Error(1, "umma_linear: residual ring does not fit");
                 launch_ek<MODE, TERMS, EK_RING, H16>(ah, al, bh, bl, gr, e, ty, qm, st);
                 return;
             }
