@@ -37,9 +37,6 @@ namespace hat {
 
 namespace {
 
-constexpr int NTHREADS = 320;
-constexpr int EPI_WARPS = 8;
-
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return (uint32_t)__cvta_generic_to_shared(p);
 }
@@ -1042,26 +1039,33 @@ __device__ __forceinline__ void tmem_st8u(uint32_t taddr, const uint32_t* r) {
 // while the hidden chunks run; the final epilogue adds fc2 + bias into that tile in place
 // and stores it by TMA, so no global load sits on the epilogue's critical path.
 constexpr int MLP_RT = 4;
+// Epilogue warps of a k_mlp variant: the fp16-pair, residual-tile one (whose GELU phase bounds
+// it) runs three per TMEM lane quarter, each taking 32 of a hidden chunk's 96 columns; the
+// others two (48 columns each).
+constexpr int mlp_epi_warps(bool H16, int SK) { return H16 && SK == MLP_RT ? 12 : 8; }
 template <int TERMS, bool H16, int SK>
-__global__ void __launch_bounds__(NTHREADS, 1)
+__global__ void __launch_bounds__(64 + 32 * mlp_epi_warps(H16, SK), 1)
     k_mlp(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
           const __grid_constant__ CUtensorMap tmW1h, const __grid_constant__ CUtensorMap tmW1l,
           const __grid_constant__ CUtensorMap tmW2h, const __grid_constant__ CUtensorMap tmW2l, const MlpArgs g,
           const Epi e, const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmR) {
     constexpr bool RT = SK == MLP_RT;
+    constexpr int EW = mlp_epi_warps(H16, SK), NT = 64 + 32 * EW, PARTS = EW / 4;
+    constexpr int CW = MLP_HC / PARTS;  // hidden columns of a chunk per epilogue warp
+    static_assert(CW % 16 == 0, "whole 16-column TMEM loads per warp");
     extern __shared__ __align__(1024) uint8_t smraw[];
     __shared__ uint64_t full[6], empty[6], d1_full, d1_free, h_full, h_empty, d2_full, d2_free, drain;
     __shared__ uint64_t res_full, res_empty;
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int abort_flag;
-    __shared__ __align__(1024) float stg[RT ? 1 : EPI_WARPS][32][16];
+    __shared__ __align__(1024) float stg[RT ? 1 : EW][32][16];
     __shared__ float no_colsum[256];
     __shared__ float b1s[MLP_MAXH];  // fc1 bias, zero past HID (read by every chunk)
 
     uint8_t* sm = (uint8_t*)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
     const int S = g.stages;
     const uint32_t A_B = 128 * 128, W1_B = MLP_HC * 128, W2_B = (uint32_t)g.CP * 128;
-    for (int i = threadIdx.x; i < MLP_MAXH; i += NTHREADS) b1s[i] = i < g.HID ? g.b1[i] : 0.f;
+    for (int i = threadIdx.x; i < MLP_MAXH; i += NT) b1s[i] = i < g.HID ? g.b1[i] : 0.f;
     const uint32_t st_bytes = max(2 * A_B + 2 * W1_B, 2 * W2_B);
     float* rtile = reinterpret_cast<float*>(sm + S * st_bytes);  // MLP_RT: the residual / output tile
     int* gerr = g.st.err;
@@ -1073,14 +1077,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             mbar_init(&empty[s], 1);
         }
         mbar_init(&d1_full, 1);
-        mbar_init(&d1_free, 32 * EPI_WARPS);
-        mbar_init(&h_full, 32 * EPI_WARPS);
+        mbar_init(&d1_free, 32 * EW);
+        mbar_init(&h_full, 32 * EW);
         mbar_init(&h_empty, 1);
         mbar_init(&d2_full, 1);
-        mbar_init(&d2_free, 32 * EPI_WARPS);
+        mbar_init(&d2_free, 32 * EW);
         mbar_init(&drain, 1);
         mbar_init(&res_full, 1);
-        mbar_init(&res_empty, EPI_WARPS);
+        mbar_init(&res_empty, EW);
         abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -1262,7 +1266,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int q4 = warp & 3;
         const int row = q4 * 32 + lane;
         const int ew = warp - 2;
-        const int half = ew >> 2;
+        const int part = ew >> 2;  // which of the quarter's PARTS column sets
         const uint32_t lanes = (uint32_t)(q4 * 32) << 16;
         uint32_t qc = 0, tl = 0;
         for (long t = blockIdx.x; t < g.mtiles; t += gridDim.x, ++tl) {
@@ -1275,16 +1279,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     break;
                 }
                 tc_fence_after();
-                // This warp's 48 columns of the chunk.
-                float v[48];
-                tmem_ld16(tmem + lanes + T_D1 + half * 48, v);
-                tmem_ld16(tmem + lanes + T_D1 + half * 48 + 16, v + 16);
-                tmem_ld16(tmem + lanes + T_D1 + half * 48 + 32, v + 32);
+                // This warp's CW columns of the chunk.
+                float v[CW];
+#pragma unroll
+                for (int i = 0; i < CW / 16; ++i) tmem_ld16(tmem + lanes + T_D1 + part * CW + 16 * i, v + 16 * i);
                 tc_fence_before();
                 mbar_arrive(&d1_free);
-                const int nb = h * MLP_HC + half * 48;
+                const int nb = h * MLP_HC + part * CW;
 #pragma unroll
-                for (int j = 0; j < 48; ++j) {
+                for (int j = 0; j < CW; ++j) {
                     const float x = v[j] * g.s1 + b1s[nb + j];
                     v[j] = gelu_fast(x);
                 }
@@ -1296,21 +1299,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 }
                 tc_fence_after();
                 if (H16) {
-                    // 48 values -> 24 packed pairs of hi and of lo (columns half*24 ..)
-                    uint32_t hp[24], lp[24];
+                    // CW values -> CW/2 packed pairs of hi and of lo (columns part*CW/2 ..)
+                    uint32_t hp[CW / 2], lp[CW / 2];
 #pragma unroll
-                    for (int j = 0; j < 24; ++j) split_h16x2(v[2 * j], v[2 * j + 1], hp[j], lp[j]);
-                    tmem_st8u(tmem + lanes + T_HH + half * 24, hp);
-                    tmem_st8u(tmem + lanes + T_HH + half * 24 + 8, hp + 8);
-                    tmem_st8u(tmem + lanes + T_HH + half * 24 + 16, hp + 16);
-                    if (TERMS == 3) {
-                        tmem_st8u(tmem + lanes + T_HL + half * 24, lp);
-                        tmem_st8u(tmem + lanes + T_HL + half * 24 + 8, lp + 8);
-                        tmem_st8u(tmem + lanes + T_HL + half * 24 + 16, lp + 16);
+                    for (int j = 0; j < CW / 2; ++j) split_h16x2(v[2 * j], v[2 * j + 1], hp[j], lp[j]);
+#pragma unroll
+                    for (int i = 0; i < CW / 16; ++i) {
+                        tmem_st8u(tmem + lanes + T_HH + part * (CW / 2) + 8 * i, hp + 8 * i);
+                        if (TERMS == 3) tmem_st8u(tmem + lanes + T_HL + part * (CW / 2) + 8 * i, lp + 8 * i);
                     }
                 } else {
 #pragma unroll
-                    for (int g16 = 0; g16 < 3; ++g16) {
+                    for (int g16 = 0; g16 < CW / 16; ++g16) {
                         float hi[16], lo[16];
 #pragma unroll
                         for (int j = 0; j < 16; ++j) {
@@ -1321,8 +1321,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                                 lo[j] = 0.f;
                             }
                         }
-                        tmem_st16(tmem + lanes + T_HH + half * 48 + 16 * g16, hi);
-                        if (TERMS == 3) tmem_st16(tmem + lanes + T_HL + half * 48 + 16 * g16, lo);
+                        tmem_st16(tmem + lanes + T_HH + part * CW + 16 * g16, hi);
+                        if (TERMS == 3) tmem_st16(tmem + lanes + T_HL + part * CW + 16 * g16, lo);
                     }
                 }
                 asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
@@ -1338,10 +1338,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 if (!__all_sync(0xffffffffu, rg)) break;
                 const int sw = (lane >> 1) & 3;  // this row's 16-byte chunk rotation (64-byte swizzle)
                 float bcur[16], bnext[16];
-                load_bias16(g.st, e, 16 * half, bcur);
+                load_bias16(g.st, e, 16 * part, bcur);
 #pragma unroll 1
-                for (int c0 = 16 * half; c0 < g.CP; c0 += 32) {
-                    if (c0 + 32 < g.CP) load_bias16(g.st, e, c0 + 32, bnext);
+                for (int c0 = 16 * part; c0 < g.CP; c0 += 16 * PARTS) {
+                    if (c0 + 16 * PARTS < g.CP) load_bias16(g.st, e, c0 + 16 * PARTS, bnext);
                     float v[16];
                     tmem_ld16(tmem + lanes + T_D2 + c0, v);
                     float* tile = rtile + (c0 >> 4) * 2048 + q4 * 512;  // this warp's 32 rows of the chunk
@@ -1375,10 +1375,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const long m = t * 128 + row;
                 const bool valid = m < g.st.M;
                 float bcur[16], bnext[16];
-                load_bias16(g.st, e, 16 * half, bcur);
+                load_bias16(g.st, e, 16 * part, bcur);
 #pragma unroll 1
-                for (int c0 = 16 * half; c0 < g.CP; c0 += 32) {
-                    if (c0 + 32 < g.CP) load_bias16(g.st, e, c0 + 32, bnext);
+                for (int c0 = 16 * part; c0 < g.CP; c0 += 16 * PARTS) {
+                    if (c0 + 16 * PARTS < g.CP) load_bias16(g.st, e, c0 + 16 * PARTS, bnext);
                     epi_chunk16<0, SK>(g.st, e, tmem + lanes + T_D2, 0, c0, t, q4, lane, valid, stg[ew], no_colsum,
                                        bcur, &tmY);
 #pragma unroll
@@ -1798,7 +1798,8 @@ long umma_mlp(int mode, Opnd x, const GemmW& w1, const float* b1, const GemmW& w
         configured[which] |= 1u << dev;
     }
     const long grid = std::min<long>(g.mtiles, num_sms());
-    kern<<<(unsigned)grid, NTHREADS, smem, st>>>(tah, tal, t1h, t1l, t2h, t2l, g, e, ty, tr);
+    const int nt = 64 + 32 * mlp_epi_warps(h16, skx == 3 ? MLP_RT : skx);
+    kern<<<(unsigned)grid, nt, smem, st>>>(tah, tal, t1h, t1l, t2h, t2l, g, e, ty, tr);
     HAT_CUDA(cudaGetLastError());
     count_launch();
     return 0;
