@@ -211,7 +211,7 @@ __global__ void k_layernorm16(const float* __restrict__ x, const float* __restri
 // with two bulk stores. Few instructions and many bytes in flight per SM. c a multiple of 8
 // and at most 144 (9 channels a lane). Waits are bounded; on expiry error 30 is recorded and
 // the CTA stops.
-constexpr int LN_TOK = 64;
+constexpr int LN_TOK = 32;
 __device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 __global__ void __launch_bounds__(256) k_layernorm_bulk(const float* __restrict__ x, const float* __restrict__ g,
                                                         const float* __restrict__ b, Dst y, long m, int c,
@@ -358,7 +358,7 @@ void launch_layernorm(const float* x, const float* g, const float* b, Dst y, lon
             configured |= 1u << dev;
         }
         const long ntiles = (m + LN_TOK - 1) / LN_TOK;
-        const long grid = std::min<long>(ntiles, 2L * sms);
+        const long grid = std::min<long>(ntiles, 4L * sms);  // four 55 KB CTAs per SM
         k_layernorm_bulk<<<(unsigned)grid, 256, smem, st>>>(x, g, b, y, m, c, err);
         HAT_CUDA(cudaGetLastError());
         count_launch();

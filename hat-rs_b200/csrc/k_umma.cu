@@ -257,6 +257,13 @@ enum { EK_STORE = 0, EK_SHUF2 = 1, EK_GENERIC = 2, EK_TMA = 3, EK_TMA_RES = 4, E
 // slot in place and stores it from there by TMA. The slot maps travel in QkvMaps:
 // qkh = the residual, qkl = the CAB output.
 constexpr int RING_SLOTS = 4;
+// Chunk k's "loaded" barrier is rfull[k % RING_FULL]. The chunks of one slot are consumed by
+// different warps in turn, and a warp may reach chunk k while the load of chunk k - 4 (the
+// slot's previous chunk, another warp's) is still in flight; with one barrier per slot its
+// parity would then read as complete. With twice as many barriers the previous use of
+// rfull[k % 8] is chunk k - 8, whose slot had to be released (so its load had landed)
+// before chunk k - 4 could be loaded.
+constexpr int RING_FULL = 2 * RING_SLOTS;
 
 // Epilogue warps of a k_umma kind. The qkv linear, whose attention-layout epilogue is its
 // bound, runs three warps per TMEM lane quarter, each taking every third 16-column chunk;
@@ -550,7 +557,7 @@ __global__ void __launch_bounds__(umma_threads(MODE, EK), 1)
     constexpr int PARTS = EW / 4;
     extern __shared__ __align__(1024) uint8_t smraw[];
     __shared__ uint64_t full[6], empty[6], acc_full[2], acc_empty[2], drain;
-    __shared__ uint64_t rfull[RING_SLOTS], rempty[RING_SLOTS];
+    __shared__ uint64_t rfull[RING_FULL], rempty[RING_SLOTS];
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int abort_flag;
     constexpr bool RING = EK == EK_RING;
@@ -593,10 +600,8 @@ __global__ void __launch_bounds__(umma_threads(MODE, EK), 1)
             mbar_init(&acc_empty[a], 32 * EW);
         }
         mbar_init(&drain, 1);
-        for (int r = 0; r < RING_SLOTS; ++r) {
-            mbar_init(&rfull[r], 1);
-            mbar_init(&rempty[r], 4);  // the four lane-quarter warps that take the chunk
-        }
+        for (int r = 0; r < RING_FULL; ++r) mbar_init(&rfull[r], 1);
+        for (int r = 0; r < RING_SLOTS; ++r) mbar_init(&rempty[r], 4);  // the four lane-quarter warps that take the chunk
         abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -658,15 +663,16 @@ __global__ void __launch_bounds__(umma_threads(MODE, EK), 1)
                         ok = false;
                         break;
                     }
-                    mbar_expect_tx(&rfull[s], tx);
+                    uint64_t* fb = &rfull[k % RING_FULL];
+                    mbar_expect_tx(fb, tx);
                     float* slot = ring + s * rstride;
-                    tma_2d(slot, &qm.qkh, n0 + 16 * c, row0, &rfull[s]);
-                    if (e.cx) tma_2d(slot + 2048, &qm.qkl, n0 + 16 * c, row0, &rfull[s]);
+                    tma_2d(slot, &qm.qkh, n0 + 16 * c, row0, fb);
+                    if (e.cx) tma_2d(slot + 2048, &qm.qkl, n0 + 16 * c, row0, fb);
                 }
             }
             if (abort_flag) {
                 for (uint32_t j = (k > (uint32_t)RING_SLOTS ? k - RING_SLOTS : 0); j < k; ++j)
-                    mbar_wait_quiet(&rfull[j % RING_SLOTS], (j / RING_SLOTS) & 1);
+                    mbar_wait_quiet(&rfull[j % RING_FULL], (j / RING_FULL) & 1);
             }
         }
     } else if (warp == 1) {
@@ -759,7 +765,7 @@ __global__ void __launch_bounds__(umma_threads(MODE, EK), 1)
                     if (c0 + 16 * PARTS < g.BN) load_bias16(g, e, n0 + c0 + 16 * PARTS, bnext);
                     const uint32_t k = tl * nc + (c0 >> 4);
                     const int s = (int)(k % RING_SLOTS);
-                    const bool in = mbar_wait(&rfull[s], (k / RING_SLOTS) & 1, &abort_flag, g.err, 7);
+                    const bool in = mbar_wait(&rfull[k % RING_FULL], (k / RING_FULL) & 1, &abort_flag, g.err, 7);
                     if (!__all_sync(0xffffffffu, in)) {
                         rok = false;
                         break;
