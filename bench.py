@@ -66,7 +66,7 @@ def baseline_mpixs():
 # DRAM bytes (read + write) per launch of a kernel kind at this workload, from one ncu
 # capture (dram__bytes_read.sum + dram__bytes_write.sum); profiles/ holds the capture's
 # summary and command. Kinds without a capture report null.
-NCU_TRAFFIC_BYTES = {"attn.window": 584.1e6}  # profiles/k_attn_tc_window_hats_x4_512.md
+NCU_TRAFFIC_BYTES = {"attn.window": 583.3e6}  # profiles/k_attn_tc_window_hats_x4_512.md
 
 
 def peaks():
