@@ -146,6 +146,20 @@ def make_checkpoint(directory: str) -> str:
     return p
 
 
+def arm_config(args, ws):
+    """The workload description both arms print (the reference arm samples a crop of it)."""
+    strip = args.shard == "strip"
+    return {"workload": (f"{VARIANT.upper()} x{SCALE}, one {H}x{W} image split into row strips over "
+                         f"{ws} GPU(s) (configs[3])") if strip else
+                        f"{VARIANT.upper()} x{SCALE}, one {H}x{W} image per GPU (configs[1])",
+            "variant": VARIANT, "scale": SCALE, "h": H, "w": W,
+            "images_per_gpu": (1.0 / ws) if strip else 1,
+            "mode": args.mode,
+            "parallelism": (f"strip{ws} (row strips, NCCL halo exchange)" if strip
+                            else f"dp{ws} (independent images)"),
+            "l2": "256 MB buffer written between timed steps (> 126 MB L2)"}
+
+
 def run_reference(args):
     """The reference arm: the CPU oracle port on all host cores, one crop per step."""
     ws, rank, _ = dist_env()
@@ -166,14 +180,14 @@ def run_reference(args):
     value = mpix / t
     cores = os.cpu_count()
     line = {
-        "impl": "reference", "metric": metric_name(), "value": value, "unit": "Mpix/s", "n_gpus": ws,
+        "impl": "reference", "metric": metric_name(args.mode), "value": value, "unit": "Mpix/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-        "config": {"workload": f"{VARIANT.upper()} x{SCALE} {crop}x{crop} crop of the {H}x{W} image per step (CPU)",
-                   "variant": VARIANT, "scale": SCALE},
+        "config": arm_config(args, ws),
         "cpu_baseline": {"value": value, "unit": "Mpix/s", "cores": cores, "kind": "port",
                          "sample": f"numpy/OpenBLAS float32 restatement of the reference forward "
-                                   f"(oracle/hat_oracle.py) on a {crop}x{crop} crop, {args.steps} steps"},
+                                   f"(oracle/hat_oracle.py) on a {crop}x{crop} crop of the workload image per "
+                                   f"step, {args.steps} steps"},
         "e2e": {"value": value, "unit": "Mpix/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -321,15 +335,7 @@ def run_ours(args):
             "vs_baseline": value / baseline_mpixs() if baseline_mpixs() else None,
             "dtype": "fp32" if mode == 0 else "tf32",
             "data": "synthetic",
-            "config": {"workload": (f"{VARIANT.upper()} x{SCALE}, one {H}x{W} image split into row strips over "
-                                    f"{ws} GPU(s) (configs[3])") if strip else
-                                   f"{VARIANT.upper()} x{SCALE}, one {H}x{W} image per GPU (configs[1])",
-                       "variant": VARIANT, "scale": SCALE, "h": H, "w": W,
-                       "images_per_gpu": (1.0 / ws) if strip else 1,
-                       "mode": args.mode,
-                       "parallelism": (f"strip{ws} (row strips, NCCL halo exchange)" if strip
-                                       else f"dp{ws} (independent images)"),
-                       "l2": "256 MB buffer written between timed steps (> 126 MB L2)"},
+            "config": arm_config(args, ws),
             # per rank: the whole input image in, this rank's output rows out (all of them
             # unless strip-sharded)
             "e2e": {"value": e2e, "unit": "Mpix/s", "h2d_bytes_per_step": 3 * H * W * 4,
