@@ -182,8 +182,8 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": metric_name(args.mode), "value": value, "unit": "Mpix/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-        "config": arm_config(args, ws),
+        "scaling": "strong" if args.shard == "strip" else "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic", "config": arm_config(args, ws),
         "cpu_baseline": {"value": value, "unit": "Mpix/s", "cores": cores, "kind": "port",
                          "sample": f"numpy/OpenBLAS float32 restatement of the reference forward "
                                    f"(oracle/hat_oracle.py) on a {crop}x{crop} crop of the workload image per "
