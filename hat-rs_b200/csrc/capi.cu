@@ -117,6 +117,16 @@ int hat_b200_forward_device(hat_b200* h, int n, int height, int width, const flo
     });
 }
 
+int hat_b200_sync(hat_b200* h, char* err, size_t errlen) {
+    if (!h) {
+        set_err(err, errlen, "hat_b200_sync: null handle");
+        return HAT_B200_EINVAL;
+    }
+    return guarded(err, errlen, [&] { h->eng->sync(); });
+}
+
+int hat_b200_fp16_pairs(const hat_b200* h) { return h && h->eng->fp16_pairs() ? 1 : 0; }
+
 size_t hat_b200_footprint_bytes(const hat_b200* h, int height, int width) {
     if (!h || height <= 0 || width <= 0) return 0;
     return h->eng->footprint_bytes(height, width);

@@ -18,6 +18,13 @@ struct Error : std::runtime_error {
     Error(int c, const std::string& m) : std::runtime_error(m), code(c) {}
 };
 
+// Codes the kernels leave in the device error word. The bounded pipeline waits use small
+// numbers (one per wait site, below 64); these two report an operand that fp16 operand
+// pairs cannot hold (|x| >= 65504), which the engine answers by redoing the pass on tf32
+// pairs.
+constexpr int ERR_RANGE_ATTN = 90;  // an attention operand (q, k or v)
+constexpr int ERR_RANGE_GEMM = 91;  // a GEMM operand plane written as fp16 pairs
+
 #define HAT_CUDA(call)                                                                   \
     do {                                                                                 \
         cudaError_t e_ = (call);                                                         \
@@ -85,7 +92,7 @@ struct Plan {
 //  * `h16`: `hi` and `lo` are fp16 arrays (element i at byte 2i, behind the float
 //    pointers): hi = fp16(x), lo = fp16(x - hi), 22 significant bits, read by
 //    kind::f16 MMAs. Values under fp16's normal range keep an absolute error of at
-//    most 2^-25; |x| >= 65504 does not fit and is reported through `err` (code 21).
+//    most 2^-25; |x| >= 65504 does not fit and is reported through `err` (ERR_RANGE_GEMM).
 //  * otherwise: fp32 arrays, hi = x rounded to tf32 and lo the rounded remainder (see
 //    split_tf32), hi + lo within 2^-22 |x| of x, read by kind::tf32 MMAs.
 // `lo == nullptr` marks a plain fp32 plane (fast mode, the CUDA-core path, and planes
@@ -170,7 +177,7 @@ __device__ __forceinline__ void put(const Dst& d, long i, float v) {
         split_h16(v, h, l);
         reinterpret_cast<__half*>(d.hi)[i] = h;
         reinterpret_cast<__half*>(d.lo)[i] = l;
-        if (beyond_h16(v) && d.err) atomicCAS(d.err, 0, 21);
+        if (beyond_h16(v) && d.err) atomicCAS(d.err, 0, ERR_RANGE_GEMM);
     } else if (d.lo) {
         float h, l;
         split_tf32(v, h, l);
@@ -189,7 +196,7 @@ __device__ __forceinline__ void put4(const Dst& d, long i, float4 v) {
         *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(d.hi) + i) = h;
         *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(d.lo) + i) = l;
         if ((beyond_h16(v.x) || beyond_h16(v.y) || beyond_h16(v.z) || beyond_h16(v.w)) && d.err)
-            atomicCAS(d.err, 0, 21);
+            atomicCAS(d.err, 0, ERR_RANGE_GEMM);
     } else if (d.lo) {
         float4 h, l;
         split_tf32(v.x, h.x, l.x);
@@ -254,6 +261,14 @@ struct Epi {
 // ---------------------------------------------------------------- kernels (launchers)
 // All launchers enqueue on `st` and throw hat::Error on a launch failure. `launches`
 // counts kernels issued (the reference's `launched()`, src/cuda.rs:542-555).
+// Lets kernel `fn` take `bytes` of dynamic shared memory on the current device. Called
+// before every launch instead of being cached per device ordinal: the setting belongs to
+// the device's context, which cudaDeviceReset (or a different context) replaces.
+template <class F>
+inline void allow_dyn_smem(F* fn, size_t bytes) {
+    HAT_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+}
+
 extern thread_local uint64_t* g_launch_counter;
 inline void count_launch(int n = 1) {
     if (g_launch_counter) *g_launch_counter += n;

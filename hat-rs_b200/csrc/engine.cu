@@ -138,12 +138,25 @@ Engine::Engine(const std::string& path, int device, int mode, bool use_graph, bo
     HAT_CUDA(cudaMalloc(&derr_, sizeof(int)));
     HAT_CUDA(cudaMemsetAsync(derr_, 0, sizeof(int), stream_));
 
-    // One device allocation: every f32 tensor as stored, then every GEMM operand in the
-    // kernels' layouts (CUDA-core layout, tensor-core hi/lo split).
+    h16_ = split() && wt_.embed % 8 == 0;
+    upload_weights();
+}
+
+// One device allocation: every f32 tensor as stored, then every GEMM operand in the
+// kernels' layouts (CUDA-core layout, tensor-core hi/lo split as fp16 pairs when `h16_`,
+// tf32 pairs otherwise). Called at construction and again when a pass falls back from
+// fp16 to tf32 operand pairs.
+void Engine::upload_weights() {
+    if (dweights_) {
+        HAT_CUDA(cudaStreamSynchronize(stream_));
+        cudaFree(dweights_);
+        dweights_ = nullptr;
+    }
+    w_.clear();
+    gw_.clear();
     const int cmid_stride = Sizes::of(wt_, Plan::make(16, 16, wt_.window)).cmid_stride;
     tap_cab_ = 9 * wt_.compressed <= 64;
     tap_ld_ = (9 * wt_.compressed + 3) / 4 * 4;
-    h16_ = split() && wt_.embed % 8 == 0;
     // fp16 stride of the middle plane: 16 (one 32-byte k-step) or a multiple of 8; it
     // fits in the buffer's cmid_stride floats (cmid_stride >= max(compressed, 8)).
     cmid_ld_ = !h16_ ? cmid_stride : wt_.compressed <= 16 ? 16 : (wt_.compressed + 7) / 8 * 8;
@@ -240,6 +253,7 @@ Engine::Engine(const std::string& path, int device, int mode, bool use_graph, bo
     if (off > total) throw Error(3, "gpu: weight arena overflow");
     HAT_CUDA(cudaStreamSynchronize(stream_));
 }
+
 
 Engine::~Engine() {
     cudaSetDevice(device_);
@@ -398,21 +412,49 @@ void Engine::check_memory(int h, int w) const {
     }
 }
 
-void Engine::check_device_error() {
+int Engine::take_device_error() {
     int v = 0;
     HAT_CUDA(cudaMemcpyAsync(&v, derr_, sizeof(int), cudaMemcpyDeviceToHost, stream_));
     HAT_CUDA(cudaStreamSynchronize(stream_));
-    if (v) {
-        HAT_CUDA(cudaMemsetAsync(derr_, 0, sizeof(int), stream_));
-        if (v == 20)
-            throw Error(3, "gpu: an attention operand (q, k or v) reached fp16's range (|x| >= 65504), which the "
-                           "tensor-core split cannot carry (code 20); the pass's output is invalid");
-        if (v == 21)
-            throw Error(3, "gpu: an activation reached fp16's range (|x| >= 65504), which the fp16 operand split "
-                           "cannot carry (code 21); the pass's output is invalid");
-        throw Error(3, "gpu: a tensor-core kernel gave up waiting on its pipeline (code " + std::to_string(v) +
-                           "); the pass's output is invalid");
+    if (v) HAT_CUDA(cudaMemsetAsync(derr_, 0, sizeof(int), stream_));
+    return v;
+}
+
+static void raise_device_error(int v) {
+    if (!v) return;
+    if (v == ERR_RANGE_ATTN)
+        throw Error(3, "gpu: an attention operand (q, k or v) reached fp16's range (|x| >= 65504), which the "
+                       "tensor-core split cannot carry (code " + std::to_string(v) + "); the pass's output is invalid");
+    if (v == ERR_RANGE_GEMM)
+        throw Error(3, "gpu: an activation reached fp16's range (|x| >= 65504), which the fp16 operand split "
+                       "cannot carry (code " + std::to_string(v) + "); the pass's output is invalid");
+    throw Error(3, "gpu: a tensor-core kernel gave up waiting on its pipeline (code " + std::to_string(v) +
+                       "); the pass's output is invalid");
+}
+
+void Engine::check_device_error() { raise_device_error(take_device_error()); }
+
+void Engine::sync() {
+    HAT_CUDA(cudaSetDevice(device_));
+    HAT_CUDA(cudaStreamSynchronize(stream_));
+    check_device_error();
+}
+
+// fp16 operand pairs carry 22 significant bits but only fp16's exponent range; a value of
+// 65504 or more sets ERR_RANGE_ATTN / ERR_RANGE_GEMM. The weights are prepared again as tf32 pairs (the same 22
+// bits with fp32's exponent range), the arena is cleared (the planes change layout) and the
+// handle stays on tf32 pairs from then on.
+void Engine::fall_back_to_tf32_pairs() {
+    HAT_CUDA(cudaStreamSynchronize(stream_));
+    if (graph_) {
+        cudaGraphExecDestroy(graph_);
+        graph_ = nullptr;
     }
+    h16_ = false;
+    upload_weights();
+    have_plan_ = false;  // the next ensure_plan clears the arena
+    eager_runs_ = 0;
+    ++fallbacks_;
 }
 
 void Engine::ensure_plan(int h, int w) {
@@ -816,15 +858,25 @@ void Engine::forward_device(int n, int h, int w, const float* din, float* dout, 
 void Engine::forward_host(int n, int h, int w, const float* in, float* out) {
     if (n <= 0 || h <= 0 || w <= 0) throw Error(1, std::to_string(h) + "x" + std::to_string(w) + " is empty");
     HAT_CUDA(cudaSetDevice(device_));
-    ensure_plan(h, w);
     const long inN = 3L * h * w, outN = 3L * h * wt_.scale * w * wt_.scale;
-    for (int i = 0; i < n; ++i) {
-        HAT_CUDA(cudaMemcpyAsync(a_->din, in + i * inN, inN * sizeof(float), cudaMemcpyHostToDevice, stream_));
-        run_graph(stream_);
-        copy_out(out + i * outN, cudaMemcpyDeviceToHost, stream_);
+    for (int attempt = 0;; ++attempt) {
+        ensure_plan(h, w);
+        for (int i = 0; i < n; ++i) {
+            HAT_CUDA(cudaMemcpyAsync(a_->din, in + i * inN, inN * sizeof(float), cudaMemcpyHostToDevice, stream_));
+            run_graph(stream_);
+            copy_out(out + i * outN, cudaMemcpyDeviceToHost, stream_);
+        }
+        HAT_CUDA(cudaStreamSynchronize(stream_));
+        const int v = take_device_error();
+        // An operand beyond fp16's range: the whole call again on tf32 pairs (not on a
+        // strip-sharded handle, whose ranks must keep one operand layout in step).
+        if ((v == ERR_RANGE_ATTN || v == ERR_RANGE_GEMM) && h16_ && !comm_ && attempt == 0) {
+            fall_back_to_tf32_pairs();
+            continue;
+        }
+        raise_device_error(v);
+        return;
     }
-    HAT_CUDA(cudaStreamSynchronize(stream_));
-    check_device_error();
 }
 
 }  // namespace hat

@@ -50,6 +50,11 @@ public:
     std::string profile(int h, int w);
     // Reads (and clears) the tensor-core kernels' error flag; throws if it was set.
     void check_device_error();
+    // Waits for the work enqueued on the engine's stream and reports a device error.
+    void sync();
+    // fp16 operand pairs (kind::f16) in use; false once a pass fell back to tf32 pairs.
+    bool fp16_pairs() const { return h16_; }
+    int fallbacks() const { return fallbacks_; }
     // Strip sharding: from now on every pass computes only this rank's window-aligned
     // row strip of the image (Plan::make_strip), exchanging halo rows with the
     // neighbouring ranks over NCCL; `id` is the communicator's unique id (the same on
@@ -60,6 +65,9 @@ public:
 private:
     struct Acts;
     Plan plan_for(int h, int w) const;
+    void upload_weights();
+    int take_device_error();  // the error word's value (cleared on the device)
+    void fall_back_to_tf32_pairs();
     void ensure_plan(int h, int w);
     // Strip mode: fill `n` halo rows on each side of `plane` (`ch` channels, at `res`
     // times the base resolution) from the neighbours' own rows; top and bottom ranks
@@ -105,6 +113,7 @@ private:
     // plane's channel stride in elements (16 or a multiple of 8 as fp16; the buffer's
     // own stride as tf32 pairs or fp32).
     bool h16_ = false;
+    int fallbacks_ = 0;
     int cmid_ld_ = 0;
     int device_ = 0, mode_ = 0;
     std::unique_ptr<Comm> comm_;

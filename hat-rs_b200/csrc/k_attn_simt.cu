@@ -129,14 +129,7 @@ static void run_attn(const float* qkv, const float* table, Dst out, const Plan& 
     constexpr int NK = OCA ? 576 : 256;
     constexpr int TROWS = OCA ? 39 * 39 : 31 * 31;
     size_t smem = (2 * NK * DP + TROWS) * sizeof(float);
-    static unsigned configured = 0;  // one bit per device ordinal
-    int dev = 0;
-    HAT_CUDA(cudaGetDevice(&dev));
-    if (!(configured & (1u << dev))) {
-        HAT_CUDA(cudaFuncSetAttribute(k_attn_simt<D, OCA>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)smem));
-        configured |= 1u << dev;
-    }
+    allow_dyn_smem(k_attn_simt<D, OCA>, smem);
     dim3 grid(p.nw(), heads);
     k_attn_simt<D, OCA><<<grid, 256, smem, st>>>(qkv, table, out, p.hp, p.wp, c, heads, shift,
                                                  1.f / sqrtf((float)D));

@@ -530,7 +530,7 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
                         *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(out.hi) + ob + i) = h;
                         *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(out.lo) + ob + i) = lo;
                     }
-                    if (big && out.err) atomicCAS(out.err, 0, 21);
+                    if (big && out.err) atomicCAS(out.err, 0, ERR_RANGE_GEMM);
                 } else if (VW == 4) {
 #pragma unroll
                     for (int i = 0; i < D; i += 4)
@@ -824,7 +824,7 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
             if (!ok) break;
             g += NBLK;
         }
-        if (!range_ok) atomicCAS(err, 0, 20);
+        if (!range_ok) atomicCAS(err, 0, ERR_RANGE_ATTN);
     }
 
     tcf_before();
@@ -843,14 +843,7 @@ static void run_tc(const float* qkv, const float* table, Dst out, const Plan& p,
     constexpr int TR = OCA ? 39 : 31;
     constexpr size_t bytes =
         2 * KH * 4096 + KVS * (2 * KH * 1024 + 2 * 2048) + TR * TSTRIDE * 4 + (OCA ? 576 * 4 : 0) + 1024;
-    static unsigned configured = 0;
-    int dev = 0;
-    HAT_CUDA(cudaGetDevice(&dev));
-    if (!(configured & (1u << dev))) {
-        HAT_CUDA(cudaFuncSetAttribute(k_attn_tc<D, OCA, TERMS, PRE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)bytes));
-        configured |= 1u << dev;
-    }
+    allow_dyn_smem(k_attn_tc<D, OCA, TERMS, PRE>, bytes);
     // The windows of this launch (see AttnGeom).
     AttnGeom gm;
     gm.rows = p.rows;
@@ -878,7 +871,8 @@ static void run_tc(const float* qkv, const float* table, Dst out, const Plan& p,
         gm.yr0 = ((p.r0 - 2 * shift) % p.hp + p.hp) % p.hp;
     }
     const long items = (long)gm.nwy * p.nx() * heads * 2;
-    int sms = 0;
+    int sms = 0, dev = 0;
+    HAT_CUDA(cudaGetDevice(&dev));
     HAT_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     // AttnShape::ctas CTAs per SM; a multiple of the head count, so every CTA keeps one head
     // (and one bias table).

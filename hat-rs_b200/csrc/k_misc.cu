@@ -82,7 +82,7 @@ __global__ void k_tapsum_gelu(const float* __restrict__ taps, int ldt, const flo
             }
             split_h16x2(v2[0], v2[1], hw[i], lw[i]);
         }
-        if (big && out.err) atomicCAS(out.err, 0, 21);
+        if (big && out.err) atomicCAS(out.err, 0, ERR_RANGE_GEMM);
         uint4* dh = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(out.hi) + p * ldo);
         uint4* dl = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(out.lo) + p * ldo);
 #pragma unroll
@@ -339,7 +339,7 @@ __global__ void __launch_bounds__(256) k_layernorm_bulk(const float* __restrict_
             asm volatile("cp.async.bulk.commit_group;" ::: "memory");
         }
     }
-    if (big && y.err) atomicCAS(y.err, 0, 21);
+    if (big && y.err) atomicCAS(y.err, 0, ERR_RANGE_GEMM);
     if (threadIdx.x == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
@@ -349,14 +349,10 @@ void launch_layernorm(const float* x, const float* g, const float* b, Dst y, lon
     if (y.lo && y.h16 && err && c % 8 == 0 && c <= 144 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
         (reinterpret_cast<uintptr_t>(y.hi) & 15) == 0 && (reinterpret_cast<uintptr_t>(y.lo) & 15) == 0) {
         const size_t smem = (size_t)LN_TOK * c * (2 * 4 + 2 * 2);
-        static unsigned configured = 0;
         int dev = 0, sms = 0;
         HAT_CUDA(cudaGetDevice(&dev));
         HAT_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-        if (!(configured & (1u << dev))) {
-            HAT_CUDA(cudaFuncSetAttribute(k_layernorm_bulk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-            configured |= 1u << dev;
-        }
+        allow_dyn_smem(k_layernorm_bulk, smem);
         const long ntiles = (m + LN_TOK - 1) / LN_TOK;
         const long grid = std::min<long>(ntiles, 4L * sms);  // four 55 KB CTAs per SM
         k_layernorm_bulk<<<(unsigned)grid, 256, smem, st>>>(x, g, b, y, m, c, err);

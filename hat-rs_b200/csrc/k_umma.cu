@@ -328,7 +328,7 @@ __device__ __forceinline__ void epi_chunk16(const UmmaArgs& g, const Epi& e, uin
             v[j] = (v[j] * g.ascale + bv[j]) * qs;
             big |= beyond_h16(v[j]);
         }
-        if (big) atomicCAS(g.err, 0, 21);
+        if (big) atomicCAS(g.err, 0, ERR_RANGE_GEMM);
         const int row0 = (int)(mt * 128 + q * 32);
         const int c2 = 2 * (g.N / 3);  // q|k columns
         __half* th = reinterpret_cast<__half*>(&stg[0][0]);
@@ -1463,19 +1463,17 @@ static size_t ring_smem(const UmmaArgs& g, const Epi& e) {
 
 // The dynamic shared memory a k_umma instantiation may take: the 227 KB a CTA can have,
 // less its static shared memory (staging tiles and channel sums vary with the kind).
+// The static size is a property of the compiled kernel (the same on every device), so it
+// is read once; the shared-memory allowance is set on the current device at every call.
 template <int MODE, int TERMS, int EK, bool H16>
 static long umma_smem_cap() {
-    static long cap[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    int dev = 0;
-    HAT_CUDA(cudaGetDevice(&dev));
-    if (!cap[dev & 7]) {
+    static const long cap = [] {
         cudaFuncAttributes fa;
         HAT_CUDA(cudaFuncGetAttributes(&fa, k_umma<MODE, TERMS, EK, H16>));
-        cap[dev & 7] = 232448 - (long)fa.sharedSizeBytes;
-        HAT_CUDA(cudaFuncSetAttribute(k_umma<MODE, TERMS, EK, H16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)cap[dev & 7]));
-    }
-    return cap[dev & 7];
+        return 232448 - (long)fa.sharedSizeBytes;
+    }();
+    allow_dyn_smem(k_umma<MODE, TERMS, EK, H16>, (size_t)cap);
+    return cap;
 }
 
 template <int MODE, int TERMS, int EK, bool H16>
@@ -1789,9 +1787,6 @@ long umma_mlp(int mode, Opnd x, const GemmW& w1, const float* b1, const GemmW& w
         u.tma_st = sk != EK_STORE;
         skx = sk == EK_TMA ? 1 : sk == EK_TMA_RES ? 2 : 0;
     }
-    static unsigned configured[12] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
-    int dev = 0;
-    HAT_CUDA(cudaGetDevice(&dev));
     const int which = (h16 ? 2 : three ? 0 : 1) * 4 + skx;
     using KFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, MlpArgs, Epi,
                          CUtensorMap, CUtensorMap);
@@ -1799,10 +1794,7 @@ long umma_mlp(int mode, Opnd x, const GemmW& w1, const float* b1, const GemmW& w
                            k_mlp<1, false, 0>, k_mlp<1, false, 1>, k_mlp<1, false, 2>, k_mlp<1, false, MLP_RT>,
                            k_mlp<3, true, 0>,  k_mlp<3, true, 1>,  k_mlp<3, true, 2>,  k_mlp<3, true, MLP_RT>};
     const KFn kern = table[which];
-    if (!(configured[which] & (1u << dev))) {
-        HAT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_CAP));
-        configured[which] |= 1u << dev;
-    }
+    allow_dyn_smem(kern, (size_t)SMEM_CAP);
     const long grid = std::min<long>(g.mtiles, num_sms());
     const int nt = 64 + 32 * mlp_epi_warps(h16, skx == 3 ? MLP_RT : skx);
     kern<<<(unsigned)grid, nt, smem, st>>>(tah, tal, t1h, t1l, t2h, t2l, g, e, ty, tr);

@@ -16,7 +16,6 @@
 // nothing else needs to start at zero.
 #include <cstdio>
 #include <cstring>
-#include <mutex>
 #include <string>
 
 #include "../../include/hat_b200.h"
@@ -30,28 +29,19 @@ static __device__ __align__(256) float g_noalloc_scratch[NOALLOC_FLOATS];
 
 namespace {
 
-constexpr int MAX_DEVICES = 64;
-std::mutex g_scratch_mu;
-float* g_scratch_addr[MAX_DEVICES] = {};
-
 size_t round64(size_t n) { return (n + 63) / 64 * 64; }
 
-// The scratch array's address on the current device, looked up once per device (with
-// that device current, as cudaGetSymbolAddress requires).
+// The scratch array's address on the current device. In host code `g_noalloc_scratch`
+// names a host-side stand-in, not device memory, so the device address is looked up with
+// that device current. The lookup is repeated on every call rather than cached: a
+// cudaDeviceReset or another context on the same ordinal loads the module again, and the
+// array can then sit at a different address.
 float* scratch_on_current_device() {
-    int dev = 0;
-    HAT_CUDA(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= MAX_DEVICES) throw Error(1, "hat_b200_linear_noalloc: device ordinal out of range");
-    std::lock_guard<std::mutex> lk(g_scratch_mu);
-    if (!g_scratch_addr[dev]) {
-        void* p = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e != cudaSuccess || !p)
-            throw Error(3, std::string("hat_b200_linear_noalloc: cudaGetSymbolAddress failed: ") +
-                               cudaGetErrorString(e));
-        g_scratch_addr[dev] = static_cast<float*>(p);
-    }
-    return g_scratch_addr[dev];
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+        throw Error(3, std::string("hat_b200_linear_noalloc: cudaGetSymbolAddress failed: ") + cudaGetErrorString(e));
+    return static_cast<float*>(p);
 }
 
 void set_msg(char* err, size_t errlen, const std::string& m) {

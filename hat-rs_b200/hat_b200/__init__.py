@@ -81,6 +81,8 @@ SIGNATURES = {
     "hat_b200_attach_strip": (_I, [_P, _I, _I, _P, _S, _C, _S]),
     "hat_b200_launch_count": (ctypes.c_uint64, [_P]),
     "hat_b200_profile": (_I, [_P, _I, _I, _C, _S, _C, _S]),
+    "hat_b200_sync": (_I, [_P, _C, _S]),
+    "hat_b200_fp16_pairs": (_I, [_P]),
 }
 
 _lib = None
@@ -213,6 +215,15 @@ class B200:
         call it with the same NCCL unique id); each pass then writes this rank's rows."""
         e = _err()
         _check(lib().hat_b200_attach_strip(self._h, rank, nranks, uid, len(uid), e, len(e)), e)
+
+    def sync(self) -> None:
+        """Wait for this handle's device work; raise if a kernel flagged an error."""
+        e = _err()
+        _check(lib().hat_b200_sync(self._h, e, len(e)), e)
+
+    def fp16_pairs(self) -> bool:
+        """Parity-mode operands are fp16 pairs (False: tf32 pairs, or another mode)."""
+        return bool(lib().hat_b200_fp16_pairs(self._h))
 
     def footprint_bytes(self, h: int, w: int) -> int:
         return int(lib().hat_b200_footprint_bytes(self._h, h, w))

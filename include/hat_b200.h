@@ -37,9 +37,13 @@ extern "C" {
 #define HAT_B200_ENOMEM 4   /* the memory guard refused the pass (src/memguard.rs:183-201) */
 #define HAT_B200_ESELFTEST 5
 
-/* Arithmetic mode. PARITY: fp32-accurate (3xTF32 split on the tensor cores, fp32
- * everywhere else); matches the reference's fp32 output to <= 1e-4. FAST: single
- * TF32 products on the tensor cores. */
+/* Arithmetic mode. PARITY: fp32-accurate; every tensor-core operand is a hi/lo pair
+ * carrying 22 significant bits and each product is three MMAs (hi*hi + hi*lo + lo*hi)
+ * with fp32 accumulation, fp32 everywhere else; matches the reference's fp32 output to
+ * <= 1e-4. The pairs are fp16 (kind::f16) when the embedding width is a multiple of 8,
+ * else tf32 (kind::tf32); fp16 pairs cannot hold |x| >= 65504, and a pass that meets
+ * such an operand is redone on tf32 pairs (see hat_b200_forward). FAST: single TF32
+ * products on the tensor cores. */
 #define HAT_B200_MODE_PARITY 0
 #define HAT_B200_MODE_FAST 1
 /* Kernel-level calls only: the CUDA-core fp32 kernels (the on-device cross-check). */
@@ -78,14 +82,29 @@ HAT_B200_API int hat_b200_get_info(const hat_b200* h, hat_b200_info* out);
  * [n][3][height*scale][width*scale] on the host after denormalisation. Pads to a
  * window multiple by edge replication (src/backend.rs:71-89) and crops after
  * (src/backend.rs:94-109). n = 1 is the reference's contract; n > 1 runs the images
- * back to back on this device. Blocks until `out` is written. */
+ * back to back on this device. Blocks until `out` is written.
+ * In parity mode with fp16 operand pairs, if any operand of the pass reaches fp16's
+ * range (|x| >= 65504) the whole call is redone with tf32 operand pairs and the handle
+ * keeps them for later calls (hat_b200_fp16_pairs then returns 0); a strip-sharded
+ * handle returns HAT_B200_ECUDA instead. */
 HAT_B200_API int hat_b200_forward(hat_b200* h, int n, int height, int width, const float* in, float* out,
                      char* err, size_t errlen);
 
 /* The same pass with `in`/`out` already in this device's memory, enqueued on `stream`
- * (a cudaStream_t, or NULL for the handle's own stream). Returns once enqueued. */
+ * (a cudaStream_t, or NULL for the handle's own stream). Returns once enqueued; errors
+ * the kernels find on the device (an expired wait, an operand beyond fp16's range; no
+ * retry here) are reported by the next hat_b200_sync or hat_b200_forward. */
 HAT_B200_API int hat_b200_forward_device(hat_b200* h, int n, int height, int width, const float* d_in,
                             float* d_out, void* stream, char* err, size_t errlen);
+
+/* Waits for the work this handle enqueued and returns HAT_B200_ECUDA with a message if a
+ * kernel flagged an error since the last check (the reference's synchronous download
+ * at the end of Gpu::forward, src/gpu.rs:799-802, is where its errors surface). */
+HAT_B200_API int hat_b200_sync(hat_b200* h, char* err, size_t errlen);
+
+/* 1 while the handle's parity-mode operands are fp16 pairs, 0 for tf32 pairs (always
+ * for widths that are not a multiple of 8, and after a fallback) or another mode. */
+HAT_B200_API int hat_b200_fp16_pairs(const hat_b200* h);
 
 /* gpu::footprint_floats (src/gpu.rs:288-290) as bytes: the device bytes a pass at
  * this size allocates, computed without touching the device. */
@@ -198,8 +217,9 @@ HAT_B200_API int hat_b200_attach_strip(hat_b200* h, int rank, int nranks, const 
  * n and k rounded up to the tile sizes. The error word is zeroed by each call before its
  * first launch; everything else is rewritten before it is read.
  *
- * The first call on each device looks up the array's address (cudaGetSymbolAddress, with
- * that device current); make that first call before any stream capture begins on it.
+ * Each call looks up the array's address on the current device (cudaGetSymbolAddress,
+ * which allocates nothing). The first call on a device also loads the library's device
+ * code there; make that first call before any stream capture begins on the device.
  * Calls share the array: two calls in flight at once on the same device (from different
  * host threads) race on it and give wrong results, so serialise them. The call blocks
  * until its result is in `y`. Arguments otherwise as hat_b200_linear. */

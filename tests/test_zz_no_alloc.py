@@ -49,3 +49,26 @@ def test_noalloc_refuses_beyond_scratch(torch_cuda):
         hat_b200.linear_noalloc(hat_b200.MODE_PARITY, x.data_ptr(), w.data_ptr(), 0, y.data_ptr(), m, n, k)
     assert ei.value.code == 1
     assert "limit" in str(ei.value)
+
+
+def test_noalloc_leaves_free_device_memory_unchanged(torch_cuda):
+    """The property the entry point exists for: after a first call (which may load the
+    library's device code on this GPU), further calls change neither the device's free
+    memory nor torch's allocator."""
+    torch = torch_cuda
+    m, n, k = 1000, 432, 144
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn(m, k, device="cuda", generator=g)
+    w = torch.randn(n, k, device="cuda", generator=g) * 0.05
+    b = torch.randn(n, device="cuda", generator=g)
+    y = torch.empty(m, n, device="cuda")
+    hat_b200.linear_noalloc(hat_b200.MODE_PARITY, x.data_ptr(), w.data_ptr(), b.data_ptr(), y.data_ptr(), m, n, k)
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    alloc0 = torch.cuda.memory_reserved()
+    for mode in (hat_b200.MODE_PARITY, hat_b200.MODE_FAST, hat_b200.MODE_SIMT):
+        hat_b200.linear_noalloc(mode, x.data_ptr(), w.data_ptr(), b.data_ptr(), y.data_ptr(), m, n, k)
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0, (free0, free1)
+    assert torch.cuda.memory_reserved() == alloc0
