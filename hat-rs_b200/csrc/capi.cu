@@ -2,8 +2,11 @@
 // engine and the kernel launchers.
 #include <cstdarg>
 #include <cstring>
+#include <exception>
 #include <memory>
 #include <string>
+#include <thread>
+#include <vector>
 
 #include "../../include/hat_b200.h"
 #include "engine.h"
@@ -12,9 +15,46 @@
 
 using namespace hat;
 
+// One engine per GPU. A one-GPU handle is engs[0] alone; a handle over several GPUs runs
+// each call's share on every engine from a host thread of its own.
 struct hat_b200 {
-    std::unique_ptr<Engine> eng;
+    std::vector<std::unique_ptr<Engine>> engs;
+    int shard = HAT_B200_SHARD_BATCH;
+    Engine& e0() const { return *engs[0]; }
+    bool multi() const { return engs.size() > 1; }
 };
+
+// Runs f(g) for every GPU g on its own thread and rethrows the first failure, naming the GPU.
+template <class F>
+static void on_every_gpu(const hat_b200* h, F&& f) {
+    const size_t G = h->engs.size();
+    if (G == 1) {
+        f(0);
+        return;
+    }
+    std::vector<std::exception_ptr> errs(G);
+    std::vector<std::thread> ts;
+    ts.reserve(G);
+    for (size_t g = 0; g < G; ++g)
+        ts.emplace_back([&, g] {
+            try {
+                f((int)g);
+            } catch (...) {
+                errs[g] = std::current_exception();
+            }
+        });
+    for (auto& t : ts) t.join();
+    for (size_t g = 0; g < G; ++g) {
+        if (!errs[g]) continue;
+        try {
+            std::rethrow_exception(errs[g]);
+        } catch (const Error& e) {
+            throw Error(e.code, "gpu " + std::to_string(h->engs[g]->device()) + ": " + e.what());
+        } catch (const std::exception& e) {
+            throw Error(HAT_B200_EINVAL, "gpu " + std::to_string(h->engs[g]->device()) + ": " + e.what());
+        }
+    }
+}
 
 static void set_err(char* err, size_t errlen, const std::string& msg) {
     if (!err || errlen == 0) return;
@@ -66,17 +106,36 @@ int hat_b200_create(const char* path, const hat_b200_opts* opts, hat_b200** out,
         return HAT_B200_EINVAL;
     }
     *out = nullptr;
-    hat_b200_opts o{0, HAT_B200_MODE_PARITY, 1, 0};
+    hat_b200_opts o;
+    memset(&o, 0, sizeof o);
+    o.mode = HAT_B200_MODE_PARITY;
+    o.use_graph = 1;
     if (opts) o = *opts;
     return guarded(err, errlen, [&] {
-        auto* h = new hat_b200;
-        try {
-            h->eng.reset(new Engine(path, o.device, o.mode, o.use_graph != 0, o.simt_only != 0));
-        } catch (...) {
-            delete h;
-            throw;
+        const int G = o.ngpus > 1 ? o.ngpus : 1;
+        if (G > 1 && o.shard != HAT_B200_SHARD_BATCH && o.shard != HAT_B200_SHARD_STRIP)
+            throw Error(1, "hat_b200_create: unknown shard mode " + std::to_string(o.shard));
+        std::vector<int> devs(G);
+        for (int g = 0; g < G; ++g) devs[g] = o.devices ? o.devices[g] : o.device + g;
+        for (int g = 0; g < G; ++g)
+            for (int k = 0; k < g; ++k)
+                if (devs[g] == devs[k])
+                    throw Error(1, "hat_b200_create: device " + std::to_string(devs[g]) + " is listed twice");
+        std::unique_ptr<hat_b200> h(new hat_b200);
+        h->shard = G > 1 ? o.shard : HAT_B200_SHARD_BATCH;
+        h->engs.resize(G);
+        // Weights are read and uploaded on every GPU at once.
+        on_every_gpu(h.get(), [&](int g) {
+            h->engs[g].reset(new Engine(path, devs[g], o.mode, o.use_graph != 0, o.simt_only != 0));
+            h->engs[g]->set_timeout(o.timeout_ms > 0 ? o.timeout_ms / 1000.0 : 120.0);
+        });
+        if (G > 1 && h->shard == HAT_B200_SHARD_STRIP) {
+            // One communicator over the handle's GPUs; each rank joins from its own thread.
+            unsigned char id[128];
+            nccl_unique_id(id, sizeof id);
+            on_every_gpu(h.get(), [&](int g) { h->engs[g]->attach_strip(g, G, id, sizeof id); });
         }
-        *out = h;
+        *out = h.release();
     });
 }
 
@@ -84,9 +143,11 @@ void hat_b200_destroy(hat_b200* h) { delete h; }
 
 int hat_b200_get_info(const hat_b200* h, hat_b200_info* out) {
     if (!h || !out) return HAT_B200_EINVAL;
-    fill_info(h->eng->weights(), out);
+    fill_info(h->e0().weights(), out);
     return HAT_B200_OK;
 }
+
+int hat_b200_gpu_count(const hat_b200* h) { return h ? (int)h->engs.size() : 0; }
 
 // Checkpoint inspection without a device: what --list-weights and the loader tests use.
 int hat_b200_inspect(const char* path, hat_b200_info* out, char* err, size_t errlen) {
@@ -103,7 +164,26 @@ int hat_b200_forward(hat_b200* h, int n, int height, int width, const float* in,
         set_err(err, errlen, "hat_b200_forward: null handle or buffer");
         return HAT_B200_EINVAL;
     }
-    return guarded(err, errlen, [&] { h->eng->forward_host(n, height, width, in, out); });
+    return guarded(err, errlen, [&] {
+        if (!h->multi()) {
+            h->e0().forward_host(n, height, width, in, out);
+            return;
+        }
+        if (n <= 0 || height <= 0 || width <= 0) throw Error(1, "hat_b200_forward: empty batch or image");
+        if (h->shard == HAT_B200_SHARD_STRIP) {
+            // Every GPU reads the whole images and writes its own rows of every output.
+            on_every_gpu(h, [&](int g) { h->engs[g]->forward_host(n, height, width, in, out); });
+            return;
+        }
+        // Batch: GPU g takes images [n*g/G, n*(g+1)/G).
+        const int G = (int)h->engs.size();
+        const int s = h->e0().weights().scale;
+        const long inN = 3L * height * width, outN = 3L * height * s * width * s;
+        on_every_gpu(h, [&](int g) {
+            const int a = (int)((long)n * g / G), b = (int)((long)n * (g + 1) / G);
+            if (b > a) h->engs[g]->forward_host(b - a, height, width, in + a * inN, out + a * outN);
+        });
+    });
 }
 
 int hat_b200_forward_device(hat_b200* h, int n, int height, int width, const float* d_in, float* d_out,
@@ -113,7 +193,8 @@ int hat_b200_forward_device(hat_b200* h, int n, int height, int width, const flo
         return HAT_B200_EINVAL;
     }
     return guarded(err, errlen, [&] {
-        h->eng->forward_device(n, height, width, d_in, d_out, (cudaStream_t)stream);
+        if (h->multi()) throw Error(1, "hat_b200_forward_device: the handle drives several GPUs; use hat_b200_forward");
+        h->e0().forward_device(n, height, width, d_in, d_out, (cudaStream_t)stream);
     });
 }
 
@@ -122,19 +203,21 @@ int hat_b200_sync(hat_b200* h, char* err, size_t errlen) {
         set_err(err, errlen, "hat_b200_sync: null handle");
         return HAT_B200_EINVAL;
     }
-    return guarded(err, errlen, [&] { h->eng->sync(); });
+    return guarded(err, errlen, [&] { on_every_gpu(h, [&](int g) { h->engs[g]->sync(); }); });
 }
 
-int hat_b200_fp16_pairs(const hat_b200* h) { return h && h->eng->fp16_pairs() ? 1 : 0; }
+int hat_b200_fp16_pairs(const hat_b200* h) { return h && h->e0().fp16_pairs() ? 1 : 0; }
 
 size_t hat_b200_footprint_bytes(const hat_b200* h, int height, int width) {
     if (!h || height <= 0 || width <= 0) return 0;
-    return h->eng->footprint_bytes(height, width);
+    return h->e0().footprint_bytes(height, width);
 }
 
 int hat_b200_check_memory(const hat_b200* h, int height, int width, char* err, size_t errlen) {
     if (!h) return HAT_B200_EINVAL;
-    return guarded(err, errlen, [&] { h->eng->check_memory(height, width); });
+    return guarded(err, errlen, [&] {
+        for (auto& e : h->engs) e->check_memory(height, width);
+    });
 }
 
 int hat_b200_free_vram(int device, size_t* free_bytes, size_t* total_bytes) {
@@ -161,13 +244,21 @@ int hat_b200_probe(void) {
     return p.major == 10 ? 1 : 0;
 }
 
-uint64_t hat_b200_launch_count(const hat_b200* h) { return h ? h->eng->launches() : 0; }
+uint64_t hat_b200_launch_count(const hat_b200* h) {
+    uint64_t n = 0;
+    if (h)
+        for (auto& e : h->engs) n += e->launches();
+    return n;
+}
 
 int hat_b200_profile(hat_b200* h, int height, int width, char* json, size_t jsonlen, char* err, size_t errlen) {
     if (!h) return HAT_B200_EINVAL;
     return guarded(err, errlen, [&] {
-        std::string j = h->eng->profile(height, width);
-        set_err(json, jsonlen, j);
+        // Every GPU runs the profiled pass (a strip-sharded pass has collectives); the
+        // first GPU's timings are reported.
+        std::vector<std::string> js(h->engs.size());
+        on_every_gpu(h, [&](int g) { js[g] = h->engs[g]->profile(height, width); });
+        set_err(json, jsonlen, js[0]);
     });
 }
 
@@ -178,8 +269,8 @@ int hat_b200_forward_tiled(hat_b200* h, int height, int width, const float* in, 
         return HAT_B200_EINVAL;
     }
     return guarded(err, errlen, [&] {
-        if (h->eng->sharded()) throw Error(1, "tiling: the handle is strip-sharded");
-        Tiling t = tile_forward(*h->eng, height, width, in, out, tile, margin);
+        if (h->multi() || h->e0().sharded()) throw Error(1, "tiling: the handle is strip-sharded or drives several GPUs");
+        Tiling t = tile_forward(h->e0(), height, width, in, out, tile, margin);
         if (info) {
             info->tile = t.tile;
             info->margin = t.margin;
@@ -203,7 +294,7 @@ int hat_b200_auto_tile(int height, int width, int window, uint64_t budget_bytes,
 int hat_b200_gpu_auto_tile(const hat_b200* h, int height, int width, int* tile, char* err, size_t errlen) {
     if (!h || !tile) return HAT_B200_EINVAL;
     return guarded(err, errlen, [&] {
-        auto t = gpu_auto_tile(*h->eng, height, width);
+        auto t = gpu_auto_tile(h->e0(), height, width);
         if (!t) throw Error(4, "one window does not fit the device's free memory");
         *tile = *t;
     });
@@ -225,7 +316,10 @@ int hat_b200_nccl_unique_id(void* id, size_t idlen, char* err, size_t errlen) {
 int hat_b200_attach_strip(hat_b200* h, int rank, int nranks, const void* id, size_t idlen, char* err,
                           size_t errlen) {
     if (!h) return HAT_B200_EINVAL;
-    return guarded(err, errlen, [&] { h->eng->attach_strip(rank, nranks, id, idlen); });
+    return guarded(err, errlen, [&] {
+        if (h->multi()) throw Error(1, "hat_b200_attach_strip: the handle already drives several GPUs");
+        h->e0().attach_strip(rank, nranks, id, idlen);
+    });
 }
 
 // The GEMM operand of one kernel-level call, prepared on the caller's stream.

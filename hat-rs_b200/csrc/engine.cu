@@ -436,8 +436,15 @@ void Engine::check_device_error() { raise_device_error(take_device_error()); }
 
 void Engine::sync() {
     HAT_CUDA(cudaSetDevice(device_));
-    HAT_CUDA(cudaStreamSynchronize(stream_));
+    wait_stream();
     check_device_error();
+}
+
+void Engine::wait_stream() {
+    if (comm_)
+        comm_->wait(stream_, timeout_s_);
+    else
+        HAT_CUDA(cudaStreamSynchronize(stream_));
 }
 
 // fp16 operand pairs carry 22 significant bits but only fp16's exponent range; a value of
@@ -467,11 +474,11 @@ void Engine::ensure_plan(int h, int w) {
     }
     if (arena_ && (size_t)s.total() <= arena_floats_) {
         // A plan no larger than the arena (a smaller tile, say) is carved out of it.
-        HAT_CUDA(cudaStreamSynchronize(stream_));
+        wait_stream();
     } else {
         check_memory(h, w);
         if (arena_) {
-            HAT_CUDA(cudaStreamSynchronize(stream_));
+            wait_stream();
             cudaFree(arena_);
             arena_ = nullptr;
             arena_floats_ = 0;
@@ -763,7 +770,7 @@ std::string Engine::profile(int h, int w) {
     }
     profiling_ = false;
     g_launch_counter = prev;
-    HAT_CUDA(cudaStreamSynchronize(stream_));
+    wait_stream();
     struct Agg {
         int n = 0;
         double ms = 0, flops = 0, bytes = 0;
@@ -866,7 +873,7 @@ void Engine::forward_host(int n, int h, int w, const float* in, float* out) {
             run_graph(stream_);
             copy_out(out + i * outN, cudaMemcpyDeviceToHost, stream_);
         }
-        HAT_CUDA(cudaStreamSynchronize(stream_));
+        wait_stream();
         const int v = take_device_error();
         // An operand beyond fp16's range: the whole call again on tf32 pairs (not on a
         // strip-sharded handle, whose ranks must keep one operand layout in step).

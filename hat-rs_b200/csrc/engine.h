@@ -61,6 +61,9 @@ public:
     // every rank). The output rows of the other ranks are not written.
     void attach_strip(int rank, int n, const void* id, size_t idlen);
     bool sharded() const { return comm_ != nullptr; }
+    // Deadline of a sharded call's device work (seconds; <= 0: none): past it the
+    // communicator is aborted and the call fails instead of blocking (see Comm::wait).
+    void set_timeout(double s) { timeout_s_ = s; }
 
 private:
     struct Acts;
@@ -68,6 +71,8 @@ private:
     void upload_weights();
     int take_device_error();  // the error word's value (cleared on the device)
     void fall_back_to_tf32_pairs();
+    // Waits for the engine's stream: plainly, or with the communicator's deadline when sharded.
+    void wait_stream();
     void ensure_plan(int h, int w);
     // Strip mode: fill `n` halo rows on each side of `plane` (`ch` channels, at `res`
     // times the base resolution) from the neighbours' own rows; top and bottom ranks
@@ -117,6 +122,7 @@ private:
     int cmid_ld_ = 0;
     int device_ = 0, mode_ = 0;
     std::unique_ptr<Comm> comm_;
+    double timeout_s_ = 120.0;
     bool use_graph_ = true, simt_only_ = false;
     cudaStream_t stream_ = nullptr;
     cudaEvent_t join_ = nullptr;

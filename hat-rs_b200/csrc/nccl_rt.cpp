@@ -7,6 +7,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "deadline.h"
 
 #ifndef HAT_NCCL_LIB
 #define HAT_NCCL_LIB "libnccl.so.2"
@@ -27,6 +28,8 @@ struct Api {
     ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                                cudaStream_t) = nullptr;
     const char* (*error_string)(ncclResult_t) = nullptr;
+    ncclResult_t (*get_async_error)(ncclComm_t, ncclResult_t*) = nullptr;
+    ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
 };
 
 template <class F>
@@ -59,6 +62,8 @@ const Api& api() {
             bind(lib, "ncclRecv", a.recv);
             bind(lib, "ncclAllReduce", a.all_reduce);
             bind(lib, "ncclGetErrorString", a.error_string);
+            bind(lib, "ncclCommGetAsyncError", a.get_async_error);
+            bind(lib, "ncclCommAbort", a.comm_abort);
         } catch (const Error& e) {
             failure = e.what();
         }
@@ -90,22 +95,75 @@ Comm::Comm(int rank, int n, const void* id, size_t idlen, int device) : rank_(ra
 }
 
 Comm::~Comm() {
-    if (comm_) api().comm_destroy(comm_);
+    // An aborted communicator has already released its resources.
+    if (comm_ && !aborted_) api().comm_destroy(comm_);
 }
 
-void Comm::group_start() { check(api().group_start(), "ncclGroupStart"); }
+void Comm::live() const {
+    if (aborted_)
+        throw Error(3, "nccl: the communicator was aborted after a failed or timed-out exchange; attach the "
+                       "strips again to continue");
+}
+
+void Comm::group_start() {
+    live();
+    check(api().group_start(), "ncclGroupStart");
+}
 void Comm::group_end() { check(api().group_end(), "ncclGroupEnd"); }
 
 void Comm::send(const float* buf, size_t count, int peer, cudaStream_t st) {
+    live();
     check(api().send(buf, count, ncclFloat32, peer, comm_, st), "ncclSend");
 }
 
 void Comm::recv(float* buf, size_t count, int peer, cudaStream_t st) {
+    live();
     check(api().recv(buf, count, ncclFloat32, peer, comm_, st), "ncclRecv");
 }
 
 void Comm::allreduce_sum(float* buf, size_t count, cudaStream_t st) {
+    live();
     check(api().all_reduce(buf, buf, count, ncclFloat32, ncclSum, comm_, st), "ncclAllReduce");
+}
+
+void Comm::wait(cudaStream_t st, double timeout_s) {
+    live();
+    ncclResult_t async = ncclSuccess;
+    cudaError_t serr = cudaSuccess;
+    const WaitEnd end = wait_with_deadline(
+        [&] {
+            serr = cudaStreamQuery(st);
+            if (serr == cudaSuccess) return 1;
+            if (serr == cudaErrorNotReady) return 0;
+            return -1;
+        },
+        [&] {
+            const ncclResult_t r = api().get_async_error(comm_, &async);
+            if (r != ncclSuccess) async = r;
+            return async != ncclSuccess && async != ncclInProgress;
+        },
+        [&] {
+            api().comm_abort(comm_);
+            aborted_ = true;
+        },
+        timeout_s);
+    switch (end) {
+        case WaitEnd::Done:
+            return;
+        case WaitEnd::StreamError:
+            throw Error(3, std::string("gpu: the strip pass failed on the device: ") + cudaGetErrorString(serr));
+        case WaitEnd::PeerError:
+            throw Error(3, std::string("nccl: rank ") + std::to_string(rank_) + " of " + std::to_string(n_) +
+                               ": the communicator reported an asynchronous error (" + api().error_string(async) +
+                               "); a peer rank failed or left, and the communicator was aborted");
+        case WaitEnd::TimedOut:
+            break;
+    }
+    char buf[64];
+    snprintf(buf, sizeof buf, "%.1f", timeout_s);
+    throw Error(3, std::string("nccl: rank ") + std::to_string(rank_) + " of " + std::to_string(n_) +
+                       ": the strip pass did not finish within " + buf +
+                       " s (a peer rank stopped calling or died); the communicator was aborted");
 }
 
 }  // namespace hat

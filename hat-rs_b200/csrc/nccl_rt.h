@@ -24,10 +24,19 @@ public:
     void send(const float* buf, size_t count, int peer, cudaStream_t st);
     void recv(float* buf, size_t count, int peer, cudaStream_t st);
     void allreduce_sum(float* buf, size_t count, cudaStream_t st);
+    // Waits for the work on `st` (which holds this communicator's calls) for at most
+    // `timeout_s` seconds (<= 0: no deadline), polling the communicator's asynchronous
+    // error state. If a peer failed or the deadline passed, the communicator is aborted
+    // (its pending kernels return) and Error(3) names the cause; an aborted communicator
+    // refuses every later call.
+    void wait(cudaStream_t st, double timeout_s);
+    bool aborted() const { return aborted_; }
 
 private:
+    void live() const;  // throws once aborted
     int rank_, n_;
     ncclComm_t comm_ = nullptr;
+    bool aborted_ = false;
 };
 
 // ncclGetUniqueId into `out` (at least sizeof(ncclUniqueId) = 128 bytes).

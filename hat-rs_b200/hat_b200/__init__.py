@@ -32,9 +32,13 @@ class HatError(RuntimeError):
         self.code = code
 
 
+SHARD_BATCH, SHARD_STRIP = 0, 1
+
+
 class Opts(ctypes.Structure):
     _fields_ = [("device", ctypes.c_int), ("mode", ctypes.c_int), ("use_graph", ctypes.c_int),
-                ("simt_only", ctypes.c_int)]
+                ("simt_only", ctypes.c_int), ("ngpus", ctypes.c_int), ("devices", ctypes.POINTER(ctypes.c_int)),
+                ("shard", ctypes.c_int), ("timeout_ms", ctypes.c_int)]
 
 
 class Info(ctypes.Structure):
@@ -83,6 +87,7 @@ SIGNATURES = {
     "hat_b200_profile": (_I, [_P, _I, _I, _C, _S, _C, _S]),
     "hat_b200_sync": (_I, [_P, _C, _S]),
     "hat_b200_fp16_pairs": (_I, [_P]),
+    "hat_b200_gpu_count": (_I, [_P]),
 }
 
 _lib = None
@@ -146,9 +151,19 @@ class B200:
     """The B200 backend behind the reference's `Backend` contract."""
 
     def __init__(self, path: str, device: int = 0, mode: int = MODE_PARITY, use_graph: bool = True,
-                 simt_only: bool = False):
+                 simt_only: bool = False, devices=None, shard: int = SHARD_BATCH, timeout_ms: int = 0):
+        """`devices`: a list of CUDA ordinals for one handle over several GPUs, whose
+        `forward` splits its work as `shard` says (SHARD_BATCH: the images; SHARD_STRIP:
+        every image's rows, NCCL halo exchange between the GPUs)."""
         self._h = ctypes.c_void_p()
         opts = Opts(device, mode, int(use_graph), int(simt_only))
+        if devices is not None and len(devices) > 1:
+            self._devs = (ctypes.c_int * len(devices))(*devices)
+            opts.ngpus = len(devices)
+            opts.devices = self._devs
+            opts.device = devices[0]
+            opts.shard = shard
+        opts.timeout_ms = timeout_ms
         e = _err()
         _check(lib().hat_b200_create(str(path).encode(), ctypes.byref(opts), ctypes.byref(self._h), e,
                                      len(e)), e)
@@ -220,6 +235,9 @@ class B200:
         """Wait for this handle's device work; raise if a kernel flagged an error."""
         e = _err()
         _check(lib().hat_b200_sync(self._h, e, len(e)), e)
+
+    def gpu_count(self) -> int:
+        return int(lib().hat_b200_gpu_count(self._h))
 
     def fp16_pairs(self) -> bool:
         """Parity-mode operands are fp16 pairs (False: tf32 pairs, or another mode)."""

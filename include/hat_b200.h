@@ -11,8 +11,9 @@
  * errlen > 0). This replaces the reference's `Result<_, String>` (src/backend.rs:29-36).
  *
  * Threading: a handle is not thread-safe (the reference's `&mut self`,
- * src/gpu.rs:751-803). Use one handle per GPU; handles on different devices may be
- * driven from different host threads.
+ * src/gpu.rs:751-803). Use one handle per GPU, driven from any host thread, or one handle
+ * over several GPUs (hat_b200_opts.ngpus), which runs one host thread per GPU inside each
+ * forward call.
  */
 #ifndef HAT_B200_H
 #define HAT_B200_H
@@ -49,13 +50,30 @@ extern "C" {
 /* Kernel-level calls only: the CUDA-core fp32 kernels (the on-device cross-check). */
 #define HAT_B200_MODE_SIMT 2
 
+/* How a handle over several GPUs (hat_b200_opts.ngpus > 1) splits a forward call. BATCH:
+ * the call's images are divided among the GPUs (contiguous, as equal as the count allows),
+ * no communication between them. STRIP: every image is split into window-aligned row
+ * strips, one per GPU, with the halo rows exchanged over NCCL before every layer that
+ * reads across a strip edge and the channel-attention sums added across GPUs; the result
+ * equals the one-GPU pass up to the order of those sums. */
+#define HAT_B200_SHARD_BATCH 0
+#define HAT_B200_SHARD_STRIP 1
+
 typedef struct hat_b200 hat_b200;
 
+/* Zero-initialise and set what is needed; the zero value of every field is its default. */
 typedef struct hat_b200_opts {
-    int device;      /* CUDA device ordinal this handle runs on */
+    int device;      /* CUDA device ordinal this handle runs on (the first one when ngpus > 1) */
     int mode;        /* HAT_B200_MODE_* */
     int use_graph;   /* 1: capture each plan's launch sequence in a CUDA graph */
     int simt_only;   /* 1: CUDA-core fp32 kernels only (debug / cross-check path) */
+    int ngpus;       /* 0 or 1: one GPU. N > 1: this handle drives N GPUs of this process,
+                        one host thread each, and hat_b200_forward splits its work over them */
+    const int* devices; /* the N device ordinals, or NULL for device, device + 1, ... */
+    int shard;       /* HAT_B200_SHARD_*, for ngpus > 1 */
+    int timeout_ms;  /* strip sharding: a call whose device work (which waits on the other
+                        GPUs) has not finished after this long aborts the communicator and
+                        returns HAT_B200_ECUDA instead of blocking; 0 = 120000 */
 } hat_b200_opts;
 
 /* What the checkpoint describes (src/weights.rs:28-57). */
@@ -68,7 +86,10 @@ typedef struct hat_b200_info {
 
 /* Gpu::new(&Weights) (src/gpu.rs:372-386) + Weights::load (src/weights.rs:60-129):
  * read and validate a checkpoint in the tools/convert.py safetensors layout, bring up
- * the device, check the weights fit (src/memguard.rs:211-225) and upload them. */
+ * the device, check the weights fit (src/memguard.rs:211-225) and upload them. With
+ * opts->ngpus > 1 this is done on every listed GPU, and in STRIP mode the GPUs are joined
+ * in an NCCL communicator (no id from the caller). opts may be NULL (one GPU, device 0,
+ * parity mode, CUDA graphs on). */
 HAT_B200_API int hat_b200_create(const char* safetensors_path, const hat_b200_opts* opts,
                     hat_b200** out, char* err, size_t errlen);
 
@@ -86,14 +107,18 @@ HAT_B200_API int hat_b200_get_info(const hat_b200* h, hat_b200_info* out);
  * In parity mode with fp16 operand pairs, if any operand of the pass reaches fp16's
  * range (|x| >= 65504) the whole call is redone with tf32 operand pairs and the handle
  * keeps them for later calls (hat_b200_fp16_pairs then returns 0); a strip-sharded
- * handle returns HAT_B200_ECUDA instead. */
+ * handle returns HAT_B200_ECUDA instead.
+ * On a handle over several GPUs the call is split as opts->shard says and returns once
+ * every GPU's part is on the host; an error on any GPU fails the call (the message names
+ * the GPU). */
 HAT_B200_API int hat_b200_forward(hat_b200* h, int n, int height, int width, const float* in, float* out,
                      char* err, size_t errlen);
 
 /* The same pass with `in`/`out` already in this device's memory, enqueued on `stream`
  * (a cudaStream_t, or NULL for the handle's own stream). Returns once enqueued; errors
  * the kernels find on the device (an expired wait, an operand beyond fp16's range; no
- * retry here) are reported by the next hat_b200_sync or hat_b200_forward. */
+ * retry here) are reported by the next hat_b200_sync or hat_b200_forward. One-GPU
+ * handles only (the buffers live on one device). */
 HAT_B200_API int hat_b200_forward_device(hat_b200* h, int n, int height, int width, const float* d_in,
                             float* d_out, void* stream, char* err, size_t errlen);
 
@@ -235,7 +260,11 @@ HAT_B200_API int hat_b200_linear_noalloc(int mode, const float* x, const float* 
 HAT_B200_API int hat_b200_profile(hat_b200* h, int height, int width, char* json, size_t jsonlen,
                                   char* err, size_t errlen);
 
-/* Kernel launches issued by this handle since creation (src/cuda.rs:542-555). */
+/* The GPUs this handle drives (1 unless created with ngpus > 1). */
+HAT_B200_API int hat_b200_gpu_count(const hat_b200* h);
+
+/* Kernel launches issued by this handle since creation, over all its GPUs
+ * (src/cuda.rs:542-555). */
 HAT_B200_API uint64_t hat_b200_launch_count(const hat_b200* h);
 
 #ifdef __cplusplus

@@ -1,0 +1,152 @@
+"""One handle over several GPUs (hat_b200_opts.ngpus), and a strip rank that stops
+calling. Skipped with fewer than two GPUs.
+
+* BATCH: the call's images divided among the GPUs; every image equals the one-GPU pass
+  bit for bit (the same kernels on the same data).
+* STRIP: every image split into row strips over the GPUs with NCCL halo exchange; equal
+  to the one-GPU pass up to the order of the channel-attention sums, and within the
+  reference's 1e-4 of the fp32 reference (the oracle's torch twin).
+* A rank of a strip-sharded job (one process per GPU) that stops calling between steps:
+  the other rank's next call must come back with an error once its deadline passes,
+  not block; afterwards the GPU still runs a fresh pass. NCCL's NVLS is off in these
+  processes, and the silent rank stays alive (no memory of it goes away under the other
+  rank's kernels).
+"""
+import os
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+import hat_b200
+from hat_b200 import checkpoint, synth
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-4
+
+
+def _n_gpus():
+    import torch
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+needs2 = pytest.mark.skipif(_n_gpus() < 2, reason="needs two GPUs")
+
+
+@pytest.fixture(scope="module")
+def ckdir(tmp_path_factory):
+    return tmp_path_factory.mktemp("ckmulti")
+
+
+def _ck(ckdir, variant, scale, seed, perturb=True):
+    p = ckdir / f"{variant}_{scale}_{seed}.safetensors"
+    if not p.exists():
+        checkpoint.make_checkpoint(str(p), variant, scale, seed, perturb)
+    return str(p)
+
+
+@needs2
+def test_batch_over_two_gpus_equals_one_gpu(ckdir):
+    p = _ck(ckdir, "hat-s", 4, 31)
+    imgs = synth.batch(5, 48, 64, 31)
+    one = hat_b200.B200(p)
+    ref = one.forward_batch(imgs)
+    one.close()
+    two = hat_b200.B200(p, devices=[0, 1], shard=hat_b200.SHARD_BATCH)
+    assert two.gpu_count() == 2
+    got = two.forward_batch(imgs)
+    assert two.launch_count() > 0
+    two.close()
+    assert np.array_equal(got, ref)
+
+
+@needs2
+@pytest.mark.parametrize("variant,scale,h,w", [("hat-s", 4, 512, 512), ("hat-l", 4, 96, 80), ("hat-s", 3, 333, 500)])
+def test_strip_over_two_gpus_one_handle(ckdir, variant, scale, h, w):
+    from oracle import hat_torch as T
+    p = _ck(ckdir, variant, scale, 32)
+    img = synth.image(h, w, 3200 + h)
+    one = hat_b200.B200(p)
+    ref = one.forward(h, w, img)
+    one.close()
+    two = hat_b200.B200(p, devices=[0, 1], shard=hat_b200.SHARD_STRIP, timeout_ms=60000)
+    got = two.forward(h, w, img)
+    again = two.forward(h, w, img)  # the captured graph's replay
+    two.close()
+    assert np.array_equal(got, again)
+    assert float(np.abs(got - ref).max()) <= 2e-5
+    want = T.forward(T.Weights.load(p, "cuda"), img)
+    err = float(np.abs(got - want).max())
+    print(f"{variant} x{scale} {h}x{w} strip2: max {err:.3e} vs fp32")
+    assert err <= TOL
+
+
+def _silent_rank_main(rank, ckpt, img, q_id, q_out, q_done):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    try:
+        import torch
+        torch.cuda.set_device(rank)
+        be = hat_b200.B200(ckpt, device=rank, timeout_ms=3000)
+        if rank == 0:
+            uid = hat_b200.nccl_unique_id()
+            q_id.put(uid)
+        else:
+            uid = q_id.get(timeout=120)
+        be.attach_strip(rank, 2, uid)
+        h, w = img.shape[1:]
+        be.forward(h, w, img)  # one step together
+        if rank == 1:
+            # stops calling: stays alive, issues nothing, until rank 0 has its answer
+            q_out.put((rank, "silent"))
+            q_done.get(timeout=300)
+            os._exit(0)
+        import time
+        t = time.perf_counter()
+        try:
+            be.forward(h, w, img)
+            q_out.put((rank, "no error"))
+            return
+        except hat_b200.HatError as e:
+            waited = time.perf_counter() - t
+            msg1, code1 = str(e), e.code
+        try:
+            be.forward(h, w, img)
+            msg2 = "no error"
+        except hat_b200.HatError as e:
+            msg2 = str(e)
+        # the GPU still works: a fresh one-GPU handle runs a pass
+        fresh = hat_b200.B200(ckpt, device=rank)
+        ok = bool(np.isfinite(fresh.forward(h, w, img)).all())
+        fresh.close()
+        q_out.put((rank, (code1, msg1, waited, msg2, ok)))
+        os._exit(0)
+    except Exception as e:
+        q_out.put((rank, repr(e)))
+
+
+@needs2
+def test_strip_rank_that_stops_calling_ends_in_an_error(ckdir):
+    p = _ck(ckdir, "hat-s", 4, 33)
+    img = synth.image(64, 48, 3300)
+    ctx = mp.get_context("spawn")
+    q_id, q_out, q_done = ctx.Queue(), ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_silent_rank_main, args=(r, p, img, q_id, q_out, q_done)) for r in range(2)]
+    for pr in procs:
+        pr.start()
+    try:
+        res = dict(q_out.get(timeout=300) for _ in range(2))
+    finally:
+        q_done.put(1)
+        for pr in procs:
+            pr.join(timeout=120)
+            if pr.exitcode is None:
+                pr.kill()
+    assert res[1] == "silent", res
+    assert isinstance(res[0], tuple), res
+    code1, msg1, waited, msg2, ok = res[0]
+    print(msg1, f"after {waited:.1f} s;", msg2)
+    assert code1 == hat_b200.E_CUDA
+    assert "did not finish" in msg1 or "asynchronous error" in msg1
+    assert 2.5 <= waited <= 60
+    assert "aborted" in msg2
+    assert ok

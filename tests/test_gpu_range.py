@@ -3,10 +3,11 @@
 HAT-S runs its parity mode on fp16 hi/lo operand pairs, which carry fp32's 22
 significant bits but not its exponent range: an operand of 65504 or more does not
 fit. The reference computes such inputs in fp32 and answers them, so the backend must
-too. These checkpoints are the seeded HAT-S weights with one layer's output scaled by
-2^14 and the consuming weights by 2^-14: exact in fp32 (powers of two), so the network
-computes the same function while an operand plane reaches values near 1e5. The pass
-must match the oracle at the reference's 1e-4 and leave the handle on tf32 pairs.
+too. These checkpoints are the seeded HAT-S weights with one layer's output scaled by a
+power of two (2^14 for LayerNorm's, 2^20 for v) and the consuming weights by its
+inverse: exact in fp32, so the network computes the same function while an operand
+plane goes past 65504. The pass must match the oracle at the reference's 1e-4 and leave
+the handle on tf32 pairs.
 """
 import numpy as np
 import pytest
@@ -18,6 +19,7 @@ from oracle import hat_oracle as O
 pytestmark = pytest.mark.gpu
 TOL = 1e-4
 BIG = np.float32(2.0 ** 14)
+HUGE = np.float32(2.0 ** 20)
 
 
 def scaled_checkpoint(path, kind):
@@ -31,11 +33,11 @@ def scaled_checkpoint(path, kind):
         t[f"{b}.attn.qkv.weight"] = t[f"{b}.attn.qkv.weight"] / BIG
         t[f"{b}.conv_block.cab.0.weight"] = t[f"{b}.conv_block.cab.0.weight"] / BIG
     else:
-        # v (an attention operand) times 2^14, proj's weight times 2^-14.
+        # v (an attention operand, |v| up to about 1 here) times 2^20, proj's weight times 2^-20.
         c = a.embed
-        t[f"{b}.attn.qkv.weight"][2 * c:] *= BIG
-        t[f"{b}.attn.qkv.bias"][2 * c:] *= BIG
-        t[f"{b}.attn.proj.weight"] = t[f"{b}.attn.proj.weight"] / BIG
+        t[f"{b}.attn.qkv.weight"][2 * c:] *= HUGE
+        t[f"{b}.attn.qkv.bias"][2 * c:] *= HUGE
+        t[f"{b}.attn.proj.weight"] = t[f"{b}.attn.proj.weight"] / HUGE
     checkpoint.write_safetensors(path, t, checkpoint.metadata(a, f"range-{kind}"))
     return path
 
