@@ -11,6 +11,7 @@
 #include "../../include/hat_b200.h"
 #include "engine.h"
 #include "nccl_rt.h"
+#include "png.h"
 #include "tile.h"
 
 using namespace hat;
@@ -145,6 +146,58 @@ int hat_b200_get_info(const hat_b200* h, hat_b200_info* out) {
     if (!h || !out) return HAT_B200_EINVAL;
     fill_info(h->e0().weights(), out);
     return HAT_B200_OK;
+}
+
+static void png_out(const PngImage& img, float* out, size_t out_floats, int* width, int* height) {
+    if (width) *width = img.w;
+    if (height) *height = img.h;
+    if (!out) return;
+    if (out_floats < img.data.size())
+        throw Error(1, "png: the output buffer holds " + std::to_string(out_floats) + " floats; the image needs " +
+                           std::to_string(img.data.size()));
+    memcpy(out, img.data.data(), img.data.size() * sizeof(float));
+}
+
+int hat_b200_png_load(const char* path, float* out, size_t out_floats, int* width, int* height, char* err,
+                      size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (!path) throw Error(1, "png: null path");
+        png_out(png_load(path), out, out_floats, width, height);
+    });
+}
+
+int hat_b200_png_decode(const uint8_t* bytes, size_t len, float* out, size_t out_floats, int* width, int* height,
+                        char* err, size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (!bytes) throw Error(1, "png: null buffer");
+        png_out(png_decode(bytes, len), out, out_floats, width, height);
+    });
+}
+
+int hat_b200_to_rgb8(const float* planar, int width, int height, uint8_t* rgb) {
+    if (!planar || !rgb || width <= 0 || height <= 0) return HAT_B200_EINVAL;
+    to_rgb8(planar, width, height, rgb);
+    return HAT_B200_OK;
+}
+
+int hat_b200_png_save(const char* path, int width, int height, const uint8_t* rgb, char* err, size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (!path || !rgb) throw Error(1, "png: null path or pixels");
+        png_save_rgb8(path, width, height, rgb);
+    });
+}
+
+int hat_b200_png_encode(int width, int height, const uint8_t* rgb, uint8_t* out, size_t cap, size_t* len, char* err,
+                        size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (!rgb) throw Error(1, "png: null pixels");
+        const std::vector<uint8_t> b = png_encode_rgb8(width, height, rgb);
+        if (len) *len = b.size();
+        if (!out || cap < b.size())
+            throw Error(1, "png: the output buffer holds " + std::to_string(cap) + " bytes; the file needs " +
+                               std::to_string(b.size()));
+        memcpy(out, b.data(), b.size());
+    });
 }
 
 int hat_b200_gpu_count(const hat_b200* h) { return h ? (int)h->engs.size() : 0; }

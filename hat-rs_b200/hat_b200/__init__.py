@@ -88,6 +88,11 @@ SIGNATURES = {
     "hat_b200_sync": (_I, [_P, _C, _S]),
     "hat_b200_fp16_pairs": (_I, [_P]),
     "hat_b200_gpu_count": (_I, [_P]),
+    "hat_b200_png_load": (_I, [_C, _P, _S, ctypes.POINTER(_I), ctypes.POINTER(_I), _C, _S]),
+    "hat_b200_png_decode": (_I, [_P, _S, _P, _S, ctypes.POINTER(_I), ctypes.POINTER(_I), _C, _S]),
+    "hat_b200_to_rgb8": (_I, [_P, _I, _I, _P]),
+    "hat_b200_png_save": (_I, [_C, _I, _I, _P, _C, _S]),
+    "hat_b200_png_encode": (_I, [_I, _I, _P, _P, _S, ctypes.POINTER(_S), _C, _S]),
 }
 
 _lib = None
@@ -330,3 +335,55 @@ def overlap_attention(mode, qkv, table, out, hp, wp, c, heads, stream=0):
     rc = lib().hat_b200_overlap_attention(mode, qkv, table, out, hp, wp, c, heads, stream)
     if rc:
         raise HatError(rc, "overlap attention launch failed")
+
+
+# PNG file I/O around the forward pass (src/image.rs).
+def png_load(path: str) -> np.ndarray:
+    """image::load_rgb: a PNG file as planar `[3][h][w]` float32 in [0, 1]."""
+    w, h, e = _I(), _I(), _err()
+    _check(lib().hat_b200_png_load(str(path).encode(), None, 0, ctypes.byref(w), ctypes.byref(h), e, len(e)), e)
+    out = np.empty((3, h.value, w.value), np.float32)
+    _check(lib().hat_b200_png_load(str(path).encode(), _ptr(out), out.size, ctypes.byref(w), ctypes.byref(h), e,
+                                   len(e)), e)
+    return out
+
+
+def png_decode(data: bytes) -> np.ndarray:
+    """image::load_rgb_stream: PNG bytes as planar `[3][h][w]` float32 in [0, 1]."""
+    buf = (ctypes.c_uint8 * len(data)).from_buffer_copy(data)
+    w, h, e = _I(), _I(), _err()
+    _check(lib().hat_b200_png_decode(buf, len(data), None, 0, ctypes.byref(w), ctypes.byref(h), e, len(e)), e)
+    out = np.empty((3, h.value, w.value), np.float32)
+    _check(lib().hat_b200_png_decode(buf, len(data), _ptr(out), out.size, ctypes.byref(w), ctypes.byref(h), e,
+                                     len(e)), e)
+    return out
+
+
+def to_rgb8(planar: np.ndarray) -> np.ndarray:
+    """Image::to_rgb8: planar `[3][h][w]` float to interleaved `[h][w][3]` uint8."""
+    x = np.ascontiguousarray(planar, np.float32)
+    _, h, w = x.shape
+    out = np.empty((h, w, 3), np.uint8)
+    rc = lib().hat_b200_to_rgb8(_ptr(x), w, h, _ptr(out))
+    if rc:
+        raise HatError(rc, "to_rgb8: bad arguments")
+    return out
+
+
+def png_save(path: str, rgb: np.ndarray) -> None:
+    """image::save_rgb: interleaved `[h][w][3]` uint8 to a PNG file."""
+    x = np.ascontiguousarray(rgb, np.uint8)
+    h, w, _ = x.shape
+    e = _err()
+    _check(lib().hat_b200_png_save(str(path).encode(), w, h, _ptr(x), e, len(e)), e)
+
+
+def png_encode(rgb: np.ndarray) -> bytes:
+    """image::save_rgb_stream: interleaved `[h][w][3]` uint8 to PNG bytes."""
+    x = np.ascontiguousarray(rgb, np.uint8)
+    h, w, _ = x.shape
+    n, e = _S(), _err()
+    lib().hat_b200_png_encode(w, h, _ptr(x), None, 0, ctypes.byref(n), e, len(e))
+    out = (ctypes.c_uint8 * n.value)()
+    _check(lib().hat_b200_png_encode(w, h, _ptr(x), out, n.value, ctypes.byref(n), e, len(e)), e)
+    return bytes(out)[:n.value]

@@ -75,7 +75,7 @@ def build(verbose: bool = False) -> Path:
     newest = max(o.stat().st_mtime for o in objs)
     if LIB.exists() and LIB.stat().st_mtime >= newest:
         return LIB
-    cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-cudart", "static", "-ldl"]
+    cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-cudart", "static", "-ldl", "-lz"]
     if verbose:
         print(" ".join(cmd), file=sys.stderr)
     r = subprocess.run(cmd, capture_output=True, text=True)

@@ -260,6 +260,37 @@ HAT_B200_API int hat_b200_linear_noalloc(int mode, const float* x, const float* 
 HAT_B200_API int hat_b200_profile(hat_b200* h, int height, int width, char* json, size_t jsonlen,
                                   char* err, size_t errlen);
 
+/* PNG file I/O around the forward pass (src/image.rs). Decoding accepts 8- and 16-bit grey,
+ * grey + alpha, RGB and RGBA, interlaced or not (indexed colour and other bit depths are
+ * refused as the reference refuses them); the output is planar [3][height][width] float
+ * in [0, 1], grey replicated to three channels and alpha dropped.
+ *
+ * image::load_rgb (src/image.rs:43-96): decodes the file at `path` into `out` (capacity
+ * `out_floats`; pass NULL / 0 to learn the size first) and sets *width, *height.
+ * HAT_B200_EIO for unreadable or malformed files, HAT_B200_EINVAL when `out` is too small. */
+HAT_B200_API int hat_b200_png_load(const char* path, float* out, size_t out_floats, int* width, int* height,
+                                   char* err, size_t errlen);
+
+/* image::load_rgb_stream (src/image.rs:49-96): the same decode from `len` bytes in memory
+ * (the CLI's `-i -`). */
+HAT_B200_API int hat_b200_png_decode(const uint8_t* bytes, size_t len, float* out, size_t out_floats, int* width,
+                                     int* height, char* err, size_t errlen);
+
+/* Image::to_rgb8 (src/image.rs:29-39): planar [3][height][width] float to interleaved
+ * 8-bit RGB, clamped to [0, 1], times 255, rounded half up. */
+HAT_B200_API int hat_b200_to_rgb8(const float* planar, int width, int height, uint8_t* rgb);
+
+/* image::save_rgb (src/image.rs:99-106): writes 8-bit RGB (interleaved, `width` x `height`)
+ * as a PNG file. */
+HAT_B200_API int hat_b200_png_save(const char* path, int width, int height, const uint8_t* rgb, char* err,
+                                   size_t errlen);
+
+/* image::save_rgb_stream (src/image.rs:108-114): the same encode into `out` (capacity
+ * `cap` bytes); *len is set to the encoded size, and HAT_B200_EINVAL is returned (with
+ * *len set) when `cap` is too small. */
+HAT_B200_API int hat_b200_png_encode(int width, int height, const uint8_t* rgb, uint8_t* out, size_t cap, size_t* len,
+                                     char* err, size_t errlen);
+
 /* The GPUs this handle drives (1 unless created with ngpus > 1). */
 HAT_B200_API int hat_b200_gpu_count(const hat_b200* h);
 
