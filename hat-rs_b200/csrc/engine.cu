@@ -871,6 +871,9 @@ void Engine::forward_host(int n, int h, int w, const float* in, float* out) {
         for (int i = 0; i < n; ++i) {
             HAT_CUDA(cudaMemcpyAsync(a_->din, in + i * inN, inN * sizeof(float), cudaMemcpyHostToDevice, stream_));
             run_graph(stream_);
+            // A copy into pageable host memory blocks until the pass is done; sharded, the
+            // pass waits on the other ranks, so it is awaited under the deadline first.
+            if (comm_) wait_stream();
             copy_out(out + i * outN, cudaMemcpyDeviceToHost, stream_);
         }
         wait_stream();
