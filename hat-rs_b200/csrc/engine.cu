@@ -283,6 +283,11 @@ long Engine::linear(const std::string& wname, Opnd x, Dst y, const Epi& e) {
     return gemm_linear(c, x, G(wname), y, plan_.tokens(), e, stream_);
 }
 
+long Engine::linear_m(const std::string& wname, Opnd x, Dst y, const Epi& e, long m) {
+    GemmCtx c{mode_, simt_only_, derr_};
+    return gemm_linear(c, x, G(wname), y, m, e, stream_);
+}
+
 long Engine::conv(const std::string& wname, Opnd x, Dst y, int hgt, int wid, const Epi& e) {
     GemmCtx c{mode_, simt_only_, derr_};
     return gemm_conv3x3(c, x, G(wname), y, hgt, wid, e, stream_);
@@ -527,31 +532,35 @@ void Engine::ensure_plan(int h, int w) {
 }
 
 // `out = x + fc2(gelu(fc1(norm2(x))))` (src/gpu.rs:449-466). `out` may be `x` itself,
-// or the split n1 planes when the result feeds only the stage's conv.
+// or the split n1 planes when the result feeds only the stage's conv. Strip-sharded, it
+// runs over the strip's own rows: the next layer's halo exchange overwrites the others.
 void Engine::mlp(const std::string& p, float* x, Dst out) {
-    const long P = plan_.tokens();
+    const long t0 = own_t0(), P = own_tokens();
     const int c = wt_.embed, hid = wt_.mlp_ratio * c;
+    float* xo = x + t0 * c;
+    const Dst n1 = dst_at(D(a_->n1, a_->n1lo), t0 * c);
+    const Opnd n1o = opnd_at(O(a_->n1, a_->n1lo), t0 * c);
+    const Dst yo = dst_at(out, t0 * c);
     mark("layernorm", 0, 8.0 * P * c);
-    launch_layernorm(x, W(p + ".norm2.weight"), W(p + ".norm2.bias"), D(a_->n1, a_->n1lo), P, c, stream_);
+    launch_layernorm(xo, W(p + ".norm2.weight"), W(p + ".norm2.bias"), n1, P, c, stream_);
     const GemmW& w1 = G(p + ".mlp.fc1.weight");
     const GemmW& w2 = G(p + ".mlp.fc2.weight");
     if (!simt_only_ && umma_mlp_ok(w1, w2)) {
         // fc1 + GELU + fc2 + residual in one launch, the hidden plane never written out.
         mark("mlp.fused", 4.0 * P * hid * c, 4.0 * P * (2 * c + c));
-        umma_mlp(mode_, O(a_->n1, a_->n1lo), w1, W(p + ".mlp.fc1.bias"), w2, W(p + ".mlp.fc2.bias"), x, out, P,
-                 derr_, stream_);
+        umma_mlp(mode_, n1o, w1, W(p + ".mlp.fc1.bias"), w2, W(p + ".mlp.fc2.bias"), xo, yo, P, derr_, stream_);
         return;
     }
     Epi e1;
     e1.bias = W(p + ".mlp.fc1.bias");
     e1.act = ACT_GELU;
     mark("linear.fc1", 2.0 * P * hid * c, 4.0 * P * (c + hid));
-    linear(p + ".mlp.fc1.weight", O(a_->n1, a_->n1lo), D(a_->hid, a_->hidlo), e1);
+    linear_m(p + ".mlp.fc1.weight", n1o, dst_at(D(a_->hid, a_->hidlo), t0 * hid), e1, P);
     Epi e2;
     e2.bias = W(p + ".mlp.fc2.bias");
-    e2.res = x;
+    e2.res = xo;
     mark("linear.fc2", 2.0 * P * hid * c, 4.0 * P * (hid + 2 * c));
-    linear(p + ".mlp.fc2.weight", O(a_->hid, a_->hidlo), out, e2);
+    linear_m(p + ".mlp.fc2.weight", opnd_at(O(a_->hid, a_->hidlo), t0 * hid), yo, e2, P);
 }
 
 // One HAB (hat_arch.py:266-309; src/gpu.rs:469-520): `in` is the block input, `out`
@@ -623,14 +632,16 @@ void Engine::hab(int stage, int blk, const float* in, float* out) {
     launch_window_attention(mode_, simt_only_, a_->qkv, W(p + ".attn.relative_position_bias_table"),
                             D(a_->attn, a_->attnlo), plan_, c, wt_.heads, shift, derr_, stream_, pre);
     // proj, then `(shortcut + attn) + conv_x * conv_scale` in the epilogue.
+    // (over the strip's own rows when sharded: the next block exchanges the halo rows)
+    const long t0 = own_t0(), Po = own_tokens();
     Epi ep;
     ep.bias = W(p + ".attn.proj.bias");
-    ep.res = in;
-    ep.cx = a_->convx;
+    ep.res = in + t0 * c;
+    ep.cx = a_->convx + t0 * c;
     ep.gate = a_->gate;
     ep.cscale = wt_.conv_scale;
-    mark("linear.proj", 2.0 * P * c * c, 16.0 * P * c);
-    linear(p + ".attn.proj.weight", O(a_->attn, a_->attnlo), Dst{out, nullptr}, ep);
+    mark("linear.proj", 2.0 * Po * c * c, 16.0 * Po * c);
+    linear_m(p + ".attn.proj.weight", opnd_at(O(a_->attn, a_->attnlo), t0 * c), Dst{out + t0 * c, nullptr}, ep, Po);
     mlp(p, out, Dst{out, nullptr});
 }
 
@@ -656,11 +667,12 @@ void Engine::ocab(int stage, const float* in, float* out) {
     mark("attn.overlap", 4.0 * P * 576 * c, 16.0 * P * c);
     launch_overlap_attention(mode_, simt_only_, a_->qkv, W(p + ".relative_position_bias_table"),
                              D(a_->attn, a_->attnlo), plan_, c, wt_.heads, derr_, stream_, pre);
+    const long t0 = own_t0(), Po = own_tokens();
     Epi ep;
     ep.bias = W(p + ".proj.bias");
-    ep.res = in;
-    mark("linear.proj", 2.0 * P * c * c, 12.0 * P * c);
-    linear(p + ".proj.weight", O(a_->attn, a_->attnlo), Dst{out, nullptr}, ep);
+    ep.res = in + t0 * c;
+    mark("linear.proj", 2.0 * Po * c * c, 12.0 * Po * c);
+    linear_m(p + ".proj.weight", opnd_at(O(a_->attn, a_->attnlo), t0 * c), Dst{out + t0 * c, nullptr}, ep, Po);
     mlp(p, out, D(a_->n1, a_->n1lo));
 }
 
@@ -675,9 +687,12 @@ void Engine::enqueue_pass() {
     ef.bias = W("conv_first.bias");
     mark("conv.first", 54.0 * P * c, 4.0 * P * (3 + c));
     conv_res("conv_first.weight", Opnd{a_->x0, nullptr}, 3, Dst{a_->body, nullptr}, c, 1, false, ef);
-    mark("layernorm", 0, 8.0 * P * c);
-    launch_layernorm(a_->body, W("patch_embed.norm.weight"), W("patch_embed.norm.bias"), Dst{a_->xa, nullptr}, P,
-                     c, stream_);
+    // The LayerNorms of the body run over the strip's own rows (the halo rows of their
+    // outputs are exchanged before they are read).
+    const long t0 = own_t0(), Po = own_tokens();
+    mark("layernorm", 0, 8.0 * Po * c);
+    launch_layernorm(a_->body + t0 * c, W("patch_embed.norm.weight"), W("patch_embed.norm.bias"),
+                     Dst{a_->xa + t0 * c, nullptr}, Po, c, stream_);
     // The stage input stays in `xa` (the RHAG residual); the blocks run in `xb`, the OCAB
     // leaves the stage's result split in n1, and the stage conv adds xa back into xa.
     for (size_t s = 0; s < wt_.depths.size(); ++s) {
@@ -695,8 +710,9 @@ void Engine::enqueue_pass() {
         conv_res("layers." + std::to_string(s) + ".conv.weight", O(a_->n1, a_->n1lo), c, Dst{a_->xa, nullptr}, c, 1,
                  false, er);
     }
-    mark("layernorm", 0, 8.0 * P * c);
-    launch_layernorm(a_->xa, W("norm.weight"), W("norm.bias"), D(a_->n1, a_->n1lo), P, c, stream_);
+    mark("layernorm", 0, 8.0 * Po * c);
+    launch_layernorm(a_->xa + t0 * c, W("norm.weight"), W("norm.bias"), dst_at(D(a_->n1, a_->n1lo), t0 * c), Po, c,
+                     stream_);
     Epi eb;
     eb.bias = W("conv_after_body.bias");
     eb.res = a_->body;

@@ -96,6 +96,12 @@ private:
     const float* W(const std::string& name) const;
     const GemmW& G(const std::string& name) const;
     long linear(const std::string& wname, Opnd x, Dst y, const Epi& e);
+    // The same over `m` tokens from the given operand and output positions.
+    long linear_m(const std::string& wname, Opnd x, Dst y, const Epi& e, long m);
+    // This plan's own tokens: strip-sharded, the rows between the halos (pointwise layers
+    // whose halo rows the next exchange overwrites compute only these); else the plane.
+    long own_t0() const { return (long)plan_.halo * plan_.wp; }
+    long own_tokens() const { return (long)plan_.own() * plan_.wp; }
     long conv(const std::string& wname, Opnd x, Dst y, int hgt, int wid, const Epi& e);
     // Operand planes: split into hi/lo halves when the tensor cores run in fp32-parity
     // mode (fp16 pairs when `h16_`, tf32 pairs otherwise), plain fp32 otherwise.
