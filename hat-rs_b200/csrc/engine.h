@@ -10,6 +10,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "conv_last.h"
 #include "umma.cuh"
 #include "weights.h"
 
@@ -125,6 +126,9 @@ private:
     // own stride as tf32 pairs or fp32).
     bool h16_ = false;
     int fallbacks_ = 0;
+    // conv_last's weights for the bandwidth kernel (k_conv_last.cu), when its shape fits.
+    bool cl_ok_ = false;
+    ConvLastW cl_{};
     int cmid_ld_ = 0;
     int device_ = 0, mode_ = 0;
     std::unique_ptr<Comm> comm_;
