@@ -464,17 +464,23 @@ void Engine::wait_stream() {
 }
 
 // fp16 operand pairs carry 22 significant bits but only fp16's exponent range; a value of
-// 65504 or more sets ERR_RANGE_ATTN / ERR_RANGE_GEMM. The weights are prepared again as tf32 pairs (the same 22
-// bits with fp32's exponent range), the arena is cleared (the planes change layout) and the
-// handle stays on tf32 pairs from then on.
-void Engine::fall_back_to_tf32_pairs() {
+// 65504 or more sets ERR_RANGE_GEMM (a GEMM operand plane) or ERR_RANGE_ATTN (q, k or v).
+// The weights are prepared again as tf32 pairs (the same 22 bits with fp32's exponent
+// range), the arena is cleared (the planes change layout) and the handle stays on tf32
+// pairs from then on. The tensor-core attention splits its operands into fp16 pairs in
+// every mode, so an attention operand out of that range moves the attention to the fp32
+// CUDA-core kernels as well.
+void Engine::fall_back(int code) {
     HAT_CUDA(cudaStreamSynchronize(stream_));
     if (graph_) {
         cudaGraphExecDestroy(graph_);
         graph_ = nullptr;
     }
-    h16_ = false;
-    upload_weights();
+    if (code == ERR_RANGE_ATTN) attn_simt_ = true;
+    if (h16_) {
+        h16_ = false;
+        upload_weights();
+    }
     have_plan_ = false;  // the next ensure_plan clears the arena
     eager_runs_ = 0;
     ++fallbacks_;
@@ -640,7 +646,7 @@ void Engine::hab(int stage, int blk, const float* in, float* out) {
     linear(p + ".attn.qkv.weight", O(a_->n1, a_->n1lo), Dst{a_->qkv, nullptr}, eq);
     const int shift = blk % 2 ? plan_.shift : 0;
     mark("attn.window", 4.0 * P * 256 * c, 16.0 * P * c);
-    launch_window_attention(mode_, simt_only_, a_->qkv, W(p + ".attn.relative_position_bias_table"),
+    launch_window_attention(mode_, simt_only_ || attn_simt_, a_->qkv, W(p + ".attn.relative_position_bias_table"),
                             D(a_->attn, a_->attnlo), plan_, c, wt_.heads, shift, derr_, stream_, pre);
     // proj, then `(shortcut + attn) + conv_x * conv_scale` in the epilogue.
     // (over the strip's own rows when sharded: the next block exchanges the halo rows)
@@ -676,7 +682,7 @@ void Engine::ocab(int stage, const float* in, float* out) {
     mark("linear.qkv", 6.0 * P * c * c, 16.0 * P * c);
     linear(p + ".qkv.weight", O(a_->n1, a_->n1lo), Dst{a_->qkv, nullptr}, eq);
     mark("attn.overlap", 4.0 * P * 576 * c, 16.0 * P * c);
-    launch_overlap_attention(mode_, simt_only_, a_->qkv, W(p + ".relative_position_bias_table"),
+    launch_overlap_attention(mode_, simt_only_ || attn_simt_, a_->qkv, W(p + ".relative_position_bias_table"),
                              D(a_->attn, a_->attnlo), plan_, c, wt_.heads, derr_, stream_, pre);
     const long t0 = own_t0(), Po = own_tokens();
     Epi ep;
@@ -905,10 +911,12 @@ void Engine::forward_host(int n, int h, int w, const float* in, float* out) {
         }
         wait_stream();
         const int v = take_device_error();
-        // An operand beyond fp16's range: the whole call again on tf32 pairs (not on a
-        // strip-sharded handle, whose ranks must keep one operand layout in step).
-        if ((v == ERR_RANGE_ATTN || v == ERR_RANGE_GEMM) && h16_ && !comm_ && attempt == 0) {
-            fall_back_to_tf32_pairs();
+        // An operand beyond fp16's range: the whole call again on tf32 pairs, then with the
+        // attention on the CUDA cores if q, k or v is the one (not on a strip-sharded handle,
+        // whose ranks must keep one operand layout in step).
+        const bool can = (v == ERR_RANGE_GEMM && h16_) || (v == ERR_RANGE_ATTN && !attn_simt_);
+        if (can && !simt_only_ && !comm_ && attempt < 2) {
+            fall_back(v);
             continue;
         }
         raise_device_error(v);

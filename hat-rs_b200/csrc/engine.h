@@ -71,7 +71,7 @@ private:
     Plan plan_for(int h, int w) const;
     void upload_weights();
     int take_device_error();  // the error word's value (cleared on the device)
-    void fall_back_to_tf32_pairs();
+    void fall_back(int code);  // after ERR_RANGE_*: tf32 pairs (and the attention on CUDA cores)
     // Waits for the engine's stream: plainly, or with the communicator's deadline when sharded.
     void wait_stream();
     void ensure_plan(int h, int w);
@@ -125,6 +125,7 @@ private:
     // plane's channel stride in elements (16 or a multiple of 8 as fp16; the buffer's
     // own stride as tf32 pairs or fp32).
     bool h16_ = false;
+    bool attn_simt_ = false;  // the attention on the fp32 CUDA-core kernels (after ERR_RANGE_ATTN)
     int fallbacks_ = 0;
     // conv_last's weights for the bandwidth kernel (k_conv_last.cu), when its shape fits.
     bool cl_ok_ = false;

@@ -51,21 +51,23 @@ namespace hat {
 
 namespace {
 
-// SLIM (window attention on the pre-split layout): two copying loader warps, 224 threads,
-// three CTAs per SM (80 registers a thread). Otherwise four loader warps, 288 threads, two
-// CTAs per SM (96 registers). Measured: the slim shape is faster for the window attention;
-// the OCAB kernel spills at 80 registers and keeps the wide one.
-template <bool SLIM>
+// H2 (window attention on the pre-split layout): a work item is a whole window of one head,
+// both 128-query halves, so its keys and values are copied once for 256 queries; eight softmax
+// warps (four per half, each half's S, P and O in tensor memory of its own), two copying loader
+// warps, 352 threads, two CTAs per SM (93 registers a thread). Otherwise a work item is one
+// half: four softmax warps, four loader warps, 288 threads, two CTAs per SM (96 registers).
+template <bool H2>
 struct AttnShape {
-    static constexpr int loaders = SLIM ? 2 : 4;        // loader warps
-    static constexpr int threads = 160 + 32 * loaders;  // + MMA warp + 4 softmax warps
-    static constexpr int ctas = SLIM ? 3 : 2;           // CTAs per SM
+    static constexpr int halves = H2 ? 2 : 1;           // query halves per work item
+    static constexpr int loaders = H2 ? 2 : 4;          // loader warps
+    static constexpr int softmax = 4 * halves;          // softmax warps
+    static constexpr int threads = 32 * (1 + softmax + loaders);
+    static constexpr int ctas = 2;                      // CTAs per SM
 };
 constexpr int KBLK = 32;     // keys per block
 constexpr int MT = 128;      // query rows per work item
 constexpr int KVS = 4;       // K/V pipeline stages
 constexpr int TSTRIDE = 48;  // shared bias-table row stride (floats)
-constexpr int TMEM_COLS = 128;
 constexpr float RESCALE_LOG2 = 8.f;
 constexpr float P_SHIFT = 6.f;
 constexpr float F16_LIMIT = 65504.f;  // the largest finite fp16
@@ -233,18 +235,23 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
     constexpr uint32_t K_BYTES = KH * 1024;         // 32 keys x 32 B per k-step
     constexpr uint32_t V_BYTES = 2 * 1024;          // V^T: 32 features x 32 B per 16-key k-step
     constexpr uint32_t KV_BYTES = 2 * K_BYTES + 2 * V_BYTES;
-    constexpr uint32_t OFF_KV = 2 * Q_BYTES;
+    using Shape = AttnShape<PRE && !OCA>;
+    constexpr int HV = Shape::halves;               // query halves of a work item
+    constexpr uint32_t OFF_KV = HV * 2 * Q_BYTES;
     constexpr uint32_t OFF_TAB = OFF_KV + KVS * KV_BYTES;
     constexpr uint32_t OFF_KOFF = OFF_TAB + TR * TSTRIDE * 4;
-    // TMEM columns: S blocks at 0 and 32 (fp32); once read, a block's first 16 columns
-    // hold P_hi and the next 16 P_lo (fp16 pairs); O (per item parity) at 64 and 96.
-    constexpr uint32_t T_PLO = 16, T_O = 64;
+    // TMEM columns: half h's S blocks at 64h and 64h + 32 (fp32); once read, a block's first
+    // 16 columns hold P_hi and the next 16 P_lo (fp16 pairs); half h's O (per item parity)
+    // at 64 HV + 64h and 64 HV + 64h + 32.
+    constexpr uint32_t T_PLO = 16, T_O = 64 * HV;
+    constexpr uint32_t TMEM_COLS = 128 * HV;
 
     extern __shared__ __align__(1024) uint8_t raw[];
     uint8_t* sm = (uint8_t*)(((uintptr_t)raw + 1023) & ~(uintptr_t)1023);
     float* tab = reinterpret_cast<float*>(sm + OFF_TAB);
     int* koff = reinterpret_cast<int*>(sm + OFF_KOFF);  // OCAB: key (ky, kx) -> ky*48 + kx
-    __shared__ uint64_t q_full, q_empty, kv_full[KVS], kv_empty[KVS], s_full[2], p_full[2], o_done, o_free[2], drain;
+    __shared__ uint64_t q_full, q_empty, kv_full[KVS], kv_empty[KVS], s_full[HV][2], p_full[HV][2], o_done[HV],
+        o_free[HV][2], drain;
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int abort_flag;
 
@@ -256,7 +263,7 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
     // Bias table of this head, rows TSTRIDE apart. SA: tab[r][s] = table[r*31 + s], the
     // bias of (qy - ky + 15, qx - kx + 15). OCAB: tab[r][s] is the bias of key - query
     // offset (r - 22, s - 22), i.e. table[((r - 22)*39 + (s - 22)) mod 1521].
-    constexpr int NT = AttnShape<PRE && !OCA>::threads, NLT = 32 * AttnShape<PRE && !OCA>::loaders;
+    constexpr int NT = Shape::threads, NLT = 32 * Shape::loaders, LW0 = 1 + Shape::softmax;  // first loader warp
     for (int i = threadIdx.x; i < TR * TR; i += NT) {
         const int r = i / TR, s = i - r * TR;
         int src = OCA ? (r - 22) * TW + (s - 22) : r * TW + s;
@@ -272,26 +279,28 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
             bar_init(&kv_full[s], NLT);
             bar_init(&kv_empty[s], 1);
         }
-        for (int s = 0; s < 2; ++s) {
-            bar_init(&s_full[s], 1);
-            bar_init(&p_full[s], 128);
-            bar_init(&o_free[s], 128);
+        for (int h = 0; h < HV; ++h) {
+            for (int s = 0; s < 2; ++s) {
+                bar_init(&s_full[h][s], 1);
+                bar_init(&p_full[h][s], 128);
+                bar_init(&o_free[h][s], 128);
+            }
+            bar_init(&o_done[h], 1);
         }
-        bar_init(&o_done, 1);
         bar_init(&drain, 1);
         abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su(&tmem_slot)),
-                     "n"(TMEM_COLS));
+                     "r"(TMEM_COLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     if (PRE) {
         // The head dim's padding (24 -> 32) is never copied: zero it once. Q and K: the second
         // 16-byte piece of k-step 1 of every row; V^T: feature rows 24..31.
         const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-        for (int i = threadIdx.x; i < 2 * MT; i += NT)
+        for (int i = threadIdx.x; i < HV * 2 * MT; i += NT)
             *reinterpret_cast<uint4*>(sm + (i / MT) * Q_BYTES + 4096 + off_sw32(i % MT, 1)) = z;
         for (int i = threadIdx.x; i < KVS * 2 * KBLK; i += NT) {
             const int st = i / (2 * KBLK), lo = (i / KBLK) & 1, key = i % KBLK;
@@ -313,71 +322,82 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
             const uint32_t id_s = idesc_h(32), id_o = idesc_h(32);
-            const uint32_t qh = su(sm), ql = su(sm + Q_BYTES);
             long g = 0;  // global key-block counter
             uint32_t ti = 0;
             bool ok = true;
             for (long w = blockIdx.x; w < items && ok; w += gridDim.x, ++ti) {
                 if (!bar_wait(&q_full, ti & 1, &abort_flag, err, 11)) break;
-                // The O block of this item's parity must have been read by the softmax.
-                if (!bar_wait(&o_free[ti & 1], ((ti >> 1) & 1) ^ 1, &abort_flag, err, 19)) break;
-                const uint32_t od = tmem + T_O + (ti & 1) * 32;
+                // Each half's O block of this item's parity must have been read by the softmax.
+                for (int h = 0; h < HV && ok; ++h)
+                    ok = bar_wait(&o_free[h][ti & 1], ((ti >> 1) & 1) ^ 1, &abort_flag, err, 19);
+                if (!ok) break;
+                // S of key block gb for every half (each into its own buffer gb & 1)
                 auto issue_s = [&](long gb) -> bool {
                     const int s = (int)(gb & 1), kvs = (int)(gb % KVS);
                     if (!bar_wait(&kv_full[kvs], (uint32_t)((gb / KVS) & 1), &abort_flag, err, 12)) return false;
                     tcf_after();
                     const uint32_t kb = su(sm + OFF_KV + kvs * KV_BYTES);
-                    const uint32_t d = tmem + s * 32;
 #pragma unroll
-                    for (int k = 0; k < KH; ++k) {
-                        const uint64_t aH = mdesc(qh + k * 4096, 32, 256), aL = mdesc(ql + k * 4096, 32, 256);
-                        const uint64_t bH = mdesc(kb + k * 1024, 32, 256), bL = mdesc(kb + K_BYTES + k * 1024, 32, 256);
-                        if (TERMS == 3) {
-                            mma_ss(d, aL, bH, id_s, k ? 1u : 0u);
-                            mma_ss(d, aH, bL, id_s, 1u);
-                            mma_ss(d, aH, bH, id_s, 1u);
-                        } else {
-                            mma_ss(d, aH, bH, id_s, k ? 1u : 0u);
+                    for (int h = 0; h < HV; ++h) {
+                        const uint32_t qh = su(sm + h * 2 * Q_BYTES), ql = qh + Q_BYTES;
+                        const uint32_t d = tmem + h * 64 + s * 32;
+#pragma unroll
+                        for (int k = 0; k < KH; ++k) {
+                            const uint64_t aH = mdesc(qh + k * 4096, 32, 256), aL = mdesc(ql + k * 4096, 32, 256);
+                            const uint64_t bH = mdesc(kb + k * 1024, 32, 256),
+                                           bL = mdesc(kb + K_BYTES + k * 1024, 32, 256);
+                            if (TERMS == 3) {
+                                mma_ss(d, aL, bH, id_s, k ? 1u : 0u);
+                                mma_ss(d, aH, bL, id_s, 1u);
+                                mma_ss(d, aH, bH, id_s, 1u);
+                            } else {
+                                mma_ss(d, aH, bH, id_s, k ? 1u : 0u);
+                            }
                         }
+                        commit(&s_full[h][s]);
                     }
-                    commit(&s_full[s]);
                     return true;
                 };
                 if (!issue_s(g)) break;
                 for (int j = 0; j < NBLK; ++j) {
                     const long gb = g + j;
-                    // S of the next block goes into the other S buffer, whose P the
-                    // previous PV (issued earlier, executed in order) has consumed.
+                    // S of the next block goes into the other S buffers, whose P the previous
+                    // PVs (issued earlier, executed in order) have consumed.
                     if (j + 1 < NBLK) {
                         if (!issue_s(gb + 1)) {
                             ok = false;
                             break;
                         }
-                        // Once the item's last S MMA is issued, Q may be replaced.
+                        // Once the item's last S MMAs are issued, Q may be replaced.
                         if (j + 1 == NBLK - 1) commit(&q_empty);
                     }
                     const int s = (int)(gb & 1);
-                    if (!bar_wait(&p_full[s], (uint32_t)((gb >> 1) & 1), &abort_flag, err, 13)) {
-                        ok = false;
-                        break;
-                    }
-                    tcf_after();
                     const int kvs = (int)(gb % KVS);
                     const uint32_t vb = su(sm + OFF_KV + kvs * KV_BYTES + 2 * K_BYTES);
-                    const uint32_t ph = tmem + s * 32, pl = ph + T_PLO;
-#pragma unroll
-                    for (int k = 0; k < KBLK / 16; ++k) {
-                        const uint64_t bH = mdesc(vb + k * 1024, 32, 256), bL = mdesc(vb + V_BYTES + k * 1024, 32, 256);
-                        const uint32_t acc = (j | k) ? 1u : 0u;
-                        if (TERMS == 3) {
-                            mma_ts(od, pl + k * 8, bH, id_o, acc);
-                            mma_ts(od, ph + k * 8, bL, id_o, 1u);
-                            mma_ts(od, ph + k * 8, bH, id_o, 1u);
-                        } else {
-                            mma_ts(od, ph + k * 8, bH, id_o, acc);
+                    for (int h = 0; h < HV; ++h) {
+                        if (!bar_wait(&p_full[h][s], (uint32_t)((gb >> 1) & 1), &abort_flag, err, 13)) {
+                            ok = false;
+                            break;
                         }
+                        tcf_after();
+                        const uint32_t od = tmem + T_O + h * 64 + (ti & 1) * 32;
+                        const uint32_t ph = tmem + h * 64 + s * 32, pl = ph + T_PLO;
+#pragma unroll
+                        for (int k = 0; k < KBLK / 16; ++k) {
+                            const uint64_t bH = mdesc(vb + k * 1024, 32, 256),
+                                           bL = mdesc(vb + V_BYTES + k * 1024, 32, 256);
+                            const uint32_t acc = (j | k) ? 1u : 0u;
+                            if (TERMS == 3) {
+                                mma_ts(od, pl + k * 8, bH, id_o, acc);
+                                mma_ts(od, ph + k * 8, bL, id_o, 1u);
+                                mma_ts(od, ph + k * 8, bH, id_o, 1u);
+                            } else {
+                                mma_ts(od, ph + k * 8, bH, id_o, acc);
+                            }
+                        }
+                        commit(&o_done[h]);
                     }
-                    commit(&o_done);
+                    if (!ok) break;
                     commit(&kv_empty[kvs]);
                 }
                 g += NBLK;
@@ -385,9 +405,11 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
             commit(&drain);
             bar_wait_quiet(&drain, 0);
         }
-    } else if (warp <= 4) {
+    } else if (warp <= Shape::softmax) {
         // ------------------------------------------------------------ softmax
-        const int q4 = warp & 3;
+        const int q4 = warp & 3;       // TMEM lane quarter (a warp reaches lanes 32 (warp % 4) ..)
+        const int hh = (warp - 1) >> 2;  // the query half of the item this warp works on
+        const uint32_t th = (uint32_t)hh * 64;
         const int row = q4 * 32 + lane;
         const uint32_t trow = (uint32_t)(q4 * 32) << 16;
         constexpr int VW = (D % 4 == 0) ? 4 : 2;
@@ -396,7 +418,7 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
         for (long w = blockIdx.x; w < items; w += gridDim.x, ++ti) {
             if (__any_sync(0xffffffffu, abort_flag != 0)) break;
             const long rest = w / heads;
-            const int win = (int)(rest >> 1), mtile = (int)(rest & 1);
+            const int win = HV == 2 ? (int)rest : (int)(rest >> 1), mtile = HV == 2 ? hh : (int)(rest & 1);
             const int wy = win / nx, wx = win - wy * nx;
             const int qi = mtile * MT + row, qy = qi >> 4, qx = qi & 15;
             const bool masked = !OCA && gm.mshift > 0;
@@ -418,20 +440,20 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
                         if (by * 3 + bx != lq) cm[by] |= 1u << kx;
                 }
             }
-            const uint32_t t_o = tmem + trow + T_O + (ti & 1) * 32;
+            const uint32_t t_o = tmem + trow + T_O + th + (ti & 1) * 32;
             float m = 0.f, l = 0.f;
             bool ok = true;
             for (int j = 0; j < NBLK; ++j) {
                 const long gb = g + j;
                 const int s = (int)(gb & 1);
-                const bool got = bar_wait(&s_full[s], (uint32_t)((gb >> 1) & 1), &abort_flag, err, 16);
+                const bool got = bar_wait(&s_full[hh][s], (uint32_t)((gb >> 1) & 1), &abort_flag, err, 16);
                 if (!__all_sync(0xffffffffu, got)) {
                     ok = false;
                     break;
                 }
                 tcf_after();
                 float sv[32];
-                tld32(tmem + trow + s * 32, sv);
+                tld32(tmem + trow + th + s * 32, sv);
                 uint32_t mrow0 = 0, mrow1 = 0;
                 if (masked) {
                     // the block's two key rows ky = 2j, 2j+1
@@ -476,14 +498,14 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
                     psum += p0 + p1;
                     split_h16x2(p0, p1, ph[k >> 1], pl[k >> 1]);
                 }
-                tst16(tmem + trow + s * 32, ph);
-                if (TERMS == 3) tst16(tmem + trow + s * 32 + T_PLO, pl);
+                tst16(tmem + trow + th + s * 32, ph);
+                if (TERMS == 3) tst16(tmem + trow + th + s * 32 + T_PLO, pl);
                 l += psum;
                 if (j > 0) {
                     // PV of the previous block has finished (this also keeps every
                     // o_done phase consumed in order); a moved max then rescales the
                     // row's O before this block's PV adds to it.
-                    const bool done = bar_wait(&o_done, (uint32_t)((gb - 1) & 1), &abort_flag, err, 15);
+                    const bool done = bar_wait(&o_done[hh], (uint32_t)((gb - 1) & 1), &abort_flag, err, 15);
                     if (!__all_sync(0xffffffffu, done)) {
                         ok = false;
                         break;
@@ -499,17 +521,17 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
                 }
                 tst_wait();
                 tcf_before();
-                bar_arrive(&p_full[s]);
+                bar_arrive(&p_full[hh][s]);
             }
             if (!ok) break;
             // O / l at the query's plane position (the roll of the shifted windows undone).
-            const bool done = bar_wait(&o_done, (uint32_t)((g + NBLK - 1) & 1), &abort_flag, err, 15);
+            const bool done = bar_wait(&o_done[hh], (uint32_t)((g + NBLK - 1) & 1), &abort_flag, err, 15);
             if (!__all_sync(0xffffffffu, done)) break;
             tcf_after();
             float ov[32];
             tld32(t_o, ov);
             tcf_before();
-            bar_arrive(&o_free[ti & 1]);
+            bar_arrive(&o_free[hh][ti & 1]);
             const float inv = 1.f / l;
             const int qrow = OCA ? gm.oy + wy * 16 + qy : (gm.oy + wy * 16 + qy + gm.sy) % gm.rows;
             const long qpos = (long)qrow * wp + (OCA ? wx * 16 + qx : (wx * 16 + qx + gm.sx) % wp);
@@ -552,7 +574,7 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
         // left of the query window). OCAB keys outside the image are zeros, a whole piece at
         // a time (the image edges fall on multiples of 4).
         static_assert(D == 24 && TERMS == 3, "the copy loaders are for parity attention, D = 24");
-        const int t = threadIdx.x - 160;  // 0..NLT-1
+        const int t = threadIdx.x - 32 * LW0;  // 0..NLT-1
         const long P = (long)gm.rows * wp, c2 = 2L * c;
         constexpr int R = 6;  // copies in flight a thread (registers), rounds of R
         const __half* qkh = reinterpret_cast<const __half*>(qkv);
@@ -573,23 +595,25 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
         for (long w = blockIdx.x; w < items; w += gridDim.x, ++ti) {
             if (__any_sync(0xffffffffu, abort_flag != 0)) break;
             const long rest = w / heads;
-            const int win = (int)(rest >> 1), mtile = (int)(rest & 1);
+            const int win = HV == 2 ? (int)rest : (int)(rest >> 1), mtile = HV == 2 ? 0 : (int)(rest & 1);
             const int wy = win / nx, wx = win - wy * nx;
             {
-                // Q: 768 copies, R at a time per thread (the first round issued before the wait)
+                // Q: 768 copies per half, R at a time per thread (the first round issued before
+                // the wait)
                 bool got = true;
 #pragma unroll 1
-                for (int r0 = 0; r0 < 768; r0 += R * NLT) {
+                for (int r0 = 0; r0 < 768 * HV; r0 += R * NLT) {
                     uint4 qv[R];
                     uint32_t qd[R];
 #pragma unroll
                     for (int u = 0; u < R; ++u) {
-                        const int cid = r0 + t + NLT * u, row = cid / 6, part = cid % 6, lo = part / 3, ch = part % 3;
-                        const int qi = mtile * MT + row;
+                        const int cid0 = r0 + t + NLT * u, half = cid0 / 768, cid = cid0 - 768 * half;
+                        const int row = cid / 6, part = cid % 6, lo = part / 3, ch = part % 3;
+                        const int qi = (mtile + half) * MT + row;
                         const long qpos = OCA ? (long)(gm.oy + wy * 16 + (qi >> 4)) * wp + wx * 16 + (qi & 15)
                                               : pos(wy, wx, qi >> 4, qi & 15);
                         qv[u] = *reinterpret_cast<const uint4*>((lo ? qkl : qkh) + qpos * c2 + head * D + 8 * ch);
-                        qd[u] = lo * Q_BYTES + (ch >> 1) * 4096 + off_sw32(row, ch & 1);
+                        qd[u] = (2 * half + lo) * Q_BYTES + (ch >> 1) * 4096 + off_sw32(row, ch & 1);
                     }
                     if (r0 == 0) {
                         got = bar_wait(&q_empty, (ti & 1) ^ 1, &abort_flag, err, 17);
@@ -832,7 +856,7 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
     if (warp == 0) {
         __syncwarp();
         tcf_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(TMEM_COLS));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
     }
 }
 
@@ -841,8 +865,9 @@ static void run_tc(const float* qkv, const float* table, Dst out, const Plan& p,
                    cudaStream_t st) {
     constexpr int KH = (D + 15) / 16;
     constexpr int TR = OCA ? 39 : 31;
-    constexpr size_t bytes =
-        2 * KH * 4096 + KVS * (2 * KH * 1024 + 2 * 2048) + TR * TSTRIDE * 4 + (OCA ? 576 * 4 : 0) + 1024;
+    using Shape = AttnShape<PRE && !OCA>;
+    constexpr size_t bytes = Shape::halves * 2 * KH * 4096 + KVS * (2 * KH * 1024 + 2 * 2048) + TR * TSTRIDE * 4 +
+                             (OCA ? 576 * 4 : 0) + 1024;
     allow_dyn_smem(k_attn_tc<D, OCA, TERMS, PRE>, bytes);
     // The windows of this launch (see AttnGeom).
     AttnGeom gm;
@@ -870,13 +895,12 @@ static void run_tc(const float* qkv, const float* table, Dst out, const Plan& p,
         gm.sx = gm.mshift = shift;
         gm.yr0 = ((p.r0 - 2 * shift) % p.hp + p.hp) % p.hp;
     }
-    const long items = (long)gm.nwy * p.nx() * heads * 2;
+    const long items = (long)gm.nwy * p.nx() * heads * (2 / Shape::halves);
     int sms = 0, dev = 0;
     HAT_CUDA(cudaGetDevice(&dev));
     HAT_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     // AttnShape::ctas CTAs per SM; a multiple of the head count, so every CTA keeps one head
     // (and one bias table).
-    using Shape = AttnShape<PRE && !OCA>;
     long grid = std::min<long>(items, (long)(Shape::ctas * sms / heads) * heads);
     k_attn_tc<D, OCA, TERMS, PRE><<<(unsigned)grid, Shape::threads, bytes, st>>>(qkv, table, out, gm, c, heads,
                                                                              1.f / sqrtf((float)D), items, err);

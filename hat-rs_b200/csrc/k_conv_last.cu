@@ -56,13 +56,27 @@ __global__ void __launch_bounds__(TW * TH, 2)
     extern __shared__ float4 sm4[];
     const int x0 = blockIdx.x * TW, y0 = g.y_lo + blockIdx.y * TH;
     // Stage the input tile: pixel (r, c) of the tile is view pixel (y0 - 1 + r, x0 - 1 + c).
-    for (int i = threadIdx.x; i < SH * SW * (CL_CIN / 4); i += TW * TH) {
-        const int pix = i / (CL_CIN / 4), c4 = i % (CL_CIN / 4);
-        const int r = pix / SW, c = pix % SW;
-        const int gy = y0 - 1 + r, gx = x0 - 1 + c;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (gy >= 0 && gy < g.hgt && gx >= 0 && gx < g.wid) v = load4(x, ((long)gy * g.wid + gx) * CL_CIN + 4 * c4);
-        sm4[pix * (PS / 4) + c4] = v;
+    // Each thread issues a round's loads before any of its stores, so that a round's memory
+    // latency is paid once rather than once per 16-byte piece.
+    constexpr int PIECES = SH * SW * (CL_CIN / 4), PER = (PIECES + TW * TH - 1) / (TW * TH), RND = (PER + 1) / 2;
+#pragma unroll 1
+    for (int r0 = 0; r0 < PER; r0 += RND) {
+        float4 v[RND];
+#pragma unroll
+        for (int u = 0; u < RND; ++u) {
+            const int i = threadIdx.x + (r0 + u) * TW * TH;
+            const int pix = i / (CL_CIN / 4), c4 = i % (CL_CIN / 4);
+            const int r = pix / SW, c = pix % SW;
+            const int gy = y0 - 1 + r, gx = x0 - 1 + c;
+            v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (i < PIECES && gy >= 0 && gy < g.hgt && gx >= 0 && gx < g.wid)
+                v[u] = load4(x, ((long)gy * g.wid + gx) * CL_CIN + 4 * c4);
+        }
+#pragma unroll
+        for (int u = 0; u < RND; ++u) {
+            const int i = threadIdx.x + (r0 + u) * TW * TH;
+            if (i < PIECES) sm4[(i / (CL_CIN / 4)) * (PS / 4) + i % (CL_CIN / 4)] = v[u];
+        }
     }
     __syncthreads();
     const int tx = threadIdx.x % TW, ty = threadIdx.x / TW;

@@ -104,10 +104,11 @@ HAT_B200_API int hat_b200_get_info(const hat_b200* h, hat_b200_info* out);
  * window multiple by edge replication (src/backend.rs:71-89) and crops after
  * (src/backend.rs:94-109). n = 1 is the reference's contract; n > 1 runs the images
  * back to back on this device. Blocks until `out` is written.
- * In parity mode with fp16 operand pairs, if any operand of the pass reaches fp16's
- * range (|x| >= 65504) the whole call is redone with tf32 operand pairs and the handle
- * keeps them for later calls (hat_b200_fp16_pairs then returns 0); a strip-sharded
- * handle returns HAT_B200_ECUDA instead.
+ * If an operand of the pass reaches fp16's range (|x| >= 65504), the whole call is redone:
+ * with tf32 operand pairs when it was a GEMM operand (parity mode), and with the
+ * attention on the fp32 CUDA-core kernels when it was q, k or v (any mode); the handle
+ * keeps that setting for later calls (hat_b200_fp16_pairs then returns 0). A
+ * strip-sharded handle returns HAT_B200_ECUDA instead.
  * On a handle over several GPUs the call is split as opts->shard says and returns once
  * every GPU's part is on the host; an error on any GPU fails the call (the message names
  * the GPU). */
