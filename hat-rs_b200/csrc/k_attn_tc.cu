@@ -45,7 +45,10 @@
 // leave, and TMEM is released.
 #include <cuda_fp16.h>
 
+#include <cstring>
+
 #include "common.cuh"
+#include "umma.cuh"
 
 namespace hat {
 
@@ -197,6 +200,24 @@ __device__ __forceinline__ void tst16(uint32_t taddr, const uint32_t* r) {
 }
 __device__ __forceinline__ void tst_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// TMA tile loads into shared memory (no multicast), completing on `bar`'s transaction count.
+__device__ __forceinline__ void tma3(uint32_t dst, const CUtensorMap* m, int c0, int c1, int c2, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+        ::"r"(dst), "l"((uint64_t)m), "r"(c0), "r"(c1), "r"(c2), "r"(su(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tma4(uint32_t dst, const CUtensorMap* m, int c0, int c1, int c2, int c3, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+        "[%6];"
+        ::"r"(dst), "l"((uint64_t)m), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(su(bar))
+        : "memory");
+}
+__device__ __forceinline__ void bar_expect_tx(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su(b)), "r"(bytes) : "memory");
+}
+
 // Byte offset of the 16-byte chunk q (0 or 1) of row `row` in a SWIZZLE_32B tile of
 // 32-byte rows (16 fp16 values of K per row).
 __device__ __forceinline__ uint32_t off_sw32(int row, int q) { return row * 32 + (((q ^ (row >> 2)) & 1) << 4); }
@@ -224,7 +245,10 @@ struct AttnGeom {
 template <int D, bool OCA, int TERMS, bool PRE>
 __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE && !OCA>::ctas)
     k_attn_tc(const float* __restrict__ qkv, const float* __restrict__ table, Dst out, const AttnGeom gm, int c,
-              int heads, float scale, long items, int* err) {
+              int heads, float scale, long items, int* err, const __grid_constant__ CUtensorMap tqh,
+              const __grid_constant__ CUtensorMap tql, const __grid_constant__ CUtensorMap tkh,
+              const __grid_constant__ CUtensorMap tkl, const __grid_constant__ CUtensorMap tvh,
+              const __grid_constant__ CUtensorMap tvl) {
     const int wp = gm.wp;
     constexpr int KH = (D + 15) / 16;               // k-steps of the QK^T product (16 fp16 each)
     constexpr int NK = OCA ? 576 : 256;             // keys per window
@@ -237,7 +261,11 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
     constexpr uint32_t KV_BYTES = 2 * K_BYTES + 2 * V_BYTES;
     using Shape = AttnShape<PRE && !OCA>;
     constexpr int HV = Shape::halves;               // query halves of a work item
-    constexpr uint32_t OFF_KV = HV * 2 * Q_BYTES;
+    // Q buffers: two (the next item's Q loads while this item's last blocks run) when the
+    // window kernel's loaders use TMA, else one.
+    constexpr int QB = (PRE && !OCA) ? 2 : 1;
+    constexpr uint32_t Q_REGION = HV * 2 * Q_BYTES;  // one buffer: every half, hi and lo
+    constexpr uint32_t OFF_KV = QB * Q_REGION;
     constexpr uint32_t OFF_TAB = OFF_KV + KVS * KV_BYTES;
     constexpr uint32_t OFF_KOFF = OFF_TAB + TR * TSTRIDE * 4;
     // TMEM columns: half h's S blocks at 64h and 64h + 32 (fp32); once read, a block's first
@@ -250,8 +278,8 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
     uint8_t* sm = (uint8_t*)(((uintptr_t)raw + 1023) & ~(uintptr_t)1023);
     float* tab = reinterpret_cast<float*>(sm + OFF_TAB);
     int* koff = reinterpret_cast<int*>(sm + OFF_KOFF);  // OCAB: key (ky, kx) -> ky*48 + kx
-    __shared__ uint64_t q_full, q_empty, kv_full[KVS], kv_empty[KVS], s_full[HV][2], p_full[HV][2], o_done[HV],
-        o_free[HV][2], drain;
+    __shared__ uint64_t q_full[QB], q_empty[QB], kv_full[KVS], kv_empty[KVS], s_full[HV][2], p_full[HV][2],
+        o_done[HV], o_free[HV][2], drain;
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int abort_flag;
 
@@ -273,8 +301,10 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
     if (OCA)
         for (int i = threadIdx.x; i < NK; i += NT) koff[i] = (i / 24) * TSTRIDE + (i % 24);
     if (threadIdx.x == 0) {
-        bar_init(&q_full, NLT);
-        bar_init(&q_empty, 1);
+        for (int b = 0; b < QB; ++b) {
+            bar_init(&q_full[b], NLT);
+            bar_init(&q_empty[b], 1);
+        }
         for (int s = 0; s < KVS; ++s) {
             bar_init(&kv_full[s], NLT);
             bar_init(&kv_empty[s], 1);
@@ -300,7 +330,7 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
         // The head dim's padding (24 -> 32) is never copied: zero it once. Q and K: the second
         // 16-byte piece of k-step 1 of every row; V^T: feature rows 24..31.
         const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-        for (int i = threadIdx.x; i < HV * 2 * MT; i += NT)
+        for (int i = threadIdx.x; i < QB * HV * 2 * MT; i += NT)
             *reinterpret_cast<uint4*>(sm + (i / MT) * Q_BYTES + 4096 + off_sw32(i % MT, 1)) = z;
         for (int i = threadIdx.x; i < KVS * 2 * KBLK; i += NT) {
             const int st = i / (2 * KBLK), lo = (i / KBLK) & 1, key = i % KBLK;
@@ -326,7 +356,8 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
             uint32_t ti = 0;
             bool ok = true;
             for (long w = blockIdx.x; w < items && ok; w += gridDim.x, ++ti) {
-                if (!bar_wait(&q_full, ti & 1, &abort_flag, err, 11)) break;
+                const int qb = (int)(ti % QB);
+                if (!bar_wait(&q_full[qb], (ti / QB) & 1, &abort_flag, err, 11)) break;
                 // Each half's O block of this item's parity must have been read by the softmax.
                 for (int h = 0; h < HV && ok; ++h)
                     ok = bar_wait(&o_free[h][ti & 1], ((ti >> 1) & 1) ^ 1, &abort_flag, err, 19);
@@ -339,7 +370,7 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
                     const uint32_t kb = su(sm + OFF_KV + kvs * KV_BYTES);
 #pragma unroll
                     for (int h = 0; h < HV; ++h) {
-                        const uint32_t qh = su(sm + h * 2 * Q_BYTES), ql = qh + Q_BYTES;
+                        const uint32_t qh = su(sm + qb * Q_REGION + h * 2 * Q_BYTES), ql = qh + Q_BYTES;
                         const uint32_t d = tmem + h * 64 + s * 32;
 #pragma unroll
                         for (int k = 0; k < KH; ++k) {
@@ -369,7 +400,7 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
                             break;
                         }
                         // Once the item's last S MMAs are issued, Q may be replaced.
-                        if (j + 1 == NBLK - 1) commit(&q_empty);
+                        if (j + 1 == NBLK - 1) commit(&q_empty[qb]);
                     }
                     const int s = (int)(gb & 1);
                     const int kvs = (int)(gb % KVS);
@@ -597,7 +628,32 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
             const long rest = w / heads;
             const int win = HV == 2 ? (int)rest : (int)(rest >> 1), mtile = HV == 2 ? 0 : (int)(rest & 1);
             const int wy = win / nx, wx = win - wy * nx;
-            {
+            const int qb = (int)(ti % QB);
+            // Windows that do not wrap around the plane's edge are loaded by TMA: q|k as 4-D tiles
+            // (head dim, head, x, y) whose dims 24..31 come back as the tile's out-of-range zeros,
+            // and v^T as 3-D tiles (x, feature, y) whose rows past the head's 24 features are
+            // never read back from O. The shifted windows of the last column or row wrap around
+            // the plane and are copied by the loader threads instead.
+            const int tx0 = wx * 16 + gm.sx, ty0 = gm.oy + wy * 16 + gm.sy;
+            const bool tma = !OCA && tx0 + 16 <= wp && ty0 + 16 <= gm.rows;
+            if (tma) {
+                const bool got = bar_wait(&q_empty[qb], ((ti / QB) & 1) ^ 1, &abort_flag, err, 17);
+                if (!__all_sync(0xffffffffu, got)) break;
+                if (t == 0) {
+                    bar_expect_tx(&q_full[qb], HV * 2 * KH * 4096);
+#pragma unroll
+                    for (int h = 0; h < HV; ++h)
+#pragma unroll
+                        for (int k = 0; k < KH; ++k) {
+                            const uint32_t d = su(sm + qb * Q_REGION + 2 * h * Q_BYTES + k * 4096);
+                            const int y = ty0 + 8 * (mtile + h);
+                            tma4(d, &tqh, 16 * k, head, tx0, y, &q_full[qb]);
+                            tma4(d + Q_BYTES, &tql, 16 * k, head, tx0, y, &q_full[qb]);
+                        }
+                } else {
+                    bar_arrive(&q_full[qb]);
+                }
+            } else {
                 // Q: 768 copies per half, R at a time per thread (the first round issued before
                 // the wait)
                 bool got = true;
@@ -613,10 +669,10 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
                         const long qpos = OCA ? (long)(gm.oy + wy * 16 + (qi >> 4)) * wp + wx * 16 + (qi & 15)
                                               : pos(wy, wx, qi >> 4, qi & 15);
                         qv[u] = *reinterpret_cast<const uint4*>((lo ? qkl : qkh) + qpos * c2 + head * D + 8 * ch);
-                        qd[u] = (2 * half + lo) * Q_BYTES + (ch >> 1) * 4096 + off_sw32(row, ch & 1);
+                        qd[u] = qb * Q_REGION + (2 * half + lo) * Q_BYTES + (ch >> 1) * 4096 + off_sw32(row, ch & 1);
                     }
                     if (r0 == 0) {
-                        got = bar_wait(&q_empty, (ti & 1) ^ 1, &abort_flag, err, 17);
+                        got = bar_wait(&q_empty[qb], ((ti / QB) & 1) ^ 1, &abort_flag, err, 17);
                         if (!__all_sync(0xffffffffu, got)) break;
                     }
 #pragma unroll
@@ -624,7 +680,7 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
                 }
                 if (!__all_sync(0xffffffffu, got)) break;
                 fence_async();
-                bar_arrive(&q_full);
+                bar_arrive(&q_full[qb]);
             }
             bool ok = true;
             for (int j = 0; j < NBLK; ++j) {
@@ -633,6 +689,28 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
                 constexpr int NCOPY = OCA ? 576 : 384;  // 192 K + 384 (OCAB) or 192 V^T copies
                 bool got = true;
                 uint8_t* kvb = sm + OFF_KV + s * KV_BYTES;
+                if (tma) {
+                    got = bar_wait(&kv_empty[s], (uint32_t)(((gb / KVS) & 1) ^ 1), &abort_flag, err, 18);
+                    if (!__all_sync(0xffffffffu, got)) {
+                        ok = false;
+                        break;
+                    }
+                    if (t == 0) {
+                        bar_expect_tx(&kv_full[s], 2 * K_BYTES + 2 * V_BYTES);
+                        const uint32_t kb = su(kvb);
+                        const int y = ty0 + 2 * j;  // the block's two key rows
+#pragma unroll
+                        for (int k = 0; k < KH; ++k) {
+                            tma4(kb + k * 1024, &tkh, 16 * k, head, tx0, y, &kv_full[s]);
+                            tma4(kb + K_BYTES + k * 1024, &tkl, 16 * k, head, tx0, y, &kv_full[s]);
+                        }
+                        tma3(kb + 2 * K_BYTES, &tvh, tx0, head * D, y, &kv_full[s]);
+                        tma3(kb + 2 * K_BYTES + V_BYTES, &tvl, tx0, head * D, y, &kv_full[s]);
+                    } else {
+                        bar_arrive(&kv_full[s]);
+                    }
+                    continue;
+                }
 #pragma unroll 1
                 for (int r0 = 0; r0 < NCOPY; r0 += R * NLT) {
                 uint4 cv[R];
@@ -791,7 +869,7 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
                 if (KH > 1) load_cols(src, 16, true, qv + 16, 16);
 #pragma unroll
                 for (int i = 0; i < KH * 16; ++i) qv[i] *= scale * L2E;
-                const bool got = bar_wait(&q_empty, (ti & 1) ^ 1, &abort_flag, err, 17);
+                const bool got = bar_wait(&q_empty[0], (ti & 1) ^ 1, &abort_flag, err, 17);
                 if (!__all_sync(0xffffffffu, got)) break;
 #pragma unroll
                 for (int c8 = 0; c8 < KH * 2; ++c8) {
@@ -802,7 +880,7 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
                     if (TERMS == 3) *reinterpret_cast<uint4*>(sm + Q_BYTES + o) = lo;
                 }
                 fence_async();
-                bar_arrive(&q_full);
+                bar_arrive(&q_full[0]);
             }
             bool ok = true;
             for (int j = 0; j < NBLK; ++j) {
@@ -866,8 +944,9 @@ static void run_tc(const float* qkv, const float* table, Dst out, const Plan& p,
     constexpr int KH = (D + 15) / 16;
     constexpr int TR = OCA ? 39 : 31;
     using Shape = AttnShape<PRE && !OCA>;
-    constexpr size_t bytes = Shape::halves * 2 * KH * 4096 + KVS * (2 * KH * 1024 + 2 * 2048) + TR * TSTRIDE * 4 +
-                             (OCA ? 576 * 4 : 0) + 1024;
+    constexpr int QB = (PRE && !OCA) ? 2 : 1;
+    constexpr size_t bytes = QB * Shape::halves * 2 * KH * 4096 + KVS * (2 * KH * 1024 + 2 * 2048) +
+                             TR * TSTRIDE * 4 + (OCA ? 576 * 4 : 0) + 1024;
     allow_dyn_smem(k_attn_tc<D, OCA, TERMS, PRE>, bytes);
     // The windows of this launch (see AttnGeom).
     AttnGeom gm;
@@ -902,8 +981,32 @@ static void run_tc(const float* qkv, const float* table, Dst out, const Plan& p,
     // AttnShape::ctas CTAs per SM; a multiple of the head count, so every CTA keeps one head
     // (and one bias table).
     long grid = std::min<long>(items, (long)(Shape::ctas * sms / heads) * heads);
-    k_attn_tc<D, OCA, TERMS, PRE><<<(unsigned)grid, Shape::threads, bytes, st>>>(qkv, table, out, gm, c, heads,
-                                                                             1.f / sqrtf((float)D), items, err);
+    // TMA maps of the pre-split layout for the window kernel (see the loaders): q|k hi / lo as
+    // (head dim 24, head, x, y) with 16 x 1 x 16 x {8, 2} boxes, v^T hi / lo as (x, feature,
+    // y) with 16 x 32 x 2 boxes; 32-byte swizzled rows, fp16.
+    CUtensorMap m[6];
+    memset(m, 0, sizeof m);
+    if (PRE && !OCA) {
+        const long P = (long)p.rows * p.wp;
+        const __half* qkh = reinterpret_cast<const __half*>(qkv);
+        const __half* qkl = qkh + P * 2 * c;
+        const __half* vth = qkl + P * 2 * c;
+        const __half* vtl = vth + (long)c * P;
+        const uint64_t qdims[4] = {(uint64_t)D, (uint64_t)heads, (uint64_t)p.wp, (uint64_t)p.rows};
+        const uint64_t qstr[3] = {(uint64_t)D * 2, (uint64_t)c * 4, (uint64_t)p.wp * c * 4};
+        const uint32_t qbox[4] = {16, 1, 16, 8}, kbox[4] = {16, 1, 16, 2};
+        m[0] = tensor_map(qkh, 4, qdims, qstr, qbox, 32, true);
+        m[1] = tensor_map(qkl, 4, qdims, qstr, qbox, 32, true);
+        m[2] = tensor_map(qkh + c, 4, qdims, qstr, kbox, 32, true);
+        m[3] = tensor_map(qkl + c, 4, qdims, qstr, kbox, 32, true);
+        const uint64_t vdims[3] = {(uint64_t)p.wp, (uint64_t)c, (uint64_t)p.rows};
+        const uint64_t vstr[2] = {(uint64_t)P * 2, (uint64_t)p.wp * 2};
+        const uint32_t vbox[3] = {16, 32, 2};
+        m[4] = tensor_map(vth, 3, vdims, vstr, vbox, 32, true);
+        m[5] = tensor_map(vtl, 3, vdims, vstr, vbox, 32, true);
+    }
+    k_attn_tc<D, OCA, TERMS, PRE><<<(unsigned)grid, Shape::threads, bytes, st>>>(
+        qkv, table, out, gm, c, heads, 1.f / sqrtf((float)D), items, err, m[0], m[1], m[2], m[3], m[4], m[5]);
     HAT_CUDA(cudaGetLastError());
     count_launch();
 }

@@ -1442,6 +1442,11 @@ static CUtensorMap make_map(const void* base, int rank, const uint64_t* dims, co
     return m;
 }
 
+CUtensorMap tensor_map(const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
+                       const uint32_t* box, int rowbytes, bool h16) {
+    return make_map(base, rank, dims, strides_bytes, box, rowbytes, h16);
+}
+
 static int num_sms() {
     static int n[64] = {0};
     int dev = 0;

@@ -2,6 +2,8 @@
 // CUDA-core).
 #pragma once
 
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace hat {
@@ -52,6 +54,11 @@ void launch_prep_taps(const float* w, float* out, int cout, int cin, cudaStream_
 // Tensor-core launchers (`x.lo` required in parity mode, split the same way as the
 // weight: `x.h16 == w.h16`); return the number of
 // channel-sum partial rows written when `e.colsum` is set.
+// cuTensorMapEncodeTiled over `rank` dims (innermost first) with the given byte strides of
+// dims 1.., box and swizzle row width (128, 64, 32 or 0 bytes); fp16 elements when h16.
+CUtensorMap tensor_map(const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
+                       const uint32_t* box, int rowbytes, bool h16);
+
 long umma_linear(int mode, Opnd x, const GemmW& w, Dst y, long m, const Epi& e, int* err, cudaStream_t st);
 long umma_conv3x3(int mode, Opnd x, const GemmW& w, Dst y, int hgt, int wid, const Epi& e, int* err,
                   cudaStream_t st);
