@@ -158,10 +158,6 @@ void Engine::upload_weights() {
         auto it = wt_.st.tensors.find("conv_last.weight");
         cl_ok_ = it != wt_.st.tensors.end() && it->second.shape == std::vector<int64_t>{3, CL_CIN, 3, 3} &&
                  wt_.st.tensors.count("conv_last.bias");
-        if (cl_ok_) {
-            memcpy(cl_.w, wt_.st.f32("conv_last.weight"), sizeof cl_.w);
-            memcpy(cl_.b, wt_.st.f32("conv_last.bias"), sizeof cl_.b);
-        }
     }
     const int cmid_stride = Sizes::of(wt_, Plan::make(16, 16, wt_.window)).cmid_stride;
     tap_cab_ = 9 * wt_.compressed <= 64;
@@ -299,7 +295,7 @@ long Engine::linear_m(const std::string& wname, Opnd x, Dst y, const Epi& e, lon
 
 long Engine::conv(const std::string& wname, Opnd x, Dst y, int hgt, int wid, const Epi& e) {
     if (wname == "conv_last.weight" && e.planar_out && cl_ok_ && !simt_only_ && conv_last_ok(x, CL_CIN, 3))
-        return launch_conv_last(x, cl_, y.hi, hgt, wid, e, stream_);
+        return launch_conv_last(x, W("conv_last.weight"), W("conv_last.bias"), y.hi, hgt, wid, e, stream_);
     GemmCtx c{mode_, simt_only_, derr_};
     return gemm_conv3x3(c, x, G(wname), y, hgt, wid, e, stream_);
 }

@@ -127,9 +127,8 @@ private:
     bool h16_ = false;
     bool attn_simt_ = false;  // the attention on the fp32 CUDA-core kernels (after ERR_RANGE_ATTN)
     int fallbacks_ = 0;
-    // conv_last's weights for the bandwidth kernel (k_conv_last.cu), when its shape fits.
+    // conv_last runs on the bandwidth kernel (k_conv_last.cu) when its shape fits.
     bool cl_ok_ = false;
-    ConvLastW cl_{};
     int cmid_ld_ = 0;
     int device_ = 0, mode_ = 0;
     std::unique_ptr<Comm> comm_;

@@ -55,14 +55,15 @@ namespace hat {
 namespace {
 
 // H2 (window attention on the pre-split layout): a work item is a whole window of one head,
-// both 128-query halves, so its keys and values are copied once for 256 queries; eight softmax
-// warps (four per half, each half's S, P and O in tensor memory of its own), two copying loader
-// warps, 352 threads, two CTAs per SM (93 registers a thread). Otherwise a work item is one
+// both 128-query halves, so its keys and values are loaded once for 256 queries; eight softmax
+// warps (four per half, each half's S, P and O in tensor memory of its own), one loader warp
+// (TMA, and copies for the windows that wrap around the plane), 320 threads, two CTAs per SM
+// (96 registers a thread). Otherwise a work item is one
 // half: four softmax warps, four loader warps, 288 threads, two CTAs per SM (96 registers).
 template <bool H2>
 struct AttnShape {
     static constexpr int halves = H2 ? 2 : 1;           // query halves per work item
-    static constexpr int loaders = H2 ? 2 : 4;          // loader warps
+    static constexpr int loaders = H2 ? 1 : 4;          // loader warps
     static constexpr int softmax = 4 * halves;          // softmax warps
     static constexpr int threads = 32 * (1 + softmax + loaders);
     static constexpr int ctas = 2;                      // CTAs per SM
@@ -70,7 +71,14 @@ struct AttnShape {
 constexpr int KBLK = 32;     // keys per block
 constexpr int MT = 128;      // query rows per work item
 constexpr int KVS = 4;       // K/V pipeline stages
-constexpr int TSTRIDE = 48;  // shared bias-table row stride (floats)
+constexpr int TSTRIDE = 48;  // shared bias-table row stride (floats), OCAB
+// The window attention's table is kept as four copies, copy c shifted left by c floats,
+// rows SA_TS floats apart and copies SA_CS floats apart: the 16 biases a query meets in one
+// key row are then four aligned 16-byte loads from copy (qx mod 4), and SA_CS = 8 mod 32
+// puts the eight lanes of a load phase on distinct 16-byte bank groups.
+constexpr int SA_TS = 32, SA_CS = 1000;
+template <bool OCA>
+constexpr int tab_floats() { return OCA ? 39 * TSTRIDE : 4 * SA_CS; }
 constexpr float RESCALE_LOG2 = 8.f;
 constexpr float P_SHIFT = 6.f;
 constexpr float F16_LIMIT = 65504.f;  // the largest finite fp16
@@ -267,7 +275,7 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
     constexpr uint32_t Q_REGION = HV * 2 * Q_BYTES;  // one buffer: every half, hi and lo
     constexpr uint32_t OFF_KV = QB * Q_REGION;
     constexpr uint32_t OFF_TAB = OFF_KV + KVS * KV_BYTES;
-    constexpr uint32_t OFF_KOFF = OFF_TAB + TR * TSTRIDE * 4;
+    constexpr uint32_t OFF_KOFF = OFF_TAB + tab_floats<OCA>() * 4;
     // TMEM columns: half h's S blocks at 64h and 64h + 32 (fp32); once read, a block's first
     // 16 columns hold P_hi and the next 16 P_lo (fp16 pairs); half h's O (per item parity)
     // at 64 HV + 64h and 64 HV + 64h + 32.
@@ -288,15 +296,23 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
     const int nx = wp / 16;
     const long c3 = 3L * c;
 
-    // Bias table of this head, rows TSTRIDE apart. SA: tab[r][s] = table[r*31 + s], the
-    // bias of (qy - ky + 15, qx - kx + 15). OCAB: tab[r][s] is the bias of key - query
-    // offset (r - 22, s - 22), i.e. table[((r - 22)*39 + (s - 22)) mod 1521].
+    // Bias table of this head (in log2 units). SA: copy c holds tab_c[r*SA_TS + s - c] =
+    // table[r*31 + s], the bias of (qy - ky + 15, qx - kx + 15). OCAB: tab[r][s], rows
+    // TSTRIDE apart, is the bias of key - query offset (r - 22, s - 22), i.e.
+    // table[((r - 22)*39 + (s - 22)) mod 1521].
     constexpr int NT = Shape::threads, NLT = 32 * Shape::loaders, LW0 = 1 + Shape::softmax;  // first loader warp
-    for (int i = threadIdx.x; i < TR * TR; i += NT) {
-        const int r = i / TR, s = i - r * TR;
-        int src = OCA ? (r - 22) * TW + (s - 22) : r * TW + s;
-        if (src < 0) src += TR * TW;
-        tab[r * TSTRIDE + s] = table[(long)src * heads + head] * L2E;
+    if (OCA) {
+        for (int i = threadIdx.x; i < TR * TR; i += NT) {
+            const int r = i / TR, s = i - r * TR;
+            int src = (r - 22) * TW + (s - 22);
+            if (src < 0) src += TR * TW;
+            tab[r * TSTRIDE + s] = table[(long)src * heads + head] * L2E;
+        }
+    } else {
+        for (int i = threadIdx.x; i < 4 * SA_CS; i += NT) {
+            const int c = i / SA_CS, at = i - c * SA_CS + c, r = at / SA_TS, s = at - r * SA_TS;
+            tab[i] = r < TR && s < TR ? table[(long)(r * TW + s) * heads + head] * L2E : 0.f;
+        }
     }
     if (OCA)
         for (int i = threadIdx.x; i < NK; i += NT) koff[i] = (i / 24) * TSTRIDE + (i % 24);
@@ -336,10 +352,14 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
             const int st = i / (2 * KBLK), lo = (i / KBLK) & 1, key = i % KBLK;
             *reinterpret_cast<uint4*>(sm + OFF_KV + st * KV_BYTES + lo * K_BYTES + 1024 + off_sw32(key, 1)) = z;
         }
+        // V^T row 24 of the hi tile is all ones (fp16 1.0) and every other padding row zero: the
+        // PV product then leaves the row sum of P in column 24 of O (P_lo.1 + P_hi.1 + P_hi.0),
+        // accumulated and rescaled along with O.
+        const uint4 one = make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);
         for (int i = threadIdx.x; i < KVS * 2 * 8 * 4; i += NT) {
             const int st = i / 64, lo = (i / 32) & 1, f = 24 + ((i / 4) & 7), ks = (i / 2) & 1, pc = i & 1;
             *reinterpret_cast<uint4*>(sm + OFF_KV + st * KV_BYTES + 2 * K_BYTES + lo * V_BYTES + ks * 1024 +
-                                      off_sw32(f, pc)) = z;
+                                      off_sw32(f, pc)) = (f == 24 && !lo) ? one : z;
         }
         fence_async();
     }
@@ -455,9 +475,8 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
             const bool masked = !OCA && gm.mshift > 0;
             const int shift = gm.mshift, ghp = gm.ghp;
             const int yrw = gm.yr0 + wy * 16;  // rolled-frame row of the window's first row (mod ghp)
-            // Bias of key (ky, kx): SA tab[(qy-ky+15)*48 + (qx-kx+15)] = tab[A0 - (ky*48 + kx)];
-            // OCAB tab[(ky-qy+15)*48 + (kx-qx+15)] = tab[koff[k] - B0].
-            const int A0 = qy * TSTRIDE + qx + 15 * TSTRIDE + 15, B0 = qy * TSTRIDE + qx - 15 * TSTRIDE - 15;
+            // OCAB bias of key k = (ky, kx): tab[(ky-qy+15)*48 + (kx-qx+15)] = tab[koff[k] - B0].
+            const int B0 = qy * TSTRIDE + qx - 15 * TSTRIDE - 15;
             // Shift mask: key column kx is masked against target label t when
             // band(wx*16+kx) != t; one 16-bit mask per possible row band.
             uint32_t cm[3] = {0, 0, 0};
@@ -492,21 +511,46 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
                     mrow0 = b0 == 0 ? cm[0] : (b0 == 1 ? cm[1] : cm[2]);  // selects: no local memory
                     mrow1 = b1 == 0 ? cm[0] : (b1 == 1 ? cm[1] : cm[2]);
                 }
-                const float* trow_sa = tab + (A0 - 2 * TSTRIDE * j);  // SA: minus (k>>4)*48 + (k&15)
+                if (OCA) {
 #pragma unroll
-                for (int k = 0; k < 32; ++k) {
-                    float v;
-                    if (OCA) {
-                        v = sv[k] + tab[koff[j * KBLK + k] - B0];
-                    } else {
-                        v = sv[k] + trow_sa[-((k >> 4) * TSTRIDE + (k & 15))];
+                    for (int k = 0; k < 32; ++k) sv[k] += tab[koff[j * KBLK + k] - B0];
+                } else if (!PRE) {
+                    // tab[(ky - ... )]: scalar loads from copy 0 (even query rows) or copy 2 (odd
+                    // ones), which keeps the two half-warps apart in the banks but for two lanes
+                    const int cp = (qy & 1) * 2;
+                    const float* t0 = tab + cp * SA_CS + (qy + 15 - 2 * j) * SA_TS + qx + 15 - cp;
+#pragma unroll
+                    for (int k = 0; k < 32; ++k) {
+                        sv[k] += t0[-(k >> 4) * SA_TS - (k & 15)];
                         if (masked) {
                             const uint32_t mr = (k >> 4) ? mrow1 : mrow0;
-                            if ((mr >> (k & 15)) & 1u) v += -100.f * L2E;
+                            if ((mr >> (k & 15)) & 1u) sv[k] += -100.f * L2E;
                         }
                     }
-                    sv[k] = v;  // log2 units: q carries scale * log2(e), the table log2(e)
+                } else {
+                    // key row ky = 2j + kyl: the biases for kx = 15 .. 0 are 16 consecutive
+                    // floats of copy (qx mod 4), four aligned 16-byte loads
+                    const float4* b4 = reinterpret_cast<const float4*>(tab + (qx & 3) * SA_CS) +
+                                       (qy + 15 - 2 * j) * (SA_TS / 4) + (qx >> 2);
+#pragma unroll
+                    for (int kyl = 0; kyl < 2; ++kyl)
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            const float4 t = b4[q - kyl * (SA_TS / 4)];
+                            sv[kyl * 16 + 15 - 4 * q] += t.x;
+                            sv[kyl * 16 + 14 - 4 * q] += t.y;
+                            sv[kyl * 16 + 13 - 4 * q] += t.z;
+                            sv[kyl * 16 + 12 - 4 * q] += t.w;
+                        }
+                    if (masked) {
+#pragma unroll
+                        for (int k = 0; k < 32; ++k) {
+                            const uint32_t mr = (k >> 4) ? mrow1 : mrow0;
+                            if ((mr >> (k & 15)) & 1u) sv[k] += -100.f * L2E;
+                        }
+                    }
                 }
+                // sv is in log2 units: q carries scale * log2(e), the table log2(e)
                 // the block max: 16 three-input maxes
                 float bmax = fmaxf(sv[0], sv[1]);
 #pragma unroll
@@ -526,12 +570,12 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
 #pragma unroll
                 for (int k = 0; k < 32; k += 2) {
                     const float p0 = ex2(sv[k] - mo), p1 = ex2(sv[k + 1] - mo);
-                    psum += p0 + p1;
+                    if (!PRE) psum += p0 + p1;  // PRE: the row sum comes from O's column 24
                     split_h16x2(p0, p1, ph[k >> 1], pl[k >> 1]);
                 }
                 tst16(tmem + trow + th + s * 32, ph);
                 if (TERMS == 3) tst16(tmem + trow + th + s * 32 + T_PLO, pl);
-                l += psum;
+                if (!PRE) l += psum;
                 if (j > 0) {
                     // PV of the previous block has finished (this also keeps every
                     // o_done phase consumed in order); a moved max then rescales the
@@ -563,7 +607,7 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
             tld32(t_o, ov);
             tcf_before();
             bar_arrive(&o_free[hh][ti & 1]);
-            const float inv = 1.f / l;
+            const float inv = 1.f / (PRE ? ov[24] : l);
             const int qrow = OCA ? gm.oy + wy * 16 + qy : (gm.oy + wy * 16 + qy + gm.sy) % gm.rows;
             const long qpos = (long)qrow * wp + (OCA ? wx * 16 + qx : (wx * 16 + qx + gm.sx) % wp);
             const long ob = qpos * c + (long)head * D;
@@ -696,7 +740,7 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
                         break;
                     }
                     if (t == 0) {
-                        bar_expect_tx(&kv_full[s], 2 * K_BYTES + 2 * V_BYTES);
+                        bar_expect_tx(&kv_full[s], 2 * K_BYTES + 4 * 768);
                         const uint32_t kb = su(kvb);
                         const int y = ty0 + 2 * j;  // the block's two key rows
 #pragma unroll
@@ -704,8 +748,13 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
                             tma4(kb + k * 1024, &tkh, 16 * k, head, tx0, y, &kv_full[s]);
                             tma4(kb + K_BYTES + k * 1024, &tkl, 16 * k, head, tx0, y, &kv_full[s]);
                         }
-                        tma3(kb + 2 * K_BYTES, &tvh, tx0, head * D, y, &kv_full[s]);
-                        tma3(kb + 2 * K_BYTES + V_BYTES, &tvl, tx0, head * D, y, &kv_full[s]);
+                        // v^T: per key row, the head's 24 feature rows of a 16-key k-step (768
+                        // bytes); rows 24..31 keep their ones / zeros
+#pragma unroll
+                        for (int ks = 0; ks < 2; ++ks) {
+                            tma3(kb + 2 * K_BYTES + ks * 1024, &tvh, tx0, head * D, y + ks, &kv_full[s]);
+                            tma3(kb + 2 * K_BYTES + V_BYTES + ks * 1024, &tvl, tx0, head * D, y + ks, &kv_full[s]);
+                        }
                     } else {
                         bar_arrive(&kv_full[s]);
                     }
@@ -946,7 +995,7 @@ static void run_tc(const float* qkv, const float* table, Dst out, const Plan& p,
     using Shape = AttnShape<PRE && !OCA>;
     constexpr int QB = (PRE && !OCA) ? 2 : 1;
     constexpr size_t bytes = QB * Shape::halves * 2 * KH * 4096 + KVS * (2 * KH * 1024 + 2 * 2048) +
-                             TR * TSTRIDE * 4 + (OCA ? 576 * 4 : 0) + 1024;
+                             tab_floats<OCA>() * 4 + (OCA ? 576 * 4 : 0) + 1024;
     allow_dyn_smem(k_attn_tc<D, OCA, TERMS, PRE>, bytes);
     // The windows of this launch (see AttnGeom).
     AttnGeom gm;
@@ -1001,7 +1050,7 @@ static void run_tc(const float* qkv, const float* table, Dst out, const Plan& p,
         m[3] = tensor_map(qkl + c, 4, qdims, qstr, kbox, 32, true);
         const uint64_t vdims[3] = {(uint64_t)p.wp, (uint64_t)c, (uint64_t)p.rows};
         const uint64_t vstr[2] = {(uint64_t)P * 2, (uint64_t)p.wp * 2};
-        const uint32_t vbox[3] = {16, 32, 2};
+        const uint32_t vbox[3] = {16, 24, 1};
         m[4] = tensor_map(vth, 3, vdims, vstr, vbox, 32, true);
         m[5] = tensor_map(vtl, 3, vdims, vstr, vbox, 32, true);
     }

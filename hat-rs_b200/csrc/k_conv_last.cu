@@ -5,10 +5,13 @@
 // N = 3 leaves a tensor-core tile almost empty, and the implicit GEMM reads each input
 // pixel once per tap (nine times, from L2). This kernel is a bandwidth kernel instead:
 // a CTA stages an 8 x 32 output tile's (8+2) x (32+2) input pixels, all 64 channels, as
-// fp32 in shared memory (the hi + lo pair summed, so the arithmetic is fp32), each thread
-// computes one output pixel's 3 channels with fp32 FMAs, and the 1728 weights ride in the
-// kernel's parameters, where every FMA takes its weight straight from the constant bank.
-// Per output pixel it reads 256 bytes of input (x1.33 for the halo) and writes 12.
+// fp32 in shared memory (the hi + lo pair summed, so the arithmetic is fp32), and each
+// thread computes one output pixel's 3 channels with fp32 FMAs. The 1728 weights sit in
+// shared memory too, ordered (tap, 4 input channels, output channel, 4) so that the 12
+// weights one input float4 meets are three broadcast 16-byte loads. (Weights as kernel
+// parameters, read as constant operands, measured 1.8 ms a launch at 2048x2048: the
+// constant cache could not hold the 6.9 KB.) Per output pixel it reads 256 bytes of input
+// (x1.33 for the halo) and writes 12.
 #include "common.cuh"
 #include "conv_last.h"
 
@@ -19,7 +22,8 @@ namespace {
 constexpr int TW = 32, TH = 8;            // output tile: columns x rows (one thread per pixel)
 constexpr int SW = TW + 2, SH = TH + 2;   // staged input tile with the 3x3 halo
 constexpr int PS = CL_CIN + 4;            // floats per staged pixel: 68 keeps LDS.128 conflict-free
-constexpr size_t SMEM = (size_t)SH * SW * PS * sizeof(float);
+constexpr int NW = 3 * CL_CIN * 9;          // weights
+constexpr size_t SMEM = ((size_t)SH * SW * PS + NW) * sizeof(float);
 
 struct Geo {
     int hgt, wid;       // the input view (rows outside it are the conv's zero padding)
@@ -52,9 +56,15 @@ __device__ __forceinline__ float4 load4(const Opnd& x, long e) {
 }
 
 __global__ void __launch_bounds__(TW * TH, 2)
-    k_conv_last(const Opnd x, const ConvLastW p, float* __restrict__ out, const Geo g) {
+    k_conv_last(const Opnd x, const float* __restrict__ w, const float* __restrict__ bias, float* __restrict__ out,
+                const Geo g) {
     extern __shared__ float4 sm4[];
+    float4* wsm = sm4 + SH * SW * (PS / 4);  // [tap][ci / 4][co][4]
     const int x0 = blockIdx.x * TW, y0 = g.y_lo + blockIdx.y * TH;
+    for (int i = threadIdx.x; i < NW; i += TW * TH) {
+        const int co = i / (CL_CIN * 9), r = i - co * CL_CIN * 9, ci = r / 9, tap = r - ci * 9;  // [co][ci][ky][kx]
+        reinterpret_cast<float*>(wsm)[((tap * (CL_CIN / 4) + ci / 4) * 3 + co) * 4 + (ci & 3)] = w[i];
+    }
     // Stage the input tile: pixel (r, c) of the tile is view pixel (y0 - 1 + r, x0 - 1 + c).
     // Each thread issues a round's loads before any of its stores, so that a round's memory
     // latency is paid once rather than once per 16-byte piece.
@@ -82,23 +92,19 @@ __global__ void __launch_bounds__(TW * TH, 2)
     const int tx = threadIdx.x % TW, ty = threadIdx.x / TW;
     const int oy = y0 + ty, ox = x0 + tx;
     if (oy >= g.y_hi || ox >= g.wid) return;
-    float a0 = p.b[0], a1 = p.b[1], a2 = p.b[2];
+    float a0 = bias[0], a1 = bias[1], a2 = bias[2];
 #pragma unroll
     for (int ky = 0; ky < 3; ++ky)
 #pragma unroll
         for (int kx = 0; kx < 3; ++kx) {
             const float4* px = sm4 + ((ty + ky) * SW + tx + kx) * (PS / 4);
-#pragma unroll
+            const float4* wt = wsm + (ky * 3 + kx) * (CL_CIN / 4) * 3;
+#pragma unroll 4
             for (int c4 = 0; c4 < CL_CIN / 4; ++c4) {
-                const float4 v = px[c4];
-                const float vv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int k = (4 * c4 + i) * 9 + ky * 3 + kx;  // [co][ci][ky][kx]
-                    a0 = fmaf(vv[i], p.w[k], a0);
-                    a1 = fmaf(vv[i], p.w[CL_CIN * 9 + k], a1);
-                    a2 = fmaf(vv[i], p.w[2 * CL_CIN * 9 + k], a2);
-                }
+                const float4 v = px[c4], w0 = wt[3 * c4], w1 = wt[3 * c4 + 1], w2 = wt[3 * c4 + 2];
+                a0 = fmaf(v.x, w0.x, fmaf(v.y, w0.y, fmaf(v.z, w0.z, fmaf(v.w, w0.w, a0))));
+                a1 = fmaf(v.x, w1.x, fmaf(v.y, w1.y, fmaf(v.z, w1.z, fmaf(v.w, w1.w, a1))));
+                a2 = fmaf(v.x, w2.x, fmaf(v.y, w2.y, fmaf(v.z, w2.z, fmaf(v.w, w2.w, a2))));
             }
         }
     const int gy = oy + g.oy0;
@@ -118,7 +124,7 @@ bool conv_last_ok(const Opnd& x, int cin, int cout) {
     return (a & 15) == 0;
 }
 
-long launch_conv_last(const Opnd& x, const ConvLastW& w, float* out, int hgt, int wid, const Epi& e,
+long launch_conv_last(const Opnd& x, const float* w, const float* bias, float* out, int hgt, int wid, const Epi& e,
                       cudaStream_t st) {
     Geo g;
     g.hgt = hgt;
@@ -133,7 +139,7 @@ long launch_conv_last(const Opnd& x, const ConvLastW& w, float* out, int hgt, in
     if (g.y_hi <= g.y_lo) return 0;
     allow_dyn_smem(k_conv_last, SMEM);
     dim3 grid((unsigned)((wid + TW - 1) / TW), (unsigned)((g.y_hi - g.y_lo + TH - 1) / TH));
-    k_conv_last<<<grid, TW * TH, SMEM, st>>>(x, w, out, g);
+    k_conv_last<<<grid, TW * TH, SMEM, st>>>(x, w, bias, out, g);
     HAT_CUDA(cudaGetLastError());
     count_launch();
     return 0;
