@@ -269,9 +269,10 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
     constexpr uint32_t KV_BYTES = 2 * K_BYTES + 2 * V_BYTES;
     using Shape = AttnShape<PRE && !OCA>;
     constexpr int HV = Shape::halves;               // query halves of a work item
-    // Q buffers: two (the next item's Q loads while this item's last blocks run) when the
-    // window kernel's loaders use TMA, else one.
-    constexpr int QB = (PRE && !OCA) ? 2 : 1;
+    // Q buffers. One: a second (the next item's Q loading while this item's last key blocks
+    // run) measured no faster with three K/V stages, and with four it left room for only one
+    // CTA per SM (12.3 ms per pass -> 18.6 ms).
+    constexpr int QB = 1;
     constexpr uint32_t Q_REGION = HV * 2 * Q_BYTES;  // one buffer: every half, hi and lo
     constexpr uint32_t OFF_KV = QB * Q_REGION;
     constexpr uint32_t OFF_TAB = OFF_KV + KVS * KV_BYTES;
@@ -993,7 +994,7 @@ static void run_tc(const float* qkv, const float* table, Dst out, const Plan& p,
     constexpr int KH = (D + 15) / 16;
     constexpr int TR = OCA ? 39 : 31;
     using Shape = AttnShape<PRE && !OCA>;
-    constexpr int QB = (PRE && !OCA) ? 2 : 1;
+    constexpr int QB = 1;  // Q buffers (see the kernel)
     constexpr size_t bytes = QB * Shape::halves * 2 * KH * 4096 + KVS * (2 * KH * 1024 + 2 * 2048) +
                              tab_floats<OCA>() * 4 + (OCA ? 576 * 4 : 0) + 1024;
     allow_dyn_smem(k_attn_tc<D, OCA, TERMS, PRE>, bytes);
