@@ -268,6 +268,9 @@ Engine::~Engine() {
     if (dweights_) cudaFree(dweights_);
     if (derr_) cudaFree(derr_);
     if (join_) cudaEventDestroy(join_);
+    for (cudaEvent_t ev : {ev_fork_, ev_halo_, ev_ca_})
+        if (ev) cudaEventDestroy(ev);
+    if (cstream_) cudaStreamDestroy(cstream_);
     if (stream_) cudaStreamDestroy(stream_);
 }
 
@@ -329,11 +332,20 @@ void Engine::attach_strip(int rank, int n, const void* id, size_t idlen) {
     }
     have_plan_ = false;
     comm_.reset(new Comm(rank, n, id, idlen, device_));
+    if (!cstream_) {
+        HAT_CUDA(cudaStreamCreateWithFlags(&cstream_, cudaStreamNonBlocking));
+        HAT_CUDA(cudaEventCreateWithFlags(&ev_fork_, cudaEventDisableTiming));
+        HAT_CUDA(cudaEventCreateWithFlags(&ev_halo_, cudaEventDisableTiming));
+        HAT_CUDA(cudaEventCreateWithFlags(&ev_ca_, cudaEventDisableTiming));
+    }
 }
 
-void Engine::exchange(float* plane, int ch, int res, int n) { exchange_rows(plane, (long)plan_.wp * res * ch, res, n); }
+void Engine::exchange(float* plane, int ch, int res, int n, cudaStream_t st) {
+    exchange_rows(plane, (long)plan_.wp * res * ch, res, n, st);
+}
 
-void Engine::exchange_rows(float* plane, long rowf, int res, int n) {
+void Engine::exchange_rows(float* plane, long rowf, int res, int n, cudaStream_t st) {
+    if (!st) st = stream_;
     if (!comm_) return;
     const Plan& p = plan_;
     if (n > p.halo * res) throw Error(1, "exchange: more rows than the halo holds");
@@ -343,10 +355,10 @@ void Engine::exchange_rows(float* plane, long rowf, int res, int n) {
     // Matched per peer in posting order: a rank's first send (its top rows, to `up`) is
     // the up rank's first receive (from its `down`), and likewise for the second pair.
     comm_->group_start();
-    comm_->send(plane + top * rowf, n * rowf, up, stream_);
-    comm_->send(plane + (bot - n) * rowf, n * rowf, down, stream_);
-    comm_->recv(plane + bot * rowf, n * rowf, down, stream_);
-    comm_->recv(plane + (top - n) * rowf, n * rowf, up, stream_);
+    comm_->send(plane + top * rowf, n * rowf, up, st);
+    comm_->send(plane + (bot - n) * rowf, n * rowf, down, st);
+    comm_->recv(plane + bot * rowf, n * rowf, down, st);
+    comm_->recv(plane + (top - n) * rowf, n * rowf, up, st);
     comm_->group_end();
 }
 
@@ -583,10 +595,25 @@ void Engine::hab(int stage, int blk, const float* in, float* out) {
     const int c = wt_.embed, cc = wt_.compressed;
     const std::string p = "layers." + std::to_string(stage) + ".residual_group.blocks." + std::to_string(blk);
     const std::string cb = p + ".conv_block.cab";
-    // Sharded: the block input's halo rows (the shifted windows reach 8 rows out).
-    exchange(const_cast<float*>(in), c, 1, plan_.halo);
     mark("layernorm", 0, 8.0 * P * c);
-    launch_layernorm(in, W(p + ".norm1.weight"), W(p + ".norm1.bias"), D(a_->n1, a_->n1lo), P, c, stream_);
+    const float *g1 = W(p + ".norm1.weight"), *b1 = W(p + ".norm1.bias");
+    if (comm_) {
+        // Sharded: the block input's halo rows (the shifted windows reach 8 rows out) travel on
+        // the communication stream while LayerNorm runs over the strip's own rows; the halo rows'
+        // LayerNorm follows once they have arrived.
+        const long t0 = own_t0(), Po = own_tokens(), rowt = plan_.wp;
+        HAT_CUDA(cudaEventRecord(ev_fork_, stream_));
+        HAT_CUDA(cudaStreamWaitEvent(cstream_, ev_fork_, 0));
+        exchange(const_cast<float*>(in), c, 1, plan_.halo, cstream_);
+        HAT_CUDA(cudaEventRecord(ev_halo_, cstream_));
+        launch_layernorm(in + t0 * c, g1, b1, dst_at(D(a_->n1, a_->n1lo), t0 * c), Po, c, stream_);
+        HAT_CUDA(cudaStreamWaitEvent(stream_, ev_halo_, 0));
+        const long tb = t0 + Po, nb = P - tb;  // the bottom halo rows
+        launch_layernorm(in, g1, b1, D(a_->n1, a_->n1lo), (long)plan_.halo * rowt, c, stream_);
+        launch_layernorm(in + tb * c, g1, b1, dst_at(D(a_->n1, a_->n1lo), tb * c), nb, c, stream_);
+    } else {
+        launch_layernorm(in, g1, b1, D(a_->n1, a_->n1lo), P, c, stream_);
+    }
     // CAB: conv c→cc + GELU; conv cc→c with per-tile channel sums of its output; the gate.
     Epi ec1;
     ec1.bias = W(cb + ".0.bias");
@@ -613,20 +640,20 @@ void Engine::hab(int stage, int blk, const float* in, float* out) {
     mark("conv.cab2", 18.0 * P * c * cc, 4.0 * P * (c + cc));
     long rows = conv_res(cb + ".2.weight", O(a_->cmid, a_->cmidlo), cmid_ld_, Dst{a_->convx, nullptr}, c, 1,
                          false, ec2);
-    mark("ca_gate", 0, 4.0 * rows * c);
     // The pool averages over the whole padded plane (src/gpu.rs:435); sharded, the
-    // strips' channel sums are added across ranks first.
+    // strips' channel sums are added across ranks first, on the communication stream while
+    // the qkv linear and the attention run (the gate is first needed by proj).
     const float inv_count = 1.f / (float)((long)plan_.hp * plan_.wp);
     const float* pooled = a_->chsum;
     if (comm_) {
         launch_rowsum(a_->chsum, rows, c, a_->casum, stream_);
-        comm_->allreduce_sum(a_->casum, c, stream_);
+        HAT_CUDA(cudaEventRecord(ev_fork_, stream_));
+        HAT_CUDA(cudaStreamWaitEvent(cstream_, ev_fork_, 0));
+        comm_->allreduce_sum(a_->casum, c, cstream_);
+        HAT_CUDA(cudaEventRecord(ev_ca_, cstream_));
         pooled = a_->casum;
         rows = 1;
     }
-    launch_ca_gate(pooled, rows, inv_count, W(cb + ".3.attention.1.weight"), W(cb + ".3.attention.1.bias"),
-                   W(cb + ".3.attention.3.weight"), W(cb + ".3.attention.3.bias"), a_->gate, c, wt_.squeezed,
-                   stream_);
     // Attention on the normed plane; odd blocks are shifted by win/2 with the mask. With fp16
     // operand pairs and head dim 24, the qkv linear writes q (pre-scaled by scale * log2(e)),
     // k and v^T as the pairs the attention kernel copies (Epi::qkv_split).
@@ -644,6 +671,12 @@ void Engine::hab(int stage, int blk, const float* in, float* out) {
     mark("attn.window", 4.0 * P * 256 * c, 16.0 * P * c);
     launch_window_attention(mode_, simt_only_ || attn_simt_, a_->qkv, W(p + ".attn.relative_position_bias_table"),
                             D(a_->attn, a_->attnlo), plan_, c, wt_.heads, shift, derr_, stream_, pre);
+    // The channel-attention gate.
+    mark("ca_gate", 0, 4.0 * rows * c);
+    if (comm_) HAT_CUDA(cudaStreamWaitEvent(stream_, ev_ca_, 0));
+    launch_ca_gate(pooled, rows, inv_count, W(cb + ".3.attention.1.weight"), W(cb + ".3.attention.1.bias"),
+                   W(cb + ".3.attention.3.weight"), W(cb + ".3.attention.3.bias"), a_->gate, c, wt_.squeezed,
+                   stream_);
     // proj, then `(shortcut + attn) + conv_x * conv_scale` in the epilogue.
     // (over the strip's own rows when sharded: the next block exchanges the halo rows)
     const long t0 = own_t0(), Po = own_tokens();

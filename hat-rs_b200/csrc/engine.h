@@ -79,7 +79,7 @@ private:
     // times the base resolution) from the neighbours' own rows; top and bottom ranks
     // wrap around to each other (what the shifted windows need; elsewhere the rows
     // beyond the image are never read as data). No-op when not sharded.
-    void exchange(float* plane, int ch, int res, int n);
+    void exchange(float* plane, int ch, int res, int n, cudaStream_t st = nullptr);
     void exchange(Dst d, int ch, int res, int n);
     // A 3x3 conv over a plane at `res` times the base resolution. Sharded, the input is
     // read over the local rows that hold image data (the halo rows beyond the image's
@@ -112,7 +112,7 @@ private:
     }
     Opnd O(const float* hi, const float* lo) const { return split() ? Opnd{hi, lo, h16_} : Opnd{hi, nullptr, false}; }
     // Halo rows of a plane of `rowf` floats per row at `res` times the base resolution.
-    void exchange_rows(float* plane, long rowf, int res, int n);
+    void exchange_rows(float* plane, long rowf, int res, int n, cudaStream_t st = nullptr);
 
     Weights wt_;
     // The CAB's first conv as a per-tap linear + tap sum when its output is narrow
@@ -133,6 +133,10 @@ private:
     int device_ = 0, mode_ = 0;
     std::unique_ptr<Comm> comm_;
     double timeout_s_ = 120.0;
+    // Sharded: a second stream for the collectives that overlap compute (the HABs' halo
+    // exchange and channel-sum all-reduce), joined back by events.
+    cudaStream_t cstream_ = nullptr;
+    cudaEvent_t ev_fork_ = nullptr, ev_halo_ = nullptr, ev_ca_ = nullptr;
     bool use_graph_ = true, simt_only_ = false;
     cudaStream_t stream_ = nullptr;
     cudaEvent_t join_ = nullptr;

@@ -71,14 +71,16 @@ struct AttnShape {
 constexpr int KBLK = 32;     // keys per block
 constexpr int MT = 128;      // query rows per work item
 constexpr int KVS = 4;       // K/V pipeline stages
-constexpr int TSTRIDE = 48;  // shared bias-table row stride (floats), OCAB
 // The window attention's table is kept as four copies, copy c shifted left by c floats,
 // rows SA_TS floats apart and copies SA_CS floats apart: the 16 biases a query meets in one
 // key row are then four aligned 16-byte loads from copy (qx mod 4), and SA_CS = 8 mod 32
 // puts the eight lanes of a load phase on distinct 16-byte bank groups.
 constexpr int SA_TS = 32, SA_CS = 1000;
+// The OCAB's 39 x 39 table the same way: rows OCA_TS apart, copies OCA_CS (= 8 mod 32) apart;
+// a block's 32 keys are four runs of 8 keys within one key row, two aligned loads each.
+constexpr int OCA_TS = 40, OCA_CS = 1576;
 template <bool OCA>
-constexpr int tab_floats() { return OCA ? 39 * TSTRIDE : 4 * SA_CS; }
+constexpr int tab_floats() { return OCA ? 4 * OCA_CS : 4 * SA_CS; }
 constexpr float RESCALE_LOG2 = 8.f;
 constexpr float P_SHIFT = 6.f;
 constexpr float F16_LIMIT = 65504.f;  // the largest finite fp16
@@ -276,7 +278,7 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
     constexpr uint32_t Q_REGION = HV * 2 * Q_BYTES;  // one buffer: every half, hi and lo
     constexpr uint32_t OFF_KV = QB * Q_REGION;
     constexpr uint32_t OFF_TAB = OFF_KV + KVS * KV_BYTES;
-    constexpr uint32_t OFF_KOFF = OFF_TAB + tab_floats<OCA>() * 4;
+
     // TMEM columns: half h's S blocks at 64h and 64h + 32 (fp32); once read, a block's first
     // 16 columns hold P_hi and the next 16 P_lo (fp16 pairs); half h's O (per item parity)
     // at 64 HV + 64h and 64 HV + 64h + 32.
@@ -286,7 +288,6 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
     extern __shared__ __align__(1024) uint8_t raw[];
     uint8_t* sm = (uint8_t*)(((uintptr_t)raw + 1023) & ~(uintptr_t)1023);
     float* tab = reinterpret_cast<float*>(sm + OFF_TAB);
-    int* koff = reinterpret_cast<int*>(sm + OFF_KOFF);  // OCAB: key (ky, kx) -> ky*48 + kx
     __shared__ uint64_t q_full[QB], q_empty[QB], kv_full[KVS], kv_empty[KVS], s_full[HV][2], p_full[HV][2],
         o_done[HV], o_free[HV][2], drain;
     __shared__ uint32_t tmem_slot;
@@ -297,26 +298,24 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
     const int nx = wp / 16;
     const long c3 = 3L * c;
 
-    // Bias table of this head (in log2 units). SA: copy c holds tab_c[r*SA_TS + s - c] =
-    // table[r*31 + s], the bias of (qy - ky + 15, qx - kx + 15). OCAB: tab[r][s], rows
-    // TSTRIDE apart, is the bias of key - query offset (r - 22, s - 22), i.e.
-    // table[((r - 22)*39 + (s - 22)) mod 1521].
+    // Bias table of this head (in log2 units), as four copies, copy c shifted left by c
+    // floats. SA: tab_c[r*SA_TS + s - c] = table[r*31 + s], the bias of (qy - ky + 15,
+    // qx - kx + 15). OCAB: tab_c[r*OCA_TS + s - c] is the bias of key - query offset
+    // (r - 22, s - 22), i.e. table[((r - 22)*39 + (s - 22)) mod 1521].
     constexpr int NT = Shape::threads, NLT = 32 * Shape::loaders, LW0 = 1 + Shape::softmax;  // first loader warp
-    if (OCA) {
-        for (int i = threadIdx.x; i < TR * TR; i += NT) {
-            const int r = i / TR, s = i - r * TR;
-            int src = (r - 22) * TW + (s - 22);
-            if (src < 0) src += TR * TW;
-            tab[r * TSTRIDE + s] = table[(long)src * heads + head] * L2E;
-        }
-    } else {
-        for (int i = threadIdx.x; i < 4 * SA_CS; i += NT) {
-            const int c = i / SA_CS, at = i - c * SA_CS + c, r = at / SA_TS, s = at - r * SA_TS;
-            tab[i] = r < TR && s < TR ? table[(long)(r * TW + s) * heads + head] * L2E : 0.f;
+    {
+        constexpr int TS = OCA ? OCA_TS : SA_TS, CS = OCA ? OCA_CS : SA_CS;
+        for (int i = threadIdx.x; i < 4 * CS; i += NT) {
+            const int cp = i / CS, at = i - cp * CS + cp, r = at / TS, s = at - r * TS;
+            float v = 0.f;
+            if (r < TR && s < TR) {
+                int src = OCA ? (r - 22) * TW + (s - 22) : r * TW + s;
+                if (src < 0) src += TR * TW;
+                v = table[(long)src * heads + head] * L2E;
+            }
+            tab[i] = v;
         }
     }
-    if (OCA)
-        for (int i = threadIdx.x; i < NK; i += NT) koff[i] = (i / 24) * TSTRIDE + (i % 24);
     if (threadIdx.x == 0) {
         for (int b = 0; b < QB; ++b) {
             bar_init(&q_full[b], NLT);
@@ -476,8 +475,8 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
             const bool masked = !OCA && gm.mshift > 0;
             const int shift = gm.mshift, ghp = gm.ghp;
             const int yrw = gm.yr0 + wy * 16;  // rolled-frame row of the window's first row (mod ghp)
-            // OCAB bias of key k = (ky, kx): tab[(ky-qy+15)*48 + (kx-qx+15)] = tab[koff[k] - B0].
-            const int B0 = qy * TSTRIDE + qx - 15 * TSTRIDE - 15;
+            // OCAB: the copy whose runs of key biases start 16-byte aligned for this query column
+            const int occ = (15 - qx) & 3;
             // Shift mask: key column kx is masked against target label t when
             // band(wx*16+kx) != t; one 16-bit mask per possible row band.
             uint32_t cm[3] = {0, 0, 0};
@@ -514,7 +513,22 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
                 }
                 if (OCA) {
 #pragma unroll
-                    for (int k = 0; k < 32; ++k) sv[k] += tab[koff[j * KBLK + k] - B0];
+                    for (int g8 = 0; g8 < 4; ++g8) {
+                        // keys k0 .. k0 + 7 lie in key row ky, columns kx0 .. kx0 + 7 (kx0 a multiple of
+                        // 8): biases tab[(ky - qy + 15)*OCA_TS + kx - qx + 15], ascending
+                        const int k0 = j * KBLK + 8 * g8, ky = k0 / 24, kx0 = k0 - 24 * ky;
+                        const float4* b = reinterpret_cast<const float4*>(
+                            tab + occ * OCA_CS + (ky - qy + 15) * OCA_TS + kx0 - qx + 15 - occ);
+                        const float4 t0 = b[0], t1 = b[1];
+                        sv[8 * g8 + 0] += t0.x;
+                        sv[8 * g8 + 1] += t0.y;
+                        sv[8 * g8 + 2] += t0.z;
+                        sv[8 * g8 + 3] += t0.w;
+                        sv[8 * g8 + 4] += t1.x;
+                        sv[8 * g8 + 5] += t1.y;
+                        sv[8 * g8 + 6] += t1.z;
+                        sv[8 * g8 + 7] += t1.w;
+                    }
                 } else if (!PRE) {
                     // tab[(ky - ... )]: scalar loads from copy 0 (even query rows) or copy 2 (odd
                     // ones), which keeps the two half-warps apart in the banks but for two lanes
@@ -996,7 +1010,7 @@ static void run_tc(const float* qkv, const float* table, Dst out, const Plan& p,
     using Shape = AttnShape<PRE && !OCA>;
     constexpr int QB = 1;  // Q buffers (see the kernel)
     constexpr size_t bytes = QB * Shape::halves * 2 * KH * 4096 + KVS * (2 * KH * 1024 + 2 * 2048) +
-                             tab_floats<OCA>() * 4 + (OCA ? 576 * 4 : 0) + 1024;
+                             tab_floats<OCA>() * 4 + 1024;
     allow_dyn_smem(k_attn_tc<D, OCA, TERMS, PRE>, bytes);
     // The windows of this launch (see AttnGeom).
     AttnGeom gm;
