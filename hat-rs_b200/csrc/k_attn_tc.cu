@@ -224,6 +224,21 @@ __device__ __forceinline__ void tma4(uint32_t dst, const CUtensorMap* m, int c0,
         ::"r"(dst), "l"((uint64_t)m), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(su(bar))
         : "memory");
 }
+__device__ __forceinline__ void tma4_store(const CUtensorMap* m, uint32_t src, int c0, int c1, int c2, int c3) {
+    asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%1, %2, %3, %4}], [%5];"
+                 ::"l"((uint64_t)m), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// named barrier 1 or 2 (a query half's softmax warps) over 128 threads
+__device__ __forceinline__ void half_sync(int hh) {
+    if (hh == 0)
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+    else
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+}
 __device__ __forceinline__ void bar_expect_tx(uint64_t* b, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su(b)), "r"(bytes) : "memory");
 }
@@ -258,7 +273,8 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
               int heads, float scale, long items, int* err, const __grid_constant__ CUtensorMap tqh,
               const __grid_constant__ CUtensorMap tql, const __grid_constant__ CUtensorMap tkh,
               const __grid_constant__ CUtensorMap tkl, const __grid_constant__ CUtensorMap tvh,
-              const __grid_constant__ CUtensorMap tvl) {
+              const __grid_constant__ CUtensorMap tvl, const __grid_constant__ CUtensorMap toh,
+              const __grid_constant__ CUtensorMap tol) {
     const int wp = gm.wp;
     constexpr int KH = (D + 15) / 16;               // k-steps of the QK^T product (16 fp16 each)
     constexpr int NK = OCA ? 576 : 256;             // keys per window
@@ -278,6 +294,10 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
     constexpr uint32_t Q_REGION = HV * 2 * Q_BYTES;  // one buffer: every half, hi and lo
     constexpr uint32_t OFF_KV = QB * Q_REGION;
     constexpr uint32_t OFF_TAB = OFF_KV + KVS * KV_BYTES;
+    // The window kernel's output staging: per half, 128 rows of 24 fp16 (48 bytes), hi then lo,
+    // stored by TMA (see the softmax's output).
+    constexpr uint32_t OFF_OST = (OFF_TAB + tab_floats<OCA>() * 4 + 1023) & ~1023u;
+    constexpr uint32_t OST_BYTES = 128 * 48;
 
     // TMEM columns: half h's S blocks at 64h and 64h + 32 (fp32); once read, a block's first
     // 16 columns hold P_hi and the next 16 P_lo (fp16 pairs); half h's O (per item parity)
@@ -623,6 +643,41 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
             tcf_before();
             bar_arrive(&o_free[hh][ti & 1]);
             const float inv = 1.f / (PRE ? ov[24] : l);
+            if constexpr (PRE && !OCA) {
+                const int tx0 = wx * 16 + gm.sx, ty0 = gm.oy + wy * 16 + gm.sy;
+                if (tx0 + 16 <= wp && ty0 + 16 <= gm.rows) {
+                    // A window that does not wrap: the half's 128 rows of 24 features as fp16 pairs
+                    // into the staging tile, then two TMA stores by the half's first thread. (A
+                    // strip's shifted windows also write rows of the halo, which no one reads.)
+                    uint8_t* stg = sm + OFF_OST + hh * 2 * OST_BYTES;
+                    const bool issuer = (warp - 1) % 4 == 0 && lane == 0;
+                    if (issuer) bulk_wait_read();  // the half's previous stores have read the tile
+                    half_sync(hh);
+                    bool big = false;
+#pragma unroll
+                    for (int i = 0; i < D; i += 8) {
+                        uint4 h, lo;
+                        split_h16x2(ov[i] * inv, ov[i + 1] * inv, h.x, lo.x);
+                        split_h16x2(ov[i + 2] * inv, ov[i + 3] * inv, h.y, lo.y);
+                        split_h16x2(ov[i + 4] * inv, ov[i + 5] * inv, h.z, lo.z);
+                        split_h16x2(ov[i + 6] * inv, ov[i + 7] * inv, h.w, lo.w);
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) big |= beyond_h16(ov[i + u] * inv);
+                        *reinterpret_cast<uint4*>(stg + row * 48 + 2 * i) = h;
+                        *reinterpret_cast<uint4*>(stg + OST_BYTES + row * 48 + 2 * i) = lo;
+                    }
+                    if (big && out.err) atomicCAS(out.err, 0, ERR_RANGE_GEMM);
+                    fence_async();
+                    half_sync(hh);
+                    if (issuer) {
+                        tma4_store(&toh, su(stg), 0, head, tx0, ty0 + 8 * hh);
+                        tma4_store(&tol, su(stg + OST_BYTES), 0, head, tx0, ty0 + 8 * hh);
+                        bulk_commit();
+                    }
+                    g += NBLK;
+                    continue;
+                }
+            }
             const int qrow = OCA ? gm.oy + wy * 16 + qy : (gm.oy + wy * 16 + qy + gm.sy) % gm.rows;
             const long qpos = (long)qrow * wp + (OCA ? wx * 16 + qx : (wx * 16 + qx + gm.sx) % wp);
             const long ob = qpos * c + (long)head * D;
@@ -654,6 +709,8 @@ __global__ void __launch_bounds__(AttnShape<PRE && !OCA>::threads, AttnShape<PRE
             }
             g += NBLK;
         }
+        // the output stores have finished before the CTA (and its shared memory) goes away
+        if (PRE && !OCA && (warp - 1) % 4 == 0 && lane == 0) bulk_wait_all();
     } else if constexpr (PRE) {
         // ------------------------------------------------------------ loaders (copies)
         // Per item, Q: 128 rows x 3 pieces of 8 dims x (hi, lo) = 6 copies a thread. Per key
@@ -1009,8 +1066,11 @@ static void run_tc(const float* qkv, const float* table, Dst out, const Plan& p,
     constexpr int TR = OCA ? 39 : 31;
     using Shape = AttnShape<PRE && !OCA>;
     constexpr int QB = 1;  // Q buffers (see the kernel)
-    constexpr size_t bytes = QB * Shape::halves * 2 * KH * 4096 + KVS * (2 * KH * 1024 + 2 * 2048) +
-                             tab_floats<OCA>() * 4 + 1024;
+    constexpr size_t tab_end = QB * Shape::halves * 2 * KH * 4096 + KVS * (2 * KH * 1024 + 2 * 2048) +
+                               tab_floats<OCA>() * 4;
+    // + the window kernel's output staging (1 KB aligned), + 1 KB to align the base
+    constexpr size_t bytes = (PRE && !OCA ? ((tab_end + 1023) & ~(size_t)1023) + 2 * Shape::halves * 128 * 48
+                                          : tab_end) + 1024;
     allow_dyn_smem(k_attn_tc<D, OCA, TERMS, PRE>, bytes);
     // The windows of this launch (see AttnGeom).
     AttnGeom gm;
@@ -1048,7 +1108,7 @@ static void run_tc(const float* qkv, const float* table, Dst out, const Plan& p,
     // TMA maps of the pre-split layout for the window kernel (see the loaders): q|k hi / lo as
     // (head dim 24, head, x, y) with 16 x 1 x 16 x {8, 2} boxes, v^T hi / lo as (x, feature,
     // y) with 16 x 32 x 2 boxes; 32-byte swizzled rows, fp16.
-    CUtensorMap m[6];
+    CUtensorMap m[8];
     memset(m, 0, sizeof m);
     if (PRE && !OCA) {
         const long P = (long)p.rows * p.wp;
@@ -1068,9 +1128,15 @@ static void run_tc(const float* qkv, const float* table, Dst out, const Plan& p,
         const uint32_t vbox[3] = {16, 24, 1};
         m[4] = tensor_map(vth, 3, vdims, vstr, vbox, 32, true);
         m[5] = tensor_map(vtl, 3, vdims, vstr, vbox, 32, true);
+        // the output: fp16 pairs [P][c] as (head dim, head, x, y), 24 x 1 x 16 x 8 boxes
+        const uint64_t ostr[3] = {(uint64_t)D * 2, (uint64_t)c * 2, (uint64_t)p.wp * c * 2};
+        const uint32_t obox[4] = {(uint32_t)D, 1, 16, 8};
+        m[6] = tensor_map(out.hi, 4, qdims, ostr, obox, 0, true);
+        m[7] = tensor_map(out.lo, 4, qdims, ostr, obox, 0, true);
     }
     k_attn_tc<D, OCA, TERMS, PRE><<<(unsigned)grid, Shape::threads, bytes, st>>>(
-        qkv, table, out, gm, c, heads, 1.f / sqrtf((float)D), items, err, m[0], m[1], m[2], m[3], m[4], m[5]);
+        qkv, table, out, gm, c, heads, 1.f / sqrtf((float)D), items, err, m[0], m[1], m[2], m[3], m[4], m[5], m[6],
+        m[7]);
     HAT_CUDA(cudaGetLastError());
     count_launch();
 }
