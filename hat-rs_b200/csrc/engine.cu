@@ -458,7 +458,16 @@ static void raise_device_error(int v) {
 
 void Engine::check_device_error() { raise_device_error(take_device_error()); }
 
+void Engine::refuse_if_aborted() const {
+    // After an abort the communicator's buffers are gone, while the captured pass still names
+    // them: nothing may be enqueued any more, and the stream is not waited on either.
+    if (comm_ && comm_->aborted())
+        throw Error(3, "nccl: the communicator was aborted after a failed or timed-out exchange; attach the "
+                       "strips again to continue");
+}
+
 void Engine::sync() {
+    refuse_if_aborted();
     HAT_CUDA(cudaSetDevice(device_));
     wait_stream();
     check_device_error();
@@ -816,6 +825,7 @@ void Engine::mark(const char* kind, double flops, double bytes) {
 // One eager pass with an event between every launch: per kind of kernel, the number of
 // launches, their summed device time and their algorithmic FLOPs and bytes.
 std::string Engine::profile(int h, int w) {
+    refuse_if_aborted();
     HAT_CUDA(cudaSetDevice(device_));
     ensure_plan(h, w);
     for (auto& m : marks_) cudaEventDestroy(m.ev);
@@ -913,6 +923,7 @@ void Engine::run_graph(cudaStream_t run) {
 
 void Engine::forward_device(int n, int h, int w, const float* din, float* dout, cudaStream_t st) {
     if (n <= 0 || h <= 0 || w <= 0) throw Error(1, std::to_string(h) + "x" + std::to_string(w) + " is empty");
+    refuse_if_aborted();
     HAT_CUDA(cudaSetDevice(device_));
     ensure_plan(h, w);
     cudaStream_t run = st ? st : stream_;
@@ -926,6 +937,7 @@ void Engine::forward_device(int n, int h, int w, const float* din, float* dout, 
 
 void Engine::forward_host(int n, int h, int w, const float* in, float* out) {
     if (n <= 0 || h <= 0 || w <= 0) throw Error(1, std::to_string(h) + "x" + std::to_string(w) + " is empty");
+    refuse_if_aborted();
     HAT_CUDA(cudaSetDevice(device_));
     const long inN = 3L * h * w, outN = 3L * h * wt_.scale * w * wt_.scale;
     for (int attempt = 0;; ++attempt) {

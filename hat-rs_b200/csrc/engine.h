@@ -74,6 +74,7 @@ private:
     void fall_back(int code);  // after ERR_RANGE_*: tf32 pairs (and the attention on CUDA cores)
     // Waits for the engine's stream: plainly, or with the communicator's deadline when sharded.
     void wait_stream();
+    void refuse_if_aborted() const;  // throws once the communicator was aborted
     void ensure_plan(int h, int w);
     // Strip mode: fill `n` halo rows on each side of `plane` (`ch` channels, at `res`
     // times the base resolution) from the neighbours' own rows; top and bottom ranks
