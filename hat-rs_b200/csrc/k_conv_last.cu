@@ -4,8 +4,9 @@
 //
 // N = 3 leaves a tensor-core tile almost empty, and the implicit GEMM reads each input
 // pixel once per tap (nine times, from L2). This kernel is a bandwidth kernel instead:
-// a CTA stages an 8 x 32 output tile's (8+2) x (32+2) input pixels, all 64 channels, as
-// fp32 in shared memory (the hi + lo pair summed, so the arithmetic is fp32), and each
+// a CTA stages an 8 x 32 output tile's (8+2) x (32+2) input pixels as fp32 in shared
+// memory (the hi + lo pair summed, so the arithmetic is fp32), 32 channels at a time so
+// that three CTAs fit an SM and one CTA's staging overlaps another's arithmetic, and each
 // thread computes one output pixel's 3 channels with fp32 FMAs. The 1728 weights sit in
 // shared memory too, ordered (tap, 4 input channels, output channel, 4) so that the 12
 // weights one input float4 meets are three broadcast 16-byte loads. (Weights as kernel
@@ -21,7 +22,8 @@ namespace {
 
 constexpr int TW = 32, TH = 8;            // output tile: columns x rows (one thread per pixel)
 constexpr int SW = TW + 2, SH = TH + 2;   // staged input tile with the 3x3 halo
-constexpr int PS = CL_CIN + 4;            // floats per staged pixel: 68 keeps LDS.128 conflict-free
+constexpr int CH = 32;                    // channels staged at a time
+constexpr int PS = CH + 4;                // floats per staged pixel: 36 keeps LDS.128 conflict-free
 constexpr int NW = 3 * CL_CIN * 9;          // weights
 constexpr size_t SMEM = ((size_t)SH * SW * PS + NW) * sizeof(float);
 
@@ -55,7 +57,7 @@ __device__ __forceinline__ float4 load4(const Opnd& x, long e) {
     return v;
 }
 
-__global__ void __launch_bounds__(TW * TH, 2)
+__global__ void __launch_bounds__(TW * TH, 3)
     k_conv_last(const Opnd x, const float* __restrict__ w, const float* __restrict__ bias, float* __restrict__ out,
                 const Geo g) {
     extern __shared__ float4 sm4[];
@@ -65,48 +67,53 @@ __global__ void __launch_bounds__(TW * TH, 2)
         const int co = i / (CL_CIN * 9), r = i - co * CL_CIN * 9, ci = r / 9, tap = r - ci * 9;  // [co][ci][ky][kx]
         reinterpret_cast<float*>(wsm)[((tap * (CL_CIN / 4) + ci / 4) * 3 + co) * 4 + (ci & 3)] = w[i];
     }
-    // Stage the input tile: pixel (r, c) of the tile is view pixel (y0 - 1 + r, x0 - 1 + c).
-    // Each thread issues a round's loads before any of its stores, so that a round's memory
-    // latency is paid once rather than once per 16-byte piece.
-    constexpr int PIECES = SH * SW * (CL_CIN / 4), PER = (PIECES + TW * TH - 1) / (TW * TH), RND = (PER + 1) / 2;
-#pragma unroll 1
-    for (int r0 = 0; r0 < PER; r0 += RND) {
-        float4 v[RND];
-#pragma unroll
-        for (int u = 0; u < RND; ++u) {
-            const int i = threadIdx.x + (r0 + u) * TW * TH;
-            const int pix = i / (CL_CIN / 4), c4 = i % (CL_CIN / 4);
-            const int r = pix / SW, c = pix % SW;
-            const int gy = y0 - 1 + r, gx = x0 - 1 + c;
-            v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (i < PIECES && gy >= 0 && gy < g.hgt && gx >= 0 && gx < g.wid)
-                v[u] = load4(x, ((long)gy * g.wid + gx) * CL_CIN + 4 * c4);
-        }
-#pragma unroll
-        for (int u = 0; u < RND; ++u) {
-            const int i = threadIdx.x + (r0 + u) * TW * TH;
-            if (i < PIECES) sm4[(i / (CL_CIN / 4)) * (PS / 4) + i % (CL_CIN / 4)] = v[u];
-        }
-    }
-    __syncthreads();
     const int tx = threadIdx.x % TW, ty = threadIdx.x / TW;
     const int oy = y0 + ty, ox = x0 + tx;
-    if (oy >= g.y_hi || ox >= g.wid) return;
     float a0 = bias[0], a1 = bias[1], a2 = bias[2];
+#pragma unroll 1
+    for (int c0 = 0; c0 < CL_CIN; c0 += CH) {
+        // Stage channels [c0, c0 + CH) of the input tile: pixel (r, c) of the tile is view pixel
+        // (y0 - 1 + r, x0 - 1 + c). Each thread issues a round's loads before any of its stores.
+        constexpr int PIECES = SH * SW * (CH / 4), PER = (PIECES + TW * TH - 1) / (TW * TH), RND = (PER + 1) / 2;
+        if (c0) __syncthreads();  // the previous channels' arithmetic is done with the tile
+#pragma unroll 1
+        for (int r0 = 0; r0 < PER; r0 += RND) {
+            float4 v[RND];
 #pragma unroll
-    for (int ky = 0; ky < 3; ++ky)
+            for (int u = 0; u < RND; ++u) {
+                const int i = threadIdx.x + (r0 + u) * TW * TH;
+                const int pix = i / (CH / 4), c4 = i % (CH / 4);
+                const int r = pix / SW, c = pix % SW;
+                const int gy = y0 - 1 + r, gx = x0 - 1 + c;
+                v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (i < PIECES && gy >= 0 && gy < g.hgt && gx >= 0 && gx < g.wid)
+                    v[u] = load4(x, ((long)gy * g.wid + gx) * CL_CIN + c0 + 4 * c4);
+            }
 #pragma unroll
-        for (int kx = 0; kx < 3; ++kx) {
-            const float4* px = sm4 + ((ty + ky) * SW + tx + kx) * (PS / 4);
-            const float4* wt = wsm + (ky * 3 + kx) * (CL_CIN / 4) * 3;
-#pragma unroll 4
-            for (int c4 = 0; c4 < CL_CIN / 4; ++c4) {
-                const float4 v = px[c4], w0 = wt[3 * c4], w1 = wt[3 * c4 + 1], w2 = wt[3 * c4 + 2];
-                a0 = fmaf(v.x, w0.x, fmaf(v.y, w0.y, fmaf(v.z, w0.z, fmaf(v.w, w0.w, a0))));
-                a1 = fmaf(v.x, w1.x, fmaf(v.y, w1.y, fmaf(v.z, w1.z, fmaf(v.w, w1.w, a1))));
-                a2 = fmaf(v.x, w2.x, fmaf(v.y, w2.y, fmaf(v.z, w2.z, fmaf(v.w, w2.w, a2))));
+            for (int u = 0; u < RND; ++u) {
+                const int i = threadIdx.x + (r0 + u) * TW * TH;
+                if (i < PIECES) sm4[(i / (CH / 4)) * (PS / 4) + i % (CH / 4)] = v[u];
             }
         }
+        __syncthreads();
+        if (oy < g.y_hi && ox < g.wid) {
+#pragma unroll
+            for (int ky = 0; ky < 3; ++ky)
+#pragma unroll
+                for (int kx = 0; kx < 3; ++kx) {
+                    const float4* px = sm4 + ((ty + ky) * SW + tx + kx) * (PS / 4);
+                    const float4* wt = wsm + ((ky * 3 + kx) * (CL_CIN / 4) + c0 / 4) * 3;
+#pragma unroll 4
+                    for (int c4 = 0; c4 < CH / 4; ++c4) {
+                        const float4 v = px[c4], w0 = wt[3 * c4], w1 = wt[3 * c4 + 1], w2 = wt[3 * c4 + 2];
+                        a0 = fmaf(v.x, w0.x, fmaf(v.y, w0.y, fmaf(v.z, w0.z, fmaf(v.w, w0.w, a0))));
+                        a1 = fmaf(v.x, w1.x, fmaf(v.y, w1.y, fmaf(v.z, w1.z, fmaf(v.w, w1.w, a1))));
+                        a2 = fmaf(v.x, w2.x, fmaf(v.y, w2.y, fmaf(v.z, w2.z, fmaf(v.w, w2.w, a2))));
+                    }
+                }
+        }
+    }
+    if (oy >= g.y_hi || ox >= g.wid) return;
     const int gy = oy + g.oy0;
     if (gy < 0 || gy >= g.oh || ox >= g.ow) return;
     const long plane = (long)g.oh * g.ow, o = (long)gy * g.ow + ox;
