@@ -117,6 +117,7 @@ void launch_tapsum_gelu(const float* taps, int ldt, const float* bias, Dst out, 
 __global__ void k_rowsum(const float* __restrict__ partial, long rows, int c, float* __restrict__ sum) {
     for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < c; j += gridDim.x * blockDim.x) {
         float s = 0.f;
+#pragma unroll 8
         for (long r = 0; r < rows; ++r) s += partial[r * c + j];
         sum[j] = s;
     }
@@ -405,7 +406,8 @@ __global__ void k_ca_gate(const float* __restrict__ partial, long rows, float in
     float acc[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-    for (long r = warp; r < rows; r += 32) {
+#pragma unroll 4
+    for (long r = warp; r < rows; r += 32) {  // four rows' loads in flight a warp
         const float* row = partial + r * c;
 #pragma unroll
         for (int j = 0; j < 8; ++j)
