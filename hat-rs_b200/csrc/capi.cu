@@ -200,6 +200,12 @@ int hat_b200_png_encode(int width, int height, const uint8_t* rgb, uint8_t* out,
     });
 }
 
+int hat_b200_set_timeout(hat_b200* h, int ms) {
+    if (!h) return HAT_B200_EINVAL;
+    for (auto& e : h->engs) e->set_timeout(ms > 0 ? ms / 1000.0 : 120.0);
+    return HAT_B200_OK;
+}
+
 int hat_b200_gpu_count(const hat_b200* h) { return h ? (int)h->engs.size() : 0; }
 
 // Checkpoint inspection without a device: what --list-weights and the loader tests use.

@@ -88,6 +88,7 @@ SIGNATURES = {
     "hat_b200_sync": (_I, [_P, _C, _S]),
     "hat_b200_fp16_pairs": (_I, [_P]),
     "hat_b200_gpu_count": (_I, [_P]),
+    "hat_b200_set_timeout": (_I, [_P, _I]),
     "hat_b200_png_load": (_I, [_C, _P, _S, ctypes.POINTER(_I), ctypes.POINTER(_I), _C, _S]),
     "hat_b200_png_decode": (_I, [_P, _S, _P, _S, ctypes.POINTER(_I), ctypes.POINTER(_I), _C, _S]),
     "hat_b200_to_rgb8": (_I, [_P, _I, _I, _P]),
@@ -240,6 +241,10 @@ class B200:
         """Wait for this handle's device work; raise if a kernel flagged an error."""
         e = _err()
         _check(lib().hat_b200_sync(self._h, e, len(e)), e)
+
+    def set_timeout(self, ms: int) -> None:
+        """Deadline of a strip-sharded call's device work (0: the 120 s default)."""
+        lib().hat_b200_set_timeout(self._h, ms)
 
     def gpu_count(self) -> int:
         return int(lib().hat_b200_gpu_count(self._h))

@@ -292,6 +292,12 @@ HAT_B200_API int hat_b200_png_save(const char* path, int width, int height, cons
 HAT_B200_API int hat_b200_png_encode(int width, int height, const uint8_t* rgb, uint8_t* out, size_t cap, size_t* len,
                                      char* err, size_t errlen);
 
+/* Sets the deadline of a strip-sharded call's device work (hat_b200_opts.timeout_ms) on every
+ * GPU of the handle; ms <= 0 restores the default (120000). A first call, which also sets up the
+ * NCCL connections and may find its peers still starting, can run under a longer deadline than
+ * the calls after it. (No counterpart in the reference, which runs on one device.) */
+HAT_B200_API int hat_b200_set_timeout(hat_b200* h, int ms);
+
 /* The GPUs this handle drives (1 unless created with ngpus > 1). */
 HAT_B200_API int hat_b200_gpu_count(const hat_b200* h);
 

@@ -88,7 +88,7 @@ def _silent_rank_main(rank, ckpt, img, q_id, q_out, q_done):
         import time
         import torch
         torch.cuda.set_device(rank)
-        be = hat_b200.B200(ckpt, device=rank, timeout_ms=3000)
+        be = hat_b200.B200(ckpt, device=rank)  # the first call sets up NCCL: default deadline
         if rank == 0:
             uid = hat_b200.nccl_unique_id()
             q_id.put(uid)
@@ -96,8 +96,10 @@ def _silent_rank_main(rank, ckpt, img, q_id, q_out, q_done):
             uid = q_id.get(timeout=120)
         be.attach_strip(rank, 2, uid)
         h, w = img.shape[1:]
+        t0 = time.perf_counter()
         be.forward(h, w, img)  # one step together
-        q_out.put((rank, "step", None))
+        q_out.put((rank, "step", time.perf_counter() - t0))
+        be.set_timeout(3000)
         if rank == 1:
             # stops calling: stays alive, issues nothing, until rank 0 has its answer
             q_done.get(timeout=300)
@@ -140,6 +142,7 @@ def test_strip_rank_that_stops_calling_ends_in_an_error(ckdir):
             if stage in ("exception", "no error"):
                 break
     finally:
+        print("stages:", got)
         q_done.put(1)
         for pr in procs:
             pr.join(timeout=60)
