@@ -331,7 +331,7 @@ void Engine::attach_strip(int rank, int n, const void* id, size_t idlen) {
         arena_floats_ = 0;
     }
     have_plan_ = false;
-    comm_.reset(new Comm(rank, n, id, idlen, device_));
+    comm_.reset(new Comm(rank, n, id, idlen, device_, timeout_s_));
     if (!cstream_) {
         HAT_CUDA(cudaStreamCreateWithFlags(&cstream_, cudaStreamNonBlocking));
         HAT_CUDA(cudaEventCreateWithFlags(&ev_fork_, cudaEventDisableTiming));
@@ -457,6 +457,11 @@ static void raise_device_error(int v) {
 }
 
 void Engine::check_device_error() { raise_device_error(take_device_error()); }
+
+void Engine::set_timeout(double s) {
+    timeout_s_ = s;
+    if (comm_) comm_->set_timeout(s);
+}
 
 void Engine::refuse_if_aborted() const {
     // After an abort the communicator's buffers are gone, while the captured pass still names
@@ -902,8 +907,15 @@ void Engine::run_graph(cudaStream_t run) {
                 try {
                     enqueue_pass();
                 } catch (...) {
+                    // A sharded pass may have left the communication stream forked into the
+                    // capture: join it back so that the capture can end (errors ignored).
+                    if (cstream_) {
+                        cudaEventRecord(ev_fork_, cstream_);
+                        cudaStreamWaitEvent(stream_, ev_fork_, 0);
+                    }
                     cudaStreamEndCapture(stream_, &g);
                     if (g) cudaGraphDestroy(g);
+                    cudaGetLastError();
                     throw;
                 }
                 HAT_CUDA(cudaStreamEndCapture(stream_, &g));

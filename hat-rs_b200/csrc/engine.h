@@ -64,7 +64,7 @@ public:
     bool sharded() const { return comm_ != nullptr; }
     // Deadline of a sharded call's device work (seconds; <= 0: none): past it the
     // communicator is aborted and the call fails instead of blocking (see Comm::wait).
-    void set_timeout(double s) { timeout_s_ = s; }
+    void set_timeout(double s);
 
 private:
     struct Acts;

@@ -30,6 +30,7 @@ struct Api {
     const char* (*error_string)(ncclResult_t) = nullptr;
     ncclResult_t (*get_async_error)(ncclComm_t, ncclResult_t*) = nullptr;
     ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
+    ncclResult_t (*comm_init_rank_config)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
 };
 
 template <class F>
@@ -64,6 +65,7 @@ const Api& api() {
             bind(lib, "ncclGetErrorString", a.error_string);
             bind(lib, "ncclCommGetAsyncError", a.get_async_error);
             bind(lib, "ncclCommAbort", a.comm_abort);
+            bind(lib, "ncclCommInitRankConfig", a.comm_init_rank_config);
         } catch (const Error& e) {
             failure = e.what();
         }
@@ -85,13 +87,50 @@ void nccl_unique_id(void* out, size_t len) {
     memcpy(out, &id, sizeof id);
 }
 
-Comm::Comm(int rank, int n, const void* id, size_t idlen, int device) : rank_(rank), n_(n) {
+Comm::Comm(int rank, int n, const void* id, size_t idlen, int device, double timeout_s)
+    : rank_(rank), n_(n), timeout_s_(timeout_s) {
     if (n < 1 || rank < 0 || rank >= n) throw Error(1, "nccl: bad rank / size");
     if (!id || idlen < sizeof(ncclUniqueId)) throw Error(1, "nccl: the unique id needs 128 bytes");
     ncclUniqueId uid;
     memcpy(&uid, id, sizeof uid);
     HAT_CUDA(cudaSetDevice(device));
-    check(api().comm_init_rank(&comm_, n, uid, rank), "ncclCommInitRank");
+    // Non-blocking: no NCCL call waits on the peers inside NCCL (connection set-up, the buffer
+    // registration of a graph capture, group launches); each returns at once and settle()
+    // waits for the communicator's state under the deadline instead.
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    const ncclResult_t r = api().comm_init_rank_config(&comm_, n, uid, rank, &cfg);
+    if (r != ncclSuccess && r != ncclInProgress) check(r, "ncclCommInitRankConfig");
+    settle("ncclCommInitRankConfig");
+}
+
+void Comm::settle(const char* what) {
+    ncclResult_t state = ncclSuccess;
+    const WaitEnd end = wait_with_deadline(
+        [&] {
+            const ncclResult_t r = api().get_async_error(comm_, &state);
+            if (r != ncclSuccess) state = r;
+            if (state == ncclSuccess) return 1;
+            return state == ncclInProgress ? 0 : -1;
+        },
+        [] { return false; },
+        [&] {
+            api().comm_abort(comm_);
+            aborted_ = true;
+        },
+        timeout_s_);
+    if (end == WaitEnd::Done) return;
+    if (end == WaitEnd::StreamError) {
+        api().comm_abort(comm_);
+        aborted_ = true;
+        throw Error(3, std::string("nccl: ") + what + " failed on rank " + std::to_string(rank_) + ": " +
+                           api().error_string(state) + "; the communicator was aborted");
+    }
+    char buf[64];
+    snprintf(buf, sizeof buf, "%.1f", timeout_s_);
+    throw Error(3, std::string("nccl: rank ") + std::to_string(rank_) + " of " + std::to_string(n_) + ": " + what +
+                       " did not complete within " + buf +
+                       " s (a peer rank stopped calling or died); the communicator was aborted");
 }
 
 Comm::~Comm() {
@@ -109,7 +148,11 @@ void Comm::group_start() {
     live();
     check(api().group_start(), "ncclGroupStart");
 }
-void Comm::group_end() { check(api().group_end(), "ncclGroupEnd"); }
+void Comm::group_end() {
+    const ncclResult_t r = api().group_end();
+    if (r != ncclSuccess && r != ncclInProgress) check(r, "ncclGroupEnd");
+    settle("ncclGroupEnd");
+}
 
 void Comm::send(const float* buf, size_t count, int peer, cudaStream_t st) {
     live();
@@ -122,8 +165,9 @@ void Comm::recv(float* buf, size_t count, int peer, cudaStream_t st) {
 }
 
 void Comm::allreduce_sum(float* buf, size_t count, cudaStream_t st) {
-    live();
+    group_start();  // a group, so that group_end() settles the non-blocking call
     check(api().all_reduce(buf, buf, count, ncclFloat32, ncclSum, comm_, st), "ncclAllReduce");
+    group_end();
 }
 
 void Comm::wait(cudaStream_t st, double timeout_s) {

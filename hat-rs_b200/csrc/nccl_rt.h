@@ -14,7 +14,9 @@ namespace hat {
 // A communicator over `n` ranks, one GPU each, created collectively from one unique id.
 class Comm {
 public:
-    Comm(int rank, int n, const void* id, size_t idlen, int device);
+    // `timeout_s`: the deadline of every host-side wait on the peers (initialisation, group
+    // launches) and of wait(); <= 0 waits without one.
+    Comm(int rank, int n, const void* id, size_t idlen, int device, double timeout_s);
     ~Comm();
     int rank() const { return rank_; }
     int size() const { return n_; }
@@ -31,10 +33,15 @@ public:
     // refuses every later call.
     void wait(cudaStream_t st, double timeout_s);
     bool aborted() const { return aborted_; }
+    void set_timeout(double s) { timeout_s_ = s; }
 
 private:
     void live() const;  // throws once aborted
+    // Waits until the communicator's state leaves ncclInProgress, under the deadline; on an
+    // error or at the deadline aborts the communicator and throws.
+    void settle(const char* what);
     int rank_, n_;
+    double timeout_s_ = 120.0;
     ncclComm_t comm_ = nullptr;
     bool aborted_ = false;
 };
