@@ -6,9 +6,10 @@ calling. Skipped with fewer than two GPUs.
 * STRIP: every image split into row strips over the GPUs with NCCL halo exchange; equal
   to the one-GPU pass up to the order of the channel-attention sums, and within the
   reference's 1e-4 of the fp32 reference (the oracle's torch twin).
-* A rank of a strip-sharded job (one process per GPU) that stops calling between steps:
-  the other rank's next call must come back with an error once its deadline passes,
-  not block; afterwards the GPU still runs a fresh pass. NCCL's NVLS is off in these
+* A rank of a strip-sharded job (one process per GPU) that stops calling between steps
+  (after two joint steps: the eager pass and the captured one): the other rank's next call
+  must come back with an error once its deadline passes, not block; later calls are refused
+  at once; afterwards the GPU still runs a fresh pass. NCCL's NVLS is off in these
   processes, and the silent rank stays alive (no memory of it goes away under the other
   rank's kernels).
 """
@@ -97,7 +98,8 @@ def _silent_rank_main(rank, ckpt, img, q_id, q_out, q_done):
         be.attach_strip(rank, 2, uid)
         h, w = img.shape[1:]
         t0 = time.perf_counter()
-        be.forward(h, w, img)  # one step together
+        be.forward(h, w, img)  # two steps together: the eager pass, then the captured one
+        be.forward(h, w, img)
         q_out.put((rank, "step", time.perf_counter() - t0))
         be.set_timeout(3000)
         if rank == 1:
