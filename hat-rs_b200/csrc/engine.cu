@@ -835,6 +835,7 @@ std::string Engine::profile(int h, int w) {
     ensure_plan(h, w);
     for (auto& m : marks_) cudaEventDestroy(m.ev);
     marks_.clear();
+    if (comm_) comm_->begin_pass();
     profiling_ = true;
     uint64_t* prev = g_launch_counter;
     g_launch_counter = &launches_;
@@ -880,6 +881,8 @@ std::string Engine::profile(int h, int w) {
 }
 
 void Engine::run_graph(cudaStream_t run) {
+    // Sharded: the ranks meet on the host before any of them enqueues the pass's exchanges.
+    if (comm_) comm_->begin_pass();
     uint64_t* prev = g_launch_counter;
     g_launch_counter = &launches_;
     try {

@@ -3,8 +3,11 @@
 
 #include <dlfcn.h>
 
+#include <atomic>
 #include <cstring>
+#include <memory>
 #include <mutex>
+#include <thread>
 
 #include "common.cuh"
 #include "deadline.h"
@@ -93,6 +96,8 @@ Comm::Comm(int rank, int n, const void* id, size_t idlen, int device, double tim
     if (!id || idlen < sizeof(ncclUniqueId)) throw Error(1, "nccl: the unique id needs 128 bytes");
     ncclUniqueId uid;
     memcpy(&uid, id, sizeof uid);
+    rv_.reset(new Rendezvous(&uid, sizeof uid, rank, n));
+    if (!rv_->ok()) throw Error(3, "nccl: cannot map the shared-memory rendezvous " + rv_->name());
     HAT_CUDA(cudaSetDevice(device));
     // Non-blocking: no NCCL call waits on the peers inside NCCL (connection set-up, the buffer
     // registration of a graph capture, group launches); each returns at once and settle()
@@ -114,15 +119,10 @@ void Comm::settle(const char* what) {
             return state == ncclInProgress ? 0 : -1;
         },
         [] { return false; },
-        [&] {
-            api().comm_abort(comm_);
-            aborted_ = true;
-        },
-        timeout_s_);
+        [&] { abort_comm(); }, timeout_s_);
     if (end == WaitEnd::Done) return;
     if (end == WaitEnd::StreamError) {
-        api().comm_abort(comm_);
-        aborted_ = true;
+        abort_comm();
         throw Error(3, std::string("nccl: ") + what + " failed on rank " + std::to_string(rank_) + ": " +
                            api().error_string(state) + "; the communicator was aborted");
     }
@@ -131,6 +131,35 @@ void Comm::settle(const char* what) {
     throw Error(3, std::string("nccl: rank ") + std::to_string(rank_) + " of " + std::to_string(n_) + ": " + what +
                        " did not complete within " + buf +
                        " s (a peer rank stopped calling or died); the communicator was aborted");
+}
+
+void Comm::abort_comm() {
+    if (aborted_) return;
+    aborted_ = true;
+    auto done = std::make_shared<std::atomic<int>>(0);
+    ncclComm_t c = comm_;
+    std::thread([c, done] {
+        api().comm_abort(c);
+        done->store(1, std::memory_order_release);
+    }).detach();
+    wait_with_deadline([&] { return done->load(std::memory_order_acquire); }, [] { return false; }, [] {},
+                       ABORT_WAIT_S, 200);
+}
+
+void Comm::begin_pass() {
+    live();
+    const uint64_t k = rv_->pass();
+    const Rendezvous::Result r = rv_->arrive(timeout_s_);
+    if (r == Rendezvous::Met) return;
+    char buf[64];
+    snprintf(buf, sizeof buf, "%.1f", timeout_s_);
+    if (r == Rendezvous::TimedOut)
+        throw Error(3, std::string("nccl: rank ") + std::to_string(rank_) + " of " + std::to_string(n_) +
+                           ": the other ranks did not start pass " + std::to_string(k) + " within " + buf +
+                           " s (a peer rank stopped calling or died); nothing was enqueued and the "
+                           "communicator is intact, so the call can be repeated");
+    throw Error(3, std::string("nccl: rank ") + std::to_string(rank_) + " of " + std::to_string(n_) +
+                       ": the ranks are not at the same pass (their calls were not matched one for one)");
 }
 
 Comm::~Comm() {
@@ -186,11 +215,7 @@ void Comm::wait(cudaStream_t st, double timeout_s) {
             if (r != ncclSuccess) async = r;
             return async != ncclSuccess && async != ncclInProgress;
         },
-        [&] {
-            api().comm_abort(comm_);
-            aborted_ = true;
-        },
-        timeout_s);
+        [&] { abort_comm(); }, timeout_s);
     switch (end) {
         case WaitEnd::Done:
             return;

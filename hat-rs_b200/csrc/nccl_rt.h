@@ -7,7 +7,10 @@
 #include <cuda_runtime.h>
 #include <nccl.h>
 
+#include <memory>
 #include <string>
+
+#include "rendezvous.h"
 
 namespace hat {
 
@@ -26,6 +29,11 @@ public:
     void send(const float* buf, size_t count, int peer, cudaStream_t st);
     void recv(float* buf, size_t count, int peer, cudaStream_t st);
     void allreduce_sum(float* buf, size_t count, cudaStream_t st);
+    // The start of a pass, before any of its NCCL calls is enqueued: waits, under the
+    // deadline, until every rank has reached the same pass (rendezvous.h). A peer that does
+    // not come ends the wait with Error(3); nothing was enqueued, the communicator stays
+    // intact and the call can be repeated.
+    void begin_pass();
     // Waits for the work on `st` (which holds this communicator's calls) for at most
     // `timeout_s` seconds (<= 0: no deadline), polling the communicator's asynchronous
     // error state. If a peer failed or the deadline passed, the communicator is aborted
@@ -40,10 +48,16 @@ private:
     // Waits until the communicator's state leaves ncclInProgress, under the deadline; on an
     // error or at the deadline aborts the communicator and throws.
     void settle(const char* what);
+    // Marks the communicator aborted and runs ncclCommAbort (which makes its pending kernels
+    // return), waiting for it at most ABORT_WAIT_S seconds: the caller gets its error even if
+    // the abort itself does not return.
+    void abort_comm();
+    static constexpr double ABORT_WAIT_S = 10.0;
     int rank_, n_;
     double timeout_s_ = 120.0;
     ncclComm_t comm_ = nullptr;
     bool aborted_ = false;
+    std::unique_ptr<Rendezvous> rv_;
 };
 
 // ncclGetUniqueId into `out` (at least sizeof(ncclUniqueId) = 128 bytes).

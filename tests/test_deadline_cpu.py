@@ -17,3 +17,18 @@ def test_deadline_wait_outcomes(tmp_path):
     print(r.stdout)
     assert r.returncode == 0, r.stdout + r.stderr
     assert r.stdout.count("ok ") == 5
+
+
+def test_pass_rendezvous(tmp_path):
+    """The host rendezvous that starts each strip-sharded pass (hat-rs_b200/csrc/rendezvous.h):
+    a rank whose peer stops calling gets its error at the deadline with nothing enqueued, can
+    repeat the call, and meets the peer again when it comes back; under races with short
+    deadlines no rank ever proceeds before all have arrived."""
+    exe = tmp_path / "rendezvous_check"
+    subprocess.run(["g++", "-std=c++17", "-O1", "-I", str(ROOT / "hat-rs_b200" / "csrc"),
+                    str(ROOT / "tests" / "native" / "rendezvous_check.cpp"), "-o", str(exe), "-pthread", "-lrt"],
+                   check=True, capture_output=True, text=True)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    print(r.stdout)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert r.stdout.count("ok ") == 6
