@@ -306,9 +306,33 @@ void launch_tapsum_gelu(const float* taps, int ldt, const float* bias, Dst out, 
 // sum[c] = the sum of `rows` partial rows [rows][c], in row order.
 void launch_rowsum(const float* partial, long rows, int c, float* sum, cudaStream_t st);
 
+// The gate folded into the CAB's second conv and proj (k_proj_cab), written by the gate
+// kernel when `hi` is set: hi/lo[n][tap * cinp + ci] (row stride k_pad) = the split of
+// cs * gate[n] * w[n][ci][tap] * factor (fp16 pairs when h16, else tf32 pairs; a value
+// beyond fp16's range sets ERR_RANGE_GEMM in `err`), and bias[n] = bp[n] + cs * gate[n] * b2[n].
+struct CabFold {
+    const float* w = nullptr;   // the conv weight [c][cc][3][3]
+    const float* b2 = nullptr;  // its bias [c]
+    const float* bp = nullptr;  // proj's bias [c]
+    float cs = 0.f, factor = 1.f;
+    int cc = 0, cinp = 0, k_pad = 0;
+    bool h16 = false;
+    float* hi = nullptr;
+    float* lo = nullptr;
+    float* bias = nullptr;
+    int* err = nullptr;
+};
+
 // gate[c] = sigmoid(W2 relu(W1 mean + b1) + b2) (hat_arch.py:40-57), where the mean
 // over the plane is the sum of `rows` partial rows [rows][c] times `inv_count`.
 void launch_ca_gate(const float* partial, long rows, float inv_count, const float* w1, const float* b1,
-                    const float* w2, const float* b2, float* gate, int c, int sq, cudaStream_t st);
+                    const float* w2, const float* b2, float* gate, int c, int sq, cudaStream_t st,
+                    const CabFold& fold = CabFold());
+
+// The sum over the output rows [y0, y1) of a 3x3 conv (weight w [c][cc][3][3], bias b) of
+// the view x ([vrows][wid][ld], zero outside), computed from x's row and edge sums without
+// the conv's output: sum[c]. `stat` is scratch of 3 * cc * (y1 - y0 + 2) floats.
+void launch_cab_pool(Opnd x, int ld, int cc, int wid, int vrows, int y0, int y1, float* stat, const float* w,
+                     const float* b, int c, float* sum, cudaStream_t st);
 
 }  // namespace hat

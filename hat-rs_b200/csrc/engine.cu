@@ -37,6 +37,7 @@ Sizes Sizes::of(const Weights& wt, const Plan& p) {
     s.chsum = (P + 127) / 128 * 4 * c;
     s.casum = c;
     s.gate = c;
+    s.cabstat = 3L * wt.compressed * (p.rows + 2);
     // The head's planes ping-pong between two buffers: plane 0 (conv_before_upsample's
     // output, at P) and every other shuffled plane go to A, the rest to B.
     long res = P, a = P * wt.head_feat, b = 0;
@@ -61,7 +62,7 @@ Sizes Sizes::of(const Weights& wt, const Plan& p) {
 
 struct Engine::Acts {
     float *x0, *body, *xa, *xb, *n1, *n1lo, *cmid, *cmidlo, *convx, *qkv, *attn, *attnlo, *hid, *hidlo, *chsum,
-        *casum, *gate, *headA, *headAlo, *headB, *headBlo, *din, *dout;
+        *casum, *gate, *headA, *headAlo, *headB, *headBlo, *din, *dout, *cabstat;
 };
 
 // ------------------------------------------------------------------ attention dispatch
@@ -201,7 +202,22 @@ void Engine::upload_weights() {
             }
         }
     }
+    // The folded conv weight and bias (one set, rewritten by each HAB's gate kernel).
+    size_t fold_off = total, fold_n = 0;
+    for (auto& kv : gw_)
+        if (kv.first.find("conv_block.cab.2.weight") != std::string::npos && kv.second.umma) {
+            fold_n = ((size_t)kv.second.n_pad * kv.second.k_pad + 63) / 64 * 64;
+            total += 2 * fold_n + ((size_t)kv.second.n_pad + 63) / 64 * 64;
+            break;
+        }
     HAT_CUDA(cudaMalloc(&dweights_, total * sizeof(float)));
+    fold_hi_ = fold_lo_ = fold_bias_ = nullptr;
+    if (fold_n) {
+        fold_hi_ = dweights_ + fold_off;
+        fold_lo_ = fold_hi_ + fold_n;
+        fold_bias_ = fold_lo_ + fold_n;
+        HAT_CUDA(cudaMemsetAsync(fold_hi_, 0, (total - fold_off) * sizeof(float), stream_));
+    }
     size_t off = 0;
     uint64_t* prev = g_launch_counter;
     g_launch_counter = &launches_;
@@ -255,7 +271,7 @@ void Engine::upload_weights() {
         throw;
     }
     g_launch_counter = prev;
-    if (off > total) throw Error(3, "gpu: weight arena overflow");
+    if (off > fold_off) throw Error(3, "gpu: weight arena overflow");
     HAT_CUDA(cudaStreamSynchronize(stream_));
 }
 
@@ -562,6 +578,7 @@ void Engine::ensure_plan(int h, int w) {
     a_->headBlo = take(s.headBlo);
     a_->din = take(s.din);
     a_->dout = take(s.dout);
+    a_->cabstat = take(s.cabstat);
     // THE PREDICTION IS HELD TO THE ALLOCATION (src/gpu.rs:779-786).
     if (q - arena_ != s.total()) throw Error(3, "gpu: the buffer set does not match the guard's prediction");
     plan_ = p;
@@ -600,6 +617,18 @@ void Engine::mlp(const std::string& p, float* x, Dst out) {
     e2.res = xo;
     mark("linear.fc2", 2.0 * P * hid * c, 4.0 * P * (hid + 2 * c));
     linear_m(p + ".mlp.fc2.weight", opnd_at(O(a_->hid, a_->hidlo), t0 * hid), yo, e2, P);
+}
+
+// Whether block `blk`'s CAB conv folds into its proj (k_proj_cab): tensor cores in use,
+// both weights in layouts the fused kernel takes, and patch-aligned planes.
+bool Engine::fold_ok(const std::string& blk) const {
+    if (simt_only_ || !fold_hi_ || plan_.wp % 16 || plan_.rows % 8 || wt_.compressed > 64) return false;
+    if (plan_.strip() && (plan_.halo % 8 || plan_.own() % 8)) return false;
+    const GemmW& w2 = G(blk + ".conv_block.cab.2.weight");
+    const GemmW& wpj = G(blk + ".attn.proj.weight");
+    if (!umma_proj_cab_ok(wpj, w2)) return false;
+    // parity mode: the operand planes are split the way the weights are
+    return mode_ != 0 || wpj.h16 == h16_;
 }
 
 // One HAB (hat_arch.py:266-309; src/gpu.rs:469-520): `in` is the block input, `out`
@@ -648,12 +677,30 @@ void Engine::hab(int stage, int blk, const float* in, float* out) {
         // Every row: the second conv reads one row past the strip's own rows.
         conv_res(cb + ".0.weight", O(a_->n1, a_->n1lo), c, D(a_->cmid, a_->cmidlo), cmid_ld_, 1, true, ec1);
     }
-    Epi ec2;
-    ec2.bias = W(cb + ".2.bias");
-    ec2.colsum = a_->chsum;
-    mark("conv.cab2", 18.0 * P * c * cc, 4.0 * P * (c + cc));
-    long rows = conv_res(cb + ".2.weight", O(a_->cmid, a_->cmidlo), cmid_ld_, Dst{a_->convx, nullptr}, c, 1,
-                         false, ec2);
+    // The second conv: folded into proj (its output never written; the pool's sums taken
+    // from its input), or on its own with per-tile channel sums of its output.
+    const bool fold = fold_ok(p);
+    // its input view: the plane's rows inside the image; output rows: the strip's own
+    int vlo = 0, vhi = plan_.rows;
+    if (plan_.strip()) {
+        if (plan_.r0 == 0) vlo = plan_.halo;
+        if (plan_.r1 == plan_.hp) vhi = plan_.halo + plan_.own();
+    }
+    const int ylo = plan_.strip() ? plan_.halo : 0, yhi = plan_.strip() ? plan_.halo + plan_.own() : plan_.rows;
+    long rows = 1;
+    if (fold) {
+        mark("cab.pool", 0, 4.0 * P * cc);
+        launch_cab_pool(opnd_at(O(a_->cmid, a_->cmidlo), (long)vlo * plan_.wp * cmid_ld_), cmid_ld_, cc, plan_.wp,
+                        vhi - vlo, ylo - vlo, yhi - vlo, a_->cabstat, W(cb + ".2.weight"), W(cb + ".2.bias"), c,
+                        a_->chsum, stream_);
+    } else {
+        Epi ec2;
+        ec2.bias = W(cb + ".2.bias");
+        ec2.colsum = a_->chsum;
+        mark("conv.cab2", 18.0 * P * c * cc, 4.0 * P * (c + cc));
+        rows = conv_res(cb + ".2.weight", O(a_->cmid, a_->cmidlo), cmid_ld_, Dst{a_->convx, nullptr}, c, 1, false,
+                        ec2);
+    }
     // The pool averages over the whole padded plane (src/gpu.rs:435); sharded, the
     // strips' channel sums are added across ranks first, on the communication stream while
     // the qkv linear and the attention run (the gate is first needed by proj).
@@ -688,12 +735,40 @@ void Engine::hab(int stage, int blk, const float* in, float* out) {
     // The channel-attention gate.
     mark("ca_gate", 0, 4.0 * rows * c);
     if (comm_) HAT_CUDA(cudaStreamWaitEvent(stream_, ev_ca_, 0));
+    CabFold cf;
+    if (fold) {
+        const GemmW& w2 = G(cb + ".2.weight");
+        const GemmW& wpj = G(p + ".attn.proj.weight");
+        cf.w = W(cb + ".2.weight");
+        cf.b2 = W(cb + ".2.bias");
+        cf.bp = W(p + ".attn.proj.bias");
+        cf.cs = wt_.conv_scale;
+        cf.factor = wpj.h16 ? 1.f / wpj.scale : 1.f;
+        cf.cc = cc;
+        cf.cinp = w2.cinp;
+        cf.k_pad = w2.k_pad;
+        cf.h16 = w2.h16;
+        cf.hi = fold_hi_;
+        cf.lo = fold_lo_;
+        cf.bias = fold_bias_;
+        cf.err = derr_;
+    }
     launch_ca_gate(pooled, rows, inv_count, W(cb + ".3.attention.1.weight"), W(cb + ".3.attention.1.bias"),
                    W(cb + ".3.attention.3.weight"), W(cb + ".3.attention.3.bias"), a_->gate, c, wt_.squeezed,
-                   stream_);
-    // proj, then `(shortcut + attn) + conv_x * conv_scale` in the epilogue.
+                   stream_, cf);
     // (over the strip's own rows when sharded: the next block exchanges the halo rows)
     const long t0 = own_t0(), Po = own_tokens();
+    if (fold) {
+        // proj + the gated conv in one accumulator, the residual in its epilogue.
+        mark("linear.proj_cab", 2.0 * Po * c * c + 18.0 * Po * c * cc, 12.0 * Po * c);
+        const Opnd cm = opnd_at(O(a_->cmid, a_->cmidlo), (long)vlo * plan_.wp * cmid_ld_);
+        umma_proj_cab(mode_, O(a_->attn, a_->attnlo), G(p + ".attn.proj.weight"), cm, cmid_ld_, vhi - vlo, vlo,
+                      G(cb + ".2.weight"), fold_hi_, fold_lo_, fold_bias_, in, out, plan_.rows, plan_.wp, ylo, yhi,
+                      derr_, stream_);
+        mlp(p, out, Dst{out, nullptr});
+        return;
+    }
+    // proj, then `(shortcut + attn) + conv_x * conv_scale` in the epilogue.
     Epi ep;
     ep.bias = W(p + ".attn.proj.bias");
     ep.res = in + t0 * c;

@@ -25,11 +25,12 @@ struct Sizes {
     long x0 = 0, body = 0, xa = 0, xb = 0, n1 = 0, n1lo = 0, cmid = 0, cmidlo = 0, convx = 0, qkv = 0, attn = 0,
          attnlo = 0, hid = 0, hidlo = 0;
     long chsum = 0, casum = 0, gate = 0, headA = 0, headAlo = 0, headB = 0, headBlo = 0, din = 0, dout = 0;
+    long cabstat = 0;  // per-row sums of the CAB's middle plane (launch_cab_pool)
     int cmid_stride = 0;  // channel stride of the CAB's middle plane
     static Sizes of(const Weights& wt, const Plan& p);
     long total() const {
         return x0 + body + xa + xb + n1 + n1lo + cmid + cmidlo + convx + qkv + attn + attnlo + hid + hidlo + chsum +
-               casum + gate + headA + headAlo + headB + headBlo + din + dout;
+               casum + gate + headA + headAlo + headB + headBlo + din + dout + cabstat;
     }
 };
 
@@ -130,6 +131,11 @@ private:
     int fallbacks_ = 0;
     // conv_last runs on the bandwidth kernel (k_conv_last.cu) when its shape fits.
     bool cl_ok_ = false;
+    // The CAB's second conv folded into proj (k_proj_cab): the gate-scaled conv weight in
+    // the tensor-core layout (hi, lo) and the folded bias, rewritten by every HAB's gate
+    // kernel; zero padding written once at upload.
+    float *fold_hi_ = nullptr, *fold_lo_ = nullptr, *fold_bias_ = nullptr;
+    bool fold_ok(const std::string& blk) const;
     int cmid_ld_ = 0;
     int device_ = 0, mode_ = 0;
     std::unique_ptr<Comm> comm_;

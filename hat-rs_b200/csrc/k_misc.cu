@@ -397,7 +397,7 @@ void launch_split(const float* x, float* hi, float* lo, long n, cudaStream_t st)
 // sums of the CAB's second conv over the plane; one CTA computes the gate.
 __global__ void k_ca_gate(const float* __restrict__ partial, long rows, float inv_count,
                           const float* __restrict__ w1, const float* __restrict__ b1, const float* __restrict__ w2,
-                          const float* __restrict__ b2, float* __restrict__ gate, int c, int sq) {
+                          const float* __restrict__ b2, float* __restrict__ gate, int c, int sq, const CabFold f) {
     // c <= 256: lanes cover channels (coalesced rows), warps stride the partial rows, and
     // the per-warp sums are combined in warp order, so the result is identical every run.
     __shared__ float red[32][257];
@@ -431,17 +431,190 @@ __global__ void k_ca_gate(const float* __restrict__ partial, long rows, float in
         if (lane == 0) hid[j] = fmaxf(a + b1[j], 0.f);
     }
     __syncthreads();
+    __shared__ float gs[256];
     for (int i = threadIdx.x; i < c; i += blockDim.x) {
         float a = b2[i];
         for (int j = 0; j < sq; ++j) a += w2[(long)i * sq + j] * hid[j];
-        gate[i] = 1.f / (1.f + expf(-a));
+        gs[i] = 1.f / (1.f + expf(-a));
+        gate[i] = gs[i];
+    }
+    if (!f.hi) return;
+    __syncthreads();
+    // The gate folded into the CAB conv's weight rows and proj's bias (k_proj_cab):
+    // W'[n][tap * cinp + ci] = conv_scale * gate[n] * w[n][ci][tap], times proj's factor.
+    for (int i = threadIdx.x; i < c; i += blockDim.x) f.bias[i] = f.bp[i] + f.cs * gs[i] * f.b2[i];
+    const int per = f.cc * 9;
+    bool big = false;
+    for (int i = threadIdx.x; i < c * per; i += blockDim.x) {
+        const int n = i / per, r = i - n * per, ci = r / 9, tap = r - ci * 9;
+        const float v = f.cs * gs[n] * f.w[i] * f.factor;  // w: [c][cc][3][3]
+        const long o = (long)n * f.k_pad + tap * f.cinp + ci;
+        if (f.h16) {
+            __half h, l;
+            split_h16(v, h, l);
+            reinterpret_cast<__half*>(f.hi)[o] = h;
+            reinterpret_cast<__half*>(f.lo)[o] = l;
+            big |= beyond_h16(v);
+        } else {
+            float h, l;
+            split_tf32(v, h, l);
+            f.hi[o] = h;
+            f.lo[o] = l;
+        }
+    }
+    if (big && f.err) atomicCAS(f.err, 0, ERR_RANGE_GEMM);
+}
+
+// ---------------------------------------------------------------- CAB pool, analytically
+// The channel-attention pool needs the sum over the output pixels of the CAB's second conv
+// (src/gpu.rs:435; hat_arch.py:40-57). As that conv is folded into proj (k_proj_cab), its
+// output is never written; the sum is taken from its input instead:
+//   sum_p conv(x)[p][n] = P * b[n] + sum_{tap, ci} w[n][ci][tap] * T[tap][ci],
+//   T[tap][ci] = sum over the output pixels p of x[p + tap offset][ci] (zero outside),
+// and T follows from per-row sums of x and its first and last columns: a tap shifted by
+// dy sums the rows [y0 + dy, y1 + dy) of the view, one shifted by dx = -1 (+1) leaves out
+// the last (first) column.
+
+// One CTA per view row r in [r_lo, r_hi): stat[r - r_lo] = {row sum, first, last}[cc].
+// The row is read as 16-byte vectors (8 fp16 or 4 fp32 channels of one pixel); thread t
+// takes the vectors t, t + nt, ..., all of one channel group since nt is a multiple of the
+// vectors per pixel, and the threads of a group are added in thread order.
+template <int VEC>
+__global__ void k_cab_rowstat(Opnd x, int ld, int cc, int wid, int r_lo, float* __restrict__ stat) {
+    __shared__ float part[256][VEC + 1];
+    const int vp = ld / VEC, nt = blockDim.x / vp * vp, t = threadIdx.x;
+    const long row = (long)(r_lo + blockIdx.x) * wid * ld;
+    const long nv = (long)wid * vp;
+    float a[VEC];
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) a[j] = 0.f;
+    if (t < nt) {
+        if (VEC == 8) {
+            const uint4* hv = reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(x.hi) + row);
+            const uint4* lv = reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(x.lo) + row);
+#pragma unroll 4
+            for (long v = t; v < nv; v += nt) {
+                const uint4 h = hv[v], l = lv[v];
+                const __half2* h2 = reinterpret_cast<const __half2*>(&h);
+                const __half2* l2 = reinterpret_cast<const __half2*>(&l);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float2 fh = __half22float2(h2[j]), fl = __half22float2(l2[j]);
+                    a[2 * j] += fh.x + fl.x;
+                    a[2 * j + 1] += fh.y + fl.y;
+                }
+            }
+        } else {
+            const float4* hv = reinterpret_cast<const float4*>(x.hi + row);
+            const float4* lv = x.lo ? reinterpret_cast<const float4*>(x.lo + row) : nullptr;
+#pragma unroll 4
+            for (long v = t; v < nv; v += nt) {
+                float4 h = hv[v];
+                if (lv) {
+                    const float4 l = lv[v];
+                    h.x += l.x;
+                    h.y += l.y;
+                    h.z += l.z;
+                    h.w += l.w;
+                }
+                a[0] += h.x;
+                a[1] += h.y;
+                a[2] += h.z;
+                a[3] += h.w;
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) part[t][j] = a[j];
+    __syncthreads();
+    auto val = [&](long e) {
+        if (x.lo && x.h16)
+            return __half2float(reinterpret_cast<const __half*>(x.hi)[e]) +
+                   __half2float(reinterpret_cast<const __half*>(x.lo)[e]);
+        return x.lo ? x.hi[e] + x.lo[e] : x.hi[e];
+    };
+    float* o = stat + (long)blockIdx.x * 3 * cc;
+    for (int ci = t; ci < cc; ci += blockDim.x) {
+        const int grp = ci / VEC, j = ci % VEC;
+        float s = 0.f;
+        for (int u = grp; u < nt; u += vp) s += part[u][j];
+        o[ci] = s;
+        o[cc + ci] = val(row + ci);
+        o[2 * cc + ci] = val(row + (long)(wid - 1) * ld + ci);
     }
 }
 
+// sum[n] for the output rows [y0, y1) of a view of `vrows` rows; `stat` holds the rows
+// [r_lo, r_hi) = [y0 - 1, y1 + 1) clipped to the view. The rows [y0, y1) are summed in
+// parallel (per value, PARTS interleaved partial sums added in order); a tap shifted by dy
+// = -1 / +1 then swaps the range's last / first row for the one beyond it.
+__global__ void k_cab_pool(const float* __restrict__ stat, int r_lo, int r_hi, int y0, int y1, int cc, int wid,
+                           const float* __restrict__ w, const float* __restrict__ b, int c, float* __restrict__ sum) {
+    __shared__ float part[1024];
+    __shared__ float S[3 * 64], T[9 * 64];
+    const int nvals = 3 * cc, parts = blockDim.x / nvals;
+    const int t = threadIdx.x, j = t % nvals, pp = t / nvals;
+    if (pp < parts) {
+        float a = 0.f;
+        for (int r = y0 + pp; r < y1; r += parts) a += stat[(long)(r - r_lo) * nvals + j];
+        part[t] = a;
+    }
+    __syncthreads();
+    if (t < nvals) {
+        float a = 0.f;
+        for (int u = 0; u < parts; ++u) a += part[u * nvals + t];
+        S[t] = a;
+    }
+    __syncthreads();
+    auto row = [&](int r, int k) { return r >= r_lo && r < r_hi ? stat[(long)(r - r_lo) * nvals + k] : 0.f; };
+    for (int i = t; i < 9 * cc; i += blockDim.x) {
+        const int tap = i / cc, ci = i - tap * cc, dy = tap / 3 - 1, dx = tap % 3 - 1;
+        float v[3];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {  // row sum, first column, last column over rows [y0 + dy, y1 + dy)
+            const int q = k * cc + ci;
+            v[k] = S[q];
+            if (dy < 0) v[k] = (v[k] - row(y1 - 1, q)) + row(y0 - 1, q);
+            if (dy > 0) v[k] = (v[k] - row(y0, q)) + row(y1, q);
+        }
+        T[i] = v[0] - (dx < 0 ? v[2] : 0.f) - (dx > 0 ? v[1] : 0.f);
+    }
+    __syncthreads();
+    const float pix = (float)((long)(y1 - y0) * wid);
+    for (int n = t; n < c; n += blockDim.x) {
+        float a = 0.f;
+        for (int ci = 0; ci < cc; ++ci)
+            for (int tap = 0; tap < 9; ++tap) a += w[((long)n * cc + ci) * 9 + tap] * T[tap * cc + ci];
+        sum[n] = pix * b[n] + a;
+    }
+}
+
+void launch_cab_pool(Opnd x, int ld, int cc, int wid, int vrows, int y0, int y1, float* stat, const float* w,
+                     const float* b, int c, float* sum, cudaStream_t st) {
+    if (cc > 64) throw Error(1, "cab pool: at most 64 compressed channels");
+    const int r_lo = max(0, y0 - 1), r_hi = min(vrows, y1 + 1);
+    if (r_hi <= r_lo) throw Error(1, "cab pool: empty row range");
+    const bool h16 = x.lo && x.h16;
+    const int vec = h16 ? 8 : 4;
+    if (ld % vec || ld / vec > 256 || (reinterpret_cast<uintptr_t>(x.hi) & 15) ||
+        (x.lo && (reinterpret_cast<uintptr_t>(x.lo) & 15)))
+        throw Error(1, "cab pool: the plane's rows must be whole 16-byte vectors");
+    if (h16)
+        k_cab_rowstat<8><<<(unsigned)(r_hi - r_lo), 256, 0, st>>>(x, ld, cc, wid, r_lo, stat);
+    else
+        k_cab_rowstat<4><<<(unsigned)(r_hi - r_lo), 256, 0, st>>>(x, ld, cc, wid, r_lo, stat);
+    HAT_CUDA(cudaGetLastError());
+    count_launch();
+    k_cab_pool<<<1, 1024, 0, st>>>(stat, r_lo, r_hi, y0, y1, cc, wid, w, b, c, sum);
+    HAT_CUDA(cudaGetLastError());
+    count_launch();
+}
+
 void launch_ca_gate(const float* partial, long rows, float inv_count, const float* w1, const float* b1,
-                    const float* w2, const float* b2, float* gate, int c, int sq, cudaStream_t st) {
+                    const float* w2, const float* b2, float* gate, int c, int sq, cudaStream_t st,
+                    const CabFold& fold) {
     if (c > 256 || sq > 64) throw Error(1, "channel attention: c > 256 or squeeze > 64 is not supported");
-    k_ca_gate<<<1, 1024, 0, st>>>(partial, rows, inv_count, w1, b1, w2, b2, gate, c, sq);
+    k_ca_gate<<<1, 1024, 0, st>>>(partial, rows, inv_count, w1, b1, w2, b2, gate, c, sq, fold);
     HAT_CUDA(cudaGetLastError());
     count_launch();
 }

@@ -1406,6 +1406,306 @@ __global__ void __launch_bounds__(64 + 32 * mlp_epi_warps(H16, SK), 1)
     }
 }
 
+// ------------------------------------------------------------------ proj + CAB conv2
+// The HAB's proj linear with the CAB's second conv folded into the same accumulator
+// (hat_arch.py:299-309: x = shortcut + attn_x + conv_x * conv_scale, conv_x = the CAB's
+// 3x3 conv cc -> c times its channel-attention gate):
+//
+//   out = res + bias' + Wp . attn + W2' (*) cmid       W2'[n] = conv_scale * gate[n] * W2[n]
+//                                                      bias'  = bp + conv_scale * gate * b2
+//
+// The gate scales whole output channels, so it folds into the conv's weight rows (written
+// for each block by the gate kernel, k_ca_gate) and the conv's output never exists as a
+// plane: no c-channel fp32 plane is written by the conv and read back by proj. The tiles
+// are the conv's 8 x 16 pixel patches of the [rows][W][*] planes; a tile's K loop runs
+// first over the attention output's channel chunks at the patch itself (128-byte k-block
+// rows), then over (tap, channel chunk) of the cmid view (`ckb_b`-byte rows, the patch
+// shifted by the tap, TMA's zero fill outside the view as the conv's zero padding). Both
+// weight parts carry proj's power-of-two factor, so one accumulator serves both. The
+// With 32-byte conv rows, four of the conv's k-blocks share one pipeline stage (a stage is
+// sized for 128-byte rows), so the short conv steps do not each wait out a load. The
+// epilogue is the residual ring of k_umma (EK_RING) on patches: a producer warp streams
+// the residual's 16-column chunks of the patch by TMA, the epilogue adds bias' and the
+// accumulator in place and stores two pixel rows per warp by TMA.
+struct ProjCabArgs {
+    int N, BN, ntn;
+    int KBa, klast_a;               // proj: k-blocks of 128-byte rows, k-steps of the last
+    int ckb_b, cchunks_b, klast_b;  // conv: bytes per k-block row, chunks per tap, k-steps of a tap's last
+    int tx, ty0, yoff_b;            // patches along x, first patch row, cmid view row of plane row 0
+    long ntiles;
+    float ascale;
+    int stages;
+    int slots;          // residual ring slots (at most PC_SLOTS_MAX)
+    const float* bias;  // bias' [N]
+    int* err;
+};
+
+// The residual ring of k_proj_cab takes the shared memory the two pipeline stages leave:
+// up to a tile and a half of 16-column chunks in flight, so that the residual's DRAM
+// latency is hidden behind the previous chunks (with four slots the epilogue waited on it).
+constexpr int PC_SLOTS_MAX = 12;
+
+template <int TERMS, bool H16>
+__global__ void __launch_bounds__(32 * 11, 1)
+    k_proj_cab(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
+               const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
+               const __grid_constant__ CUtensorMap tmCh, const __grid_constant__ CUtensorMap tmCl,
+               const __grid_constant__ CUtensorMap tmDh, const __grid_constant__ CUtensorMap tmDl,
+               const __grid_constant__ CUtensorMap tmR, const __grid_constant__ CUtensorMap tmY,
+               const ProjCabArgs g) {
+    constexpr int LEAD = 3, EW = 8, NT = 32 * (LEAD + EW), PARTS = EW / 4;
+    constexpr int ES = H16 ? 2 : 4;  // bytes per element
+    extern __shared__ __align__(1024) uint8_t smraw[];
+    __shared__ uint64_t full[6], empty[6], acc_full[2], acc_empty[2], drain;
+    __shared__ uint64_t rfull[2 * PC_SLOTS_MAX], rempty[PC_SLOTS_MAX];
+    __shared__ uint32_t tmem_slot;
+    __shared__ volatile int abort_flag;
+
+    uint8_t* sm = (uint8_t*)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
+    const int S = g.stages;
+    // per stage, sized for 128-byte rows: A hi | A lo | B hi | B lo
+    const uint32_t a_max = 128 * 128, b_max = (uint32_t)g.BN * 128;
+    const uint32_t st_bytes = 2 * a_max + 2 * b_max;
+    float* ring = reinterpret_cast<float*>(sm + S * st_bytes);  // RS x [128][16] fp32
+    const int RS = g.slots, RF = 2 * RS;  // slots, and "loaded" barriers as in EK_RING
+    // Pipeline steps of a tile: KBa proj k-blocks, then the conv's k-blocks G to a step.
+    const int KBb = 9 * g.cchunks_b, G = 128 / g.ckb_b;
+    const int NSTEP = g.KBa + (KBb + G - 1) / G;
+    const uint32_t a_sub = 128u * (uint32_t)g.ckb_b, b_sub = (uint32_t)g.BN * (uint32_t)g.ckb_b;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&acc_full[a], 1);
+            mbar_init(&acc_empty[a], 32 * EW);
+        }
+        mbar_init(&drain, 1);
+        for (int r = 0; r < RF; ++r) mbar_init(&rfull[r], 1);
+        for (int r = 0; r < RS; ++r) mbar_init(&rempty[r], 4);
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(&tmem_slot)));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            uint32_t it = 0;
+            bool ok = true;
+            for (long t = blockIdx.x; t < g.ntiles && ok && !abort_flag; t += gridDim.x) {
+                const long mt = t / g.ntn;
+                const int nt = (int)(t % g.ntn);
+                const int py = g.ty0 + (int)(mt / g.tx), px = (int)(mt % g.tx);
+                for (int st = 0; st < NSTEP; ++st, ++it) {
+                    const int s = it % S;
+                    const bool seg_a = st < g.KBa;
+                    const int kb0 = seg_a ? 0 : (st - g.KBa) * G, cnt = seg_a ? 1 : min(G, KBb - kb0);
+                    const uint32_t bytes = seg_a ? 128 * 128 + (uint32_t)g.BN * 128 : (uint32_t)cnt * (a_sub + b_sub);
+                    if (!mbar_wait(&empty[s], ((it / S) & 1) ^ 1, &abort_flag, g.err, 41)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(&full[s], TERMS == 3 ? 2 * bytes : bytes);
+                    uint8_t* b = sm + s * st_bytes;
+                    if (seg_a) {
+                        const int kel = st * (128 / ES);
+                        tma_3d(b, &tmAh, kel, px * 16, py * 8, &full[s]);
+                        if (TERMS == 3) tma_3d(b + a_max, &tmAl, kel, px * 16, py * 8, &full[s]);
+                        tma_2d(b + 2 * a_max, &tmBh, kel, nt * g.BN, &full[s]);
+                        if (TERMS == 3) tma_2d(b + 2 * a_max + b_max, &tmBl, kel, nt * g.BN, &full[s]);
+                    } else {
+                        const int cke = g.ckb_b / ES;
+                        for (int i = 0; i < cnt; ++i) {
+                            const int kb2 = kb0 + i, tap = kb2 / g.cchunks_b, cc = kb2 - tap * g.cchunks_b;
+                            const int x0 = px * 16 + tap % 3 - 1, y0 = py * 8 + tap / 3 - 1 + g.yoff_b;
+                            tma_3d(b + i * a_sub, &tmCh, cc * cke, x0, y0, &full[s]);
+                            if (TERMS == 3) tma_3d(b + a_max + i * a_sub, &tmCl, cc * cke, x0, y0, &full[s]);
+                            tma_2d(b + 2 * a_max + i * b_sub, &tmDh, kb2 * cke, nt * g.BN, &full[s]);
+                            if (TERMS == 3)
+                                tma_2d(b + 2 * a_max + b_max + i * b_sub, &tmDl, kb2 * cke, nt * g.BN, &full[s]);
+                        }
+                    }
+                }
+            }
+            if (abort_flag) {
+                for (uint32_t j = (it > (uint32_t)S ? it - S : 0); j < it; ++j) mbar_wait_quiet(&full[j % S], (j / S) & 1);
+            }
+        }
+    } else if (warp == 2) {
+        // ------------------------------------------------------------ residual stream
+        if (lane == 0) {
+            uint32_t k = 0;
+            const int nc = g.BN / 16;
+            bool ok = true;
+            for (long t = blockIdx.x; t < g.ntiles && ok && !abort_flag; t += gridDim.x) {
+                const long mt = t / g.ntn;
+                const int n0 = (int)(t % g.ntn) * g.BN;
+                const int py = g.ty0 + (int)(mt / g.tx), px = (int)(mt % g.tx);
+                for (int c = 0; c < nc; ++c, ++k) {
+                    const int s = (int)(k % RS);
+                    if (!mbar_wait(&rempty[s], ((k / RS) & 1) ^ 1, &abort_flag, g.err, 42)) {
+                        ok = false;
+                        break;
+                    }
+                    uint64_t* fb = &rfull[k % RF];
+                    mbar_expect_tx(fb, 8192u);
+                    tma_3d(ring + s * 2048, &tmR, n0 + 16 * c, px * 16, py * 8, fb);
+                }
+            }
+            if (abort_flag) {
+                for (uint32_t j = (k > (uint32_t)RS ? k - RS : 0); j < k; ++j) mbar_wait_quiet(&rfull[j % RF], (j / RF) & 1);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            uint32_t it = 0, tl = 0;
+            const uint32_t idesc = idesc_k<H16>(128, g.BN);
+            for (long t = blockIdx.x; t < g.ntiles && !abort_flag; t += gridDim.x, ++tl) {
+                const int a = tl & 1;
+                if (!mbar_wait(&acc_empty[a], ((tl >> 1) & 1) ^ 1, &abort_flag, g.err, 43)) break;
+                tc_fence_after();
+                const uint32_t d = tmem + a * 256;
+                bool ok = true;
+                for (int st = 0; st < NSTEP; ++st, ++it) {
+                    const int s = it % S;
+                    if (!mbar_wait(&full[s], (it / S) & 1, &abort_flag, g.err, 44)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const bool seg_a = st < g.KBa;
+                    const int ckb = seg_a ? 128 : g.ckb_b;
+                    const int kb0 = seg_a ? 0 : (st - g.KBa) * G, cnt = seg_a ? 1 : min(G, KBb - kb0);
+                    const uint32_t base = smem_u32(sm + s * st_bytes);
+#pragma unroll 1
+                    for (int i = 0; i < cnt; ++i) {
+                        int kst;
+                        if (seg_a)
+                            kst = st == g.KBa - 1 ? g.klast_a : 4;
+                        else
+                            kst = (kb0 + i) % g.cchunks_b == g.cchunks_b - 1 ? g.klast_b : ckb / 32;
+                        const uint32_t ah = base + (seg_a ? 0u : i * a_sub), al = ah + a_max;
+                        const uint32_t bh = base + 2 * a_max + (seg_a ? 0u : i * b_sub), bl = bh + b_max;
+#pragma unroll 1
+                        for (int k = 0; k < kst; ++k) {
+                            const uint32_t off = k * 32;
+                            const uint32_t acc0 = (st | i | k) ? 1u : 0u;
+                            if (TERMS == 3) {
+                                mma_k<H16>(d, smem_desc(al + off, ckb), smem_desc(bh + off, ckb), idesc, acc0);
+                                mma_k<H16>(d, smem_desc(ah + off, ckb), smem_desc(bl + off, ckb), idesc, 1u);
+                                mma_k<H16>(d, smem_desc(ah + off, ckb), smem_desc(bh + off, ckb), idesc, 1u);
+                            } else {
+                                mma_k<H16>(d, smem_desc(ah + off, ckb), smem_desc(bh + off, ckb), idesc, acc0);
+                            }
+                        }
+                    }
+                    mma_commit(&empty[s]);
+                }
+                if (!ok) break;
+                mma_commit(&acc_full[a]);
+            }
+            mma_commit(&drain);
+            mbar_wait_quiet(&drain, 0);
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int q = warp & 3;
+        const int ew = warp - LEAD;
+        const int part = ew >> 2;
+        const int sw = (lane >> 1) & 3;
+        const int nc = g.BN / 16;
+        uint32_t tl = 0;
+        for (long t = blockIdx.x; t < g.ntiles; t += gridDim.x, ++tl) {
+            if (__any_sync(0xffffffffu, abort_flag != 0)) break;
+            const int a = tl & 1;
+            const bool got = mbar_wait(&acc_full[a], (tl >> 1) & 1, &abort_flag, g.err, 45);
+            if (!__all_sync(0xffffffffu, got)) break;
+            tc_fence_after();
+            const long mt = t / g.ntn;
+            const int n0 = (int)(t % g.ntn) * g.BN;
+            const int py = g.ty0 + (int)(mt / g.tx), px = (int)(mt % g.tx);
+            const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + a * 256;
+            float bcur[16], bnext[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) bcur[j] = n0 + 16 * part + j < g.N ? __ldg(g.bias + n0 + 16 * part + j) : 0.f;
+            int pend = -1;
+            bool rok = true;
+#pragma unroll 1
+            for (int c0 = 16 * part; c0 < g.BN; c0 += 16 * PARTS) {
+                if (c0 + 16 * PARTS < g.BN) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int n = n0 + c0 + 16 * PARTS + j;
+                        bnext[j] = n < g.N ? __ldg(g.bias + n) : 0.f;
+                    }
+                }
+                const uint32_t k = tl * nc + (c0 >> 4);
+                const int s = (int)(k % RS);
+                const bool in = mbar_wait(&rfull[k % RF], (k / RF) & 1, &abort_flag, g.err, 46);
+                if (!__all_sync(0xffffffffu, in)) {
+                    rok = false;
+                    break;
+                }
+                float v[16];
+                tmem_ld16(taddr + c0, v);
+                float* rt = ring + s * 2048 + q * 512;  // this warp's 32 rows (two pixel rows) of the chunk
+#pragma unroll
+                for (int qq = 0; qq < 4; ++qq) {
+                    float4* p = reinterpret_cast<float4*>(rt + lane * 16 + 4 * (qq ^ sw));
+                    float4 r = *p;
+                    r.x = r.x + (v[4 * qq] * g.ascale + bcur[4 * qq]);
+                    r.y = r.y + (v[4 * qq + 1] * g.ascale + bcur[4 * qq + 1]);
+                    r.z = r.z + (v[4 * qq + 2] * g.ascale + bcur[4 * qq + 2]);
+                    r.w = r.w + (v[4 * qq + 3] * g.ascale + bcur[4 * qq + 3]);
+                    *p = r;
+                }
+                fence_proxy_async();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_3d(&tmY, rt, n0 + c0, px * 16, py * 8 + 2 * q);
+                    bulk_commit();
+                    if (pend >= 0) {
+                        asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+                        mbar_arrive(&rempty[pend]);
+                    }
+                }
+                pend = s;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) bcur[j] = bnext[j];
+            }
+            if (lane == 0 && pend >= 0) {
+                bulk_wait_read();
+                mbar_arrive(&rempty[pend]);
+            }
+            __syncwarp();
+            tc_fence_before();
+            mbar_arrive(&acc_empty[a]);
+            if (!rok) break;
+        }
+    }
+
+    if (warp >= LEAD && lane == 0) bulk_wait_all();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+    }
+}
+
 // ------------------------------------------------------------------ host side
 
 // cuTensorMapEncodeTiled, fetched from the driver through the runtime so the library
@@ -1702,6 +2002,113 @@ long umma_conv3x3(int mode, Opnd x, const GemmW& w, Dst y, int hgt, int wid, con
     g.ntiles = g.mtiles * g.ntn;
     launch_mode<1>(three, h16, tah, tal, tbh, tbl, g, e, st);
     return colsum_rows(g);
+}
+
+
+bool umma_proj_cab_ok(const GemmW& wp, const GemmW& w2) {
+    if (!wp.umma || !w2.umma || wp.conv || !w2.conv || wp.h16 != w2.h16) return false;
+    const int es = wp.h16 ? 2 : 4;
+    return wp.n == w2.n && wp.bn == w2.bn && wp.n_pad == w2.n_pad && wp.bn % 16 == 0 && wp.bn <= 256 &&
+           wp.n % 4 == 0 && (w2.ckb == 128 || w2.ckb == 32) &&
+           w2.cinp == (w2.cin + w2.ckb / es - 1) / (w2.ckb / es) * (w2.ckb / es) &&
+           w2.cin_plane % (16 / es) == 0;
+}
+
+template <int TERMS, bool H16>
+static void launch_proj_cab(const CUtensorMap* m, const ProjCabArgs& g0, cudaStream_t st) {
+    static const long cap = [] {
+        cudaFuncAttributes fa;
+        HAT_CUDA(cudaFuncGetAttributes(&fa, k_proj_cab<TERMS, H16>));
+        return 232448 - (long)fa.sharedSizeBytes;
+    }();
+    allow_dyn_smem(k_proj_cab<TERMS, H16>, (size_t)cap);
+    ProjCabArgs g = g0;
+    // two stages, the rest of the shared memory to the residual ring
+    const long per = 2L * 128 * 128 + 2L * g.BN * 128;
+    g.stages = 2;
+    g.slots = (int)std::min<long>(PC_SLOTS_MAX, (cap - 1024 - 2 * per) / 8192);
+    if (g.slots < 4) throw Error(1, "umma_proj_cab: the pipeline does not fit in shared memory");
+    const size_t smem = (size_t)g.stages * per + (size_t)g.slots * 8192 + 1024;
+    const long grid = std::min<long>(g.ntiles, num_sms());
+    k_proj_cab<TERMS, H16><<<(unsigned)grid, 32 * 11, smem, st>>>(m[0], m[1], m[2], m[3], m[4], m[5], m[6], m[7],
+                                                                    m[8], m[9], g);
+    HAT_CUDA(cudaGetLastError());
+    count_launch();
+}
+
+long umma_proj_cab(int mode, Opnd attn, const GemmW& wp, Opnd cmid, int cm_ld, int cm_rows, int cm_lo,
+                   const GemmW& w2, const float* w2hi, const float* w2lo, const float* bias, const float* res,
+                   float* out, int rows, int wid, int y_lo, int y_hi, int* err, cudaStream_t st) {
+    if (!umma_proj_cab_ok(wp, w2)) throw Error(1, "umma_proj_cab: weights not in the fused layout");
+    const bool three = mode == 0;
+    if (three && (!attn.lo || !cmid.lo)) throw Error(1, "umma_proj_cab: fp32-parity mode needs split operands");
+    const bool h16 = three && wp.h16;
+    if (three && (attn.h16 != h16 || cmid.h16 != h16)) throw Error(1, "umma_proj_cab: operand split kinds differ");
+    if (wid % 16 || y_lo % 8 || y_hi % 8 || y_lo < 0 || y_hi > rows || y_lo >= y_hi || cm_lo < 0 ||
+        cm_lo + cm_rows > rows || cm_ld < w2.cin)
+        throw Error(1, "umma_proj_cab: bad geometry");
+    auto a16 = [](const void* p) { return !(reinterpret_cast<uintptr_t>(p) & 15); };
+    if (!a16(res) || !a16(out) || !a16(attn.hi) || !a16(cmid.hi) || (three && (!a16(attn.lo) || !a16(cmid.lo))))
+        throw Error(1, "umma_proj_cab: planes must be 16-byte aligned");
+    const int es = h16 ? 2 : 4, kel = 128 / es, kstep = 32 / es, cke = w2.ckb / es;
+    const int c = wp.k, N = wp.n;
+    CUtensorMap m[10];
+    {   // attention output [rows][wid][c], patches of 16 x 8 pixels, 128-byte k-block rows
+        uint64_t d[3] = {(uint64_t)c, (uint64_t)wid, (uint64_t)rows};
+        uint64_t s2[2] = {(uint64_t)c * es, (uint64_t)wid * c * es};
+        uint32_t b[3] = {(uint32_t)kel, 16, 8};
+        m[0] = make_map(attn.hi, 3, d, s2, b, 128, h16);
+        m[1] = make_map(three ? attn.lo : attn.hi, 3, d, s2, b, 128, h16);
+    }
+    {   // proj weight [n_pad][k_pad]
+        uint64_t d[2] = {(uint64_t)wp.k_pad, (uint64_t)wp.n_pad}, s1[1] = {(uint64_t)wp.k_pad * es};
+        uint32_t b[2] = {(uint32_t)kel, (uint32_t)wp.bn};
+        m[2] = make_map(wp.hi, 2, d, s1, b, 128, h16);
+        m[3] = make_map(three ? wp.lo : wp.hi, 2, d, s1, b, 128, h16);
+    }
+    {   // the cmid view [cm_rows][wid][cm_ld]
+        uint64_t d[3] = {(uint64_t)cm_ld, (uint64_t)wid, (uint64_t)cm_rows};
+        uint64_t s2[2] = {(uint64_t)cm_ld * es, (uint64_t)wid * cm_ld * es};
+        uint32_t b[3] = {(uint32_t)cke, 16, 8};
+        m[4] = make_map(cmid.hi, 3, d, s2, b, w2.ckb, h16);
+        m[5] = make_map(three ? cmid.lo : cmid.hi, 3, d, s2, b, w2.ckb, h16);
+    }
+    {   // the folded conv weight [n_pad][9 * cinp]
+        uint64_t d[2] = {(uint64_t)w2.k_pad, (uint64_t)w2.n_pad}, s1[1] = {(uint64_t)w2.k_pad * es};
+        uint32_t b[2] = {(uint32_t)cke, (uint32_t)w2.bn};
+        m[6] = make_map(w2hi, 2, d, s1, b, w2.ckb, h16);
+        m[7] = make_map(three ? w2lo : w2hi, 2, d, s1, b, w2.ckb, h16);
+    }
+    {   // residual (patches, 16-column chunks) and output (two pixel rows per warp), fp32
+        uint64_t d[3] = {(uint64_t)N, (uint64_t)wid, (uint64_t)rows};
+        uint64_t s2[2] = {(uint64_t)N * 4, (uint64_t)wid * N * 4};
+        uint32_t br[3] = {16, 16, 8}, by[3] = {16, 16, 2};
+        m[8] = make_map(res, 3, d, s2, br, 64);
+        m[9] = make_map(out, 3, d, s2, by, 64);
+    }
+    ProjCabArgs g{};
+    g.N = N;
+    g.BN = wp.bn;
+    g.ntn = wp.n_pad / wp.bn;
+    g.KBa = (c + kel - 1) / kel;
+    g.klast_a = (c - (g.KBa - 1) * kel + kstep - 1) / kstep;
+    g.ckb_b = w2.ckb;
+    g.cchunks_b = (w2.cin + cke - 1) / cke;
+    g.klast_b = (w2.cin - (g.cchunks_b - 1) * cke + kstep - 1) / kstep;
+    g.tx = wid / 16;
+    g.ty0 = y_lo / 8;
+    g.yoff_b = -cm_lo;
+    g.ntiles = (long)((y_hi - y_lo) / 8) * g.tx * g.ntn;
+    g.ascale = h16 ? wp.scale : 1.f;
+    g.bias = bias;
+    g.err = err;
+    if (three && h16)
+        launch_proj_cab<3, true>(m, g, st);
+    else if (three)
+        launch_proj_cab<3, false>(m, g, st);
+    else
+        launch_proj_cab<1, false>(m, g, st);
+    return 0;
 }
 
 }  // namespace hat

@@ -71,6 +71,17 @@ bool umma_mlp_ok(const GemmW& w1, const GemmW& w2);
 long umma_mlp(int mode, Opnd x, const GemmW& w1, const float* b1, const GemmW& w2, const float* b2, const float* res,
               Dst y, long m, int* err, cudaStream_t st);
 
+// The HAB's proj linear with the CAB's second conv folded in (k_umma.cu, k_proj_cab):
+//   out = res + bias + wp . attn + W2' (*) cmid
+// over output rows [y_lo, y_hi) of the [rows][wid][*] planes. W2' (`w2hi`/`w2lo`) is
+// the conv weight `w2`'s tensor-core layout with each output row scaled by its gate and
+// conv_scale and by proj's power-of-two factor (k_ca_gate writes it); `cmid` is the view
+// of cm_rows rows starting at plane row cm_lo (zeros outside it), channel stride cm_ld.
+bool umma_proj_cab_ok(const GemmW& wp, const GemmW& w2);
+long umma_proj_cab(int mode, Opnd attn, const GemmW& wp, Opnd cmid, int cm_ld, int cm_rows, int cm_lo,
+                   const GemmW& w2, const float* w2hi, const float* w2lo, const float* bias, const float* res,
+                   float* out, int rows, int wid, int y_lo, int y_hi, int* err, cudaStream_t st);
+
 // CUDA-core launchers (read hi + lo when the operand is split); same return value.
 long simt_linear(Opnd x, const GemmW& w, Dst y, long m, const Epi& e, cudaStream_t st);
 long simt_conv3x3(Opnd x, const GemmW& w, Dst y, int hgt, int wid, const Epi& e, cudaStream_t st);

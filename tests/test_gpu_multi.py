@@ -85,7 +85,14 @@ def test_strip_over_two_gpus_one_handle(ckdir, variant, scale, h, w):
 
 def _silent_rank_main(rank, ckpt, img, q_id, q_out, q_resume, q_done):
     """One rank of a 2-rank strip job; every stage is reported to the parent as it ends."""
+    def leave():
+        q_out.close()
+        q_out.join_thread()  # the queue's feeder thread delivers what was put before the exit
+        os._exit(0)
+
     os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import faulthandler
+    faulthandler.enable()
     try:
         import time
         import torch
@@ -98,30 +105,37 @@ def _silent_rank_main(rank, ckpt, img, q_id, q_out, q_resume, q_done):
             uid = q_id.get(timeout=120)
         be.attach_strip(rank, 2, uid)
         h, w = img.shape[1:]
+        s = be.scale
+        r0, r1 = hat_b200.strip_rows(h, 2, rank)
+        mine = slice(r0 * s, min(r1, h) * s)  # the output rows this rank writes
         t0 = time.perf_counter()
         be.forward(h, w, img)  # two steps together: the eager pass, then the captured one
-        first = be.forward(h, w, img)
+        first = be.forward(h, w, img)[:, mine]
         q_out.put((rank, "step", time.perf_counter() - t0))
         be.set_timeout(3000)
         if rank == 1:
             # stops calling: stays alive and issues nothing until rank 0 has had its errors
             q_resume.get(timeout=300)
-            out = be.forward(h, w, img)
+            faulthandler.dump_traceback_later(30)
+            out = be.forward(h, w, img)[:, mine]
+            faulthandler.cancel_dump_traceback_later()
             q_out.put((rank, "resumed", bool(np.array_equal(out, first))))
             q_done.get(timeout=300)
-            os._exit(0)
+            leave()
         for stage in ("error", "again"):
             t = time.perf_counter()
             try:
                 be.forward(h, w, img)
                 q_out.put((rank, "no error", stage))
-                os._exit(0)
+                leave()
             except hat_b200.HatError as e:
                 q_out.put((rank, stage, (e.code, str(e), time.perf_counter() - t)))
         q_resume.put(1)
-        out = be.forward(h, w, img)
+        faulthandler.dump_traceback_later(30)
+        out = be.forward(h, w, img)[:, mine]
+        faulthandler.cancel_dump_traceback_later()
         q_out.put((rank, "resumed", bool(np.array_equal(out, first))))
-        os._exit(0)
+        leave()
     except Exception as e:
         q_out.put((rank, "exception", repr(e)))
 
@@ -152,6 +166,7 @@ def test_strip_rank_that_stops_calling_ends_in_an_error(ckdir):
             pr.join(timeout=60)
             if pr.exitcode is None:
                 pr.kill()
+        print("exit codes:", [pr.exitcode for pr in procs])
     assert (0, "step") in got and (1, "step") in got, got
     for stage in ("error", "again"):
         code, msg, waited = got[(0, stage)]
