@@ -56,6 +56,16 @@ CONFIGS = {
 }
 WEIGHT_SEED = 2024
 REF_GPU_S = 8.6      # seconds, README.md:18 of the reference (HAT-S x4 512x512, GPU, hardware unstated)
+# DRAM bytes (read + write) per launch of a kernel kind, each from one ncu capture of the
+# configuration-1 workload whose summary is committed under profiles/ (dram__bytes_read.sum +
+# dram__bytes_write.sum); reported as the roofline's `traffic` when that kind is the top one.
+TRAFFIC = {
+    "attn.window": (454.2e6 + 129.6e6, "profiles/k_attn_tc_window_hats_x4_512.md"),
+    "attn.overlap": (453.4e6 + 133.3e6, "profiles/k_attn_tc_overlap_hats_x4_512.md"),
+    "mlp.fused": (302.5e6 + 109.8e6, "profiles/k_mlp_fused_hats_x4_512.md"),
+    "linear.qkv": (151.4e6 + 399.8e6, "profiles/k_umma_linear_qkv_hats_x4_512.md"),
+    "layernorm": (151.0e6 + 98.9e6, "profiles/k_layernorm_bulk_hats_x4_512.md"),
+}
 PARITY_TOL = 1e-4    # src/main.rs:310 VERIFY_TOL
 PSNR_MIN = 50.0      # fast-mode bar
 
@@ -356,6 +366,8 @@ def run_ours(args, wl: Workload):
                         key=lambda kv: kv[1]["ms"])
     hbm, tf, src = peaks()
     total_ms = sum(v["ms"] for v in prof.values())
+    traffic, traffic_src = TRAFFIC.get(top_kind, (None, None)) if wl.cfg == 1 and mode == hat_b200.MODE_PARITY \
+        else (None, None)
     parity = mode == hat_b200.MODE_PARITY
     h16 = be.fp16_pairs()
     if top["flops"] > 0:
@@ -366,7 +378,7 @@ def run_ours(args, wl: Workload):
         terms = 3 if parity else 1
         pipe_peak = tf if h16 else tf / 2
         roof = {"kernel": top_kind, "bound": "tensor", "achieved": achieved, "peak": tf,
-                "unit": "TFLOP/s", "frac": achieved / tf, "traffic": None,
+                "unit": "TFLOP/s", "frac": achieved / tf, "traffic": traffic, "traffic_source": traffic_src,
                 "peak_source": f"{src} bf16 dense (MEASURED_PEAKS.json)",
                 "pipe_frac": terms * achieved / pipe_peak, "pipe_kind": "f16" if h16 else "tf32",
                 "share_of_pass": top["ms"] / total_ms, "launches": top["launches"],
@@ -375,7 +387,8 @@ def run_ours(args, wl: Workload):
     else:
         achieved = top["bytes"] / (top["ms"] / 1e3) / 1e9
         roof = {"kernel": top_kind, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                "frac": achieved / hbm, "traffic": None, "peak_source": f"{src} HBM copy",
+                "frac": achieved / hbm, "traffic": traffic, "traffic_source": traffic_src,
+                "peak_source": f"{src} HBM copy",
                 "share_of_pass": top["ms"] / total_ms, "launches": top["launches"],
                 "alg_bytes_per_launch": top["bytes"] / max(top["launches"], 1)}
 
