@@ -18,7 +18,8 @@ import pytest
 from golden_io import GOLDEN, cases, checkpoint_for, read_hatf
 from oracle import hat_oracle as O
 
-REFERENCE = Path(os.environ.get("HAT_REFERENCE", "/root/reference"))
+# The reference checkout: $HAT_REFERENCE, else a `reference` directory beside this repository.
+REFERENCE = Path(os.environ.get("HAT_REFERENCE", Path(__file__).resolve().parents[2] / "reference"))
 
 
 @pytest.fixture(scope="module")
