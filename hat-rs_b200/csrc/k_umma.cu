@@ -102,14 +102,14 @@ __device__ __forceinline__ void tma_3d(void* dst, const CUtensorMap* map, int c0
 }
 
 // Shared-memory matrix descriptor: K-major, rows of `rowbytes` (128: SWIZZLE_128B,
-// 32: SWIZZLE_32B), 8-row core groups `8*rowbytes` apart.
+// 64: SWIZZLE_64B, 32: SWIZZLE_32B), 8-row core groups `8*rowbytes` apart.
 __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, int rowbytes) {
     uint64_t d = 0;
     d |= (uint64_t)((saddr & 0x3FFFF) >> 4);
     d |= (uint64_t)1 << 16;                              // leading byte offset (unused here)
     d |= (uint64_t)((8 * rowbytes) >> 4) << 32;          // stride byte offset
     d |= (uint64_t)1 << 46;                              // descriptor version (sm_100)
-    d |= (uint64_t)(rowbytes == 128 ? 2 : 6) << 61;      // swizzle mode
+    d |= (uint64_t)(rowbytes == 128 ? 2 : rowbytes == 64 ? 4 : 6) << 61;  // swizzle mode
     return d;
 }
 // Instruction descriptor: f32 accumulate, both operands K-major; A/B format 2 (tf32)
@@ -1429,7 +1429,7 @@ __global__ void __launch_bounds__(64 + 32 * mlp_epi_warps(H16, SK), 1)
 // accumulator in place and stores two pixel rows per warp by TMA.
 struct ProjCabArgs {
     int N, BN, ntn;
-    int KBa, klast_a;               // proj: k-blocks of 128-byte rows, k-steps of the last
+    int KBa, klast_a;               // proj: k-blocks of 64-byte rows, k-steps of the last
     int ckb_b, cchunks_b, klast_b;  // conv: bytes per k-block row, chunks per tap, k-steps of a tap's last
     int tx, ty0, yoff_b;            // patches along x, first patch row, cmid view row of plane row 0
     long ntiles;
@@ -1440,10 +1440,10 @@ struct ProjCabArgs {
     int* err;
 };
 
-// The residual ring of k_proj_cab takes the shared memory the two pipeline stages leave:
-// up to a tile and a half of 16-column chunks in flight, so that the residual's DRAM
-// latency is hidden behind the previous chunks (with four slots the epilogue waited on it).
-constexpr int PC_SLOTS_MAX = 12;
+// Pipeline stages of k_proj_cab hold 64-byte k-block rows (a 128-byte row per stage left
+// room for two stages only, and the K loop waited out every load); the residual ring
+// takes PC_SLOTS of 16-column chunks.
+constexpr int PC_SLOTS_MAX = 12, PC_SLOTS = 6;
 
 template <int TERMS, bool H16>
 __global__ void __launch_bounds__(32 * 11, 1)
@@ -1463,13 +1463,13 @@ __global__ void __launch_bounds__(32 * 11, 1)
 
     uint8_t* sm = (uint8_t*)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
     const int S = g.stages;
-    // per stage, sized for 128-byte rows: A hi | A lo | B hi | B lo
-    const uint32_t a_max = 128 * 128, b_max = (uint32_t)g.BN * 128;
+    // per stage, sized for 64-byte rows: A hi | A lo | B hi | B lo
+    const uint32_t a_max = 128 * 64, b_max = (uint32_t)g.BN * 64;
     const uint32_t st_bytes = 2 * a_max + 2 * b_max;
     float* ring = reinterpret_cast<float*>(sm + S * st_bytes);  // RS x [128][16] fp32
     const int RS = g.slots, RF = 2 * RS;  // slots, and "loaded" barriers as in EK_RING
     // Pipeline steps of a tile: KBa proj k-blocks, then the conv's k-blocks G to a step.
-    const int KBb = 9 * g.cchunks_b, G = 128 / g.ckb_b;
+    const int KBb = 9 * g.cchunks_b, G = 64 / g.ckb_b;
     const int NSTEP = g.KBa + (KBb + G - 1) / G;
     const uint32_t a_sub = 128u * (uint32_t)g.ckb_b, b_sub = (uint32_t)g.BN * (uint32_t)g.ckb_b;
 
@@ -1511,7 +1511,7 @@ __global__ void __launch_bounds__(32 * 11, 1)
                     const int s = it % S;
                     const bool seg_a = st < g.KBa;
                     const int kb0 = seg_a ? 0 : (st - g.KBa) * G, cnt = seg_a ? 1 : min(G, KBb - kb0);
-                    const uint32_t bytes = seg_a ? 128 * 128 + (uint32_t)g.BN * 128 : (uint32_t)cnt * (a_sub + b_sub);
+                    const uint32_t bytes = seg_a ? a_max + b_max : (uint32_t)cnt * (a_sub + b_sub);
                     if (!mbar_wait(&empty[s], ((it / S) & 1) ^ 1, &abort_flag, g.err, 41)) {
                         ok = false;
                         break;
@@ -1519,7 +1519,7 @@ __global__ void __launch_bounds__(32 * 11, 1)
                     mbar_expect_tx(&full[s], TERMS == 3 ? 2 * bytes : bytes);
                     uint8_t* b = sm + s * st_bytes;
                     if (seg_a) {
-                        const int kel = st * (128 / ES);
+                        const int kel = st * (64 / ES);
                         tma_3d(b, &tmAh, kel, px * 16, py * 8, &full[s]);
                         if (TERMS == 3) tma_3d(b + a_max, &tmAl, kel, px * 16, py * 8, &full[s]);
                         tma_2d(b + 2 * a_max, &tmBh, kel, nt * g.BN, &full[s]);
@@ -1586,14 +1586,14 @@ __global__ void __launch_bounds__(32 * 11, 1)
                     }
                     tc_fence_after();
                     const bool seg_a = st < g.KBa;
-                    const int ckb = seg_a ? 128 : g.ckb_b;
+                    const int ckb = seg_a ? 64 : g.ckb_b;
                     const int kb0 = seg_a ? 0 : (st - g.KBa) * G, cnt = seg_a ? 1 : min(G, KBb - kb0);
                     const uint32_t base = smem_u32(sm + s * st_bytes);
 #pragma unroll 1
                     for (int i = 0; i < cnt; ++i) {
                         int kst;
                         if (seg_a)
-                            kst = st == g.KBa - 1 ? g.klast_a : 4;
+                            kst = st == g.KBa - 1 ? g.klast_a : 2;
                         else
                             kst = (kb0 + i) % g.cchunks_b == g.cchunks_b - 1 ? g.klast_b : ckb / 32;
                         const uint32_t ah = base + (seg_a ? 0u : i * a_sub), al = ah + a_max;
@@ -2007,10 +2007,10 @@ long umma_conv3x3(int mode, Opnd x, const GemmW& w, Dst y, int hgt, int wid, con
 
 bool umma_proj_cab_ok(const GemmW& wp, const GemmW& w2) {
     if (!wp.umma || !w2.umma || wp.conv || !w2.conv || wp.h16 != w2.h16) return false;
-    const int es = wp.h16 ? 2 : 4;
+    // the kernel's conv chunk (64-byte rows at most) must tile the weight's K layout per tap
+    const int es = wp.h16 ? 2 : 4, cke = std::min(w2.ckb, 64) / es;
     return wp.n == w2.n && wp.bn == w2.bn && wp.n_pad == w2.n_pad && wp.bn % 16 == 0 && wp.bn <= 256 &&
-           wp.n % 4 == 0 && (w2.ckb == 128 || w2.ckb == 32) &&
-           w2.cinp == (w2.cin + w2.ckb / es - 1) / (w2.ckb / es) * (w2.ckb / es) &&
+           wp.n % 4 == 0 && (w2.ckb == 128 || w2.ckb == 32) && w2.cinp == (w2.cin + cke - 1) / cke * cke &&
            w2.cin_plane % (16 / es) == 0;
 }
 
@@ -2023,11 +2023,10 @@ static void launch_proj_cab(const CUtensorMap* m, const ProjCabArgs& g0, cudaStr
     }();
     allow_dyn_smem(k_proj_cab<TERMS, H16>, (size_t)cap);
     ProjCabArgs g = g0;
-    // two stages, the rest of the shared memory to the residual ring
-    const long per = 2L * 128 * 128 + 2L * g.BN * 128;
-    g.stages = 2;
-    g.slots = (int)std::min<long>(PC_SLOTS_MAX, (cap - 1024 - 2 * per) / 8192);
-    if (g.slots < 4) throw Error(1, "umma_proj_cab: the pipeline does not fit in shared memory");
+    const long per = 2L * 128 * 64 + 2L * g.BN * 64;
+    g.slots = PC_SLOTS;
+    g.stages = (int)std::min<long>(6, (cap - 1024 - (long)g.slots * 8192) / per);
+    if (g.stages < 2) throw Error(1, "umma_proj_cab: the pipeline does not fit in shared memory");
     const size_t smem = (size_t)g.stages * per + (size_t)g.slots * 8192 + 1024;
     const long grid = std::min<long>(g.ntiles, num_sms());
     k_proj_cab<TERMS, H16><<<(unsigned)grid, 32 * 11, smem, st>>>(m[0], m[1], m[2], m[3], m[4], m[5], m[6], m[7],
@@ -2050,34 +2049,37 @@ long umma_proj_cab(int mode, Opnd attn, const GemmW& wp, Opnd cmid, int cm_ld, i
     auto a16 = [](const void* p) { return !(reinterpret_cast<uintptr_t>(p) & 15); };
     if (!a16(res) || !a16(out) || !a16(attn.hi) || !a16(cmid.hi) || (three && (!a16(attn.lo) || !a16(cmid.lo))))
         throw Error(1, "umma_proj_cab: planes must be 16-byte aligned");
-    const int es = h16 ? 2 : 4, kel = 128 / es, kstep = 32 / es, cke = w2.ckb / es;
+    // 64-byte k-block rows for both parts (32 fp16 or 16 tf32 elements); the conv's chunk
+    // of a tap is its weight layout's chunk, or half of it for 128-byte chunks.
+    const int ckb_b = std::min(w2.ckb, 64);
+    const int es = h16 ? 2 : 4, kel = 64 / es, kstep = 32 / es, cke = ckb_b / es;
     const int c = wp.k, N = wp.n;
     CUtensorMap m[10];
     {   // attention output [rows][wid][c], patches of 16 x 8 pixels, 128-byte k-block rows
         uint64_t d[3] = {(uint64_t)c, (uint64_t)wid, (uint64_t)rows};
         uint64_t s2[2] = {(uint64_t)c * es, (uint64_t)wid * c * es};
         uint32_t b[3] = {(uint32_t)kel, 16, 8};
-        m[0] = make_map(attn.hi, 3, d, s2, b, 128, h16);
-        m[1] = make_map(three ? attn.lo : attn.hi, 3, d, s2, b, 128, h16);
+        m[0] = make_map(attn.hi, 3, d, s2, b, 64, h16);
+        m[1] = make_map(three ? attn.lo : attn.hi, 3, d, s2, b, 64, h16);
     }
     {   // proj weight [n_pad][k_pad]
         uint64_t d[2] = {(uint64_t)wp.k_pad, (uint64_t)wp.n_pad}, s1[1] = {(uint64_t)wp.k_pad * es};
         uint32_t b[2] = {(uint32_t)kel, (uint32_t)wp.bn};
-        m[2] = make_map(wp.hi, 2, d, s1, b, 128, h16);
-        m[3] = make_map(three ? wp.lo : wp.hi, 2, d, s1, b, 128, h16);
+        m[2] = make_map(wp.hi, 2, d, s1, b, 64, h16);
+        m[3] = make_map(three ? wp.lo : wp.hi, 2, d, s1, b, 64, h16);
     }
     {   // the cmid view [cm_rows][wid][cm_ld]
         uint64_t d[3] = {(uint64_t)cm_ld, (uint64_t)wid, (uint64_t)cm_rows};
         uint64_t s2[2] = {(uint64_t)cm_ld * es, (uint64_t)wid * cm_ld * es};
         uint32_t b[3] = {(uint32_t)cke, 16, 8};
-        m[4] = make_map(cmid.hi, 3, d, s2, b, w2.ckb, h16);
-        m[5] = make_map(three ? cmid.lo : cmid.hi, 3, d, s2, b, w2.ckb, h16);
+        m[4] = make_map(cmid.hi, 3, d, s2, b, ckb_b, h16);
+        m[5] = make_map(three ? cmid.lo : cmid.hi, 3, d, s2, b, ckb_b, h16);
     }
     {   // the folded conv weight [n_pad][9 * cinp]
         uint64_t d[2] = {(uint64_t)w2.k_pad, (uint64_t)w2.n_pad}, s1[1] = {(uint64_t)w2.k_pad * es};
         uint32_t b[2] = {(uint32_t)cke, (uint32_t)w2.bn};
-        m[6] = make_map(w2hi, 2, d, s1, b, w2.ckb, h16);
-        m[7] = make_map(three ? w2lo : w2hi, 2, d, s1, b, w2.ckb, h16);
+        m[6] = make_map(w2hi, 2, d, s1, b, ckb_b, h16);
+        m[7] = make_map(three ? w2lo : w2hi, 2, d, s1, b, ckb_b, h16);
     }
     {   // residual (patches, 16-column chunks) and output (two pixel rows per warp), fp32
         uint64_t d[3] = {(uint64_t)N, (uint64_t)wid, (uint64_t)rows};
@@ -2092,7 +2094,7 @@ long umma_proj_cab(int mode, Opnd attn, const GemmW& wp, Opnd cmid, int cm_ld, i
     g.ntn = wp.n_pad / wp.bn;
     g.KBa = (c + kel - 1) / kel;
     g.klast_a = (c - (g.KBa - 1) * kel + kstep - 1) / kstep;
-    g.ckb_b = w2.ckb;
+    g.ckb_b = ckb_b;
     g.cchunks_b = (w2.cin + cke - 1) / cke;
     g.klast_b = (w2.cin - (g.cchunks_b - 1) * cke + kstep - 1) / kstep;
     g.tx = wid / 16;
