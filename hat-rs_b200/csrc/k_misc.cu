@@ -580,12 +580,20 @@ __global__ void k_cab_pool(const float* __restrict__ stat, int r_lo, int r_hi, i
         T[i] = v[0] - (dx < 0 ? v[2] : 0.f) - (dx > 0 ? v[1] : 0.f);
     }
     __syncthreads();
+    // One warp per output channel: the lanes take the channel's 9 * cc weights in turn
+    // (coalesced) and a fixed shuffle tree adds them.
     const float pix = (float)((long)(y1 - y0) * wid);
-    for (int n = t; n < c; n += blockDim.x) {
+    const int warp = t >> 5, lane = t & 31, nw = blockDim.x >> 5, K = 9 * cc;
+    for (int n = warp; n < c; n += nw) {
+        const float* wn = w + (long)n * K;  // [ci][tap]
         float a = 0.f;
-        for (int ci = 0; ci < cc; ++ci)
-            for (int tap = 0; tap < 9; ++tap) a += w[((long)n * cc + ci) * 9 + tap] * T[tap * cc + ci];
-        sum[n] = pix * b[n] + a;
+        for (int i = lane; i < K; i += 32) {
+            const int ci = i / 9, tap = i - ci * 9;
+            a += wn[i] * T[tap * cc + ci];
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+        if (lane == 0) sum[n] = pix * b[n] + a;
     }
 }
 
